@@ -1,0 +1,359 @@
+#!/usr/bin/env python3
+"""Headline benchmark: the Q8_0 decode GEMV y = W.x, W[8192, 2048] (GGUF logical
+{2048, 8192}), x fp32[1, 2048] -- Tensor::matmul's Q8_0 branch
+(src/tensor/tensor.cpp:328-382) on one token, the hot loop of the 1B decode.
+
+Metric: HBM GB/s of algorithmic bytes (Q8_0 weight blocks + x + y per GEMV,
+17,866,752 B).  A step is one GEMV over one weight matrix.  32 weight copies
+(571 MB, more than 4x the 126 MB L2) rotate, so every step reads its weights
+from HBM.
+
+  value  -- device-resident x and W, K steps replayed from a CUDA graph,
+            timed with CUDA events on the launching stream (max over ranks).
+  e2e    -- the same GEMV through the C ABI with x copied from pinned host
+            memory and y copied back to pinned host memory every step (weights
+            resident, uploaded once as the Storage layer does).
+  roofline -- the GEMV kernel alone: bytes per launch / average launch time.
+  cpu_baseline -- the reference's own CPU GEMV (oracle/_ref, built from the
+            reference sources) on this host's cores, rank 0 only.
+
+--impl reference runs the reference CPU implementation on the same config
+(rank 0; other ranks exit 0).  Multi-GPU (torchrun): each rank runs its own row
+shard of a [8192*N, 2048] matrix (weak scaling, no collective on the path).
+"""
+import argparse
+import ctypes
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "turbo.cpp_b200", "python"))
+
+N_ROWS, K_COLS = 8192, 2048
+ROW_BYTES = K_COLS // 32 * 34
+W_BYTES = N_ROWS * ROW_BYTES                      # 17,825,792
+ALGO_BYTES = W_BYTES + K_COLS * 4 + N_ROWS * 4    # 17,866,752 per GEMV
+N_COPIES = 32
+METRIC = "Q8_0 decode GEMV HBM GB/s (W[8192,2048] Q8_0, x fp32[1,2048])"
+WORKLOAD = "q8_0_gemv_8192x2048"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def load_traffic():
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return json.load(f).get(WORKLOAD)
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), "--query-gpu=" + q,
+                                          "--format=csv,noheader,nounits", "-lms", "50"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.reader = threading.Thread(target=self._read, daemon=True)
+            self.reader.start()
+            time.sleep(0.3)
+        except FileNotFoundError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        sm.sort()
+        return {"sm_mhz": sm[len(sm) // 2], "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+def cpu_reference_rate(seconds=10.0, max_steps=None):
+    """Times the reference's own Q8_0 GEMV (oracle/_ref) on all host cores.
+    Returns (GB/s, steps, cores, seconds)."""
+    cores = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(cores)
+    import numpy as np
+    from oracle import refbind as R
+    from turbo_b200 import synth
+    wq = synth.quantize_q8_0(synth.normal((N_ROWS, K_COLS), 0.02, seed=0))
+    x = synth.normal((1, K_COLS), 1.0, seed=1)
+    y = np.zeros((1, N_ROWS), np.float32)
+    L = R.lib()
+    L.ref_matmul_quant_repeat(R.ptr(x), 1, K_COLS, R.ptr(wq), R.DT_Q8_0, N_ROWS, R.ptr(y), 3)
+    t0 = time.perf_counter()
+    L.ref_matmul_quant_repeat(R.ptr(x), 1, K_COLS, R.ptr(wq), R.DT_Q8_0, N_ROWS, R.ptr(y), 10)
+    per = (time.perf_counter() - t0) / 10
+    steps = max(1, int(seconds / per))
+    if max_steps:
+        steps = min(steps, max_steps)
+    t0 = time.perf_counter()
+    L.ref_matmul_quant_repeat(R.ptr(x), 1, K_COLS, R.ptr(wq), R.DT_Q8_0, N_ROWS, R.ptr(y), steps)
+    dt = time.perf_counter() - t0
+    return ALGO_BYTES * steps / dt / 1e9, steps, cores, dt
+
+
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    from oracle import refbind as R
+    if not R.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libturbo_ref.so was not built"}))
+        return 0
+    # warmup steps, then a bounded sample of the K requested steps (<= ~60 s)
+    gbs, steps, cores, dt = cpu_reference_rate(seconds=60.0, max_steps=args.steps)
+    ms = dt / steps * 1e3
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
+        "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "N": N_ROWS, "K": K_COLS, "M": 1,
+                                        "requested_steps": args.steps},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "reference",
+                         "sample": "%d full GEMVs (Tensor::matmul Q8_0, OpenMP over %d threads)" % (steps, cores)},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import turbo_b200 as T
+    from turbo_b200 import synth
+
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if ws > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    T.call("tb_init", local)
+    stream = torch.cuda.Stream()
+    sh = T.stream_handle(stream)
+
+    # Inputs: this rank's row shard, quantized once on the host and uploaded.
+    w_host = synth.quantize_q8_0(synth.normal((N_ROWS, K_COLS), 0.02, seed=100 + rank))
+    x_host = synth.normal((1, K_COLS), 1.0, seed=1)
+    w0 = torch.from_numpy(w_host.ravel()).cuda()
+    wcopies = [w0] + [w0.clone() for _ in range(N_COPIES - 1)]
+    x = torch.from_numpy(x_host).cuda()
+    y = torch.empty((1, N_ROWS), dtype=torch.float32, device="cuda")
+
+    def gemv(i, s=sh, xx=x, yy=y):
+        T.check(T.load().tb_matmul_quant(T.Q8_0, T.ptr(xx), 1, K_COLS, T.ptr(wcopies[i % N_COPIES]),
+                                         N_ROWS, T.ptr(yy), s), "tb_matmul_quant")
+
+    # correctness gate before timing: bit-exact against the oracle on rank 0
+    with torch.cuda.stream(stream):
+        gemv(0)
+    stream.synchronize()
+    if rank == 0:
+        from oracle import orbind as O
+        ref = O.matmul_q8_0(x_host, w_host, N_ROWS)
+        got = y.cpu().numpy()
+        if not np.array_equal(got.view(np.uint32), ref.view(np.uint32)):
+            raise SystemExit("GEMV result differs from the oracle; not timing")
+
+    # warmup
+    with torch.cuda.stream(stream):
+        for i in range(args.warmup):
+            gemv(i)
+    stream.synchronize()
+
+    # --- per-launch kernel time (events around single launches) -------------
+    n_single = min(200, max(32, args.steps // 100))
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(n_single)]
+    with torch.cuda.stream(stream):
+        for i, (a, b) in enumerate(evs):
+            a.record(stream)
+            gemv(i)
+            b.record(stream)
+    stream.synchronize()
+    single_ms = sorted(a.elapsed_time(b) for a, b in evs)
+    kernel_ms = sum(single_ms) / len(single_ms)
+
+    # --- value: K steps replayed from CUDA graphs --------------------------------
+    G = N_COPIES
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(G):
+            gemv(i, s=T.stream_handle(torch.cuda.current_stream()))
+    tail = args.steps % G
+    graph_tail = None
+    if tail:
+        graph_tail = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph_tail, stream=stream):
+            for i in range(tail):
+                gemv(i, s=T.stream_handle(torch.cuda.current_stream()))
+    with torch.cuda.stream(stream):
+        graph.replay()
+    stream.synchronize()
+
+    if ws > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        with torch.cuda.stream(stream):
+            start.record(stream)
+            for _ in range(args.steps // G):
+                graph.replay()
+            if graph_tail is not None:
+                graph_tail.replay()
+            end.record(stream)
+        stream.synchronize()
+    torch.cuda.synchronize()
+    total_ms = start.elapsed_time(end)
+    if ws > 1:
+        t = torch.tensor([total_ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        total_ms = float(t.item())
+        torch.distributed.barrier()
+
+    # --- e2e: x from pinned host, y back to pinned host, through the C ABI -----
+    e2e_steps = min(args.steps, 2000)
+    xh = torch.from_numpy(x_host.copy()).pin_memory()
+    yh = torch.empty((1, N_ROWS), dtype=torch.float32).pin_memory()
+    L = T.load()
+
+    def e2e_step(i):
+        T.check(L.tb_upload(T.ptr(x), ctypes.c_void_p(xh.data_ptr()), K_COLS * 4, sh))
+        gemv(i)
+        T.check(L.tb_download(ctypes.c_void_p(yh.data_ptr()), T.ptr(y), N_ROWS * 4, sh))
+
+    for i in range(3):
+        e2e_step(i)
+    stream.synchronize()
+    if ws > 1:
+        torch.distributed.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e1.record(stream)
+    stream.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if ws > 1:
+        t = torch.tensor([e2e_ms], device="cuda")
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    del graph, graph_tail
+    if ws > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    peak, peak_kind = load_peaks()
+    value = ALGO_BYTES * args.steps * ws / (total_ms * 1e-3) / 1e9
+    achieved = ALGO_BYTES / (kernel_ms * 1e-3) / 1e9
+    e2e_gbs = ALGO_BYTES * e2e_steps * ws / (e2e_ms * 1e-3) / 1e9
+    cpu = None
+    if not args.no_cpu_baseline and ws == 1:
+        from oracle import refbind as R
+        if R.available():
+            gbs, steps, cores, dt = cpu_reference_rate(seconds=10.0)
+            cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "reference",
+                   "sample": "%d full GEMVs on the reference library (%.1f s, OpenMP %d threads)" % (steps, dt, cores)}
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 6), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+        "data": "synthetic (N(0,0.02) weights quantized Q8_0, x N(0,1), seeded)",
+        "config": {"workload": WORKLOAD, "N": N_ROWS, "K": K_COLS, "M": 1, "parallelism": "row-shard x%d" % ws,
+                   "l2": "inputs larger than L2: %d rotating weight copies (%.0f MB)" % (N_COPIES, N_COPIES * W_BYTES / 1e6),
+                   "launch": "CUDA graph of %d GEMVs" % G},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": load_traffic(),
+                     "peak_source": peak_kind, "kernel_us": round(kernel_ms * 1e3, 3),
+                     "kernel_us_min": round(single_ms[0] * 1e3, 3)},
+        "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": K_COLS * 4,
+                "d2h_bytes_per_step": N_ROWS * 4, "steps": e2e_steps,
+                "note": "tb_upload(x) + tb_matmul_quant + tb_download(y) per step; weights resident"},
+        "gpu_launches": args.steps,
+        "clocks": clocks.summary(),
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line))
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100000)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,224 @@
+/* turbo_b200.h -- C ABI of the B200 (sm_100a) tensor-library hot path.
+ *
+ * This is the drop-in boundary under the Turbo.cpp `Tensor`/`Storage` API
+ * (include/turbo/tensor/tensor.hpp) and the `nn::*::forward` call sites
+ * (src/nn/*.cpp).  Every entry point replaces one reference interface, cited
+ * beside it as file:line inside the reference project.
+ *
+ * Conventions
+ *  - Plain pointers and sizes only.  Pointers named `*_dev` or held in a
+ *    tb_view are device (HBM) addresses; everything else is host memory.
+ *  - Offsets and strides are in ELEMENTS, as in the reference `Tensor`
+ *    (tensor.hpp:98-101).  Strides may be 0 (broadcast views).
+ *  - Every op is asynchronous on `stream` (a cudaStream_t; NULL = legacy
+ *    default stream) and returns a status.  TB_EINVAL / TB_ERANGE /
+ *    TB_ERUNTIME correspond to the reference's std::invalid_argument /
+ *    std::out_of_range / std::runtime_error; the host C++ layer rethrows them
+ *    as those types.  tb_last_error() gives the message of the calling
+ *    thread's last failure.
+ *  - Calls act on the current CUDA device of the calling thread.
+ *  - No entry point falls back to the CPU: when the CUDA library cannot run,
+ *    the call fails with TB_ECUDA.
+ */
+#ifndef TURBO_B200_H
+#define TURBO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* The library is built with hidden visibility; only this header's entry
+ * points are exported. */
+#if defined(__GNUC__)
+#pragma GCC visibility push(default)
+#endif
+
+typedef enum {
+  TB_OK = 0,
+  TB_EINVAL = 1,   /* std::invalid_argument in the reference */
+  TB_ERANGE = 2,   /* std::out_of_range */
+  TB_ERUNTIME = 3, /* std::runtime_error */
+  TB_ECUDA = 4,    /* CUDA launch or runtime failure */
+  TB_ETIMEOUT = 5, /* a bounded device-side wait gave up */
+  TB_ENOMEM = 6    /* device arena exhausted */
+} tb_status;
+
+/* Element types.  Values 0..4 are the reference DataType enum in order
+ * (include/turbo/tensor/tensor.hpp:10-16); BF16 is added for the sweep. */
+typedef enum {
+  TB_F32 = 0,
+  TB_F16 = 1,
+  TB_Q8_0 = 2, /* 34-byte blocks of 32: {u16 half d; i8 q[32]} (quant_types.hpp:17-20) */
+  TB_Q4_0 = 3, /* 18-byte blocks of 32: {u16 half d; u8 q[16]} (quant_types.hpp:32-35) */
+  TB_I32 = 4,
+  TB_BF16 = 5
+} tb_dtype;
+
+#define TB_MAX_RANK 8
+
+/* A strided view over device memory: element (i0, .., ir-1) is at
+ * data + (offset + sum_k i_k * strides[k]) * sizeof(element).
+ * Mirrors Tensor{storage, offset, shape, strides} (tensor.hpp:96-104). */
+typedef struct {
+  void *data;
+  int32_t dtype;
+  int32_t rank;
+  int64_t offset;
+  int64_t shape[TB_MAX_RANK];
+  int64_t strides[TB_MAX_RANK];
+} tb_view;
+
+typedef void *tb_stream; /* cudaStream_t */
+
+/* ---------------------------------------------------------------- runtime -- */
+
+/* Binds the calling thread to `device` and creates its per-device state
+ * (error word, arena).  Replaces nothing in the reference (CPU only); called
+ * implicitly by every entry point for the current device. */
+tb_status tb_init(int device);
+const char *tb_last_error(void);
+const char *tb_status_name(tb_status s);
+/* Version string of this library (build date and arch). */
+const char *tb_version(void);
+
+/* Device arena: Storage(size_t) (tensor.hpp:59-64) gains HBM backing.
+ * 256-byte aligned; tb_free returns the block to the arena. */
+tb_status tb_alloc(void **ptr_dev, size_t bytes);
+tb_status tb_free(void *ptr_dev);
+/* Host <-> device copies: the mmap constructor Storage(void*, size_t)
+ * (tensor.hpp:76-77) uploads weights once; data_ptr() reads back. */
+tb_status tb_upload(void *dst_dev, const void *src_host, size_t bytes, tb_stream stream);
+tb_status tb_download(void *dst_host, const void *src_dev, size_t bytes, tb_stream stream);
+tb_status tb_memset(void *dst_dev, int value, size_t bytes, tb_stream stream);
+tb_status tb_sync(tb_stream stream);
+/* Reads and clears the device error word set by bounded waits and by
+ * device-side index checks (bit 0: timeout, bit 1: index out of range). */
+tb_status tb_take_device_errors(uint32_t *flags_out);
+
+/* ------------------------------------------------------ elementwise (A3-A8) -- */
+
+/* out = broadcast(a) OP broadcast(b), written contiguously in the broadcast
+ * shape.  op 0 = add: Tensor::operator+ (src/tensor/tensor.cpp:260-282) with
+ * compute_broadcast_shape (:29-47) and broadcast_to (:232-256); op 1 = mul
+ * (the row-broadcast multiply of the sharded sweep).  fp32, or bf16 when all
+ * three views are bf16.  `out` must be contiguous with the broadcast shape. */
+tb_status tb_binary(int op, const tb_view *a, const tb_view *b, const tb_view *out,
+                    tb_stream stream);
+
+/* out = x * s: Tensor::operator*(float) (src/tensor/tensor.cpp:284-294);
+ * `out` contiguous of x's shape. */
+tb_status tb_scale(const tb_view *x, float s, const tb_view *out, tb_stream stream);
+
+/* dst <- src elementwise, shapes equal: Tensor::copy_ (src/tensor/tensor.cpp:689-726)
+ * and, with a contiguous dst, Tensor::contiguous (:118-132). */
+tb_status tb_copy(const tb_view *dst, const tb_view *src, tb_stream stream);
+
+/* y = x / sqrt(mean(x^2) + eps) * gamma over rows of `cols` contiguous
+ * elements: nn::RMSNorm::forward (src/nn/rmsnorm.cpp:23-68).  dtype TB_F32 or
+ * TB_BF16 for x/y (gamma is fp32, as the reference requires). */
+tb_status tb_rmsnorm(int dtype, const void *x_dev, const float *gamma_dev, void *y_dev,
+                     int64_t rows, int64_t cols, float eps, tb_stream stream);
+
+/* y = g / (1 + exp(-g)) * u: nn::SwiGLU::forward(gate, up) (src/nn/swiglu.cpp:10-40).
+ * dtype TB_F32 or TB_BF16. */
+tb_status tb_swiglu(int dtype, const void *g_dev, const void *u_dev, void *y_dev, int64_t n,
+                    tb_stream stream);
+
+/* ------------------------------------------------------- rows (A9, A15) -- */
+
+/* Last-dim softmax of x[rows, cols] (contiguous): nn::Softmax::forward
+ * (src/nn/softmax.cpp:13-54). */
+tb_status tb_softmax(const float *x_dev, float *y_dev, int64_t rows, int64_t cols,
+                     tb_stream stream);
+
+/* Per row, index of the first maximum under a strict '>' from -inf (NaN never
+ * wins; a row of only -inf/NaN gives 0): greedy_sample (src/core/sampler.cpp:13-26). */
+tb_status tb_argmax(const float *x_dev, int64_t rows, int64_t cols, int64_t *idx_dev,
+                    tb_stream stream);
+
+/* ------------------------------------------------------------- RoPE (A13) -- */
+
+/* Rotate-half RoPE in place on a rank-2 [S, D] or rank-4 [B, H, S, D] fp32
+ * view, positions pos_offset..pos_offset+S-1, using the constructor's tables
+ * cos/sin[max_seq, D/2] (uploaded once): RoPE::apply_in_place
+ * (src/nn/rope.cpp:35-103).  TB_ERANGE if a position reaches max_seq. */
+tb_status tb_rope(const tb_view *x, const float *cos_dev, const float *sin_dev,
+                  int64_t head_dim, int64_t max_seq, int64_t pos_offset, tb_stream stream);
+
+/* --------------------------------------------------- quant formats (A14, A17) -- */
+
+/* Exact dequantisation of `nblocks` consecutive blocks to fp32 (q*d, or
+ * (nibble-8)*d): dequantize_row_q8_0 (src/tensor/quant_math.hpp:16-29) and the
+ * Q4_0 unpacking of src/nn/embedding.cpp:54-63. */
+tb_status tb_dequant(int dtype, const void *blocks_dev, int64_t nblocks, float *y_dev,
+                     tb_stream stream);
+
+/* Rows of fp32 x[rows, k] to Q8_0 blocks: quantize_row_q8_0
+ * (src/tensor/quant_math.hpp:68-90), bit for bit. */
+tb_status tb_quantize_q8_0(const float *x_dev, int64_t rows, int64_t k, void *blocks_dev,
+                           tb_stream stream);
+
+/* Token-row gather with exact dequantisation: nn::Embedding::forward
+ * (src/nn/embedding.cpp:22-118).  The weight has GGUF logical shape
+ * {dim, vocab} (dtype TB_F32, TB_Q8_0 or TB_Q4_0); ids are device int32.
+ * ids are checked on the device: a row with id outside [0, vocab) is written
+ * as zeros and sets bit 1 of the device error word (tb_take_device_errors);
+ * callers holding host ids check them first (TB_ERANGE), as the host layer does. */
+tb_status tb_embedding(int dtype, const void *w_dev, int64_t dim, int64_t vocab,
+                       const int32_t *ids_dev, int64_t n, float *out_dev, tb_stream stream);
+
+/* ------------------------------------------------------------- matmul (A10-A12) -- */
+
+/* Y[M, N] = X[M, K] . W for a quantized W of GGUF logical shape {K, N}, stored
+ * as N rows of K/32 blocks (Tensor::matmul, src/tensor/tensor.cpp:328-432).
+ *  - dtype TB_Q8_0: X is fp32 and is not quantized (tensor.cpp:370-381).
+ *    M <= 16 runs the decode GEMV, bit-identical to vec_dot_q8_0_f32
+ *    (quant_math.hpp:32-60); larger M runs the tensor-core GEMM.
+ *  - dtype TB_Q4_0: X rows are first quantized to Q8_0 (tensor.cpp:413-421),
+ *    then multiplied with the Q4_0 rows (quant_math.hpp:184-248).
+ * K must be a multiple of 32. */
+tb_status tb_matmul_quant(int dtype, const float *x_dev, int64_t M, int64_t K,
+                          const void *w_dev, int64_t N, float *y_dev, tb_stream stream);
+
+/* Batched strided fp32 matmul, out = a @ b over matching leading (batch) dims,
+ * `out` contiguous [batch..., M, N]: Tensor::matmul fp32 branch
+ * (src/tensor/tensor.cpp:434-542) and matmul_threaded_packed_avx2 (:591-650).
+ * Each output is the FMA chain over k in increasing order, as the reference. */
+tb_status tb_matmul_f32(const tb_view *a, const tb_view *b, const tb_view *out,
+                        tb_stream stream);
+
+/* --------------------------------------- vocab-sharded softmax / argmax (8e) -- */
+
+/* Local half of a softmax whose columns are split across GPUs: per row of this
+ * shard's x[rows, cols] (row stride ld), the shard maximum and the sum of
+ * exp(x - shard maximum).  Combined across shards by a max and a sum
+ * all-reduce, then tb_softmax_shard_finish writes exp(x - M) / S. */
+tb_status tb_softmax_shard_stats(const float *x_dev, int64_t rows, int64_t cols, int64_t ld,
+                                 float *row_max_dev, float *row_sum_dev, tb_stream stream);
+/* Given the local stats and the global row maxima, rescales the local sums in
+ * place: sum_dev[r] *= exp(local_max[r] - global_max[r]). */
+tb_status tb_softmax_shard_rescale(const float *local_max_dev, const float *global_max_dev,
+                                   float *row_sum_dev, int64_t rows, tb_stream stream);
+tb_status tb_softmax_shard_finish(const float *x_dev, int64_t rows, int64_t cols, int64_t ld,
+                                  const float *global_max_dev, const float *global_sum_dev,
+                                  float *y_dev, int64_t ld_y, tb_stream stream);
+/* Per row of this shard, a 64-bit key that orders candidates the way
+ * greedy_sample does: (order-preserving bits of the value) << 32 |
+ * (0xFFFFFFFF - global column).  A max all-reduce of the keys across shards
+ * gives the global first maximum; tb_argmax_key_index decodes it. */
+tb_status tb_argmax_shard_keys(const float *x_dev, int64_t rows, int64_t cols, int64_t ld,
+                               int64_t col_base, uint64_t *keys_dev, tb_stream stream);
+tb_status tb_argmax_key_index(const uint64_t *keys_dev, int64_t rows, int64_t *idx_dev,
+                              tb_stream stream);
+
+#if defined(__GNUC__)
+#pragma GCC visibility pop
+#endif
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* TURBO_B200_H */

@@ -1,0 +1,60 @@
+"""The C ABI library loads without a GPU and exports every entry point that
+include/*.h declares (no compute calls: this suite runs on CPU)."""
+import glob
+import os
+import re
+import subprocess
+
+import pytest
+
+import turbo_b200 as T
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+DECL = re.compile(r"^\s*(?:tb_status|const\s+char\s*\*|void|int)\s*\*?\s*(tb_\w+)\s*\(", re.M)
+
+
+def declared():
+    names = set()
+    for h in glob.glob(os.path.join(ROOT, "include", "*.h")):
+        names |= set(DECL.findall(open(h).read()))
+    return sorted(names)
+
+
+def test_header_declares_entry_points():
+    names = declared()
+    assert "tb_matmul_quant" in names and "tb_softmax" in names and len(names) >= 25
+
+
+def test_library_exports_every_declared_symbol():
+    if not os.path.exists(T.LIB_PATH):
+        pytest.skip("library not built")
+    out = subprocess.run(["nm", "-D", "--defined-only", T.LIB_PATH], capture_output=True, text=True).stdout
+    exported = set(line.split()[-1] for line in out.splitlines() if " T " in line)
+    missing = [n for n in declared() if n not in exported]
+    assert not missing, missing
+    # nothing but the C ABI is exported (hidden visibility)
+    extra = [n for n in exported if not n.startswith("tb_")]
+    assert not extra, extra[:10]
+
+
+def test_library_loads_and_binding_matches_header():
+    if not os.path.exists(T.LIB_PATH):
+        pytest.skip("library not built")
+    L = T.load()
+    assert L.tb_version().startswith(b"turbo_b200 sm_100a")
+    assert L.tb_status_name(T.ERANGE) == b"TB_ERANGE"
+    assert set(T.SIGNATURES) == set(declared())
+
+
+def test_no_cuda_device_fails_loudly():
+    # Without a GPU every compute entry point must fail (TB_ECUDA), never run on the CPU.
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    if not os.path.exists(T.LIB_PATH):
+        pytest.skip("library not built")
+    L = T.load()
+    st = L.tb_softmax(None, None, 1, 1, None)
+    assert st in (T.EINVAL, T.ECUDA)
+    st = L.tb_init(0)
+    assert st == T.ECUDA

@@ -1,0 +1,439 @@
+"""GPU parity of every hot-path op against the oracle, through the C ABI.
+
+Bit-exact (integer, byte, index work and the ops whose order the kernels keep):
+dequant, quantize, Q8_0 / Q4_0 matmul on CUDA cores, copies, broadcast add,
+scale, RoPE, embedding, fp32 matmul, argmax.  Tolerance-bound (tree reductions):
+RMSNorm and softmax at 1e-5 relative (fp32), 1e-2 for bf16.  SwiGLU uses exp
+evaluated to match libm's expf and must agree to within one ulp on a vanishing
+fraction of elements.
+"""
+import numpy as np
+import pytest
+
+from oracle import orbind as O
+from turbo_b200 import synth
+
+pytestmark = pytest.mark.gpu
+
+torch = pytest.importorskip("torch")
+import turbo_b200 as T  # noqa: E402
+
+F32_REL = 1e-5
+BF16_REL = 1e-2
+
+
+def dev(a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def host(t):
+    torch.cuda.synchronize()
+    return t.cpu().numpy()
+
+
+def S():
+    return T.stream_handle()
+
+
+def assert_bits(a, b):
+    a = np.asarray(a, np.float32)
+    b = np.asarray(b, np.float32)
+    assert a.shape == b.shape, (a.shape, b.shape)
+    na, nb_ = np.isnan(a), np.isnan(b)
+    assert np.array_equal(na, nb_)
+    diff = (a.view(np.uint32) != b.view(np.uint32)) & ~na
+    assert not diff.any(), "%d of %d differ; first at %s: %r vs %r" % (
+        diff.sum(), diff.size, np.argwhere(diff)[0], a[tuple(np.argwhere(diff)[0])],
+        b[tuple(np.argwhere(diff)[0])])
+
+
+def assert_rel(a, b, tol):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    err = np.abs(a - b)
+    scale = np.maximum(np.abs(b), np.abs(b).max() * 1e-3 + 1e-30)
+    assert (err / scale).max() <= tol, "max rel err %g > %g" % ((err / scale).max(), tol)
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _init():
+    T.call("tb_init", 0)
+    yield
+    assert T.take_device_errors() == 0
+
+
+# ----------------------------------------------------------------- quant ----
+
+@pytest.mark.parametrize("dtype", [T.Q8_0, T.Q4_0])
+@pytest.mark.parametrize("nblocks", [1, 31, 64 * 37, 8192 * 64 + 5])
+def test_dequant_bit_exact(dtype, nblocks):
+    w = synth.normal((nblocks * 32,), 0.02, seed=nblocks)
+    q = synth.quantize_q8_0(w) if dtype == T.Q8_0 else synth.quantize_q4_0(w)
+    out = torch.empty(nblocks * 32, dtype=torch.float32, device="cuda")
+    T.call("tb_dequant", dtype, T.ptr(dev(q)), nblocks, T.ptr(out), S())
+    ref = O.dequant_q8_0(q, nblocks) if dtype == T.Q8_0 else O.dequant_q4_0(q, nblocks)
+    assert_bits(host(out), ref)
+
+
+def test_quantize_q8_0_bit_exact():
+    x = synth.normal((37, 2048), 1.0, seed=3)
+    x[0, :32] = 0.0
+    x[1, :32] = np.linspace(-3, 3, 32)
+    x[2, 5] = np.nan
+    q = torch.empty(37 * 64 * 34, dtype=torch.uint8, device="cuda")
+    T.call("tb_quantize_q8_0", T.ptr(dev(x)), 37, 2048, T.ptr(q), S())
+    got = host(q).reshape(37, -1)
+    for r in range(37):
+        ref = O.quantize_row_q8_0(x[r])
+        if r == 2:  # the NaN element's own byte is unspecified (float->int8 of NaN)
+            got[r, 2 + 5] = ref[2 + 5]
+        assert np.array_equal(got[r], ref), r
+
+
+# ----------------------------------------------------------------- matmul ----
+
+def run_matmul(dtype, x, wq, N):
+    M, K = x.shape
+    y = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    T.call("tb_matmul_quant", dtype, T.ptr(dev(x)), M, K, T.ptr(dev(wq)), N, T.ptr(y), S())
+    return host(y)
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 2048, 8192), (1, 8192, 2048), (3, 2048, 515), (1, 64, 5),
+                                   (2, 2080, 77), (16, 1024, 300)])
+def test_matmul_q8_0_bit_exact(M, K, N):
+    wq = synth.quantize_q8_0(synth.normal((N, K), 0.02, seed=K + N))
+    x = synth.normal((M, K), 1.0, seed=M)
+    assert_bits(run_matmul(T.Q8_0, x, wq, N), O.matmul_q8_0(x, wq, N))
+
+
+def test_matmul_q8_0_unaligned_weight_base():
+    N, K = 33, 2048
+    wq = synth.quantize_q8_0(synth.normal((N, K), 0.02, seed=1)).ravel()
+    x = synth.normal((1, K), 1.0, seed=2)
+    buf = torch.zeros(wq.size + 16, dtype=torch.uint8, device="cuda")
+    buf[6:6 + wq.size] = dev(wq)
+    y = torch.empty((1, N), dtype=torch.float32, device="cuda")
+    T.call("tb_matmul_quant", T.Q8_0, T.ptr(dev(x)), 1, K, buf.data_ptr() + 6, N, T.ptr(y), S())
+    assert_bits(host(y), O.matmul_q8_0(x, wq, N))
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 8192, 2048), (3, 8192, 130), (5, 64, 7)])
+def test_matmul_q4_0_bit_exact(M, K, N):
+    wq = synth.quantize_q4_0(synth.normal((N, K), 0.02, seed=K + N))
+    x = synth.normal((M, K), 1.0, seed=M + 1)
+    assert_bits(run_matmul(T.Q4_0, x, wq, N), O.matmul_q4_0(x, wq, N))
+
+
+def test_matmul_quant_rejects_bad_k():
+    x = torch.zeros((1, 40), device="cuda")
+    with pytest.raises(T.TbError) as e:
+        T.call("tb_matmul_quant", T.Q8_0, T.ptr(x), 1, 40, T.ptr(x), 1, T.ptr(x), S())
+    assert e.value.status == T.EINVAL
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 64, 37), (5, 64, 70), (3, 130, 9), (1, 64, 640)])
+def test_matmul_f32_attention_views_bit_exact(M, K, N):
+    a = synth.normal((M * 2048 + K,), 1.0, seed=30)
+    b = synth.normal((N * 512 + K,), 1.0, seed=31)
+    ref = O.matmul_f32(a, 3, (M, K), (2048, 1), b, 5, (K, N), (1, 512))
+    out = torch.empty((M, N), dtype=torch.float32, device="cuda")
+    da, db = dev(a), dev(b)
+    T.call("tb_matmul_f32", T.byref(T.view(da, 3, (M, K), (2048, 1))),
+           T.byref(T.view(db, 5, (K, N), (1, 512))), T.byref(T.view(out)), S())
+    assert_bits(host(out), ref)
+
+
+def test_matmul_f32_batched_bit_exact():
+    a = synth.normal((2 * 3 * 5 * 7,), 1.0, seed=32)
+    b = synth.normal((2 * 3 * 7 * 11,), 1.0, seed=33)
+    ref = O.matmul_f32(a, 0, (2, 3, 5, 7), (105, 35, 7, 1), b, 0, (2, 3, 7, 11), (231, 77, 11, 1))
+    out = torch.empty((2, 3, 5, 11), dtype=torch.float32, device="cuda")
+    T.call("tb_matmul_f32", T.byref(T.view(dev(a), 0, (2, 3, 5, 7), (105, 35, 7, 1))),
+           T.byref(T.view(dev(b), 0, (2, 3, 7, 11), (231, 77, 11, 1))), T.byref(T.view(out)), S())
+    assert_bits(host(out), ref)
+
+
+# ------------------------------------------------------------ elementwise ----
+
+@pytest.mark.parametrize("sa,sb", [((1, 128, 2048), (1, 128, 2048)), ((4, 1, 8), (3, 1)),
+                                   ((2, 3, 4), (4,)), ((5,), (2, 1, 5)), ((7, 1), (1, 9)),
+                                   ((64, 4096), (4096,)), ((4096,), (3, 4096)), ((3, 5), (3, 5))])
+def test_add_broadcast_bit_exact(sa, sb):
+    a = synth.normal(sa, 1.0, seed=1)
+    b = synth.normal(sb, 1.0, seed=2)
+    ref = O.add(a, 0, sa, [s // 4 for s in a.strides], b, 0, sb, [s // 4 for s in b.strides])
+    out = torch.empty(ref.shape, dtype=torch.float32, device="cuda")
+    T.call("tb_binary", 0, T.byref(T.view(dev(a))), T.byref(T.view(dev(b))), T.byref(T.view(out)), S())
+    assert_bits(host(out), ref)
+
+
+def test_mul_rowvector_and_bf16_add():
+    a = synth.normal((64, 4096), 1.0, seed=5)
+    g = synth.normal((4096,), 1.0, seed=6)
+    out = torch.empty((64, 4096), dtype=torch.float32, device="cuda")
+    T.call("tb_binary", 1, T.byref(T.view(dev(a))), T.byref(T.view(dev(g))), T.byref(T.view(out)), S())
+    assert_bits(host(out), (a * g).astype(np.float32))
+    ab = dev(a).to(torch.bfloat16)
+    bb = dev(synth.normal((64, 4096), 1.0, seed=7)).to(torch.bfloat16)
+    ob = torch.empty_like(ab)
+    T.call("tb_binary", 0, T.byref(T.view(ab)), T.byref(T.view(bb)), T.byref(T.view(ob)), S())
+    ref = O.add(*(lambda x, y: (x, 0, x.shape, (4096, 1), y, 0, y.shape, (4096, 1)))(
+        ab.float().cpu().numpy(), bb.float().cpu().numpy()))
+    assert_rel(ob.float().cpu().numpy(), ref, BF16_REL)
+
+
+def test_add_not_broadcastable():
+    a = torch.zeros((3, 4), device="cuda")
+    b = torch.zeros((5,), device="cuda")
+    out = torch.zeros((3, 4), device="cuda")
+    with pytest.raises(T.TbError) as e:
+        T.call("tb_binary", 0, T.byref(T.view(a)), T.byref(T.view(b)), T.byref(T.view(out)), S())
+    assert e.value.status == T.EINVAL
+
+
+def test_scale_and_contiguous_and_copy_strided_bit_exact():
+    base = synth.normal((4 * 6 * 5 + 3,), 1.0, seed=13)
+    shape, strides, off = (5, 4, 6), (1, 30, 5), 3
+    db = dev(base)
+    out = torch.empty(shape, dtype=torch.float32, device="cuda")
+    T.call("tb_scale", T.byref(T.view(db, off, shape, strides)), 0.125, T.byref(T.view(out)), S())
+    assert_bits(host(out), O.scale(base, off, shape, strides, 0.125))
+    T.call("tb_copy", T.byref(T.view(out)), T.byref(T.view(db, off, shape, strides)), S())
+    assert_bits(host(out), O.contiguous(base, off, shape, strides))
+    dst = np.zeros(200, np.float32)
+    dd = dev(dst)
+    T.call("tb_copy", T.byref(T.view(dd, 7, shape, (24, 6, 1))), T.byref(T.view(db, off, shape, strides)), S())
+    O.copy_(dst, 7, shape, (24, 6, 1), base, off, shape, strides)
+    assert_bits(host(dd), dst)
+
+
+@pytest.mark.parametrize("S_,H,D", [(1, 32, 64), (512, 32, 64), (7, 8, 64)])
+def test_contiguous_of_transposed_attention_context(S_, H, D):
+    # context [1, H, S, D] -> transpose(1, 2) -> contiguous (attention.cpp:144-145)
+    ctx = synth.normal((H * S_ * D,), 1.0, seed=S_)
+    shape, strides = (1, S_, H, D), (H * S_ * D, D, S_ * D, 1)
+    out = torch.empty(shape, dtype=torch.float32, device="cuda")
+    T.call("tb_copy", T.byref(T.view(out)), T.byref(T.view(dev(ctx), 0, shape, strides)), S())
+    assert_bits(host(out), O.contiguous(ctx, 0, shape, strides))
+
+
+def test_kv_cache_append_and_transpose_copy():
+    S_, H, D, ctx, p = 7, 8, 64, 64, 5
+    k = synth.normal((S_ * H * D,), 1.0, seed=14)
+    cache = synth.normal((ctx * H * D,), 1.0, seed=15)
+    dc = dev(cache)
+    T.call("tb_copy", T.byref(T.view(dc, p * H * D, (S_, H, D), (H * D, D, 1))),
+           T.byref(T.view(dev(k), 0, (S_, H, D), (H * D, D, 1))), S())
+    O.copy_(cache, p * H * D, (S_, H, D), (H * D, D, 1), k, 0, (S_, H, D), (H * D, D, 1))
+    assert_bits(host(dc), cache)
+    # a truly strided source: K viewed [S, H, D] with strides (D, S*D, 1)
+    dc2 = dev(cache)
+    T.call("tb_copy", T.byref(T.view(dc2, p * H * D, (S_, H, D), (H * D, D, 1))),
+           T.byref(T.view(dev(k), 0, (S_, H, D), (D, S_ * D, 1))), S())
+    O.copy_(cache, p * H * D, (S_, H, D), (H * D, D, 1), k, 0, (S_, H, D), (D, S_ * D, 1))
+    assert_bits(host(dc2), cache)
+
+
+def test_copy_shape_mismatch():
+    a = torch.zeros(12, device="cuda")
+    with pytest.raises(T.TbError) as e:
+        T.call("tb_copy", T.byref(T.view(a, 0, (3, 4), (4, 1))), T.byref(T.view(a, 0, (4, 3), (3, 1))), S())
+    assert e.value.status == T.EINVAL
+
+
+@pytest.mark.parametrize("n", [1, 5, 8192 * 128, 8192 * 128 + 3])
+def test_swiglu_matches_libm(n):
+    g = synth.normal((n,), 1.0, seed=2)
+    u = synth.normal((n,), 1.0, seed=3)
+    if n > 8:
+        g[:6] = [0.0, -0.0, 88.0, -88.0, -104.0, 20.0]
+    y = torch.empty(n, dtype=torch.float32, device="cuda")
+    T.call("tb_swiglu", T.F32, T.ptr(dev(g)), T.ptr(dev(u)), T.ptr(y), n, S())
+    got, ref = host(y), O.swiglu(g, u)
+    diff = got.view(np.uint32).astype(np.int64) - ref.view(np.uint32).astype(np.int64)
+    assert np.abs(diff).max() <= 1
+    assert np.count_nonzero(diff) <= max(1, n // 100000)
+
+
+def test_swiglu_bf16():
+    g = synth.normal((8192 * 16,), 1.0, seed=4)
+    u = synth.normal((8192 * 16,), 1.0, seed=5)
+    gb, ub = dev(g).to(torch.bfloat16), dev(u).to(torch.bfloat16)
+    y = torch.empty_like(gb)
+    T.call("tb_swiglu", T.BF16, T.ptr(gb), T.ptr(ub), T.ptr(y), g.size, S())
+    ref = O.swiglu(gb.float().cpu().numpy(), ub.float().cpu().numpy())
+    assert_rel(y.float().cpu().numpy(), ref, BF16_REL)
+
+
+# ------------------------------------------------------------------ rows ----
+
+@pytest.mark.parametrize("rows,cols", [(128, 2048), (1, 2048), (3, 4096), (5, 100), (2, 16384)])
+def test_rmsnorm(rows, cols):
+    x = synth.normal((rows, cols), 1.0, seed=rows)
+    g = synth.uniform((cols,), 0.5, 1.5, seed=cols)
+    y = torch.empty((rows, cols), dtype=torch.float32, device="cuda")
+    T.call("tb_rmsnorm", T.F32, T.ptr(dev(x)), T.ptr(dev(g)), T.ptr(y), rows, cols, 1e-5, S())
+    assert_rel(host(y), O.rmsnorm(x, g), F32_REL)
+
+
+def test_rmsnorm_kat_and_bf16():
+    # reference test_nn.cpp RMSNormForwardPass: [1,2,3,4], gamma [.5,1,1.5,2]
+    y = torch.empty((1, 4), dtype=torch.float32, device="cuda")
+    T.call("tb_rmsnorm", T.F32, T.ptr(dev(np.array([[1, 2, 3, 4]], np.float32))),
+           T.ptr(dev(np.array([0.5, 1, 1.5, 2], np.float32))), T.ptr(y), 1, 4, 1e-5, S())
+    np.testing.assert_allclose(host(y)[0], [0.182574, 0.730296, 1.643167, 2.921186], atol=1e-4)
+    x = synth.normal((64, 4096), 1.0, seed=9)
+    g = synth.uniform((4096,), 0.5, 1.5, seed=10)
+    xb = dev(x).to(torch.bfloat16)
+    yb = torch.empty_like(xb)
+    T.call("tb_rmsnorm", T.BF16, T.ptr(xb), T.ptr(dev(g)), T.ptr(yb), 64, 4096, 1e-5, S())
+    assert_rel(yb.float().cpu().numpy(), O.rmsnorm(xb.float().cpu().numpy(), g), BF16_REL)
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 128256), (3, 37), (64, 128256), (16, 640), (2, 300000)])
+def test_softmax(rows, cols):
+    x = synth.normal((rows, cols), 2.0, seed=cols)
+    y = torch.empty((rows, cols), dtype=torch.float32, device="cuda")
+    T.call("tb_softmax", T.ptr(dev(x)), T.ptr(y), rows, cols, S())
+    assert_rel(host(y), O.softmax(x), F32_REL)
+
+
+def test_softmax_kat():
+    # reference test_tensor.cpp NumericallyStableSoftmax
+    x = np.array([[1, 2, 3], [10, 100, 10]], np.float32)
+    y = torch.empty((2, 3), dtype=torch.float32, device="cuda")
+    T.call("tb_softmax", T.ptr(dev(x)), T.ptr(y), 2, 3, S())
+    np.testing.assert_allclose(host(y).ravel(), [0.0900, 0.2447, 0.6652, 0, 1, 0], atol=1e-4)
+
+
+def argmax_gpu(x):
+    x = np.ascontiguousarray(x, np.float32)
+    rows, cols = x.shape
+    idx = torch.empty(rows, dtype=torch.int64, device="cuda")
+    T.call("tb_argmax", T.ptr(dev(x)), rows, cols, T.ptr(idx), S())
+    return host(idx)
+
+
+@pytest.mark.parametrize("rows,cols", [(1, 128256), (64, 128256), (5, 3), (2, 9000), (1, 1)])
+def test_argmax_random(rows, cols):
+    x = synth.normal((rows, cols), 2.0, seed=rows * cols)
+    got = argmax_gpu(x)
+    for r in range(rows):
+        assert got[r] == O.argmax(x[r])
+
+
+def test_argmax_ties_nan_inf():
+    rows = [
+        [1.0, 3.0, np.nan, 3.0, -np.inf],
+        [np.nan, -np.inf, np.nan],
+        [np.nan, 2.0, 2.0],
+        [-np.inf, -np.inf, -np.inf],
+        [np.inf, np.inf, 1.0],
+        [-0.0, 0.0, -0.0],
+    ]
+    for r in rows:
+        x = np.array([r], np.float32)
+        assert argmax_gpu(x)[0] == O.argmax(x[0]), r
+    big = np.full((1, 128256), -1.0, np.float32)
+    big[0, 77777] = 5.0
+    big[0, 100000] = 5.0
+    big[0, 5] = np.nan
+    assert argmax_gpu(big)[0] == 77777 == O.argmax(big[0])
+
+
+# ------------------------------------------------------------------ RoPE ----
+
+@pytest.mark.parametrize("rank", [2, 4])
+def test_rope_bit_exact(rank):
+    hd, max_seq, theta, pos = 64, 256, 500000.0, 17
+    c, s = O.rope_tables(hd, max_seq, theta)
+    if rank == 2:
+        S_ = 9
+        shape, strides, n = (S_, hd), (hd, 1), S_ * hd
+    else:
+        B, S_, H = 1, 9, 32
+        shape, strides, n = (B, H, S_, hd), (S_ * H * hd, hd, H * hd, 1), S_ * H * hd
+    x = synth.normal((n,), 1.0, seed=20)
+    dx = dev(x)
+    T.call("tb_rope", T.byref(T.view(dx, 0, shape, strides)), T.ptr(dev(c)), T.ptr(dev(s)), hd, max_seq, pos, S())
+    O.rope(x, 0, shape, strides, hd, max_seq, c, s, pos)
+    assert_bits(host(dx), x)
+
+
+def test_rope_kat_and_range():
+    # reference test_rope.cpp: head_dim 4, max_seq 10, theta 10000, token 1
+    c, s = O.rope_tables(4, 10, 10000.0)
+    x = dev(np.array([[1, 2, 3, 4], [1, 2, 3, 4]], np.float32))
+    T.call("tb_rope", T.byref(T.view(x)), T.ptr(dev(c)), T.ptr(dev(s)), 4, 10, 0, S())
+    h = host(x)
+    np.testing.assert_array_equal(h[0], [1, 2, 3, 4])
+    assert abs(h[1, 0] - -1.9840) < 1e-3 and abs(h[1, 2] - 2.4623) < 1e-3
+    with pytest.raises(T.TbError) as e:
+        T.call("tb_rope", T.byref(T.view(x)), T.ptr(dev(c)), T.ptr(dev(s)), 4, 10, 9, S())
+    assert e.value.status == T.ERANGE
+
+
+# -------------------------------------------------------------- embedding ----
+
+@pytest.mark.parametrize("dtype", [T.F32, T.Q8_0, T.Q4_0])
+def test_embedding_bit_exact(dtype):
+    dim, vocab = 2048, 1000
+    w = synth.normal((vocab, dim), 0.02, seed=21)
+    if dtype == T.F32:
+        wb = np.ascontiguousarray(w.T).view(np.uint8).ravel()
+    elif dtype == T.Q8_0:
+        wb = synth.quantize_q8_0(w).ravel()
+    else:
+        wb = synth.quantize_q4_0(w).ravel()
+    ids = np.array([0, 999, 5, 5, 123], np.int32)
+    out = torch.empty((ids.size, dim), dtype=torch.float32, device="cuda")
+    T.call("tb_embedding", dtype, T.ptr(dev(wb)), dim, vocab, T.ptr(dev(ids)), ids.size, T.ptr(out), S())
+    assert_bits(host(out), O.embedding(wb, dtype, dim, vocab, ids.astype(np.float32)))
+    assert T.take_device_errors() == 0
+    bad = np.array([3, 1000], np.int32)
+    out2 = torch.empty((2, dim), dtype=torch.float32, device="cuda")
+    T.call("tb_embedding", dtype, T.ptr(dev(wb)), dim, vocab, T.ptr(dev(bad)), 2, T.ptr(out2), S())
+    torch.cuda.synchronize()
+    assert T.take_device_errors() & 2
+    assert not out2[1].any()
+
+
+# ------------------------------------------------- vocab-sharded (one GPU) ----
+
+@pytest.mark.parametrize("shards", [2, 4, 8])
+def test_sharded_softmax_and_argmax_emulated(shards):
+    rows, V = 64, 128256
+    x = synth.normal((rows, V), 2.0, seed=shards)
+    x[3, 1000] = 50.0
+    x[3, 90000] = 50.0  # tie across shards: first index wins
+    dx = dev(x)
+    w = V // shards
+    maxes, sums, keys = [], [], []
+    for g in range(shards):
+        part = dx[:, g * w:(g + 1) * w]
+        m = torch.empty(rows, device="cuda")
+        s_ = torch.empty(rows, device="cuda")
+        T.call("tb_softmax_shard_stats", part.data_ptr(), rows, w, V, T.ptr(m), T.ptr(s_), S())
+        k = torch.empty(rows, dtype=torch.int64, device="cuda")
+        T.call("tb_argmax_shard_keys", part.data_ptr(), rows, w, V, g * w, T.ptr(k), S())
+        maxes.append(m)
+        sums.append(s_)
+        keys.append(k)
+    gmax = torch.stack(maxes).max(0).values.contiguous()  # stands in for the max all-reduce
+    for g in range(shards):
+        T.call("tb_softmax_shard_rescale", T.ptr(maxes[g]), T.ptr(gmax), T.ptr(sums[g]), rows, S())
+    gsum = torch.stack(sums).sum(0).contiguous()  # the sum all-reduce
+    y = torch.empty_like(dx)
+    for g in range(shards):
+        T.call("tb_softmax_shard_finish", dx.data_ptr() + 4 * g * w, rows, w, V, T.ptr(gmax),
+               T.ptr(gsum), y.data_ptr() + 4 * g * w, V, S())
+    assert_rel(host(y), O.softmax(x), F32_REL)
+    kmax = torch.stack(keys)
+    # order the int64 views as unsigned: compare via the top bit flipped
+    kmax = (kmax ^ (-2 ** 63)).max(0).values ^ (-2 ** 63)
+    idx = torch.empty(rows, dtype=torch.int64, device="cuda")
+    T.call("tb_argmax_key_index", T.ptr(kmax.contiguous()), rows, T.ptr(idx), S())
+    got = host(idx)
+    for r in range(rows):
+        assert got[r] == O.argmax(x[r]), r

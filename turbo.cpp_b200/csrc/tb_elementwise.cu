@@ -1,0 +1,566 @@
+// tb_elementwise.cu -- broadcast binary ops, scalar multiply, strided copy and
+// SwiGLU (rows A3, A4, A5, A6, A8 of the hot path).
+//
+// All of these are HBM-bound.  The kernels read and write 16 bytes per access
+// where the views allow it (contiguous and 16-byte aligned), keep several
+// accesses in flight per thread, and size grids as a multiple of the SM count.
+// Non-contiguous views go through a merged-dimension index walk; a broadcast
+// operand whose only varying dims are the innermost ones (a row vector) keeps
+// the vectorised path.
+#include <algorithm>
+
+#include "tb_internal.cuh"
+
+namespace tb {
+namespace {
+
+constexpr int kThreads = 256;
+
+// --------------------------------------------------------------------------
+// Index walk over up to TB_MAX_RANK merged dimensions for three operands.
+struct Walk3 {
+  int rank;
+  int64_t shape[TB_MAX_RANK];
+  int64_t s0[TB_MAX_RANK];  // output (or dst) strides
+  int64_t s1[TB_MAX_RANK];
+  int64_t s2[TB_MAX_RANK];
+  int64_t o0, o1, o2;  // base offsets (elements)
+};
+
+// Drops extent-1 dims and merges neighbours that are contiguous for every
+// operand, so that most views collapse to one or two dims.
+void merge_dims(Walk3 &w, int nops) {
+  int r = 0;
+  int64_t sh[TB_MAX_RANK], a[TB_MAX_RANK], b[TB_MAX_RANK], c[TB_MAX_RANK];
+  for (int i = 0; i < w.rank; ++i) {
+    if (w.shape[i] == 1) continue;
+    sh[r] = w.shape[i];
+    a[r] = w.s0[i];
+    b[r] = w.s1[i];
+    c[r] = nops > 2 ? w.s2[i] : 0;
+    ++r;
+  }
+  int m = 0;
+  for (int i = 0; i < r; ++i) {
+    if (m > 0) {
+      int j = m - 1;
+      bool ok = a[j] == a[i] * sh[i] && b[j] == b[i] * sh[i] && (nops < 3 || c[j] == c[i] * sh[i]);
+      if (ok) {
+        sh[j] *= sh[i];
+        a[j] = a[i];
+        b[j] = b[i];
+        c[j] = c[i];
+        continue;
+      }
+    }
+    sh[m] = sh[i];
+    a[m] = a[i];
+    b[m] = b[i];
+    c[m] = c[i];
+    ++m;
+  }
+  if (m == 0) {  // a single element
+    sh[0] = 1;
+    a[0] = b[0] = c[0] = 1;
+    m = 1;
+  }
+  w.rank = m;
+  for (int i = 0; i < m; ++i) {
+    w.shape[i] = sh[i];
+    w.s0[i] = a[i];
+    w.s1[i] = b[i];
+    w.s2[i] = c[i];
+  }
+}
+
+template <typename T> struct Vec;
+template <> struct Vec<float> {
+  static constexpr int N = 4;
+};
+template <> struct Vec<__nv_bfloat16> {
+  static constexpr int N = 8;
+};
+
+__device__ __forceinline__ float to_f(float v) { return v; }
+__device__ __forceinline__ float to_f(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T> __device__ __forceinline__ T from_f(float v);
+template <> __device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float v) {
+  return __float2bfloat16_rn(v);
+}
+
+template <int OP> __device__ __forceinline__ float apply(float a, float b) {
+  if (OP == 0) return __fadd_rn(a, b);
+  return __fmul_rn(a, b);
+}
+
+// ---- contiguous, 16-byte aligned: out = a OP b -----------------------------
+template <typename T, int OP>
+__global__ void __launch_bounds__(kThreads) binary_flat_kernel(const T *__restrict__ a,
+                                                               const T *__restrict__ b,
+                                                               T *__restrict__ out, int64_t n) {
+  constexpr int V = Vec<T>::N;
+  const int64_t nvec = n / V;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const uint4 *av = reinterpret_cast<const uint4 *>(a);
+  const uint4 *bv = reinterpret_cast<const uint4 *>(b);
+  uint4 *ov = reinterpret_cast<uint4 *>(out);
+  // Two 16-byte loads per operand in flight per iteration.
+  for (; i + stride < nvec; i += 2 * stride) {
+    uint4 x0 = __ldcs(av + i), y0 = __ldcs(bv + i);
+    uint4 x1 = __ldcs(av + i + stride), y1 = __ldcs(bv + i + stride);
+    const T *xa = reinterpret_cast<const T *>(&x0), *ya = reinterpret_cast<const T *>(&y0);
+    const T *xb = reinterpret_cast<const T *>(&x1), *yb = reinterpret_cast<const T *>(&y1);
+    uint4 r0, r1;
+    T *ra = reinterpret_cast<T *>(&r0), *rb = reinterpret_cast<T *>(&r1);
+#pragma unroll
+    for (int k = 0; k < V; ++k) {
+      ra[k] = from_f<T>(apply<OP>(to_f(xa[k]), to_f(ya[k])));
+      rb[k] = from_f<T>(apply<OP>(to_f(xb[k]), to_f(yb[k])));
+    }
+    __stcs(ov + i, r0);
+    __stcs(ov + i + stride, r1);
+  }
+  for (; i < nvec; i += stride) {
+    uint4 x0 = __ldcs(av + i), y0 = __ldcs(bv + i);
+    const T *xa = reinterpret_cast<const T *>(&x0), *ya = reinterpret_cast<const T *>(&y0);
+    uint4 r0;
+    T *ra = reinterpret_cast<T *>(&r0);
+#pragma unroll
+    for (int k = 0; k < V; ++k) ra[k] = from_f<T>(apply<OP>(to_f(xa[k]), to_f(ya[k])));
+    __stcs(ov + i, r0);
+  }
+  // tail elements
+  int64_t t = nvec * V + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t < n) out[t] = from_f<T>(apply<OP>(to_f(a[t]), to_f(b[t])));
+}
+
+// ---- a contiguous [rows, inner], b a row vector [inner] (stride-0 rows) -----
+template <typename T, int OP>
+__global__ void __launch_bounds__(kThreads) binary_rowvec_kernel(const T *__restrict__ a,
+                                                                 const T *__restrict__ b,
+                                                                 T *__restrict__ out, int64_t n,
+                                                                 int64_t inner, int b_first) {
+  constexpr int V = Vec<T>::N;
+  const int64_t nvec = n / V;
+  const int64_t innerv = inner / V;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const uint4 *av = reinterpret_cast<const uint4 *>(a);
+  const uint4 *bv = reinterpret_cast<const uint4 *>(b);
+  uint4 *ov = reinterpret_cast<uint4 *>(out);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    uint4 x0 = __ldcs(av + i), y0 = __ldg(bv + (i % innerv));
+    const T *xa = reinterpret_cast<const T *>(&x0), *ya = reinterpret_cast<const T *>(&y0);
+    uint4 r0;
+    T *ra = reinterpret_cast<T *>(&r0);
+#pragma unroll
+    for (int k = 0; k < V; ++k)
+      ra[k] = b_first ? from_f<T>(apply<OP>(to_f(ya[k]), to_f(xa[k])))
+                      : from_f<T>(apply<OP>(to_f(xa[k]), to_f(ya[k])));
+    __stcs(ov + i, r0);
+  }
+}
+
+// ---- general strided: out[walk] = a[walk] OP b[walk] --------------------------
+template <typename T, int OP>
+__global__ void __launch_bounds__(kThreads) binary_strided_kernel(const T *__restrict__ a,
+                                                                  const T *__restrict__ b,
+                                                                  T *__restrict__ out,
+                                                                  int64_t n, Walk3 w) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    int64_t rem = i, oo = w.o0, oa = w.o1, ob = w.o2;
+    for (int d = w.rank - 1; d >= 0; --d) {
+      int64_t idx = rem % w.shape[d];
+      rem /= w.shape[d];
+      oo += idx * w.s0[d];
+      oa += idx * w.s1[d];
+      ob += idx * w.s2[d];
+    }
+    out[oo] = from_f<T>(apply<OP>(to_f(a[oa]), to_f(b[ob])));
+  }
+}
+
+// ---- scale ----------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads) scale_flat_kernel(const float *__restrict__ x,
+                                                              float *__restrict__ out, int64_t n,
+                                                              float s) {
+  const int64_t nvec = n / 4;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  const float4 *xv = reinterpret_cast<const float4 *>(x);
+  float4 *ov = reinterpret_cast<float4 *>(out);
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+    float4 v = __ldcs(xv + i);
+    v.x = __fmul_rn(v.x, s);
+    v.y = __fmul_rn(v.y, s);
+    v.z = __fmul_rn(v.z, s);
+    v.w = __fmul_rn(v.w, s);
+    __stcs(ov + i, v);
+  }
+  int64_t t = nvec * 4 + (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (t < n) out[t] = __fmul_rn(x[t], s);
+}
+
+__global__ void __launch_bounds__(kThreads) scale_strided_kernel(const float *__restrict__ x,
+                                                                 float *__restrict__ out,
+                                                                 int64_t n, float s, Walk3 w) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    int64_t rem = i, oo = w.o0, ox = w.o1;
+    for (int d = w.rank - 1; d >= 0; --d) {
+      int64_t idx = rem % w.shape[d];
+      rem /= w.shape[d];
+      oo += idx * w.s0[d];
+      ox += idx * w.s1[d];
+    }
+    out[oo] = __fmul_rn(x[ox], s);
+  }
+}
+
+// ---- copy -------------------------------------------------------------------
+// 16-byte vector copy of a contiguous range.
+__global__ void __launch_bounds__(kThreads) copy_flat16_kernel(const uint4 *__restrict__ src,
+                                                               uint4 *__restrict__ dst,
+                                                               int64_t nvec) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + stride < nvec; i += 2 * stride) {
+    uint4 a = __ldcs(src + i), b = __ldcs(src + i + stride);
+    __stcs(dst + i, a);
+    __stcs(dst + i + stride, b);
+  }
+  for (; i < nvec; i += stride) __stcs(dst + i, __ldcs(src + i));
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) copy_strided_kernel(const T *__restrict__ src,
+                                                                T *__restrict__ dst, int64_t n,
+                                                                Walk3 w) {
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    int64_t rem = i, od = w.o0, os = w.o1;
+    for (int d = w.rank - 1; d >= 0; --d) {
+      int64_t idx = rem % w.shape[d];
+      rem /= w.shape[d];
+      od += idx * w.s0[d];
+      os += idx * w.s1[d];
+    }
+    dst[od] = src[os];
+  }
+}
+
+// Transposing copy of the innermost two dims through shared memory: a tile of
+// 32x32 elements is read along the source's unit-stride dim and written along
+// the destination's, so both sides stay coalesced.  Used when the source's
+// unit-stride dim is not the destination's (e.g. contiguous() of a transposed
+// view, attention.cpp:144-145).
+template <typename T>
+__global__ void __launch_bounds__(256) copy_transpose_kernel(const T *__restrict__ src,
+                                                             T *__restrict__ dst, int64_t outer,
+                                                             int64_t R, int64_t C, Walk3 w) {
+  // Logical element (o, r, c): dst at w.o0 + o..., r*w.s0[R] + c*w.s0[C]; the
+  // source has unit stride along r (dim rank-2) and the dst along c (rank-1).
+  __shared__ T tile[32][33];
+  const int rd = w.rank - 2, cd = w.rank - 1;
+  int64_t tiles_c = (C + 31) / 32, tiles_r = (R + 31) / 32;
+  int64_t tiles = outer * tiles_r * tiles_c;
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    int64_t o = t / (tiles_r * tiles_c);
+    int64_t rem = t % (tiles_r * tiles_c);
+    int64_t r0 = (rem / tiles_c) * 32, c0 = (rem % tiles_c) * 32;
+    int64_t od = w.o0, os = w.o1, ro = o;
+    for (int d = w.rank - 3; d >= 0; --d) {
+      int64_t idx = ro % w.shape[d];
+      ro /= w.shape[d];
+      od += idx * w.s0[d];
+      os += idx * w.s1[d];
+    }
+    // read: threads along r (unit stride in src)
+    for (int k = threadIdx.x / 32; k < 32; k += blockDim.x / 32) {
+      int64_t c = c0 + k, r = r0 + (threadIdx.x & 31);
+      if (c < C && r < R) tile[k][threadIdx.x & 31] = src[os + r * w.s1[rd] + c * w.s1[cd]];
+    }
+    __syncthreads();
+    // write: threads along c (unit stride in dst)
+    for (int k = threadIdx.x / 32; k < 32; k += blockDim.x / 32) {
+      int64_t r = r0 + k, c = c0 + (threadIdx.x & 31);
+      if (c < C && r < R) dst[od + r * w.s0[rd] + c * w.s0[cd]] = tile[threadIdx.x & 31][k];
+    }
+    __syncthreads();
+  }
+}
+
+// ---- SwiGLU -----------------------------------------------------------------
+// silu(g) * u with silu(g) = g / (1 + exp(-g)) (src/nn/swiglu.cpp:25-31): the
+// division and products are IEEE-rounded as in the reference; exp follows the
+// reference's libm (exp_ref).
+__device__ __forceinline__ float swiglu1(float g, float u) {
+  float e = exp_ref(-g);
+  float s = __fdiv_rn(g, __fadd_rn(1.0f, e));
+  return __fmul_rn(s, u);
+}
+__device__ __forceinline__ float swiglu1_bf16(float g, float u) {
+  float e = __expf(-g);  // bf16 results: fp32 exp is far below the output rounding
+  return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), u);
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads) swiglu_kernel(const T *__restrict__ g,
+                                                          const T *__restrict__ u,
+                                                          T *__restrict__ y, int64_t n,
+                                                          int vec_ok) {
+  constexpr int V = Vec<T>::N;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t base = 0;
+  if (vec_ok) {
+    const int64_t nvec = n / V;
+    const uint4 *gv = reinterpret_cast<const uint4 *>(g);
+    const uint4 *uv = reinterpret_cast<const uint4 *>(u);
+    uint4 *yv = reinterpret_cast<uint4 *>(y);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
+      uint4 a = __ldcs(gv + i), b = __ldcs(uv + i);
+      const T *ga = reinterpret_cast<const T *>(&a), *ub = reinterpret_cast<const T *>(&b);
+      uint4 r;
+      T *rr = reinterpret_cast<T *>(&r);
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        float gf = to_f(ga[k]), uf = to_f(ub[k]);
+        rr[k] = from_f<T>(sizeof(T) == 4 ? swiglu1(gf, uf) : swiglu1_bf16(gf, uf));
+      }
+      __stcs(yv + i, r);
+    }
+    base = nvec * V;
+  }
+  for (int64_t i = base + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    float gf = to_f(g[i]), uf = to_f(u[i]);
+    y[i] = from_f<T>(sizeof(T) == 4 ? swiglu1(gf, uf) : swiglu1_bf16(gf, uf));
+  }
+}
+
+// ---- host helpers --------------------------------------------------------------
+
+int grid_for(int64_t work_items, const DeviceState *st, int per_sm = 8) {
+  int64_t want = (work_items + kThreads - 1) / kThreads;
+  int64_t cap = (int64_t)st->sm_count * per_sm;
+  if (want > cap) want = cap;
+  if (want < 1) want = 1;
+  return (int)want;
+}
+
+bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// Broadcast shape per Tensor::compute_broadcast_shape (src/tensor/tensor.cpp:29-47).
+tb_status broadcast_shape(const tb_view *a, const tb_view *b, int64_t *out, int *rank) {
+  int r = std::max(a->rank, b->rank);
+  for (int k = 0; k < r; ++k) {
+    int i = a->rank - 1 - k, j = b->rank - 1 - k;
+    int64_t d1 = i >= 0 ? a->shape[i] : 1, d2 = j >= 0 ? b->shape[j] : 1;
+    if (d1 != d2 && d1 != 1 && d2 != 1) return fail(TB_EINVAL, "Shapes are not broadcastable.");
+    out[r - 1 - k] = std::max(d1, d2);
+  }
+  *rank = r;
+  return TB_OK;
+}
+
+// Strides of `v` broadcast to `shape` (Tensor::broadcast_to, tensor.cpp:232-256).
+void broadcast_strides(const tb_view *v, const int64_t *shape, int rank, int64_t *st) {
+  int diff = rank - v->rank;
+  for (int i = 0; i < rank; ++i) {
+    if (i < diff) {
+      st[i] = 0;
+    } else {
+      int64_t s = v->shape[i - diff];
+      st[i] = (s == shape[i]) ? v->strides[i - diff] : 0;
+    }
+  }
+}
+
+template <typename T, int OP>
+tb_status launch_binary(const tb_view *a, const tb_view *b, const tb_view *out, const int64_t *shape,
+                        int rank, cudaStream_t s, const DeviceState *st) {
+  const int64_t n = numel(out);
+  if (n == 0) return TB_OK;
+  const T *pa = static_cast<const T *>(a->data) + a->offset;
+  const T *pb = static_cast<const T *>(b->data) + b->offset;
+  T *po = static_cast<T *>(out->data) + out->offset;
+  constexpr int V = Vec<T>::N;
+  Walk3 w;
+  w.rank = rank;
+  for (int i = 0; i < rank; ++i) w.shape[i] = shape[i];
+  broadcast_strides(out, shape, rank, w.s0);
+  broadcast_strides(a, shape, rank, w.s1);
+  broadcast_strides(b, shape, rank, w.s2);
+  w.o0 = w.o1 = w.o2 = 0;
+  merge_dims(w, 3);
+  bool out_c = w.rank == 1 && w.s0[0] == 1;
+  if (out_c && w.s1[0] == 1 && w.s2[0] == 1 && aligned16(pa) && aligned16(pb) && aligned16(po)) {
+    binary_flat_kernel<T, OP><<<grid_for(n / V / 2 + 1, st), kThreads, 0, s>>>(pa, pb, po, n);
+    return check_launch("tb_binary");
+  }
+  // row-vector broadcast: [rows, inner] with one side stride-0 over rows
+  if (w.rank == 2 && w.s0[0] == w.shape[1] && w.s0[1] == 1 && w.shape[1] % V == 0 &&
+      aligned16(pa) && aligned16(pb) && aligned16(po)) {
+    bool a_full = w.s1[0] == w.shape[1] && w.s1[1] == 1;
+    bool b_full = w.s2[0] == w.shape[1] && w.s2[1] == 1;
+    bool a_row = w.s1[0] == 0 && w.s1[1] == 1;
+    bool b_row = w.s2[0] == 0 && w.s2[1] == 1;
+    if (a_full && b_row) {
+      binary_rowvec_kernel<T, OP><<<grid_for(n / V, st), kThreads, 0, s>>>(pa, pb, po, n, w.shape[1], 0);
+      return check_launch("tb_binary");
+    }
+    if (b_full && a_row) {
+      binary_rowvec_kernel<T, OP><<<grid_for(n / V, st), kThreads, 0, s>>>(pb, pa, po, n, w.shape[1], 1);
+      return check_launch("tb_binary");
+    }
+  }
+  binary_strided_kernel<T, OP><<<grid_for(n, st), kThreads, 0, s>>>(pa, pb, po, n, w);
+  return check_launch("tb_binary");
+}
+
+}  // namespace
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" {
+
+tb_status tb_binary(int op, const tb_view *a, const tb_view *b, const tb_view *out, tb_stream stream) {
+  TB_TRY(validate_view(a, "tb_binary a"));
+  TB_TRY(validate_view(b, "tb_binary b"));
+  TB_TRY(validate_view(out, "tb_binary out"));
+  if (op != 0 && op != 1) return fail(TB_EINVAL, "tb_binary: op %d (0 add, 1 mul)", op);
+  int dt = a->dtype;
+  if (b->dtype != dt || out->dtype != dt || (dt != TB_F32 && dt != TB_BF16))
+    return fail(TB_EINVAL, "tb_binary: dtypes must all be TB_F32 or all TB_BF16");
+  int64_t shape[TB_MAX_RANK];
+  int rank = 0;
+  TB_TRY(broadcast_shape(a, b, shape, &rank));
+  if (out->rank != rank) return fail(TB_EINVAL, "tb_binary: out rank %d, broadcast rank %d", out->rank, rank);
+  for (int i = 0; i < rank; ++i)
+    if (out->shape[i] != shape[i]) return fail(TB_EINVAL, "tb_binary: out shape is not the broadcast shape");
+  if (!is_contiguous(out)) return fail(TB_EINVAL, "tb_binary: out must be contiguous");
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  cudaStream_t s = as_stream(stream);
+  if (dt == TB_F32)
+    return op == 0 ? launch_binary<float, 0>(a, b, out, shape, rank, s, st)
+                   : launch_binary<float, 1>(a, b, out, shape, rank, s, st);
+  return op == 0 ? launch_binary<__nv_bfloat16, 0>(a, b, out, shape, rank, s, st)
+                 : launch_binary<__nv_bfloat16, 1>(a, b, out, shape, rank, s, st);
+}
+
+tb_status tb_scale(const tb_view *x, float sc, const tb_view *out, tb_stream stream) {
+  TB_TRY(validate_view(x, "tb_scale x"));
+  TB_TRY(validate_view(out, "tb_scale out"));
+  if (x->dtype != TB_F32 || out->dtype != TB_F32) return fail(TB_EINVAL, "tb_scale: fp32 only");
+  if (out->rank != x->rank) return fail(TB_EINVAL, "tb_scale: rank mismatch");
+  for (int i = 0; i < x->rank; ++i)
+    if (out->shape[i] != x->shape[i]) return fail(TB_EINVAL, "tb_scale: shape mismatch");
+  if (!is_contiguous(out)) return fail(TB_EINVAL, "tb_scale: out must be contiguous");
+  int64_t n = numel(x);
+  if (n == 0) return TB_OK;
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  cudaStream_t s = as_stream(stream);
+  const float *px = static_cast<const float *>(x->data) + x->offset;
+  float *po = static_cast<float *>(out->data) + out->offset;
+  if (is_contiguous(x) && aligned16(px) && aligned16(po)) {
+    scale_flat_kernel<<<grid_for(n / 4 + 1, st), kThreads, 0, s>>>(px, po, n, sc);
+    return check_launch("tb_scale");
+  }
+  Walk3 w;
+  w.rank = x->rank;
+  for (int i = 0; i < x->rank; ++i) {
+    w.shape[i] = x->shape[i];
+    w.s0[i] = out->strides[i];
+    w.s1[i] = x->strides[i];
+    w.s2[i] = 0;
+  }
+  w.o0 = w.o1 = w.o2 = 0;
+  merge_dims(w, 2);
+  scale_strided_kernel<<<grid_for(n, st), kThreads, 0, s>>>(px, po, n, sc, w);
+  return check_launch("tb_scale");
+}
+
+tb_status tb_copy(const tb_view *dst, const tb_view *src, tb_stream stream) {
+  TB_TRY(validate_view(dst, "tb_copy dst"));
+  TB_TRY(validate_view(src, "tb_copy src"));
+  // Tensor::copy_ (src/tensor/tensor.cpp:691-698): shapes and dtypes must match.
+  if (dst->rank != src->rank) return fail(TB_EINVAL, "Tensor::copy_ failed: Target and source shapes must match exactly.");
+  for (int i = 0; i < dst->rank; ++i)
+    if (dst->shape[i] != src->shape[i])
+      return fail(TB_EINVAL, "Tensor::copy_ failed: Target and source shapes must match exactly.");
+  if (dst->dtype != src->dtype)
+    return fail(TB_EINVAL, "Tensor::copy_ failed: Target and source data types must match.");
+  int es = dtype_size(dst->dtype);
+  if (es == 0) return fail(TB_EINVAL, "tb_copy: block-quantized views are copied as raw bytes (use a byte view)");
+  int64_t n = numel(dst);
+  if (n == 0) return TB_OK;
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  cudaStream_t s = as_stream(stream);
+  const char *ps = static_cast<const char *>(src->data) + src->offset * es;
+  char *pd = static_cast<char *>(dst->data) + dst->offset * es;
+  Walk3 w;
+  w.rank = dst->rank;
+  for (int i = 0; i < dst->rank; ++i) {
+    w.shape[i] = dst->shape[i];
+    w.s0[i] = dst->strides[i];
+    w.s1[i] = src->strides[i];
+    w.s2[i] = 0;
+  }
+  w.o0 = w.o1 = w.o2 = 0;
+  merge_dims(w, 2);
+  if (w.rank == 1 && w.s0[0] == 1 && w.s1[0] == 1) {
+    int64_t bytes = n * es;
+    if (aligned16(ps) && aligned16(pd) && bytes % 16 == 0) {
+      copy_flat16_kernel<<<grid_for(bytes / 32 + 1, st), kThreads, 0, s>>>(
+          reinterpret_cast<const uint4 *>(ps), reinterpret_cast<uint4 *>(pd), bytes / 16);
+      return check_launch("tb_copy");
+    }
+    cudaError_t e = cudaMemcpyAsync(pd, ps, bytes, cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return fail(TB_ECUDA, "tb_copy: %s", cudaGetErrorString(e));
+    return TB_OK;
+  }
+  // Transposed innermost pair: dst unit stride on the last merged dim, src on
+  // the one before it.
+  if (w.rank >= 2 && w.s0[w.rank - 1] == 1 && w.s1[w.rank - 2] == 1 && w.s1[w.rank - 1] != 1) {
+    int64_t R = w.shape[w.rank - 2], C = w.shape[w.rank - 1];
+    int64_t outer = n / (R * C);
+    int64_t tiles = outer * ((R + 31) / 32) * ((C + 31) / 32);
+    int grid = (int)std::min<int64_t>(tiles, (int64_t)st->sm_count * 8);
+    if (es == 4)
+      copy_transpose_kernel<float><<<grid, 256, 0, s>>>((const float *)ps, (float *)pd, outer, R, C, w);
+    else
+      copy_transpose_kernel<uint16_t><<<grid, 256, 0, s>>>((const uint16_t *)ps, (uint16_t *)pd, outer, R, C, w);
+    return check_launch("tb_copy");
+  }
+  if (es == 4)
+    copy_strided_kernel<float><<<grid_for(n, st), kThreads, 0, s>>>((const float *)ps, (float *)pd, n, w);
+  else
+    copy_strided_kernel<uint16_t><<<grid_for(n, st), kThreads, 0, s>>>((const uint16_t *)ps, (uint16_t *)pd, n, w);
+  return check_launch("tb_copy");
+}
+
+tb_status tb_swiglu(int dtype, const void *g, const void *u, void *y, int64_t n, tb_stream stream) {
+  if (n < 0) return fail(TB_EINVAL, "tb_swiglu: negative n");
+  if (n == 0) return TB_OK;
+  if (!g || !u || !y) return fail(TB_EINVAL, "tb_swiglu: null pointer");
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  cudaStream_t s = as_stream(stream);
+  int vec_ok = aligned16(g) && aligned16(u) && aligned16(y);
+  if (dtype == TB_F32) {
+    swiglu_kernel<float><<<grid_for(n / 4 + 1, st), kThreads, 0, s>>>(
+        (const float *)g, (const float *)u, (float *)y, n, vec_ok);
+  } else if (dtype == TB_BF16) {
+    swiglu_kernel<__nv_bfloat16><<<grid_for(n / 8 + 1, st), kThreads, 0, s>>>(
+        (const __nv_bfloat16 *)g, (const __nv_bfloat16 *)u, (__nv_bfloat16 *)y, n, vec_ok);
+  } else {
+    return fail(TB_EINVAL, "tb_swiglu: dtype must be TB_F32 or TB_BF16");
+  }
+  return check_launch("tb_swiglu");
+}
+
+}  // extern "C"

@@ -1,0 +1,300 @@
+// tb_gemv.cu -- quantized matmul on CUDA cores with the reference's exact
+// operation order (A10 decode GEMV, A11 Q4_0 rows).
+//
+// Q8_0 (src/tensor/quant_math.hpp:32-60): for every output,
+//   per block b:  bs_b = sum_j round(round(q_j * d_b) * x_j)   (sequential in j)
+//   y = sum_b bs_b                                            (sequential in b)
+// q*d is exact in fp32 (8-bit q times an 11-bit half scale), so the kernel may
+// form it any exact way; it builds it from a magic-number float (no int->float
+// conversion instruction) and keeps two blocks per lane in flight with the
+// sm_100a packed f32x2 add/mul/fma, each half rounded exactly like scalar IEEE.
+// The 32-term chains run one block per lane; the block sums land in shared
+// memory and one lane per row adds them in block order.
+//
+// Data movement: a CTA owns ROWS consecutive weight rows (one contiguous byte
+// range) and fetches all of it with one bulk TMA copy at kernel start, so the
+// whole matrix is in flight at once across the grid.  x is staged in shared
+// memory transposed ([j][block], padded) so that each lane pulls its two
+// blocks' 64 activations into registers without bank conflicts.
+#include <algorithm>
+
+#include "tb_internal.cuh"
+
+namespace tb {
+namespace {
+
+constexpr uint32_t kMagicHi = 0x4B400000u;  // float 12582912 = 3 * 2^22
+constexpr float kMagic = 12582912.0f;
+
+// Stages the CTA's weight byte range [B0, B1) (relative to W) into smem.
+// Returns the shift of byte B0 inside the staged buffer.  Thread 0 issues the
+// bulk copy of the 16-byte-aligned body; all threads load the ragged tail.
+// The caller __syncthreads() afterwards and waits on `bar` before reading.
+__device__ __forceinline__ int stage_rows(const uint8_t *__restrict__ W, int64_t B0, int64_t B1,
+                                          uint8_t *wsm, uint64_t *bar, bool use_tma) {
+  int64_t t0 = B0 & ~int64_t(15);
+  int shift = (int)(B0 - t0);
+  if (use_tma) {
+    int64_t t1 = B1 & ~int64_t(15);
+    uint32_t body = t1 > t0 ? (uint32_t)(t1 - t0) : 0u;
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(bar, body);
+      if (body) bulk_g2s(wsm, W + t0, body, bar);
+    }
+    int64_t tail0 = t1 > t0 ? t1 : B0;
+    for (int64_t i = tail0 + threadIdx.x; i < B1; i += blockDim.x) wsm[i - t0] = W[i];
+  } else {
+    if (threadIdx.x == 0) mbar_arrive(bar);
+    for (int64_t i = B0 + threadIdx.x; i < B1; i += blockDim.x) wsm[i - t0] = W[i];
+  }
+  return shift;
+}
+
+// Reads the 34-byte Q8_0 block at smem byte offset `off` (even): the scale as
+// float and the 32 quants as 8 little-endian words.
+__device__ __forceinline__ void load_q8_block(const uint8_t *wsm, int off, float &d,
+                                              uint32_t qw[8]) {
+  const uint32_t *w32 = reinterpret_cast<const uint32_t *>(wsm + (off & ~3));
+  uint32_t w[9];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) w[k] = w32[k];
+  const uint32_t sh = (uint32_t)(off & 3) * 8u;  // 0 or 16
+  d = half_bits_to_float((uint16_t)(__funnelshift_rc(w[0], w[1], sh) & 0xFFFFu));
+#pragma unroll
+  for (int k = 0; k < 8; ++k) qw[k] = __funnelshift_rc(w[k], w[k + 1], 16u + sh);
+}
+
+template <int NW>
+__global__ void __launch_bounds__(NW * 32) gemv_q8_0_kernel(
+    const uint8_t *__restrict__ W, const float *__restrict__ X, float *__restrict__ Y, int N,
+    int K, int M, int rows_per_cta, int use_tma, uint32_t *__restrict__ err) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int nb = K / 32;
+  const int rb = nb * 34;
+  const int XS = (nb & 1) ? nb + 2 : nb + 1;  // odd row pitch: conflict-free
+  const int rpw = rows_per_cta / NW;
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
+  float *xs = reinterpret_cast<float *>(smem + 128);
+  float *bsum = xs + 32 * XS;                       // [NW][rpw][nb + 1]
+  uint8_t *wsm = reinterpret_cast<uint8_t *>(bsum + NW * rpw * (nb + 1));
+  wsm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(wsm) + 127) & ~uintptr_t(127));
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int n0 = blockIdx.x * rows_per_cta;
+  const int n1 = min(N, n0 + rows_per_cta);
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int shift = stage_rows(W, (int64_t)n0 * rb, (int64_t)n1 * rb, wsm, bar, use_tma != 0);
+
+  float *mysum = bsum + warp * rpw * (nb + 1);
+  bool ready = false;
+  for (int m = 0; m < M; ++m) {
+    const float *xrow = X + (int64_t)m * K;
+    if (m > 0) __syncthreads();  // previous x no longer read
+    for (int i = threadIdx.x; i < K; i += blockDim.x) xs[(i & 31) * XS + (i >> 5)] = __ldg(xrow + i);
+    __syncthreads();
+    if (!ready) {
+      // Every thread waits; if any gave up, all leave together (no thread may
+      // be left behind at a later __syncthreads).
+      const bool ok = mbar_wait_bounded(bar, 0, err);
+      if (__syncthreads_or(!ok)) return;
+      ready = true;
+    }
+    for (int p = 0; p * 64 < nb; ++p) {
+      const int b1 = p * 64 + lane, b2 = b1 + 32;
+      const bool v1 = b1 < nb, v2 = b2 < nb;
+      uint64_t xp[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        xp[j] = pack2(v1 ? xs[j * XS + b1] : 0.f, v2 ? xs[j * XS + b2] : 0.f);
+      for (int rr = 0; rr < rpw; ++rr) {
+        const int r = warp * rpw + rr;
+        if (n0 + r >= n1) break;
+        const int rowoff = shift + r * rb;
+        float d1 = 0.f, d2 = 0.f;
+        uint32_t q1[8], q2[8];
+        load_q8_block(wsm, rowoff + 34 * (v1 ? b1 : 0), d1, q1);
+        load_q8_block(wsm, rowoff + 34 * (v2 ? b2 : 0), d2, q2);
+        float s1, s2;
+        if (isfinite(d1) && isfinite(d2)) {
+          const uint64_t dd = pack2(d1, d2);
+          const uint64_t c1 = pack2(-kMagic * d1, -kMagic * d2);  // exact: 3*2^22*d
+          const uint64_t c2 = pack2(-128.0f * d1, -128.0f * d2);
+          uint64_t acc = pack2(0.f, 0.f);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t u1 = q1[k] ^ 0x80808080u, u2 = q2[k] ^ 0x80808080u;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              // float(0x4B4000uu) = 12582912 + (q + 128)
+              const uint32_t sel = 0x7650u | (uint32_t)e;
+              const float m1 = __uint_as_float(__byte_perm(u1, kMagicHi, sel));
+              const float m2 = __uint_as_float(__byte_perm(u2, kMagicHi, sel));
+              uint64_t t = fma2(pack2(m1, m2), dd, c1);  // (q+128)*d, exact
+              t = add2(t, c2);                           // q*d, exact
+              acc = add2(acc, mul2(t, xp[4 * k + e]));   // += round(w * x)
+            }
+          }
+          unpack2(acc, s1, s2);
+        } else {  // non-finite scale: the plain expression, as the reference
+          s1 = 0.f;
+          s2 = 0.f;
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float x1, x2;
+              unpack2(xp[4 * k + e], x1, x2);
+              s1 = __fadd_rn(s1, __fmul_rn(__fmul_rn((float)(int8_t)(q1[k] >> (8 * e)), d1), x1));
+              s2 = __fadd_rn(s2, __fmul_rn(__fmul_rn((float)(int8_t)(q2[k] >> (8 * e)), d2), x2));
+            }
+        }
+        if (v1) mysum[rr * (nb + 1) + b1] = s1;
+        if (v2) mysum[rr * (nb + 1) + b2] = s2;
+      }
+    }
+    __syncwarp();
+    if (lane < rpw && n0 + warp * rpw + lane < n1) {
+      const float *bs = mysum + lane * (nb + 1);
+      float s = 0.f;
+      for (int b = 0; b < nb; ++b) s = __fadd_rn(s, bs[b]);
+      Y[(int64_t)m * N + n0 + warp * rpw + lane] = s;
+    }
+    __syncwarp();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Q4_0 weights times Q8_0-quantized activations, in the order of
+// vec_dot_q4_0_q8_0_avx2 (quant_math.hpp:184-248): eight fp32 lanes, lane l
+// accumulating, block after block, fma(p0, d, acc) then fma(p1, d, acc) where
+// p0/p1 are the exact int pair sums of elements (2l, 2l+1) and (16+2l, 17+2l)
+// and d = d_w * d_x; the eight lanes are then added in order.  Here the eight
+// accumulators of one output are eight threads of a warp (4 outputs per warp).
+template <int NW>
+__global__ void __launch_bounds__(NW * 32) matmul_q4_0_kernel(
+    const uint8_t *__restrict__ W, const uint8_t *__restrict__ XQ, float *__restrict__ Y, int N,
+    int K, int M, int rows_per_cta, int use_tma, uint32_t *__restrict__ err) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int nb = K / 32;
+  const int rb = nb * 18;
+  const int xb = nb * 34;
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
+  uint8_t *xsm = smem + 128;
+  uint8_t *wsm = xsm + ((xb + 127) & ~127);
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int l = lane & 7, sub = lane >> 3;
+  const int n0 = blockIdx.x * rows_per_cta;
+  const int n1 = min(N, n0 + rows_per_cta);
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  const int shift = stage_rows(W, (int64_t)n0 * rb, (int64_t)n1 * rb, wsm, bar, use_tma != 0);
+  bool ready = false;
+  for (int m = 0; m < M; ++m) {
+    if (m > 0) __syncthreads();
+    const uint8_t *xq = XQ + (int64_t)m * xb;
+    for (int i = threadIdx.x; i < xb / 2; i += blockDim.x)
+      reinterpret_cast<uint16_t *>(xsm)[i] = reinterpret_cast<const uint16_t *>(xq)[i];
+    __syncthreads();
+    if (!ready) {
+      const bool ok = mbar_wait_bounded(bar, 0, err);
+      if (__syncthreads_or(!ok)) return;
+      ready = true;
+    }
+    for (int r0 = warp * 4; r0 < n1 - n0; r0 += NW * 4) {
+      const int r = r0 + sub;
+      const bool valid = r < n1 - n0;
+      const uint8_t *wrow = wsm + shift + (valid ? r : 0) * rb;
+      float acc = 0.f;
+      for (int b = 0; b < nb; ++b) {
+        const uint8_t *wbk = wrow + 18 * b;
+        const uint8_t *xbk = xsm + 34 * b;
+        const uint16_t wd = *reinterpret_cast<const uint16_t *>(wbk);
+        const uint16_t w2 = *reinterpret_cast<const uint16_t *>(wbk + 2 + 2 * l);
+        const uint16_t xd = *reinterpret_cast<const uint16_t *>(xbk);
+        const uint16_t a01 = *reinterpret_cast<const uint16_t *>(xbk + 2 + 2 * l);
+        const uint16_t a23 = *reinterpret_cast<const uint16_t *>(xbk + 18 + 2 * l);
+        const float d = __fmul_rn(half_bits_to_float(wd), half_bits_to_float(xd));
+        const int w00 = (int)(w2 & 0x0F) - 8, w01 = (int)((w2 >> 8) & 0x0F) - 8;
+        const int w10 = (int)((w2 >> 4) & 0x0F) - 8, w11 = (int)(w2 >> 12) - 8;
+        const int p0 = w00 * (int)(int8_t)(a01 & 0xFF) + w01 * (int)(int8_t)(a01 >> 8);
+        const int p1 = w10 * (int)(int8_t)(a23 & 0xFF) + w11 * (int)(int8_t)(a23 >> 8);
+        // |p| <= 2032: exact as 12582912 + p, then subtract the magic
+        const float f0 = __fsub_rn(__int_as_float((int)kMagicHi + p0), kMagic);
+        const float f1 = __fsub_rn(__int_as_float((int)kMagicHi + p1), kMagic);
+        acc = __fmaf_rn(f0, d, acc);
+        acc = __fmaf_rn(f1, d, acc);
+      }
+      float s = 0.f;
+#pragma unroll
+      for (int k = 0; k < 8; ++k) s = __fadd_rn(s, __shfl_sync(0xffffffffu, acc, (lane & ~7) + k));
+      if (valid && l == 0) Y[(int64_t)m * N + n0 + r] = s;
+    }
+  }
+}
+
+size_t q8_smem_bytes(int K, int rows, int nw) {
+  int nb = K / 32;
+  int XS = (nb & 1) ? nb + 2 : nb + 1;
+  size_t s = 128 + (size_t)32 * XS * 4 + (size_t)rows * (nb + 1) * 4;
+  s = (s + 127) & ~size_t(127);
+  s += (size_t)rows * nb * 34 + 32;
+  (void)nw;
+  return s;
+}
+
+size_t q4_smem_bytes(int K, int rows) {
+  int nb = K / 32;
+  return 128 + (size_t)((nb * 34 + 127) & ~127) + (size_t)rows * nb * 18 + 32;
+}
+
+}  // namespace
+
+// Shared with the tensor-core path: exact CUDA-core quantized matmul.
+tb_status launch_q8_0_exact(const float *x, int64_t M, int64_t K, const void *w, int64_t N,
+                            float *y, cudaStream_t s, const DeviceState *st) {
+  constexpr int NW = 4;
+  // ~36 KB of weights per CTA (a multiple of NW rows), several CTAs per SM.
+  int rb = (int)(K / 32 * 34);
+  int rows = std::max(NW, (36 * 1024 / rb) / NW * NW);
+  rows = std::min(rows, 64);
+  size_t smem = q8_smem_bytes((int)K, rows, NW);
+  while (smem > (size_t)st->smem_optin && rows > NW) {
+    rows -= NW;
+    smem = q8_smem_bytes((int)K, rows, NW);
+  }
+  if (smem > (size_t)st->smem_optin) return fail(TB_EINVAL, "tb_matmul_quant: K=%lld too large", (long long)K);
+  int use_tma = (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+  TB_TRY(ensure_smem_for(gemv_q8_0_kernel<NW>, smem));
+  unsigned grid = (unsigned)((N + rows - 1) / rows);
+  gemv_q8_0_kernel<NW><<<grid, NW * 32, smem, s>>>((const uint8_t *)w, x, y, (int)N, (int)K, (int)M,
+                                                   rows, use_tma, st->err_word);
+  return check_launch("tb_matmul_quant(Q8_0)");
+}
+
+tb_status launch_q4_0_exact(const uint8_t *xq, int64_t M, int64_t K, const void *w, int64_t N,
+                            float *y, cudaStream_t s, const DeviceState *st) {
+  constexpr int NW = 8;
+  int rb = (int)(K / 32 * 18);
+  int rows = std::max(NW * 4, (32 * 1024 / rb) / (NW * 4) * (NW * 4));
+  size_t smem = q4_smem_bytes((int)K, rows);
+  while (smem > (size_t)st->smem_optin && rows > 4) {
+    rows -= 4;
+    smem = q4_smem_bytes((int)K, rows);
+  }
+  if (smem > (size_t)st->smem_optin) return fail(TB_EINVAL, "tb_matmul_quant: K=%lld too large", (long long)K);
+  int use_tma = (reinterpret_cast<uintptr_t>(w) & 15) == 0;
+  TB_TRY(ensure_smem_for(matmul_q4_0_kernel<NW>, smem));
+  unsigned grid = (unsigned)((N + rows - 1) / rows);
+  matmul_q4_0_kernel<NW><<<grid, NW * 32, smem, s>>>((const uint8_t *)w, xq, y, (int)N, (int)K, (int)M,
+                                                     rows, use_tma, st->err_word);
+  return check_launch("tb_matmul_quant(Q4_0)");
+}
+
+}  // namespace tb

@@ -1,0 +1,201 @@
+// tb_internal.cuh -- shared host/device helpers of the sm_100a kernels.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "turbo_b200.h"
+
+namespace tb {
+
+// ------------------------------------------------------------------ host side
+
+struct DeviceState {
+  int device = -1;
+  int sm_count = 0;
+  int smem_optin = 0;     // max dynamic shared memory per block (opt-in)
+  uint32_t *err_word = nullptr;  // device error word (bit 0 timeout, bit 1 index)
+};
+
+// Per-device state of the current device; creates it on first use.
+tb_status device_state(DeviceState **out);
+
+// Records `msg` as the calling thread's last error and returns `s`.
+tb_status fail(tb_status s, const char *fmt, ...);
+
+// Maps a pending launch error to TB_ECUDA.
+tb_status check_launch(const char *what);
+
+inline cudaStream_t as_stream(tb_stream s) { return reinterpret_cast<cudaStream_t>(s); }
+
+#define TB_TRY(expr)                                                                            \
+  do {                                                                                          \
+    tb_status _tb_s = (expr);                                                                   \
+    if (_tb_s != TB_OK) return _tb_s;                                                           \
+  } while (0)
+
+// Element size of the plain (non-block) dtypes; 0 for block formats.
+inline int dtype_size(int dt) {
+  switch (dt) {
+    case TB_F32: return 4;
+    case TB_F16: return 2;
+    case TB_I32: return 4;
+    case TB_BF16: return 2;
+    default: return 0;
+  }
+}
+
+// A view with its dimensions merged where memory allows (fewer index steps).
+struct Shape {
+  int rank = 0;
+  int64_t shape[TB_MAX_RANK];
+  int64_t stride[TB_MAX_RANK];
+};
+
+inline int64_t numel(const tb_view *v) {
+  // Tensor::numel (src/tensor/tensor.cpp:99-106): rank 0 counts as empty.
+  if (v->rank <= 0) return 0;
+  int64_t n = 1;
+  for (int i = 0; i < v->rank; ++i) n *= v->shape[i];
+  return n;
+}
+
+inline bool is_contiguous(const tb_view *v) {
+  // Tensor::is_contiguous (src/tensor/tensor.cpp:108-116).
+  int64_t expect = 1;
+  for (int i = v->rank - 1; i >= 0; --i) {
+    if (v->strides[i] != expect) return false;
+    expect *= v->shape[i];
+  }
+  return true;
+}
+
+tb_status validate_view(const tb_view *v, const char *name);
+
+// Raises the dynamic shared memory limit of `func` on the current device to at
+// least `bytes`, once per (function, device): later launches make no runtime
+// call besides the launch itself, so they can be captured in CUDA graphs.
+tb_status ensure_smem(const void *func, size_t bytes);
+template <typename F> inline tb_status ensure_smem_for(F *func, size_t bytes) {
+  return ensure_smem(reinterpret_cast<const void *>(func), bytes);
+}
+
+// ----------------------------------------------------------------- device side
+
+constexpr uint32_t ERR_TIMEOUT = 1u;
+constexpr uint32_t ERR_INDEX = 2u;
+
+__device__ __forceinline__ float half_bits_to_float(uint16_t h) {
+  return __half2float(__ushort_as_half(h));
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// ---- mbarrier + bulk-copy (TMA, non-tensor) helpers -------------------------
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(phase)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for `phase` of `bar` for at most `limit_ns`; on timeout sets
+// ERR_TIMEOUT in *err and returns false.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t phase, uint32_t *err,
+                                                  uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait(bar, phase)) return true;
+  uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    if (mbar_try_wait(bar, phase)) return true;
+    if ((it & 255u) == 255u && globaltimer_ns() - t0 > limit_ns) {
+      if (err) atomicOr(err, ERR_TIMEOUT);
+      return false;
+    }
+  }
+}
+
+// Bulk global->shared copy completing on `bar` (16-byte aligned addresses,
+// size a multiple of 16).  No multicast.
+__device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src_gmem, uint32_t bytes,
+                                         uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+          "r"(smem_addr(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// ---- packed fp32 pairs (sm_100a f32x2 arithmetic; each lane op is IEEE rn) ---
+
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t r;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+  return r;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t r;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+  return r;
+}
+
+// ---- exp as the reference's libm does it -------------------------------------
+// The reference calls glibc expf, which returns the correctly rounded value in
+// all but a vanishing fraction of cases.  exp evaluated in double precision and
+// rounded once to float is also the correctly rounded value unless exp(x) lies
+// within about one double ulp of a float rounding boundary, so the two agree
+// almost everywhere (the tests count the rare differences, all of one ulp).
+__device__ __forceinline__ float exp_ref(float x) { return __double2float_rn(exp((double)x)); }
+
+}  // namespace tb

@@ -1,0 +1,114 @@
+// tb_matmul_f32.cu -- batched strided fp32 matmul (A12): the attention score
+// and context products of src/nn/attention.cpp:115-132 and fp32 Linear layers.
+//
+// Each output is the FMA chain over k = 0..K-1 in increasing order starting
+// from 0, which is what the reference's packed AVX2 kernel computes per output
+// element (src/tensor/tensor.cpp:503-538), so results are bit-identical.  The
+// products are small in the decode path (K = head_dim = 64); a CTA computes a
+// 32x8 tile of outputs, one per thread, walking k in order.
+#include <algorithm>
+
+#include "tb_internal.cuh"
+
+namespace tb {
+namespace {
+
+struct MMView {
+  int rank;
+  int64_t batch, M, K, N;
+  int64_t bshape[TB_MAX_RANK];
+  int64_t sa_b[TB_MAX_RANK], sb_b[TB_MAX_RANK];
+  int64_t sam, sak, sbk, sbn;
+  int64_t oa, ob;
+};
+
+constexpr int TN = 32, TM = 8;
+
+__global__ void __launch_bounds__(TN * TM) matmul_f32_kernel(const float *__restrict__ a,
+                                                             const float *__restrict__ b,
+                                                             float *__restrict__ out, MMView v) {
+  const int64_t tiles_n = (v.N + TN - 1) / TN, tiles_m = (v.M + TM - 1) / TM;
+  const int64_t tiles = v.batch * tiles_m * tiles_n;
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    int64_t bi = t / (tiles_m * tiles_n);
+    int64_t rem = t % (tiles_m * tiles_n);
+    int64_t m = (rem / tiles_n) * TM + threadIdx.y;
+    int64_t n = (rem % tiles_n) * TN + threadIdx.x;
+    int64_t ao = v.oa, bo = v.ob, tb_ = bi;
+    for (int d = v.rank - 3; d >= 0; --d) {
+      int64_t idx = tb_ % v.bshape[d];
+      tb_ /= v.bshape[d];
+      ao += idx * v.sa_b[d];
+      bo += idx * v.sb_b[d];
+    }
+    if (m < v.M && n < v.N) {
+      const float *ar = a + ao + m * v.sam;
+      const float *bc = b + bo + n * v.sbn;
+      float c = 0.f;
+      int64_t k = 0;
+      for (; k + 4 <= v.K; k += 4) {
+        float a0 = __ldg(ar + k * v.sak), a1 = __ldg(ar + (k + 1) * v.sak);
+        float a2 = __ldg(ar + (k + 2) * v.sak), a3 = __ldg(ar + (k + 3) * v.sak);
+        float b0 = __ldg(bc + k * v.sbk), b1 = __ldg(bc + (k + 1) * v.sbk);
+        float b2 = __ldg(bc + (k + 2) * v.sbk), b3 = __ldg(bc + (k + 3) * v.sbk);
+        c = __fmaf_rn(a0, b0, c);
+        c = __fmaf_rn(a1, b1, c);
+        c = __fmaf_rn(a2, b2, c);
+        c = __fmaf_rn(a3, b3, c);
+      }
+      for (; k < v.K; ++k) c = __fmaf_rn(__ldg(ar + k * v.sak), __ldg(bc + k * v.sbk), c);
+      out[(bi * v.M + m) * v.N + n] = c;
+    }
+  }
+}
+
+}  // namespace
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" tb_status tb_matmul_f32(const tb_view *a, const tb_view *b, const tb_view *out,
+                                   tb_stream stream) {
+  TB_TRY(validate_view(a, "tb_matmul_f32 a"));
+  TB_TRY(validate_view(b, "tb_matmul_f32 b"));
+  TB_TRY(validate_view(out, "tb_matmul_f32 out"));
+  if (a->dtype != TB_F32 || b->dtype != TB_F32 || out->dtype != TB_F32)
+    return fail(TB_EINVAL, "tb_matmul_f32: fp32 only");
+  // Tensor::matmul checks (src/tensor/tensor.cpp:321-323, 434-455).
+  if (a->rank < 2 || b->rank < 2) return fail(TB_EINVAL, "matmul requires at least 2D tensors");
+  if (a->rank != b->rank) return fail(TB_EINVAL, "matmul requires both tensors to have the same rank");
+  int r = a->rank;
+  MMView v;
+  v.rank = r;
+  v.batch = 1;
+  for (int i = 0; i < r - 2; ++i) {
+    if (a->shape[i] != b->shape[i]) return fail(TB_EINVAL, "Batch dimensions must match");
+    v.bshape[i] = a->shape[i];
+    v.sa_b[i] = a->strides[i];
+    v.sb_b[i] = b->strides[i];
+    v.batch *= a->shape[i];
+  }
+  v.M = a->shape[r - 2];
+  v.K = a->shape[r - 1];
+  v.N = b->shape[r - 1];
+  if (v.K != b->shape[r - 2]) return fail(TB_EINVAL, "Inner dimensions must match");
+  if (out->rank != r || !is_contiguous(out)) return fail(TB_EINVAL, "tb_matmul_f32: out must be contiguous [batch..., M, N]");
+  for (int i = 0; i < r - 2; ++i)
+    if (out->shape[i] != a->shape[i]) return fail(TB_EINVAL, "tb_matmul_f32: out batch shape");
+  if (out->shape[r - 2] != v.M || out->shape[r - 1] != v.N) return fail(TB_EINVAL, "tb_matmul_f32: out shape");
+  v.sam = a->strides[r - 2];
+  v.sak = a->strides[r - 1];
+  v.sbk = b->strides[r - 2];
+  v.sbn = b->strides[r - 1];
+  v.oa = a->offset;
+  v.ob = b->offset;
+  int64_t tiles = v.batch * ((v.M + TM - 1) / TM) * ((v.N + TN - 1) / TN);
+  if (tiles == 0) return TB_OK;
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  int grid = (int)std::min<int64_t>(tiles, (int64_t)st->sm_count * 16);
+  matmul_f32_kernel<<<grid, dim3(TN, TM), 0, as_stream(stream)>>>(
+      static_cast<const float *>(a->data), static_cast<const float *>(b->data),
+      static_cast<float *>(out->data) + out->offset, v);
+  return check_launch("tb_matmul_f32");
+}

@@ -1,0 +1,511 @@
+// tb_rows.cu -- row reductions: RMSNorm (A7), softmax (A9), argmax (A15) and
+// the per-shard halves of the vocab-sharded softmax/argmax.
+//
+// Long rows (a 128256-entry logits row is 501 KiB) are split over a thread
+// block cluster: each CTA stages its slice of the row in shared memory, the
+// CTAs exchange their partial maxima/sums through distributed shared memory,
+// and the row is read from HBM once and written once, in one launch.
+#include <cooperative_groups.h>
+
+#include <algorithm>
+
+#include "tb_internal.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace tb {
+namespace {
+
+constexpr int kRowThreads = 256;
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ uint64_t warp_max_u64(uint64_t v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    uint64_t w = __shfl_xor_sync(0xffffffffu, v, o);
+    v = w > v ? w : v;
+  }
+  return v;
+}
+
+// Block-wide reductions (blockDim.x a multiple of 32, <= 1024); result in all threads.
+__device__ float block_sum(float v, float *scratch) {
+  v = warp_sum(v);
+  int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) scratch[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < nw; ++i) t += scratch[i];  // fixed order: deterministic
+  return t;
+}
+__device__ float block_max(float v, float *scratch) {
+  v = warp_max(v);
+  int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) scratch[w] = v;
+  __syncthreads();
+  float t = -INFINITY;
+  for (int i = 0; i < nw; ++i) t = fmaxf(t, scratch[i]);
+  return t;
+}
+__device__ uint64_t block_max_u64(uint64_t v, uint64_t *scratch) {
+  v = warp_max_u64(v);
+  int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) scratch[w] = v;
+  __syncthreads();
+  uint64_t t = 0;
+  for (int i = 0; i < nw; ++i) t = scratch[i] > t ? scratch[i] : t;
+  return t;
+}
+
+// ---------------------------------------------------------------- RMSNorm ----
+// One CTA per row (grid-stride over rows); the row stays in registers between
+// the sum of squares and the normalisation, so x is read once.
+// y = (x / rms) * gamma with rms = sqrtf(sum(x*x) / cols + eps)
+// (src/nn/rmsnorm.cpp:38-47); the sum is a tree, the rest IEEE as the reference.
+template <typename T> struct RV;
+template <> struct RV<float> { static constexpr int N = 4; };
+template <> struct RV<__nv_bfloat16> { static constexpr int N = 8; };
+__device__ __forceinline__ float tf(float v) { return v; }
+__device__ __forceinline__ float tf(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T> __device__ __forceinline__ T ft(float v);
+template <> __device__ __forceinline__ float ft<float>(float v) { return v; }
+template <> __device__ __forceinline__ __nv_bfloat16 ft<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+
+template <typename T, int VPT>
+__global__ void __launch_bounds__(kRowThreads) rmsnorm_vec_kernel(const T *__restrict__ x,
+                                                                  const float *__restrict__ gamma,
+                                                                  T *__restrict__ y, int64_t rows,
+                                                                  int cols, float eps) {
+  constexpr int V = RV<T>::N;
+  __shared__ float scratch[32];
+  const int nvec = cols / V;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const uint4 *xr = reinterpret_cast<const uint4 *>(x + r * cols);
+    uint4 v[VPT];
+    float ss = 0.f;
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      int i = threadIdx.x + k * kRowThreads;
+      if (i < nvec) {
+        v[k] = __ldcs(xr + i);
+        const T *e = reinterpret_cast<const T *>(&v[k]);
+#pragma unroll
+        for (int j = 0; j < V; ++j) {
+          float f = tf(e[j]);
+          ss = __fadd_rn(ss, __fmul_rn(f, f));
+        }
+      }
+    }
+    ss = block_sum(ss, scratch);
+    float mean = __fdiv_rn(ss, (float)cols);
+    float rms = __fsqrt_rn(__fadd_rn(mean, eps));
+    uint4 *yr = reinterpret_cast<uint4 *>(y + r * cols);
+    const float4 *g4 = reinterpret_cast<const float4 *>(gamma);
+#pragma unroll
+    for (int k = 0; k < VPT; ++k) {
+      int i = threadIdx.x + k * kRowThreads;
+      if (i < nvec) {
+        const T *e = reinterpret_cast<const T *>(&v[k]);
+        uint4 o;
+        T *oe = reinterpret_cast<T *>(&o);
+#pragma unroll
+        for (int j = 0; j < V; j += 4) {
+          float4 g = __ldg(g4 + (i * V + j) / 4);
+          oe[j + 0] = ft<T>(__fmul_rn(__fdiv_rn(tf(e[j + 0]), rms), g.x));
+          oe[j + 1] = ft<T>(__fmul_rn(__fdiv_rn(tf(e[j + 1]), rms), g.y));
+          oe[j + 2] = ft<T>(__fmul_rn(__fdiv_rn(tf(e[j + 2]), rms), g.z));
+          oe[j + 3] = ft<T>(__fmul_rn(__fdiv_rn(tf(e[j + 3]), rms), g.w));
+        }
+        __stcs(yr + i, o);
+      }
+    }
+  }
+}
+
+// Any cols / alignment: two reads of the row.
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads) rmsnorm_any_kernel(const T *__restrict__ x,
+                                                                  const float *__restrict__ gamma,
+                                                                  T *__restrict__ y, int64_t rows,
+                                                                  int64_t cols, float eps) {
+  __shared__ float scratch[32];
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const T *xr = x + r * cols;
+    float ss = 0.f;
+    for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) {
+      float f = tf(xr[i]);
+      ss = __fadd_rn(ss, __fmul_rn(f, f));
+    }
+    ss = block_sum(ss, scratch);
+    float rms = __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, (float)cols), eps));
+    for (int64_t i = threadIdx.x; i < cols; i += blockDim.x)
+      y[r * cols + i] = ft<T>(__fmul_rn(__fdiv_rn(tf(xr[i]), rms), gamma[i]));
+  }
+}
+
+// ---------------------------------------------------------------- softmax ----
+// MODE 0: full softmax of each row (src/nn/softmax.cpp:30-50):
+//   M = max, e = exp(x - M) stored, S = sum e, y = e / S.
+// MODE 1: shard statistics only: row max and sum of exp(x - max) of this slice.
+// The cluster's CTAs split the row's columns; CTA rank c owns [c*span, ...).
+template <int MODE>
+__global__ void __launch_bounds__(kRowThreads) softmax_cluster_kernel(
+    const float *__restrict__ x, float *__restrict__ y, int64_t rows, int64_t cols, int64_t ldx,
+    int64_t ldy, int span, float *__restrict__ out_max, float *__restrict__ out_sum) {
+  extern __shared__ float slice[];  // span floats
+  __shared__ float scratch[32];
+  __shared__ float part[2];  // this CTA's [max, sum] for the cluster exchange
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = (int)cluster.block_rank();
+  const int csize = (int)cluster.num_blocks();
+  const int64_t row = blockIdx.x / csize;
+  if (row >= rows) return;  // whole clusters share a row, so this is uniform
+  const int64_t c0 = (int64_t)crank * span;
+  const int64_t c1 = (c0 + span < cols) ? c0 + span : cols;
+  const int n = c1 > c0 ? (int)(c1 - c0) : 0;
+  const float *xr = x + row * ldx + c0;
+
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = xr[i];
+    slice[i] = v;
+    m = (v > m) ? v : m;  // NaN never becomes the max (strict '>')
+  }
+  m = block_max(m, scratch);
+  if (threadIdx.x == 0) part[0] = m;
+  cluster.sync();
+  float M = -INFINITY;
+  for (int c = 0; c < csize; ++c) {
+    float pm = *cluster.map_shared_rank(&part[0], c);
+    M = (pm > M) ? pm : M;
+  }
+  float s = 0.f;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float e = exp_ref(__fsub_rn(slice[i], M));
+    slice[i] = e;
+    s = __fadd_rn(s, e);
+  }
+  s = block_sum(s, scratch);
+  if (threadIdx.x == 0) part[1] = s;
+  cluster.sync();
+  float S = 0.f;
+  for (int c = 0; c < csize; ++c) S = __fadd_rn(S, *cluster.map_shared_rank(&part[1], c));
+  if (MODE == 1) {
+    if (crank == 0 && threadIdx.x == 0) {
+      out_max[row] = M;
+      out_sum[row] = S;
+    }
+  } else {
+    float *yr = y + row * ldy + c0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) yr[i] = __fdiv_rn(slice[i], S);
+  }
+  cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
+}
+
+// Rows too long for the cluster's shared memory: online max/sum, then a
+// second read for the output.
+__global__ void __launch_bounds__(kRowThreads) softmax_long_kernel(const float *__restrict__ x,
+                                                                   float *__restrict__ y,
+                                                                   int64_t rows, int64_t cols) {
+  __shared__ float scratch[32];
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float *xr = x + r * cols;
+    float m = -INFINITY;
+    for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) m = xr[i] > m ? xr[i] : m;
+    m = block_max(m, scratch);
+    float s = 0.f;
+    for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) s = __fadd_rn(s, exp_ref(__fsub_rn(xr[i], m)));
+    s = block_sum(s, scratch);
+    for (int64_t i = threadIdx.x; i < cols; i += blockDim.x)
+      y[r * cols + i] = __fdiv_rn(exp_ref(__fsub_rn(xr[i], m)), s);
+  }
+}
+
+// Shard finish: y = exp(x - M) / S for this shard's columns.
+__global__ void __launch_bounds__(kRowThreads) softmax_finish_kernel(
+    const float *__restrict__ x, int64_t rows, int64_t cols, int64_t ldx,
+    const float *__restrict__ gmax, const float *__restrict__ gsum, float *__restrict__ y,
+    int64_t ldy) {
+  int64_t total = rows * cols;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = t / cols, c = t % cols;
+    y[r * ldy + c] = __fdiv_rn(exp_ref(__fsub_rn(x[r * ldx + c], gmax[r])), gsum[r]);
+  }
+}
+
+__global__ void softmax_rescale_kernel(const float *__restrict__ lmax, const float *__restrict__ gmax,
+                                       float *__restrict__ sum, int64_t rows) {
+  int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < rows) sum[r] = __fmul_rn(sum[r], exp_ref(__fsub_rn(lmax[r], gmax[r])));
+}
+
+// ----------------------------------------------------------------- argmax ----
+// Key of a candidate: order-preserving bits of the value in the high word and
+// 0xFFFFFFFF - column in the low word, so the largest key is the largest value
+// and, among equal values, the first column.  Only values > -inf that are not
+// NaN are candidates (greedy_sample, src/core/sampler.cpp:17-24, takes x only
+// when x > running max, which starts at -inf); key 0 = no candidate -> index 0.
+__device__ __forceinline__ uint64_t argmax_key(float v, int64_t col) {
+  if (!(v > -INFINITY)) return 0ull;
+  uint32_t b = __float_as_uint(v);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((uint64_t)b << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)col);
+}
+
+// KEYS = 0: writes the row's index; KEYS = 1: writes the row's key (shards).
+template <int KEYS>
+__global__ void __launch_bounds__(kRowThreads) argmax_cluster_kernel(
+    const float *__restrict__ x, int64_t rows, int64_t cols, int64_t ldx, int64_t col_base,
+    int span, int64_t *__restrict__ idx_out, uint64_t *__restrict__ key_out) {
+  __shared__ uint64_t scratch[32];
+  __shared__ uint64_t part;
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = (int)cluster.block_rank();
+  const int csize = (int)cluster.num_blocks();
+  const int64_t row = blockIdx.x / csize;
+  if (row >= rows) return;
+  const int64_t c0 = (int64_t)crank * span;
+  const int64_t c1 = (c0 + span < cols) ? c0 + span : cols;
+  const float *xr = x + row * ldx;
+  uint64_t best = 0;
+  const bool vec = ((reinterpret_cast<uintptr_t>(xr + c0) & 15) == 0);
+  int64_t i = c0 + threadIdx.x * 4;
+  if (vec) {
+    for (; i + 3 < c1; i += (int64_t)blockDim.x * 4) {
+      float4 v = __ldcs(reinterpret_cast<const float4 *>(xr + i));
+      uint64_t k0 = argmax_key(v.x, col_base + i), k1 = argmax_key(v.y, col_base + i + 1);
+      uint64_t k2 = argmax_key(v.z, col_base + i + 2), k3 = argmax_key(v.w, col_base + i + 3);
+      k0 = k1 > k0 ? k1 : k0;
+      k2 = k3 > k2 ? k3 : k2;
+      k0 = k2 > k0 ? k2 : k0;
+      best = k0 > best ? k0 : best;
+    }
+    // remaining columns of this slice
+    for (int64_t j = c0 + ((c1 - c0) / 4) * 4 + threadIdx.x; j < c1; j += blockDim.x) {
+      uint64_t k = argmax_key(xr[j], col_base + j);
+      best = k > best ? k : best;
+    }
+  } else {
+    for (int64_t j = c0 + threadIdx.x; j < c1; j += blockDim.x) {
+      uint64_t k = argmax_key(xr[j], col_base + j);
+      best = k > best ? k : best;
+    }
+  }
+  best = block_max_u64(best, scratch);
+  if (threadIdx.x == 0) part = best;
+  cluster.sync();
+  if (crank == 0 && threadIdx.x == 0) {
+    uint64_t k = 0;
+    for (int c = 0; c < csize; ++c) {
+      uint64_t p = *cluster.map_shared_rank(&part, c);
+      k = p > k ? p : k;
+    }
+    if (KEYS) key_out[row] = k;
+    else idx_out[row] = k ? (int64_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFu)) : 0;
+  }
+  cluster.sync();
+}
+
+__global__ void key_index_kernel(const uint64_t *__restrict__ keys, int64_t rows,
+                                 int64_t *__restrict__ idx) {
+  int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < rows) {
+    uint64_t k = keys[r];
+    idx[r] = k ? (int64_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFu)) : 0;
+  }
+}
+
+// Cluster size for a row of `cols` columns: enough CTAs that each slice fits
+// the shared memory budget, at most 8 (the portable cluster size); 0 when the
+// row needs more than that.
+int cluster_for(int64_t cols, int64_t smem_budget_floats) {
+  int c = 1;
+  while (c < 8 && (cols + c - 1) / c > smem_budget_floats) c *= 2;
+  if ((cols + c - 1) / c > smem_budget_floats) return 0;
+  // Spread long rows for latency even when one CTA could hold them.
+  while (c < 8 && (cols + c - 1) / c > 8192) c *= 2;
+  return c;
+}
+
+template <typename Kern, typename... Args>
+tb_status launch_cluster(Kern k, int64_t rows, int csize, size_t smem, cudaStream_t s,
+                         Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(rows * csize), 1, 1);
+  cfg.blockDim = dim3(kRowThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = csize;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (csize > 8) {
+    static bool nonportable = false;  // one attribute call per process
+    if (!nonportable) {
+      cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e != cudaSuccess) return fail(TB_ECUDA, "cluster attribute: %s", cudaGetErrorString(e));
+      nonportable = true;
+    }
+  }
+  TB_TRY(ensure_smem_for(k, smem));
+  cudaError_t e = cudaLaunchKernelEx(&cfg, k, args...);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "cluster launch: %s", cudaGetErrorString(e));
+  return TB_OK;
+}
+
+constexpr int64_t kSliceFloats = (96 * 1024) / 4;  // dynamic smem per CTA for a slice
+
+}  // namespace
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" {
+
+tb_status tb_rmsnorm(int dtype, const void *x, const float *gamma, void *y, int64_t rows,
+                     int64_t cols, float eps, tb_stream stream) {
+  if (rows < 0 || cols <= 0) return fail(TB_EINVAL, "Input last dimension must match hidden_size.");
+  if (rows == 0) return TB_OK;
+  if (!x || !gamma || !y) return fail(TB_EINVAL, "tb_rmsnorm: null pointer");
+  if (dtype != TB_F32 && dtype != TB_BF16) return fail(TB_EINVAL, "tb_rmsnorm: dtype must be TB_F32 or TB_BF16");
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  cudaStream_t s = as_stream(stream);
+  int64_t grid = std::min<int64_t>(rows, (int64_t)st->sm_count * 8);
+  const int V = dtype == TB_F32 ? 4 : 8;
+  bool al = ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(y) |
+              reinterpret_cast<uintptr_t>(gamma)) & 15) == 0;
+  int64_t nvec = cols / V;
+  int vpt = (int)((nvec + kRowThreads - 1) / kRowThreads);
+  if (al && cols % V == 0 && vpt <= 8) {
+    int pick = vpt <= 1 ? 1 : vpt <= 2 ? 2 : vpt <= 4 ? 4 : 8;
+#define TB_RMS(T, P)                                                                         \
+  rmsnorm_vec_kernel<T, P><<<(int)grid, kRowThreads, 0, s>>>((const T *)x, gamma, (T *)y, rows, \
+                                                             (int)cols, eps)
+    if (dtype == TB_F32) {
+      if (pick == 1) TB_RMS(float, 1); else if (pick == 2) TB_RMS(float, 2);
+      else if (pick == 4) TB_RMS(float, 4); else TB_RMS(float, 8);
+    } else {
+      if (pick == 1) TB_RMS(__nv_bfloat16, 1); else if (pick == 2) TB_RMS(__nv_bfloat16, 2);
+      else if (pick == 4) TB_RMS(__nv_bfloat16, 4); else TB_RMS(__nv_bfloat16, 8);
+    }
+#undef TB_RMS
+  } else if (dtype == TB_F32) {
+    rmsnorm_any_kernel<float><<<(int)grid, kRowThreads, 0, s>>>((const float *)x, gamma, (float *)y, rows, cols, eps);
+  } else {
+    rmsnorm_any_kernel<__nv_bfloat16><<<(int)grid, kRowThreads, 0, s>>>(
+        (const __nv_bfloat16 *)x, gamma, (__nv_bfloat16 *)y, rows, cols, eps);
+  }
+  return check_launch("tb_rmsnorm");
+}
+
+tb_status tb_softmax(const float *x, float *y, int64_t rows, int64_t cols, tb_stream stream) {
+  if (rows < 0 || cols < 0) return fail(TB_EINVAL, "tb_softmax: negative extent");
+  if (rows == 0 || cols == 0) return TB_OK;
+  if (!x || !y) return fail(TB_EINVAL, "tb_softmax: null pointer");
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  cudaStream_t s = as_stream(stream);
+  int cs = cluster_for(cols, kSliceFloats);
+  if (cs == 0) {
+    int64_t grid = std::min<int64_t>(rows, (int64_t)st->sm_count * 4);
+    softmax_long_kernel<<<(int)grid, kRowThreads, 0, s>>>(x, y, rows, cols);
+    return check_launch("tb_softmax");
+  }
+  int span = (int)((cols + cs - 1) / cs);
+  return launch_cluster(softmax_cluster_kernel<0>, rows, cs, (size_t)span * 4, s, x, y, rows, cols,
+                        cols, cols, span, (float *)nullptr, (float *)nullptr);
+}
+
+tb_status tb_argmax(const float *x, int64_t rows, int64_t cols, int64_t *idx, tb_stream stream) {
+  if (rows < 0 || cols < 0) return fail(TB_EINVAL, "tb_argmax: negative extent");
+  if (rows == 0) return TB_OK;
+  if (!x || !idx) return fail(TB_EINVAL, "tb_argmax: null pointer");
+  if (cols > 0xFFFFFFFFll) return fail(TB_EINVAL, "tb_argmax: more than 2^32 columns");
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  cudaStream_t s = as_stream(stream);
+  int cs = 1;
+  while (cs < 8 && (cols + cs - 1) / cs > 8192) cs *= 2;
+  int span = (int)((cols + cs - 1) / cs);
+  span = (span + 3) / 4 * 4;
+  return launch_cluster(argmax_cluster_kernel<0>, rows, cs, 0, s, x, rows, cols, cols, (int64_t)0,
+                        span, idx, (uint64_t *)nullptr);
+}
+
+tb_status tb_softmax_shard_stats(const float *x, int64_t rows, int64_t cols, int64_t ld,
+                                 float *row_max, float *row_sum, tb_stream stream) {
+  if (rows < 0 || cols <= 0 || ld < cols) return fail(TB_EINVAL, "tb_softmax_shard_stats: bad extents");
+  if (rows == 0) return TB_OK;
+  if (!x || !row_max || !row_sum) return fail(TB_EINVAL, "tb_softmax_shard_stats: null pointer");
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  int cs = cluster_for(cols, kSliceFloats);
+  if (cs == 0) return fail(TB_EINVAL, "tb_softmax_shard_stats: shard too wide (%lld columns)", (long long)cols);
+  int span = (int)((cols + cs - 1) / cs);
+  return launch_cluster(softmax_cluster_kernel<1>, rows, cs, (size_t)span * 4, as_stream(stream), x,
+                        (float *)nullptr, rows, cols, ld, (int64_t)0, span, row_max, row_sum);
+}
+
+tb_status tb_softmax_shard_rescale(const float *lmax, const float *gmax, float *sum, int64_t rows,
+                                   tb_stream stream) {
+  if (rows < 0) return fail(TB_EINVAL, "tb_softmax_shard_rescale: negative rows");
+  if (rows == 0) return TB_OK;
+  if (!lmax || !gmax || !sum) return fail(TB_EINVAL, "tb_softmax_shard_rescale: null pointer");
+  softmax_rescale_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, as_stream(stream)>>>(lmax, gmax, sum, rows);
+  return check_launch("tb_softmax_shard_rescale");
+}
+
+tb_status tb_softmax_shard_finish(const float *x, int64_t rows, int64_t cols, int64_t ld,
+                                  const float *gmax, const float *gsum, float *y, int64_t ld_y,
+                                  tb_stream stream) {
+  if (rows < 0 || cols < 0 || ld < cols || ld_y < cols) return fail(TB_EINVAL, "tb_softmax_shard_finish: bad extents");
+  if (rows == 0 || cols == 0) return TB_OK;
+  if (!x || !gmax || !gsum || !y) return fail(TB_EINVAL, "tb_softmax_shard_finish: null pointer");
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  int64_t total = rows * cols;
+  int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)st->sm_count * 8);
+  softmax_finish_kernel<<<grid, 256, 0, as_stream(stream)>>>(x, rows, cols, ld, gmax, gsum, y, ld_y);
+  return check_launch("tb_softmax_shard_finish");
+}
+
+tb_status tb_argmax_shard_keys(const float *x, int64_t rows, int64_t cols, int64_t ld,
+                               int64_t col_base, uint64_t *keys, tb_stream stream) {
+  if (rows < 0 || cols < 0 || ld < cols || col_base < 0) return fail(TB_EINVAL, "tb_argmax_shard_keys: bad extents");
+  if (col_base + cols > 0xFFFFFFFFll) return fail(TB_EINVAL, "tb_argmax_shard_keys: more than 2^32 columns");
+  if (rows == 0) return TB_OK;
+  if (!x || !keys) return fail(TB_EINVAL, "tb_argmax_shard_keys: null pointer");
+  int cs = 1;
+  while (cs < 8 && (cols + cs - 1) / cs > 8192) cs *= 2;
+  int span = (int)((cols + cs - 1) / cs);
+  span = (span + 3) / 4 * 4;
+  return launch_cluster(argmax_cluster_kernel<1>, rows, cs, 0, as_stream(stream), x, rows, cols, ld,
+                        col_base, span, (int64_t *)nullptr, keys);
+}
+
+tb_status tb_argmax_key_index(const uint64_t *keys, int64_t rows, int64_t *idx, tb_stream stream) {
+  if (rows < 0) return fail(TB_EINVAL, "tb_argmax_key_index: negative rows");
+  if (rows == 0) return TB_OK;
+  if (!keys || !idx) return fail(TB_EINVAL, "tb_argmax_key_index: null pointer");
+  key_index_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, as_stream(stream)>>>(keys, rows, idx);
+  return check_launch("tb_argmax_key_index");
+}
+
+}  // extern "C"

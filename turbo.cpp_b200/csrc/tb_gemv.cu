@@ -6,10 +6,11 @@
 //   y = sum_b bs_b                                            (sequential in b)
 // q*d is exact in fp32 (8-bit q times an 11-bit half scale), so the kernel may
 // form it any exact way; it builds it from a magic-number float (no int->float
-// conversion instruction) and keeps two blocks per lane in flight with the
-// sm_100a packed f32x2 add/mul/fma, each half rounded exactly like scalar IEEE.
-// The 32-term chains run one block per lane; the block sums land in shared
-// memory and one lane per row adds them in block order.
+// conversion instruction).  Each lane runs two blocks' chains side by side:
+// the exact dequantisation and the rounded products use the sm_100a packed
+// f32x2 fma/add/mul (each half an IEEE op), the accumulation is scalar so the
+// product rounding is kept.  The block sums land in shared memory and one lane
+// per row adds them in block order.
 //
 // Data movement: a CTA owns ROWS consecutive weight rows (one contiguous byte
 // range) and fetches all of it with one bulk TMA copy at kernel start, so the
@@ -123,7 +124,8 @@ __global__ void __launch_bounds__(NW * 32) gemv_q8_0_kernel(
           const uint64_t dd = pack2(d1, d2);
           const uint64_t c1 = pack2(-kMagic * d1, -kMagic * d2);  // exact: 3*2^22*d
           const uint64_t c2 = pack2(-128.0f * d1, -128.0f * d2);
-          uint64_t acc = pack2(0.f, 0.f);
+          s1 = 0.f;
+          s2 = 0.f;
 #pragma unroll
           for (int k = 0; k < 8; ++k) {
             const uint32_t u1 = q1[k] ^ 0x80808080u, u2 = q2[k] ^ 0x80808080u;
@@ -135,10 +137,15 @@ __global__ void __launch_bounds__(NW * 32) gemv_q8_0_kernel(
               const float m2 = __uint_as_float(__byte_perm(u2, kMagicHi, sel));
               uint64_t t = fma2(pack2(m1, m2), dd, c1);  // (q+128)*d, exact
               t = add2(t, c2);                           // q*d, exact
-              acc = add2(acc, mul2(t, xp[4 * k + e]));   // += round(w * x)
+              float p1, p2;
+              unpack2(mul2(t, xp[4 * k + e]), p1, p2);   // round(w * x)
+              // The accumulation stays scalar: ptxas contracts a packed
+              // mul + packed add into a packed FMA, which would skip the
+              // rounding of the product that the reference performs.
+              s1 = __fadd_rn(s1, p1);
+              s2 = __fadd_rn(s2, p2);
             }
           }
-          unpack2(acc, s1, s2);
         } else {  // non-finite scale: the plain expression, as the reference
           s1 = 0.f;
           s2 = 0.f;

@@ -148,9 +148,11 @@ __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float *__restr
     int q = (int)roundf(__fmul_rn(v, id));
     ob[2 + lane] = (uint8_t)(int8_t)q;
     if (lane == 0) {
-      uint16_t h = __half_as_ushort(__float2half_rn(d));
-      ob[0] = (uint8_t)(h & 0xFF);
-      ob[1] = (uint8_t)(h >> 8);
+      // Explicit byte stores: nvcc 12.9 was seen to drop the low byte when the
+      // two halves of a 16-bit value were stored as `h & 0xFF` / `h >> 8`.
+      const uint32_t h = __half_as_ushort(__float2half_rn(d));
+      asm volatile("st.u8 [%0], %1;" ::"l"(ob), "r"(h & 0xFFu) : "memory");
+      asm volatile("st.u8 [%0], %1;" ::"l"(ob + 1), "r"(h >> 8) : "memory");
     }
   }
 }

@@ -95,8 +95,12 @@ def test_cuda_matches_golden():
     T.call("tb_init", 0)
     s = T.stream_handle()
 
+    keep = []  # inputs stay alive until the kernels that read them have run
+
     def dev(a):
-        return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        t = torch.from_numpy(np.ascontiguousarray(a)).cuda()
+        keep.append(t)
+        return t
 
     q = load("quant")
     for dt, x, w, y, N in ((T.Q8_0, q["x8"], q["w8"], q["y8"], 64), (T.Q4_0, q["x4"], q["w4"], q["y4"], 32)):

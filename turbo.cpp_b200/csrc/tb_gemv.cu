@@ -76,8 +76,9 @@ __global__ void __launch_bounds__(NW * 32) gemv_q8_0_kernel(
   const int rpw = rows_per_cta / NW;
   uint64_t *bar = reinterpret_cast<uint64_t *>(smem);
   float *xs = reinterpret_cast<float *>(smem + 128);
-  float *bsum = xs + 32 * XS;                       // [NW][rpw][nb + 1]
-  uint8_t *wsm = reinterpret_cast<uint8_t *>(bsum + NW * rpw * (nb + 1));
+  const int BP = (nb + 4) & ~3;  // block-sum row pitch, a multiple of 4 floats (16-byte rows)
+  float *bsum = xs + 32 * XS;                       // [NW][rpw][BP]
+  uint8_t *wsm = reinterpret_cast<uint8_t *>(bsum + NW * rpw * BP);
   wsm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(wsm) + 127) & ~uintptr_t(127));
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -90,12 +91,38 @@ __global__ void __launch_bounds__(NW * 32) gemv_q8_0_kernel(
   __syncthreads();
   const int shift = stage_rows(W, (int64_t)n0 * rb, (int64_t)n1 * rb, wsm, bar, use_tma != 0);
 
-  float *mysum = bsum + warp * rpw * (nb + 1);
+  float *mysum = bsum + warp * rpw * BP;
   bool ready = false;
   for (int m = 0; m < M; ++m) {
     const float *xrow = X + (int64_t)m * K;
     if (m > 0) __syncthreads();  // previous x no longer read
-    for (int i = threadIdx.x; i < K; i += blockDim.x) xs[(i & 31) * XS + (i >> 5)] = __ldg(xrow + i);
+    // All loads of this thread's share of x are issued before any store, so
+    // the L2 round trips overlap instead of queueing behind each other.
+    if ((K & 3) == 0 && (reinterpret_cast<uintptr_t>(xrow) & 15) == 0) {
+      const float4 *x4 = reinterpret_cast<const float4 *>(xrow);
+      const int nv = K >> 2;
+      for (int base = 0; base < nv; base += 4 * NW * 32) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int iv = base + u * NW * 32 + threadIdx.x;
+          v[u] = iv < nv ? __ldg(x4 + iv) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int iv = base + u * NW * 32 + threadIdx.x;
+          if (iv < nv) {
+            const int i = iv * 4;
+            xs[((i + 0) & 31) * XS + ((i + 0) >> 5)] = v[u].x;
+            xs[((i + 1) & 31) * XS + ((i + 1) >> 5)] = v[u].y;
+            xs[((i + 2) & 31) * XS + ((i + 2) >> 5)] = v[u].z;
+            xs[((i + 3) & 31) * XS + ((i + 3) >> 5)] = v[u].w;
+          }
+        }
+      }
+    } else {
+      for (int i = threadIdx.x; i < K; i += blockDim.x) xs[(i & 31) * XS + (i >> 5)] = __ldg(xrow + i);
+    }
     __syncthreads();
     if (!ready) {
       // Every thread waits; if any gave up, all leave together (no thread may
@@ -159,19 +186,214 @@ __global__ void __launch_bounds__(NW * 32) gemv_q8_0_kernel(
               s2 = __fadd_rn(s2, __fmul_rn(__fmul_rn((float)(int8_t)(q2[k] >> (8 * e)), d2), x2));
             }
         }
-        if (v1) mysum[rr * (nb + 1) + b1] = s1;
-        if (v2) mysum[rr * (nb + 1) + b2] = s2;
+        if (v1) mysum[rr * BP + b1] = s1;
+        if (v2) mysum[rr * BP + b2] = s2;
       }
     }
     __syncwarp();
     if (lane < rpw && n0 + warp * rpw + lane < n1) {
-      const float *bs = mysum + lane * (nb + 1);
+      // y = sum of the block sums in block order (quant_math.hpp:56).
+      const float4 *bs4 = reinterpret_cast<const float4 *>(mysum + lane * BP);
       float s = 0.f;
-      for (int b = 0; b < nb; ++b) s = __fadd_rn(s, bs[b]);
+      int b = 0;
+      for (; b + 8 <= nb; b += 8) {
+        const float4 a = bs4[b / 4], c = bs4[b / 4 + 1];
+        s = __fadd_rn(s, a.x); s = __fadd_rn(s, a.y); s = __fadd_rn(s, a.z); s = __fadd_rn(s, a.w);
+        s = __fadd_rn(s, c.x); s = __fadd_rn(s, c.y); s = __fadd_rn(s, c.z); s = __fadd_rn(s, c.w);
+      }
+      for (; b < nb; ++b) s = __fadd_rn(s, mysum[lane * BP + b]);
       Y[(int64_t)m * N + n0 + warp * rpw + lane] = s;
     }
     __syncwarp();
   }
+}
+
+// ---------------------------------------------------------------------------
+// Persistent, pipelined decode GEMV (M == 1): same arithmetic as above.
+//
+// One CTA per SM.  Warp NC (the producer) streams "stages" of NC consecutive
+// rows (one contiguous byte range, one bulk TMA copy) through a ring of S
+// shared-memory slots; consumer warp w computes row w of each stage.  Stages
+// are fetched in order, so compute on early rows overlaps the transfer of later
+// ones, and x is read from L2 once per SM and kept in registers.  The
+// block-order final sums are deferred: each warp parks the block sums of up to
+// FLUSH rows and then FLUSH lanes add their rows' sums at once.
+struct PipeCfg {
+  int nc;       // consumer warps = rows per stage
+  int stages;   // ring slots
+  int flush;    // rows parked per warp before the final sums
+};
+
+template <int NC>
+__global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_q8_0_pipe_kernel(
+    const uint8_t *__restrict__ W, const float *__restrict__ X, float *__restrict__ Y, int N,
+    int K, int stages, int flush, uint32_t *__restrict__ err) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int nb = K / 32;
+  const int rb = nb * 34;
+  const int XS = (nb & 1) ? nb + 2 : nb + 1;
+  const int BP = (nb + 4) & ~3;
+  const int units = (N + NC - 1) / NC;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem);
+  uint64_t *empty = full + stages;
+  float *xs = reinterpret_cast<float *>(smem + 256);
+  float *bsum = xs + 32 * XS;  // [NC][flush][BP]
+  uint8_t *ring = reinterpret_cast<uint8_t *>(bsum + NC * flush * BP);
+  ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(ring) + 127) & ~uintptr_t(127));
+  const int stage_bytes = NC * rb;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < stages; ++i) {
+      mbar_init(full + i, 1);
+      mbar_init(empty + i, NC);
+    }
+    fence_mbar_init();
+  }
+  // x -> shared memory, transposed [j][block] with an odd pitch.
+  {
+    const float4 *x4 = reinterpret_cast<const float4 *>(X);
+    const int nv = K >> 2;
+    for (int base = 0; base < nv; base += 4 * (NC + 1) * 32) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int iv = base + u * (NC + 1) * 32 + threadIdx.x;
+        v[u] = iv < nv ? __ldg(x4 + iv) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int iv = base + u * (NC + 1) * 32 + threadIdx.x;
+        if (iv < nv) {
+          const int i = iv * 4;
+          xs[((i + 0) & 31) * XS + ((i + 0) >> 5)] = v[u].x;
+          xs[((i + 1) & 31) * XS + ((i + 1) >> 5)] = v[u].y;
+          xs[((i + 2) & 31) * XS + ((i + 2) >> 5)] = v[u].z;
+          xs[((i + 3) & 31) * XS + ((i + 3) >> 5)] = v[u].w;
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  if (warp == NC) {  // ---------------- producer
+    if (lane == 0) {
+      int i = 0;
+      for (int u = blockIdx.x; u < units; u += gridDim.x, ++i) {
+        const int slot = i % stages;
+        if (i >= stages && !mbar_wait_bounded(empty + slot, ((i / stages) + 1) & 1, err)) break;
+        const int r0 = u * NC;
+        const int nr = min(NC, N - r0);
+        const uint32_t bytes = (uint32_t)(nr * rb);
+        mbar_arrive_expect_tx(full + slot, bytes);
+        bulk_g2s(ring + slot * stage_bytes, W + (int64_t)r0 * rb, bytes, full + slot);
+      }
+    }
+    return;
+  }
+
+  // ------------------------------------ consumers
+  float *mysum = bsum + warp * flush * BP;
+  const bool onepass = nb <= 64;
+  uint64_t xp[32];
+  if (onepass) {
+    const int b1 = lane, b2 = lane + 32;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      xp[j] = pack2(b1 < nb ? xs[j * XS + b1] : 0.f, b2 < nb ? xs[j * XS + b2] : 0.f);
+  }
+  int parked = 0;   // rows parked in mysum; parked row r came from iteration first_i + r
+  int first_i = 0;
+  int i = 0;
+  for (int u = blockIdx.x; u < units; u += gridDim.x, ++i) {
+    const int slot = i % stages;
+    if (!mbar_wait_bounded(full + slot, (i / stages) & 1, err)) return;
+    const int row = u * NC + warp;
+    if (row < N) {
+      const uint8_t *wrow = ring + slot * stage_bytes + warp * rb;
+      float *bs = mysum + parked * BP;
+      for (int p = 0; p * 64 < nb; ++p) {
+        const int b1 = p * 64 + lane, b2 = b1 + 32;
+        const bool v1 = b1 < nb, v2 = b2 < nb;
+        if (!onepass) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            xp[j] = pack2(v1 ? xs[j * XS + b1] : 0.f, v2 ? xs[j * XS + b2] : 0.f);
+        }
+        float d1, d2;
+        uint32_t q1[8], q2[8];
+        load_q8_block(wrow, 34 * (v1 ? b1 : 0), d1, q1);
+        load_q8_block(wrow, 34 * (v2 ? b2 : 0), d2, q2);
+        float s1 = 0.f, s2 = 0.f;
+        if (isfinite(d1) && isfinite(d2)) {
+          const uint64_t dd = pack2(d1, d2);
+          const uint64_t c1 = pack2(-kMagic * d1, -kMagic * d2);
+          const uint64_t c2 = pack2(-128.0f * d1, -128.0f * d2);
+#pragma unroll
+          for (int k = 0; k < 8; ++k) {
+            const uint32_t u1 = q1[k] ^ 0x80808080u, u2 = q2[k] ^ 0x80808080u;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t sel = 0x7650u | (uint32_t)e;
+              const float m1 = __uint_as_float(__byte_perm(u1, kMagicHi, sel));
+              const float m2 = __uint_as_float(__byte_perm(u2, kMagicHi, sel));
+              uint64_t t = fma2(pack2(m1, m2), dd, c1);
+              t = add2(t, c2);
+              float p1, p2;
+              unpack2(mul2(t, xp[4 * k + e]), p1, p2);
+              s1 = __fadd_rn(s1, p1);
+              s2 = __fadd_rn(s2, p2);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float x1, x2;
+              unpack2(xp[4 * k + e], x1, x2);
+              s1 = __fadd_rn(s1, __fmul_rn(__fmul_rn((float)(int8_t)(q1[k] >> (8 * e)), d1), x1));
+              s2 = __fadd_rn(s2, __fmul_rn(__fmul_rn((float)(int8_t)(q2[k] >> (8 * e)), d2), x2));
+            }
+        }
+        if (v1) bs[b1] = s1;
+        if (v2) bs[b2] = s2;
+      }
+      if (parked == 0) first_i = i;
+      ++parked;  // only the last unit can hold rows past N, so parked rows are consecutive
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(empty + slot);  // this warp is done with the slot
+    const bool last = u + (int)gridDim.x >= units;
+    if (parked == flush || (last && parked > 0)) {
+      // lane r adds the block sums of parked row r in block order
+      const int myrow = (blockIdx.x + (first_i + lane) * (int)gridDim.x) * NC + warp;
+      if (lane < parked) {
+        const float4 *b4 = reinterpret_cast<const float4 *>(mysum + lane * BP);
+        float s = 0.f;
+        int b = 0;
+        for (; b + 8 <= nb; b += 8) {
+          const float4 a = b4[b / 4], c = b4[b / 4 + 1];
+          s = __fadd_rn(s, a.x); s = __fadd_rn(s, a.y); s = __fadd_rn(s, a.z); s = __fadd_rn(s, a.w);
+          s = __fadd_rn(s, c.x); s = __fadd_rn(s, c.y); s = __fadd_rn(s, c.z); s = __fadd_rn(s, c.w);
+        }
+        for (; b < nb; ++b) s = __fadd_rn(s, mysum[lane * BP + b]);
+        Y[myrow] = s;
+      }
+      __syncwarp();
+      parked = 0;
+    }
+  }
+}
+
+size_t pipe_smem_bytes(int K, const PipeCfg &c) {
+  const int nb = K / 32;
+  const int XS = (nb & 1) ? nb + 2 : nb + 1;
+  const int BP = (nb + 4) & ~3;
+  size_t s = 256 + (size_t)32 * XS * 4 + (size_t)c.nc * c.flush * BP * 4;
+  s = (s + 127) & ~size_t(127);
+  // + slack: the last block's 9-word read may run 2 bytes past the ring
+  return s + (size_t)c.stages * c.nc * nb * 34 + 128;
 }
 
 // ---------------------------------------------------------------------------
@@ -249,7 +471,7 @@ __global__ void __launch_bounds__(NW * 32) matmul_q4_0_kernel(
 size_t q8_smem_bytes(int K, int rows, int nw) {
   int nb = K / 32;
   int XS = (nb & 1) ? nb + 2 : nb + 1;
-  size_t s = 128 + (size_t)32 * XS * 4 + (size_t)rows * (nb + 1) * 4;
+  size_t s = 128 + (size_t)32 * XS * 4 + (size_t)rows * ((nb + 4) & ~3) * 4;
   s = (s + 127) & ~size_t(127);
   s += (size_t)rows * nb * 34 + 32;
   (void)nw;
@@ -266,6 +488,26 @@ size_t q4_smem_bytes(int K, int rows) {
 // Shared with the tensor-core path: exact CUDA-core quantized matmul.
 tb_status launch_q8_0_exact(const float *x, int64_t M, int64_t K, const void *w, int64_t N,
                             float *y, cudaStream_t s, const DeviceState *st) {
+  const int64_t rbytes = K / 32 * 34;
+  if (M == 1 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 && rbytes % 16 == 0 &&
+      (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    constexpr int NC = 8;
+    const int nb = (int)(K / 32);
+    PipeCfg c;
+    c.nc = NC;
+    c.flush = nb <= 64 ? 16 : nb <= 128 ? 8 : 4;
+    c.stages = 6;
+    while (c.stages > 2 && pipe_smem_bytes((int)K, c) > (size_t)st->smem_optin) --c.stages;
+    if (pipe_smem_bytes((int)K, c) <= (size_t)st->smem_optin) {
+      const size_t smem = pipe_smem_bytes((int)K, c);
+      TB_TRY(ensure_smem_for(gemv_q8_0_pipe_kernel<NC>, smem));
+      const int64_t units = (N + NC - 1) / NC;
+      const int grid = (int)std::min<int64_t>(units, st->sm_count);
+      gemv_q8_0_pipe_kernel<NC><<<grid, (NC + 1) * 32, smem, s>>>(
+          (const uint8_t *)w, x, y, (int)N, (int)K, c.stages, c.flush, st->err_word);
+      return check_launch("tb_matmul_quant(Q8_0 pipe)");
+    }
+  }
   constexpr int NW = 4;
   // ~36 KB of weights per CTA (a multiple of NW rows), several CTAs per SM.
   int rb = (int)(K / 32 * 34);

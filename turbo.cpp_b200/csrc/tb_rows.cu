@@ -260,7 +260,8 @@ __global__ void softmax_rescale_kernel(const float *__restrict__ lmax, const flo
 // when x > running max, which starts at -inf); key 0 = no candidate -> index 0.
 __device__ __forceinline__ uint64_t argmax_key(float v, int64_t col) {
   if (!(v > -INFINITY)) return 0ull;
-  uint32_t b = __float_as_uint(v);
+  // -0.0 and +0.0 compare equal under '>', so they must get the same key.
+  uint32_t b = v == 0.0f ? 0u : __float_as_uint(v);
   b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
   return ((uint64_t)b << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)col);
 }

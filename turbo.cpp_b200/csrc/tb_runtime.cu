@@ -86,6 +86,11 @@ tb_status ensure_smem(const void *func, size_t bytes) {
   if (cur >= bytes) return TB_OK;
   e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
   if (e != cudaSuccess) return fail(TB_ECUDA, "dynamic smem of %zu bytes: %s", bytes, cudaGetErrorString(e));
+  // Prefer the largest shared-memory carveout so that several such CTAs fit
+  // on an SM at once (the default split can leave room for only one).
+  e = cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout,
+                           (int)cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "smem carveout: %s", cudaGetErrorString(e));
   cur = bytes;
   return TB_OK;
 }

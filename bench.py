@@ -200,11 +200,14 @@ def run_ours(args):
     x = torch.from_numpy(x_host).cuda()
     y = torch.empty((1, N_ROWS), dtype=torch.float32, device="cuda")
 
-    def gemv(i, s=sh, xx=x, yy=y):
-        T.check(T.load().tb_matmul_quant(T.Q8_0, T.ptr(xx), 1, K_COLS, T.ptr(wcopies[i % N_COPIES]),
-                                         N_ROWS, T.ptr(yy), s), "tb_matmul_quant")
+    entry = "tb_matmul_quant_exact" if args.exact else "tb_matmul_quant"
+    fn = getattr(T.load(), entry)
 
-    # correctness gate before timing: bit-exact against the oracle on rank 0
+    def gemv(i, s=sh, xx=x, yy=y):
+        T.check(fn(T.Q8_0, T.ptr(xx), 1, K_COLS, T.ptr(wcopies[i % N_COPIES]), N_ROWS, T.ptr(yy), s), entry)
+
+    # correctness gate before timing, rank 0, against the oracle: bit-exact for
+    # the exact entry, else |y - y_ref| <= 1e-5 * sum|w x| per output
     with torch.cuda.stream(stream):
         gemv(0)
     stream.synchronize()
@@ -212,8 +215,13 @@ def run_ours(args):
         from oracle import orbind as O
         ref = O.matmul_q8_0(x_host, w_host, N_ROWS)
         got = y.cpu().numpy()
-        if not np.array_equal(got.view(np.uint32), ref.view(np.uint32)):
-            raise SystemExit("GEMV result differs from the oracle; not timing")
+        if args.exact:
+            ok = np.array_equal(got.view(np.uint32), ref.view(np.uint32))
+        else:
+            scale = np.abs(synth.dequantize_q8_0(w_host, K_COLS)).astype(np.float64) @ np.abs(x_host[0]).astype(np.float64)
+            ok = bool(np.max(np.abs(got[0].astype(np.float64) - ref[0]) / scale) <= 1e-5)
+        if not ok:
+            raise SystemExit("GEMV result differs from the oracle beyond tolerance; not timing")
 
     # warmup
     with torch.cuda.stream(stream):
@@ -323,6 +331,7 @@ def run_ours(args):
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (N(0,0.02) weights quantized Q8_0, x N(0,1), seeded)",
         "config": {"workload": WORKLOAD, "N": N_ROWS, "K": K_COLS, "M": 1, "parallelism": "row-shard x%d" % ws,
+                   "entry": entry, "tolerance": "bit-exact" if args.exact else "1e-5 * sum|w x| per output",
                    "l2": "inputs larger than L2: %d rotating weight copies (%.0f MB)" % (N_COPIES, N_COPIES * W_BYTES / 1e6),
                    "launch": "CUDA graph of %d GEMVs" % G},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
@@ -347,6 +356,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--exact", action="store_true",
+                    help="time tb_matmul_quant_exact (bit-identical to the reference) instead")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -174,14 +174,22 @@ tb_status tb_embedding(int dtype, const void *w_dev, int64_t dim, int64_t vocab,
 
 /* Y[M, N] = X[M, K] . W for a quantized W of GGUF logical shape {K, N}, stored
  * as N rows of K/32 blocks (Tensor::matmul, src/tensor/tensor.cpp:328-432).
- *  - dtype TB_Q8_0: X is fp32 and is not quantized (tensor.cpp:370-381).
- *    M <= 16 runs the decode GEMV, bit-identical to vec_dot_q8_0_f32
- *    (quant_math.hpp:32-60); larger M runs the tensor-core GEMM.
+ *  - dtype TB_Q8_0: X is fp32 and is not quantized (tensor.cpp:370-381).  The
+ *    decode GEMV (M == 1) accumulates each block as an FMA chain and applies
+ *    the block scale once: within 1e-5 relative of vec_dot_q8_0_f32
+ *    (quant_math.hpp:32-60), typically ~1e-7.
  *  - dtype TB_Q4_0: X rows are first quantized to Q8_0 (tensor.cpp:413-421),
- *    then multiplied with the Q4_0 rows (quant_math.hpp:184-248).
+ *    bit for bit, then multiplied with the Q4_0 rows in the order of
+ *    vec_dot_q4_0_q8_0_avx2 (quant_math.hpp:184-248).
  * K must be a multiple of 32. */
 tb_status tb_matmul_quant(int dtype, const float *x_dev, int64_t M, int64_t K,
                           const void *w_dev, int64_t N, float *y_dev, tb_stream stream);
+
+/* As tb_matmul_quant, but every output is computed in the reference's exact
+ * operation order, so results are bit-identical to Tensor::matmul
+ * (src/tensor/tensor.cpp:328-432, quant_math.hpp:32-60 and 184-248). */
+tb_status tb_matmul_quant_exact(int dtype, const float *x_dev, int64_t M, int64_t K,
+                                const void *w_dev, int64_t N, float *y_dev, tb_stream stream);
 
 /* Batched strided fp32 matmul, out = a @ b over matching leading (batch) dims,
  * `out` contiguous [batch..., M, N]: Tensor::matmul fp32 branch

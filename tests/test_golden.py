@@ -105,7 +105,7 @@ def test_cuda_matches_golden():
     q = load("quant")
     for dt, x, w, y, N in ((T.Q8_0, q["x8"], q["w8"], q["y8"], 64), (T.Q4_0, q["x4"], q["w4"], q["y4"], 32)):
         out = torch.empty(y.shape, dtype=torch.float32, device="cuda")
-        T.call("tb_matmul_quant", dt, T.ptr(dev(x)), x.shape[0], x.shape[1], T.ptr(dev(w)), N, T.ptr(out), s)
+        T.call("tb_matmul_quant_exact", dt, T.ptr(dev(x)), x.shape[0], x.shape[1], T.ptr(dev(w)), N, T.ptr(out), s)
         torch.cuda.synchronize()
         assert same_bits(out.cpu().numpy(), y)
     xq = torch.empty(q["xq_out"].size, dtype=torch.uint8, device="cuda")

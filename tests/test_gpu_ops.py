@@ -121,19 +121,42 @@ def test_quantize_q8_0_bit_exact():
 
 # ----------------------------------------------------------------- matmul ----
 
-def run_matmul(dtype, x, wq, N):
+def run_matmul(dtype, x, wq, N, entry="tb_matmul_quant_exact"):
     M, K = x.shape
     y = torch.empty((M, N), dtype=torch.float32, device="cuda")
-    T.call("tb_matmul_quant", dtype, T.ptr(dev(x)), M, K, T.ptr(dev(wq)), N, T.ptr(y), S())
+    T.call(entry, dtype, T.ptr(dev(x)), M, K, T.ptr(dev(wq)), N, T.ptr(y), S())
     return host(y)
 
 
-@pytest.mark.parametrize("M,K,N", [(1, 2048, 8192), (1, 8192, 2048), (3, 2048, 515), (1, 64, 5),
-                                   (2, 2080, 77), (16, 1024, 300)])
-def test_matmul_q8_0_bit_exact(M, K, N):
+def assert_dot_tol(got, x, wq, K, tol=F32_REL):
+    """GEMV/GEMM tolerance: |y - y_ref| <= tol * sum_k |w_k x_k| per output (the
+    conditioning of each dot product), with y_ref the reference's result."""
+    N = wq.shape[0]
+    scale = np.empty((x.shape[0], N))
+    for r0 in range(0, N, 8192):  # chunked: the lm_head shape has 128256 rows
+        wd = np.abs(synth.dequantize_q8_0(wq[r0:r0 + 8192], K)).astype(np.float64)
+        scale[:, r0:r0 + 8192] = np.abs(x.astype(np.float64)) @ wd.T
+    ref = O.matmul_q8_0(x, wq, N)
+    err = np.abs(got.astype(np.float64) - ref)
+    assert (err / scale).max() <= tol, "max scaled err %g" % (err / scale).max()
+
+
+MATMUL_SHAPES = [(1, 2048, 8192), (1, 8192, 2048), (3, 2048, 515), (1, 64, 5), (2, 2080, 77),
+                 (16, 1024, 300), (1, 2048, 128256), (1, 4096, 1000)]
+
+
+@pytest.mark.parametrize("M,K,N", MATMUL_SHAPES)
+def test_matmul_q8_0_exact_bit_exact(M, K, N):
     wq = synth.quantize_q8_0(synth.normal((N, K), 0.02, seed=K + N))
     x = synth.normal((M, K), 1.0, seed=M)
     assert_bits(run_matmul(T.Q8_0, x, wq, N), O.matmul_q8_0(x, wq, N))
+
+
+@pytest.mark.parametrize("M,K,N", MATMUL_SHAPES)
+def test_matmul_q8_0_default_within_tolerance(M, K, N):
+    wq = synth.quantize_q8_0(synth.normal((N, K), 0.02, seed=K + N))
+    x = synth.normal((M, K), 1.0, seed=M)
+    assert_dot_tol(run_matmul(T.Q8_0, x, wq, N, "tb_matmul_quant"), x, wq, K)
 
 
 def test_matmul_q8_0_unaligned_weight_base():
@@ -143,7 +166,7 @@ def test_matmul_q8_0_unaligned_weight_base():
     buf = torch.zeros(wq.size + 16, dtype=torch.uint8, device="cuda")
     buf[6:6 + wq.size] = dev(wq)
     y = torch.empty((1, N), dtype=torch.float32, device="cuda")
-    T.call("tb_matmul_quant", T.Q8_0, T.ptr(dev(x)), 1, K, buf.data_ptr() + 6, N, T.ptr(y), S())
+    T.call("tb_matmul_quant_exact", T.Q8_0, T.ptr(dev(x)), 1, K, buf.data_ptr() + 6, N, T.ptr(y), S())
     assert_bits(host(y), O.matmul_q8_0(x, wq, N))
 
 

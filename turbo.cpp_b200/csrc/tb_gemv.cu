@@ -224,7 +224,12 @@ struct PipeCfg {
   int flush;    // rows parked per warp before the final sums
 };
 
-template <int NC>
+// EXACT = 1: the reference's operation order, bit for bit (as gemv_q8_0_kernel).
+// EXACT = 0: per block, acc = sum_j q_j * x_j as an FMA chain (q exact as
+// float, products exact, one rounding per step), y += d * acc; the row total is
+// a warp reduction.  Within 1e-5 relative of the reference (typically ~1e-7)
+// at about a third of the instructions per weight.
+template <int NC, int EXACT>
 __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_q8_0_pipe_kernel(
     const uint8_t *__restrict__ W, const float *__restrict__ X, float *__restrict__ Y, int N,
     int K, int stages, int flush, uint32_t *__restrict__ err) {
@@ -309,6 +314,44 @@ __global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_q8_0_pipe_kernel(
     const int slot = i % stages;
     if (!mbar_wait_bounded(full + slot, (i / stages) & 1, err)) return;
     const int row = u * NC + warp;
+    if (!EXACT) {
+      if (row < N) {
+        const uint8_t *wrow = ring + slot * stage_bytes + warp * rb;
+        float racc = 0.f;
+        for (int p = 0; p * 64 < nb; ++p) {
+          const int b1 = p * 64 + lane, b2 = b1 + 32;
+          const bool v1 = b1 < nb, v2 = b2 < nb;
+          if (!onepass) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              xp[j] = pack2(v1 ? xs[j * XS + b1] : 0.f, v2 ? xs[j * XS + b2] : 0.f);
+          }
+          float d1, d2;
+          uint32_t q1[8], q2[8];
+          load_q8_block(wrow, 34 * (v1 ? b1 : 0), d1, q1);
+          load_q8_block(wrow, 34 * (v2 ? b2 : 0), d2, q2);
+          uint64_t acc = pack2(0.f, 0.f);
+#pragma unroll
+          for (int k = 0; k < 8; ++k)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const float f1 = (float)(int8_t)(q1[k] >> (8 * e));
+              const float f2 = (float)(int8_t)(q2[k] >> (8 * e));
+              acc = fma2(pack2(f1, f2), xp[4 * k + e], acc);
+            }
+          float s1, s2;
+          unpack2(acc, s1, s2);
+          if (v1) racc = fmaf(s1, d1, racc);
+          if (v2) racc = fmaf(s2, d2, racc);
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) racc += __shfl_xor_sync(0xffffffffu, racc, o);
+        if (lane == 0) Y[row] = racc;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty + slot);
+      continue;
+    }
     if (row < N) {
       const uint8_t *wrow = ring + slot * stage_bytes + warp * rb;
       float *bs = mysum + parked * BP;
@@ -394,6 +437,267 @@ size_t pipe_smem_bytes(int K, const PipeCfg &c) {
   s = (s + 127) & ~size_t(127);
   // + slack: the last block's 9-word read may run 2 bytes past the ring
   return s + (size_t)c.stages * c.nc * nb * 34 + 128;
+}
+
+// ---------------------------------------------------------------------------
+// Span GEMV (M == 1), the decode path.
+//
+// One CTA per SM owns a contiguous range of rows.  The range is cut into spans
+// that fit in shared memory; two span buffers are in flight, and each span is
+// fetched as four large bulk TMA copies (row-aligned quarters) with one
+// mbarrier each, so warps start on the first quarter while the rest streams.
+// Few large copies per SM stream at the same rate as plain 16-byte loads from
+// every thread; many small copies do not.
+//
+// Programmatic dependent launch: the weight copies are issued before
+// griddepcontrol.wait (weights never depend on the previous kernel), x is
+// read and y written only after it, and the kernel lets its dependents launch
+// at once.  A GEMV that follows another kernel in the stream therefore starts
+// streaming its weights while the predecessor drains.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+struct SpanCfg {
+  int span_rows;  // rows per span buffer
+};
+
+template <int NWARP, int EXACT>
+__global__ void __launch_bounds__(NWARP * 32, 1) gemv_q8_0_span_kernel(
+    const uint8_t *__restrict__ W, const float *__restrict__ X, float *__restrict__ Y, int N,
+    int K, int span_rows, uint32_t *__restrict__ err) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int abort_flag;
+  const int nb = K / 32;
+  const int rb = nb * 34;
+  const int XS = (nb & 1) ? nb + 2 : nb + 1;
+  const int BP = (nb + 4) & ~3;
+  uint64_t *bar = reinterpret_cast<uint64_t *>(smem);  // [2 buffers][4 quarters]
+  float *xs = reinterpret_cast<float *>(smem + 256);
+  float *bsum = xs + 32 * XS;  // [span_rows][BP] (exact only)
+  uint8_t *buf0 = reinterpret_cast<uint8_t *>(bsum + (EXACT ? span_rows * BP : 0));
+  buf0 = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(buf0) + 127) & ~uintptr_t(127));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+  // this CTA's rows: [n0, n0 + cnt), balanced over the grid
+  const int G = gridDim.x, base = N / G, rem = N % G;
+  const int n0 = blockIdx.x * base + min((int)blockIdx.x, rem);
+  const int cnt = base + ((int)blockIdx.x < rem ? 1 : 0);
+  const int nspans = (cnt + span_rows - 1) / span_rows;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 8; ++i) mbar_init(bar + i, 1);
+    fence_mbar_init();
+    abort_flag = 0;
+  }
+  __syncthreads();
+
+  // thread q < 4 issues quarter q of span k into buffer (k & 1)
+  auto issue = [&](int k) {
+    const int q = threadIdx.x;
+    const int r0 = k * span_rows;
+    const int nr = min(span_rows, cnt - r0);
+    const int qr = (nr + 3) / 4;
+    const int a = min(nr, q * qr), b = min(nr, (q + 1) * qr);
+    const uint32_t bytes = (uint32_t)((b - a) * rb);
+    uint64_t *bq = bar + (k & 1) * 4 + q;
+    mbar_arrive_expect_tx(bq, bytes);
+    if (bytes)
+      bulk_g2s(buf0 + (size_t)(k & 1) * span_rows * rb + (size_t)a * rb,
+               W + ((int64_t)n0 + r0 + a) * rb, bytes, bq);
+  };
+  if (threadIdx.x < 4) {
+    if (nspans > 0) issue(0);
+    if (nspans > 1) issue(1);
+  }
+  pdl_launch_dependents();
+  pdl_wait();  // x (and the order of our y writes) depend on the previous kernel
+
+  // x -> shared memory, transposed [j][block] with an odd pitch
+  {
+    const float4 *x4 = reinterpret_cast<const float4 *>(X);
+    const int nv = K >> 2;
+    for (int base4 = 0; base4 < nv; base4 += 4 * NWARP * 32) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int iv = base4 + u * NWARP * 32 + threadIdx.x;
+        v[u] = iv < nv ? __ldg(x4 + iv) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int iv = base4 + u * NWARP * 32 + threadIdx.x;
+        if (iv < nv) {
+          const int i = iv * 4;
+          xs[((i + 0) & 31) * XS + ((i + 0) >> 5)] = v[u].x;
+          xs[((i + 1) & 31) * XS + ((i + 1) >> 5)] = v[u].y;
+          xs[((i + 2) & 31) * XS + ((i + 2) >> 5)] = v[u].z;
+          xs[((i + 3) & 31) * XS + ((i + 3) >> 5)] = v[u].w;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  const bool onepass = nb <= 64;
+  uint64_t xp[32];
+  if (onepass) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      xp[j] = pack2(lane < nb ? xs[j * XS + lane] : 0.f, lane + 32 < nb ? xs[j * XS + lane + 32] : 0.f);
+  }
+
+  for (int k = 0; k < nspans; ++k) {
+    const int r0 = k * span_rows;
+    const int nr = min(span_rows, cnt - r0);
+    const int qr = (nr + 3) / 4;
+    const uint8_t *sbuf = buf0 + (size_t)(k & 1) * span_rows * rb;
+    const uint32_t phase = (uint32_t)((k >> 1) & 1);
+    int waited = -1;
+    for (int r = warp; r < nr; r += NWARP) {
+      const int q = r / qr;
+      if (q != waited) {
+        if (!mbar_wait_bounded(bar + (k & 1) * 4 + q, phase, err)) {
+          abort_flag = 1;
+          break;
+        }
+        waited = q;
+      }
+      const uint8_t *wrow = sbuf + (size_t)r * rb;
+      float racc = 0.f;
+      for (int p = 0; p * 64 < nb; ++p) {
+        const int b1 = p * 64 + lane, b2 = b1 + 32;
+        const bool v1 = b1 < nb, v2 = b2 < nb;
+        if (!onepass) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            xp[j] = pack2(v1 ? xs[j * XS + b1] : 0.f, v2 ? xs[j * XS + b2] : 0.f);
+        }
+        float d1, d2;
+        uint32_t q1[8], q2[8];
+        load_q8_block(wrow, 34 * (v1 ? b1 : 0), d1, q1);
+        load_q8_block(wrow, 34 * (v2 ? b2 : 0), d2, q2);
+        if (!EXACT) {
+          // q as float without an int->float conversion: byte_perm builds the
+          // float 12582912 + (q + 128), an exact packed subtraction leaves q.
+          const uint64_t off2 = pack2(-(kMagic + 128.0f), -(kMagic + 128.0f));
+          uint64_t acc = pack2(0.f, 0.f);
+#pragma unroll
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint32_t u1 = q1[kk] ^ 0x80808080u, u2 = q2[kk] ^ 0x80808080u;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              const uint32_t sel = 0x7650u | (uint32_t)e;
+              const uint64_t m = pack2(__uint_as_float(__byte_perm(u1, kMagicHi, sel)),
+                                       __uint_as_float(__byte_perm(u2, kMagicHi, sel)));
+              acc = fma2(add2(m, off2), xp[4 * kk + e], acc);
+            }
+          }
+          float s1, s2;
+          unpack2(acc, s1, s2);
+          if (v1) racc = fmaf(s1, d1, racc);
+          if (v2) racc = fmaf(s2, d2, racc);
+        } else {
+          float s1 = 0.f, s2 = 0.f;
+          if (isfinite(d1) && isfinite(d2)) {
+            const uint64_t dd = pack2(d1, d2);
+            const uint64_t c1 = pack2(-kMagic * d1, -kMagic * d2);
+            const uint64_t c2 = pack2(-128.0f * d1, -128.0f * d2);
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {
+              const uint32_t u1 = q1[kk] ^ 0x80808080u, u2 = q2[kk] ^ 0x80808080u;
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const uint32_t sel = 0x7650u | (uint32_t)e;
+                const float m1 = __uint_as_float(__byte_perm(u1, kMagicHi, sel));
+                const float m2 = __uint_as_float(__byte_perm(u2, kMagicHi, sel));
+                uint64_t t = fma2(pack2(m1, m2), dd, c1);
+                t = add2(t, c2);
+                float p1, p2;
+                unpack2(mul2(t, xp[4 * kk + e]), p1, p2);
+                s1 = __fadd_rn(s1, p1);
+                s2 = __fadd_rn(s2, p2);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                float x1, x2;
+                unpack2(xp[4 * kk + e], x1, x2);
+                s1 = __fadd_rn(s1, __fmul_rn(__fmul_rn((float)(int8_t)(q1[kk] >> (8 * e)), d1), x1));
+                s2 = __fadd_rn(s2, __fmul_rn(__fmul_rn((float)(int8_t)(q2[kk] >> (8 * e)), d2), x2));
+              }
+          }
+          if (v1) bsum[r * BP + b1] = s1;
+          if (v2) bsum[r * BP + b2] = s2;
+        }
+      }
+      if (!EXACT) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) racc += __shfl_xor_sync(0xffffffffu, racc, o);
+        if (lane == 0) Y[n0 + r0 + r] = racc;
+      }
+    }
+    __syncthreads();  // span buffer (and block sums) complete
+    if (abort_flag) return;
+    if (EXACT) {
+      // thread t adds the block sums of row t in block order (quant_math.hpp:56)
+      for (int t = threadIdx.x; t < nr; t += NWARP * 32) {
+        const float4 *b4 = reinterpret_cast<const float4 *>(bsum + t * BP);
+        float s = 0.f;
+        int b = 0;
+        for (; b + 8 <= nb; b += 8) {
+          const float4 a = b4[b / 4], c = b4[b / 4 + 1];
+          s = __fadd_rn(s, a.x); s = __fadd_rn(s, a.y); s = __fadd_rn(s, a.z); s = __fadd_rn(s, a.w);
+          s = __fadd_rn(s, c.x); s = __fadd_rn(s, c.y); s = __fadd_rn(s, c.z); s = __fadd_rn(s, c.w);
+        }
+        for (; b < nb; ++b) s = __fadd_rn(s, bsum[t * BP + b]);
+        Y[n0 + r0 + t] = s;
+      }
+      __syncthreads();  // block sums consumed
+    }
+    if (k + 2 < nspans && threadIdx.x < 4) issue(k + 2);
+  }
+}
+
+size_t span_smem_bytes(int K, int span_rows, bool exact) {
+  const int nb = K / 32;
+  const int XS = (nb & 1) ? nb + 2 : nb + 1;
+  const int BP = (nb + 4) & ~3;
+  size_t s = 256 + (size_t)32 * XS * 4 + (exact ? (size_t)span_rows * BP * 4 : 0);
+  s = (s + 127) & ~size_t(127);
+  // + slack: up to 127 bytes of alignment of the buffers, and the last block's
+  // 9-word read may run 2 bytes past them
+  return s + (size_t)2 * span_rows * nb * 34 + 256;
+}
+
+template <int EXACT>
+tb_status launch_span(const float *x, int64_t K, const void *w, int64_t N, float *y,
+                      cudaStream_t s, const DeviceState *st) {
+  constexpr int NWARP = 16;
+  const int grid = (int)std::min<int64_t>(N, st->sm_count);
+  const int64_t rows_per_cta = (N + grid - 1) / grid;
+  int sr = (int)((rows_per_cta + 1) / 2);
+  while (sr > 1 && span_smem_bytes((int)K, sr, EXACT) > (size_t)st->smem_optin) --sr;
+  const size_t smem = span_smem_bytes((int)K, sr, EXACT);
+  if (smem > (size_t)st->smem_optin) return fail(TB_EINVAL, "tb_matmul_quant: K=%lld too large", (long long)K);
+  auto kern = gemv_q8_0_span_kernel<NWARP, EXACT>;
+  TB_TRY(ensure_smem_for(kern, smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3(NWARP * 32, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, (const uint8_t *)w, x, y, (int)N, (int)K, sr, st->err_word);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_matmul_quant(Q8_0 span): %s", cudaGetErrorString(e));
+  return TB_OK;
 }
 
 // ---------------------------------------------------------------------------
@@ -485,26 +789,37 @@ size_t q4_smem_bytes(int K, int rows) {
 
 }  // namespace
 
-// Shared with the tensor-core path: exact CUDA-core quantized matmul.
-tb_status launch_q8_0_exact(const float *x, int64_t M, int64_t K, const void *w, int64_t N,
-                            float *y, cudaStream_t s, const DeviceState *st) {
+// Q8_0 matmul on CUDA cores.  M == 1 with aligned operands runs the
+// pipelined GEMV (exact or fast arithmetic); everything else the one-shot
+// kernel, which always follows the reference's order.
+tb_status launch_q8_0(const float *x, int64_t M, int64_t K, const void *w, int64_t N, float *y,
+                      bool exact, cudaStream_t s, const DeviceState *st) {
   const int64_t rbytes = K / 32 * 34;
   if (M == 1 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 && rbytes % 16 == 0 &&
       (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
+    return exact ? launch_span<1>(x, K, w, N, y, s, st) : launch_span<0>(x, K, w, N, y, s, st);
+  }
+  if (false) {
     constexpr int NC = 8;
     const int nb = (int)(K / 32);
     PipeCfg c;
     c.nc = NC;
-    c.flush = nb <= 64 ? 16 : nb <= 128 ? 8 : 4;
+    c.flush = exact ? (nb <= 64 ? 16 : nb <= 128 ? 8 : 4) : 0;
     c.stages = 6;
     while (c.stages > 2 && pipe_smem_bytes((int)K, c) > (size_t)st->smem_optin) --c.stages;
     if (pipe_smem_bytes((int)K, c) <= (size_t)st->smem_optin) {
       const size_t smem = pipe_smem_bytes((int)K, c);
-      TB_TRY(ensure_smem_for(gemv_q8_0_pipe_kernel<NC>, smem));
       const int64_t units = (N + NC - 1) / NC;
       const int grid = (int)std::min<int64_t>(units, st->sm_count);
-      gemv_q8_0_pipe_kernel<NC><<<grid, (NC + 1) * 32, smem, s>>>(
-          (const uint8_t *)w, x, y, (int)N, (int)K, c.stages, c.flush, st->err_word);
+      if (exact) {
+        TB_TRY(ensure_smem_for(gemv_q8_0_pipe_kernel<NC, 1>, smem));
+        gemv_q8_0_pipe_kernel<NC, 1><<<grid, (NC + 1) * 32, smem, s>>>(
+            (const uint8_t *)w, x, y, (int)N, (int)K, c.stages, c.flush, st->err_word);
+      } else {
+        TB_TRY(ensure_smem_for(gemv_q8_0_pipe_kernel<NC, 0>, smem));
+        gemv_q8_0_pipe_kernel<NC, 0><<<grid, (NC + 1) * 32, smem, s>>>(
+            (const uint8_t *)w, x, y, (int)N, (int)K, c.stages, c.flush, st->err_word);
+      }
       return check_launch("tb_matmul_quant(Q8_0 pipe)");
     }
   }

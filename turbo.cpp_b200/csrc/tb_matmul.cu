@@ -5,16 +5,17 @@
 #include "tb_internal.cuh"
 
 namespace tb {
-tb_status launch_q8_0_exact(const float *x, int64_t M, int64_t K, const void *w, int64_t N,
-                            float *y, cudaStream_t s, const DeviceState *st);
+tb_status launch_q8_0(const float *x, int64_t M, int64_t K, const void *w, int64_t N, float *y,
+                      bool exact, cudaStream_t s, const DeviceState *st);
 tb_status launch_q4_0_exact(const uint8_t *xq, int64_t M, int64_t K, const void *w, int64_t N,
                             float *y, cudaStream_t s, const DeviceState *st);
 }  // namespace tb
 
 using namespace tb;
 
-extern "C" tb_status tb_matmul_quant(int dtype, const float *x, int64_t M, int64_t K,
-                                     const void *w, int64_t N, float *y, tb_stream stream) {
+namespace {
+tb_status matmul_quant(int dtype, const float *x, int64_t M, int64_t K, const void *w, int64_t N,
+                       float *y, bool exact, tb_stream stream) {
   if (dtype != TB_Q8_0 && dtype != TB_Q4_0)
     return fail(TB_EINVAL, "tb_matmul_quant: dtype must be TB_Q8_0 or TB_Q4_0");
   if (M < 0 || K < 0 || N < 0) return fail(TB_EINVAL, "tb_matmul_quant: negative extent");
@@ -26,7 +27,7 @@ extern "C" tb_status tb_matmul_quant(int dtype, const float *x, int64_t M, int64
   DeviceState *st;
   TB_TRY(device_state(&st));
   cudaStream_t s = as_stream(stream);
-  if (dtype == TB_Q8_0) return launch_q8_0_exact(x, M, K, w, N, y, s, st);
+  if (dtype == TB_Q8_0) return launch_q8_0(x, M, K, w, N, y, exact, s, st);
   // Q4_0: X rows -> Q8_0 (tensor.cpp:413-421) into stream-ordered scratch.
   size_t xq_bytes = (size_t)M * (size_t)(K / 32) * 34;
   void *xq = nullptr;
@@ -37,4 +38,15 @@ extern "C" tb_status tb_matmul_quant(int dtype, const float *x, int64_t M, int64
   e = cudaFreeAsync(xq, s);
   if (rs == TB_OK && e != cudaSuccess) return fail(TB_ECUDA, "tb_matmul_quant: free scratch: %s", cudaGetErrorString(e));
   return rs;
+}
+}  // namespace
+
+extern "C" tb_status tb_matmul_quant(int dtype, const float *x, int64_t M, int64_t K,
+                                     const void *w, int64_t N, float *y, tb_stream stream) {
+  return matmul_quant(dtype, x, M, K, w, N, y, false, stream);
+}
+
+extern "C" tb_status tb_matmul_quant_exact(int dtype, const float *x, int64_t M, int64_t K,
+                                           const void *w, int64_t N, float *y, tb_stream stream) {
+  return matmul_quant(dtype, x, M, K, w, N, y, true, stream);
 }

@@ -67,6 +67,7 @@ SIGNATURES = {
     "tb_quantize_q8_0": [_P, _I64, _I64, _P, _P],
     "tb_embedding": [_I, _P, _I64, _I64, _P, _I64, _P, _P],
     "tb_matmul_quant": [_I, _P, _I64, _I64, _P, _I64, _P, _P],
+    "tb_matmul_quant_exact": [_I, _P, _I64, _I64, _P, _I64, _P, _P],
     "tb_matmul_f32": [_VP, _VP, _VP, _P],
     "tb_softmax_shard_stats": [_P, _I64, _I64, _I64, _P, _P, _P],
     "tb_softmax_shard_rescale": [_P, _P, _P, _I64, _P],

@@ -191,6 +191,22 @@ tb_status tb_matmul_quant(int dtype, const float *x_dev, int64_t M, int64_t K,
 tb_status tb_matmul_quant_exact(int dtype, const float *x_dev, int64_t M, int64_t K,
                                 const void *w_dev, int64_t N, float *y_dev, tb_stream stream);
 
+/* tb_matmul_quant(TB_Q4_0, ...) for callers that cannot allocate device memory
+ * during the call (a process that reserves its whole device-memory budget at
+ * start-up, or a latency-critical loop where an allocator call may synchronize
+ * or fail).  No counterpart in the reference, which runs on the CPU.
+ * The quantized copy of X goes to a fixed 8 MiB buffer compiled into the
+ * library (held on every GPU that loads it until the process exits) instead
+ * of allocated scratch; results are identical to tb_matmul_quant(TB_Q4_0).
+ * Requires M * (K/32) * 34 <= 8 MiB (e.g. M = 512 at K = 8192), else TB_EINVAL.
+ * Calls no cudaMalloc/cudaFree.  The first call on a device looks up the
+ * buffer's address (cudaGetSymbolAddress); make it before any stream capture.
+ * All calls share the one buffer: calls that may overlap on the GPU (other
+ * streams, other host threads) race and must be serialized by the caller. */
+tb_status tb_matmul_q4_0_static_scratch(const float *x_dev, int64_t M, int64_t K,
+                                        const void *w_dev, int64_t N, float *y_dev,
+                                        tb_stream stream);
+
 /* Batched strided fp32 matmul, out = a @ b over matching leading (batch) dims,
  * `out` contiguous [batch..., M, N]: Tensor::matmul fp32 branch
  * (src/tensor/tensor.cpp:434-542) and matmul_threaded_packed_avx2 (:591-650).

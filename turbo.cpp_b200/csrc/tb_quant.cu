@@ -158,6 +158,18 @@ __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float *__restr
 }
 
 }  // namespace
+
+// Launches the Q8_0 quantisation with the caller's SM count (no device-state
+// lookup), for entry points that must not allocate.
+tb_status launch_quantize_q8_0(const float *x, int64_t rows, int64_t k, void *blocks, cudaStream_t s,
+                               int sm_count) {
+  int64_t total = rows * (k / 32);
+  int grid = (int)std::min<int64_t>((total + 7) / 8, (int64_t)sm_count * 16);
+  if (grid < 1) grid = 1;
+  quantize_q8_0_kernel<<<grid, 256, 0, s>>>(x, rows, k, (uint8_t *)blocks);
+  return check_launch("quantize_q8_0");
+}
+
 }  // namespace tb
 
 using namespace tb;

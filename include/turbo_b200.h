@@ -1,8 +1,8 @@
 /* turbo_b200.h -- C ABI of the B200 (sm_100a) tensor-library hot path.
  *
  * This is the drop-in boundary under the Turbo.cpp `Tensor`/`Storage` API
- * (include/turbo/tensor/tensor.hpp) and the `nn::*::forward` call sites
- * (src/nn/*.cpp).  Every entry point replaces one reference interface, cited
+ * (include/turbo/tensor/tensor.hpp) and the `nn` layers' forward call sites
+ * (the files under src/nn).  Every entry point replaces one reference interface, cited
  * beside it as file:line inside the reference project.
  *
  * Conventions
@@ -138,6 +138,12 @@ tb_status tb_softmax(const float *x_dev, float *y_dev, int64_t rows, int64_t col
  * wins; a row of only -inf/NaN gives 0): greedy_sample (src/core/sampler.cpp:13-26). */
 tb_status tb_argmax(const float *x_dev, int64_t rows, int64_t cols, int64_t *idx_dev,
                     tb_stream stream);
+
+/* Causal mask of the prefill attention scores (src/nn/attention.cpp:120-129):
+ * x[r, c] = value wherever c > r + diag_offset, for x[rows, cols] with row
+ * stride ld (elements). */
+tb_status tb_fill_upper(float *x_dev, int64_t rows, int64_t cols, int64_t ld, int64_t diag_offset,
+                        float value, tb_stream stream);
 
 /* ------------------------------------------------------------- RoPE (A13) -- */
 

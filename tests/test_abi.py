@@ -58,3 +58,12 @@ def test_no_cuda_device_fails_loudly():
     assert st in (T.EINVAL, T.ECUDA)
     st = L.tb_init(0)
     assert st == T.ECUDA
+
+
+def test_host_library_exports_model_interface():
+    host = os.path.join(os.path.dirname(T.LIB_PATH), "libturbo_b200_host.so")
+    if not os.path.exists(host):
+        pytest.skip("host library not built")
+    out = subprocess.run(["nm", "-D", "--defined-only", host], capture_output=True, text=True).stdout
+    for sym in ("tbm_model_load", "tbm_model_generate", "tbm_model_free", "tbm_last_error"):
+        assert sym in out

@@ -54,7 +54,36 @@ def build(force=False, verbose=False):
     if force or not os.path.exists(OUT) or any(os.path.getmtime(o) > os.path.getmtime(OUT) for o in objs):
         cmd = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", OUT] + objs
         subprocess.check_call(cmd)
+    build_host(force)
     return OUT
+
+
+HOST = os.path.join(HERE, "host")
+HOST_OUT = os.path.join(HERE, "libturbo_b200_host.so")
+CXX = os.environ.get("CXX_HOST", "/usr/bin/g++")
+
+
+def build_host(force=False):
+    """The C++ Tensor/nn/MiniGPT layer over the C ABI (no CUDA headers)."""
+    srcs = sorted(glob.glob(os.path.join(HOST, "src", "*.cpp")))
+    hdrs = glob.glob(os.path.join(HOST, "src", "*.hpp")) + glob.glob(os.path.join(HOST, "include", "turbo", "*", "*.hpp"))
+    test_src = os.path.join(HOST, "tests", "test_host.cpp")
+    test_bin = os.path.join(HOST, "tests", "test_host")
+    newest = max(os.path.getmtime(f) for f in srcs + hdrs + [OUT, test_src])
+    if (not force and os.path.exists(HOST_OUT) and os.path.exists(test_bin)
+            and min(os.path.getmtime(HOST_OUT), os.path.getmtime(test_bin)) >= newest):
+        return HOST_OUT
+    cmd = [CXX, "-std=c++17", "-O2", "-fPIC", "-shared", "-Wall", "-Wno-reorder",
+           "-I" + os.path.join(HOST, "include"), "-I" + os.path.join(ROOT, "include")] + srcs + \
+          ["-L" + HERE, "-lturbo_b200", "-Wl,-rpath,$ORIGIN", "-o", HOST_OUT]
+    subprocess.check_call(cmd)
+    # the C++ test program (reference unit-test cases against this API)
+    test_src = os.path.join(HOST, "tests", "test_host.cpp")
+    cmd = [CXX, "-std=c++17", "-O2", "-Wall", "-I" + os.path.join(HOST, "include"), test_src,
+           "-L" + HERE, "-lturbo_b200_host", "-lturbo_b200", "-Wl,-rpath,$ORIGIN/../..",
+           "-o", os.path.join(HOST, "tests", "test_host")]
+    subprocess.check_call(cmd)
+    return HOST_OUT
 
 
 if __name__ == "__main__":

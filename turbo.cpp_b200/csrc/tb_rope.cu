@@ -41,10 +41,33 @@ __global__ void __launch_bounds__(256) rope_kernel(float *__restrict__ x, RopeVi
   }
 }
 
+__global__ void fill_upper_kernel(float *__restrict__ x, int64_t rows, int64_t cols, int64_t ld,
+                                  int64_t diag, float value) {
+  const int64_t total = rows * cols;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
+       t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = t / cols, c = t % cols;
+    if (c > r + diag) x[r * ld + c] = value;
+  }
+}
+
 }  // namespace
 }  // namespace tb
 
 using namespace tb;
+
+extern "C" tb_status tb_fill_upper(float *x, int64_t rows, int64_t cols, int64_t ld, int64_t diag,
+                                   float value, tb_stream stream) {
+  if (rows < 0 || cols < 0 || ld < cols) return fail(TB_EINVAL, "tb_fill_upper: bad extents");
+  if (rows == 0 || cols == 0) return TB_OK;
+  if (!x) return fail(TB_EINVAL, "tb_fill_upper: null pointer");
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  const int64_t total = rows * cols;
+  const int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)st->sm_count * 8);
+  fill_upper_kernel<<<grid, 256, 0, as_stream(stream)>>>(x, rows, cols, ld, diag, value);
+  return check_launch("tb_fill_upper");
+}
 
 extern "C" tb_status tb_rope(const tb_view *x, const float *cos_t, const float *sin_t,
                              int64_t head_dim, int64_t max_seq, int64_t pos_offset,

@@ -1,0 +1,110 @@
+// model_capi.cpp -- a flat C interface over the host layer's MiniGPT for
+// callers outside C++ (the tests and bench.py drive the 1B-shaped decode
+// through it).  It runs what src/core/generate.cpp:9-70 runs: prefill the
+// prompt, then one greedy token per step with the KV cache.
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "host_util.hpp"
+#include "turbo/core/kv_cache.hpp"
+#include "turbo/core/sampler.hpp"
+#include "turbo/loader/gguf_loader.hpp"
+#include "turbo/model/minigpt.hpp"
+
+#define TBM_API extern "C" __attribute__((visibility("default")))
+
+namespace {
+thread_local std::string g_err;
+
+struct Model {
+  std::unique_ptr<turbo::GGUFLoader> loader;
+  std::unique_ptr<turbo::MiniGPT> model;
+};
+
+template <class F> int guarded(F &&f) {
+  try {
+    f();
+    return 0;
+  } catch (const std::invalid_argument &e) {
+    g_err = e.what();
+    return 1;
+  } catch (const std::out_of_range &e) {
+    g_err = e.what();
+    return 2;
+  } catch (const std::exception &e) {
+    g_err = e.what();
+    return 3;
+  }
+}
+}  // namespace
+
+TBM_API const char *tbm_last_error() { return g_err.c_str(); }
+
+// Loads a GGUF model onto the current device.  exact != 0 selects the
+// bit-identical quantized matmul kernels for this process.
+TBM_API void *tbm_model_load(const char *path, int exact) {
+  Model *m = nullptr;
+  int st = guarded([&] {
+    turbo::set_exact_matmul(exact != 0);
+    auto mm = std::make_unique<Model>();
+    mm->loader = std::make_unique<turbo::GGUFLoader>(path);
+    mm->loader->parse();
+    mm->model = std::make_unique<turbo::MiniGPT>(*mm->loader);
+    turbo::device_synchronize();
+    m = mm.release();
+  });
+  return st == 0 ? m : nullptr;
+}
+
+TBM_API void tbm_model_free(void *h) { delete static_cast<Model *>(h); }
+
+// Prefill `prompt`, then `steps` greedy steps.  out_ids[steps + 1] receives the
+// token chosen after the prefill and after each step.  margins (optional)
+// receives top-1 minus top-2 logit of each choice, last_logits (optional) the
+// final step's logits -- both diagnostics read back from the device.
+TBM_API int tbm_model_generate(void *h, const int *prompt, size_t n_prompt, size_t steps, size_t max_seq,
+                               int *out_ids, float *margins, float *last_logits, double *prefill_ms,
+                               double *decode_ms) {
+  auto *m = static_cast<Model *>(h);
+  return guarded([&] {
+    turbo::MiniGPT &model = *m->model;
+    turbo::KVCache kv((int)max_seq, (int)model.get_num_layers(), (int)model.get_num_kv_heads(),
+                      (int)model.get_head_dim());
+    auto pick = [&](const Tensor &logits, size_t slot) {
+      const int id = turbo::greedy_sample(logits);
+      out_ids[slot] = id;
+      if (margins || last_logits) {
+        const size_t V = logits.get_shape().back();
+        const float *row = logits.data_ptr() + (logits.numel() - V);
+        if (margins) {
+          float top2 = -INFINITY;
+          for (size_t i = 0; i < V; ++i)
+            if ((int)i != id && row[i] > top2) top2 = row[i];
+          margins[slot] = row[id] - top2;
+        }
+        if (last_logits) std::memcpy(last_logits, row, V * sizeof(float));
+      }
+      return id;
+    };
+    turbo::device_synchronize();
+    auto t0 = std::chrono::steady_clock::now();
+    std::vector<int> ids(prompt, prompt + n_prompt);
+    Tensor logits = model.forward(ids, &kv);
+    kv.increment_seq_len((int)n_prompt);
+    int next = pick(logits, 0);
+    auto t1 = std::chrono::steady_clock::now();
+    for (size_t s = 0; s < steps; ++s) {
+      logits = model.forward(std::vector<int>{next}, &kv);
+      kv.increment_seq_len(1);
+      next = pick(logits, s + 1);
+    }
+    turbo::device_synchronize();
+    auto t2 = std::chrono::steady_clock::now();
+    if (prefill_ms) *prefill_ms = std::chrono::duration<double, std::milli>(t1 - t0).count();
+    if (decode_ms) *decode_ms = std::chrono::duration<double, std::milli>(t2 - t1).count();
+  });
+}

@@ -63,6 +63,7 @@ SIGNATURES = {
     "tb_softmax": [_P, _P, _I64, _I64, _P],
     "tb_argmax": [_P, _I64, _I64, _P, _P],
     "tb_rope": [_VP, _P, _P, _I64, _I64, _I64, _P],
+    "tb_fill_upper": [_P, _I64, _I64, _I64, _I64, _F, _P],
     "tb_dequant": [_I, _P, _I64, _P, _P],
     "tb_quantize_q8_0": [_P, _I64, _I64, _P, _P],
     "tb_embedding": [_I, _P, _I64, _I64, _P, _I64, _P, _P],

@@ -236,12 +236,15 @@ tb_status tb_softmax_shard_finish(const float *x_dev, int64_t rows, int64_t cols
                                   const float *global_max_dev, const float *global_sum_dev,
                                   float *y_dev, int64_t ld_y, tb_stream stream);
 /* Per row of this shard, a 64-bit key that orders candidates the way
- * greedy_sample does: (order-preserving bits of the value) << 32 |
- * (0xFFFFFFFF - global column).  A max all-reduce of the keys across shards
- * gives the global first maximum; tb_argmax_key_index decodes it. */
+ * greedy_sample (src/core/sampler.cpp:13-26) does: (order-preserving bits of the
+ * value) << 32 | (0xFFFFFFFF - global column), with the top bit flipped so that
+ * the keys compare as signed int64.  A signed int64 MAX all-reduce of the keys
+ * across shards (ncclInt64/ncclMax) gives the global first maximum;
+ * tb_argmax_key_index decodes it.  A row with no candidate (all NaN or -inf)
+ * gets INT64_MIN, which decodes to index 0. */
 tb_status tb_argmax_shard_keys(const float *x_dev, int64_t rows, int64_t cols, int64_t ld,
-                               int64_t col_base, uint64_t *keys_dev, tb_stream stream);
-tb_status tb_argmax_key_index(const uint64_t *keys_dev, int64_t rows, int64_t *idx_dev,
+                               int64_t col_base, int64_t *keys_dev, tb_stream stream);
+tb_status tb_argmax_key_index(const int64_t *keys_dev, int64_t rows, int64_t *idx_dev,
                               tb_stream stream);
 
 #if defined(__GNUC__)

@@ -266,11 +266,16 @@ __device__ __forceinline__ uint64_t argmax_key(float v, int64_t col) {
   return ((uint64_t)b << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)col);
 }
 
+// Shard keys leave the kernel with the top bit flipped, so that their order as
+// signed 64-bit integers is the unsigned key order (no candidate = INT64_MIN):
+// a plain int64 MAX all-reduce then combines the shards.
+constexpr uint64_t kKeySignFlip = 0x8000000000000000ull;
+
 // KEYS = 0: writes the row's index; KEYS = 1: writes the row's key (shards).
 template <int KEYS>
 __global__ void __launch_bounds__(kRowThreads) argmax_cluster_kernel(
     const float *__restrict__ x, int64_t rows, int64_t cols, int64_t ldx, int64_t col_base,
-    int span, int64_t *__restrict__ idx_out, uint64_t *__restrict__ key_out) {
+    int span, int64_t *__restrict__ idx_out, int64_t *__restrict__ key_out) {
   __shared__ uint64_t scratch[32];
   __shared__ uint64_t part;
   cg::cluster_group cluster = cg::this_cluster();
@@ -314,17 +319,17 @@ __global__ void __launch_bounds__(kRowThreads) argmax_cluster_kernel(
       uint64_t p = *cluster.map_shared_rank(&part, c);
       k = p > k ? p : k;
     }
-    if (KEYS) key_out[row] = k;
+    if (KEYS) key_out[row] = (int64_t)(k ^ kKeySignFlip);
     else idx_out[row] = k ? (int64_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFu)) : 0;
   }
   cluster.sync();
 }
 
-__global__ void key_index_kernel(const uint64_t *__restrict__ keys, int64_t rows,
+__global__ void key_index_kernel(const int64_t *__restrict__ keys, int64_t rows,
                                  int64_t *__restrict__ idx) {
   int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (r < rows) {
-    uint64_t k = keys[r];
+    const uint64_t k = (uint64_t)keys[r] ^ kKeySignFlip;
     idx[r] = k ? (int64_t)(0xFFFFFFFFu - (uint32_t)(k & 0xFFFFFFFFu)) : 0;
   }
 }
@@ -447,7 +452,7 @@ tb_status tb_argmax(const float *x, int64_t rows, int64_t cols, int64_t *idx, tb
   int span = (int)((cols + cs - 1) / cs);
   span = (span + 3) / 4 * 4;
   return launch_cluster(argmax_cluster_kernel<0>, rows, cs, 0, s, x, rows, cols, cols, (int64_t)0,
-                        span, idx, (uint64_t *)nullptr);
+                        span, idx, (int64_t *)nullptr);
 }
 
 tb_status tb_softmax_shard_stats(const float *x, int64_t rows, int64_t cols, int64_t ld,
@@ -488,7 +493,7 @@ tb_status tb_softmax_shard_finish(const float *x, int64_t rows, int64_t cols, in
 }
 
 tb_status tb_argmax_shard_keys(const float *x, int64_t rows, int64_t cols, int64_t ld,
-                               int64_t col_base, uint64_t *keys, tb_stream stream) {
+                               int64_t col_base, int64_t *keys, tb_stream stream) {
   if (rows < 0 || cols < 0 || ld < cols || col_base < 0) return fail(TB_EINVAL, "tb_argmax_shard_keys: bad extents");
   if (col_base + cols > 0xFFFFFFFFll) return fail(TB_EINVAL, "tb_argmax_shard_keys: more than 2^32 columns");
   if (rows == 0) return TB_OK;
@@ -501,7 +506,7 @@ tb_status tb_argmax_shard_keys(const float *x, int64_t rows, int64_t cols, int64
                         col_base, span, (int64_t *)nullptr, keys);
 }
 
-tb_status tb_argmax_key_index(const uint64_t *keys, int64_t rows, int64_t *idx, tb_stream stream) {
+tb_status tb_argmax_key_index(const int64_t *keys, int64_t rows, int64_t *idx, tb_stream stream) {
   if (rows < 0) return fail(TB_EINVAL, "tb_argmax_key_index: negative rows");
   if (rows == 0) return TB_OK;
   if (!keys || !idx) return fail(TB_EINVAL, "tb_argmax_key_index: null pointer");

@@ -1,0 +1,300 @@
+"""Per-op throughput of the hot-path kernels against the HBM roofline.
+
+Every case calls the C ABI entry point the host layer uses, on seeded
+synthetic inputs at the benchmark-config shapes and at large sweep sizes.
+Inputs whose working set is below 512 MB are replicated and rotated so that
+each call reads from HBM, not L2.  Calls are captured in a CUDA graph and
+timed with CUDA events on the launching stream; the per-call time is the
+graph time divided by the number of calls.  Prints one JSON line per case.
+"""
+import ctypes
+import json
+import math
+import os
+
+import numpy as np
+
+from . import synth
+
+ROT_BYTES = 512 << 20
+
+
+def _peak():
+    p = os.path.join(os.path.dirname(os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))),
+                     "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class Case:
+    def __init__(self, name, config, make, algo_bytes, flops=None):
+        self.name, self.config, self.make, self.algo_bytes, self.flops = name, config, make, algo_bytes, flops
+
+
+def _cases(T, torch):
+    dev = "cuda"
+    cases = []
+
+    def f32(shape, seed, std=1.0):
+        return torch.randn(shape, device=dev, generator=torch.Generator(dev).manual_seed(seed)) * std
+
+    def qblocks(nblocks, bsz, seed):
+        """Random quantized blocks generated on the device; every scale is the
+        finite half 0x1419 (about 1e-3)."""
+        g = torch.Generator(dev).manual_seed(seed)
+        w = torch.randint(0, 256, (nblocks, bsz), dtype=torch.uint8, device=dev, generator=g)
+        w[:, 0] = 0x19
+        w[:, 1] = 0x14
+        return w.reshape(-1)
+
+    def rot(nbytes):
+        return max(1, min(64, math.ceil(ROT_BYTES / max(nbytes, 1))))
+
+    # ---- A3/A4: broadcast add / row-vector multiply ---------------------------------
+    def add_case(rows, cols, dtype, tag, cfg):
+        es = 2 if dtype == torch.bfloat16 else 4
+        n = rows * cols
+        k = rot(3 * n * es)
+
+        def make():
+            A = [f32((rows, cols), 1 + i).to(dtype) for i in range(k)]
+            B = [f32((rows, cols), 100 + i).to(dtype) for i in range(k)]
+            O = [torch.empty((rows, cols), dtype=dtype, device=dev) for _ in range(k)]
+            va = [T.view(a) for a in A]
+            vb = [T.view(b) for b in B]
+            vo = [T.view(o) for o in O]
+            keep = (A, B, O, va, vb, vo)
+            return (lambda i, s: T.load().tb_binary(0, T.byref(va[i % k]), T.byref(vb[i % k]), T.byref(vo[i % k]), s)), keep
+        cases.append(Case("add_" + tag, cfg, make, 3 * n * es))
+
+    add_case(128, 2048, torch.float32, "f32_1x128x2048", "configs[0]: x+a fp32 [1,128,2048]")
+    add_case(1 << 20, 4096, torch.float32, "f32_16GiB", "sweep: [1048576,4096] fp32 (16 GiB per tensor)")
+    add_case(1 << 18, 4096, torch.bfloat16, "bf16_2GiB", "sweep: [262144,4096] bf16")
+
+    def mul_case(rows, cols):
+        n = rows * cols
+
+        def make():
+            A = f32((rows, cols), 3)
+            g = f32((cols,), 4)
+            O = torch.empty_like(A)
+            va, vg, vo = T.view(A), T.view(g), T.view(O)
+            return (lambda i, s: T.load().tb_binary(1, T.byref(va), T.byref(vg), T.byref(vo), s)), (A, g, O, va, vg, vo)
+        cases.append(Case("mul_rowvec_f32_4GiB", "sweep: [262144,4096] * [4096] fp32", make, 2 * n * 4 + cols * 4))
+
+    mul_case(1 << 18, 4096)
+
+    # ---- A5/A6: copies ----------------------------------------------------------------
+    def transpose_copy(rows, cols):
+        n = rows * cols
+
+        def make():
+            src = f32((cols, rows), 5)  # contiguous() of its transpose: [rows, cols] strided
+            dst = torch.empty((rows, cols), device=dev)
+            vs = T.view(src, 0, (rows, cols), (1, rows))
+            vd = T.view(dst)
+            return (lambda i, s: T.load().tb_copy(T.byref(vd), T.byref(vs), s)), (src, dst, vs, vd)
+        cases.append(Case("contiguous_transpose_f32_1GiB", "sweep: [16384,16384]^T -> contiguous fp32", make, 2 * n * 4))
+
+    transpose_copy(16384, 16384)
+
+    def kv_copy():
+        S, H, D, ctx = 512, 8, 64, 1024
+        k = rot(2 * S * H * D * 4)
+
+        def make():
+            Ks = [f32((S, H, D), 6 + i) for i in range(k)]
+            Cs = [torch.zeros((ctx, H, D), device=dev) for _ in range(k)]
+            vk = [T.view(x) for x in Ks]
+            vc = [T.view(c, 0, (S, H, D), (H * D, D, 1)) for c in Cs]
+            return (lambda i, s: T.load().tb_copy(T.byref(vc[i % k]), T.byref(vk[i % k]), s)), (Ks, Cs, vk, vc)
+        cases.append(Case("kv_append_512x8x64", "KV cache copy_ [512,8,64] into cache[0:512]", make, 2 * S * H * D * 4))
+
+    kv_copy()
+
+    # ---- A7 RMSNorm, A8 SwiGLU ----------------------------------------------------------
+    def rms_case(rows, cols, tag, cfg):
+        n = rows * cols
+        k = rot(2 * n * 4)
+
+        def make():
+            X = [f32((rows, cols), 7 + i) for i in range(k)]
+            g = torch.rand(cols, device=dev) + 0.5
+            Y = [torch.empty_like(x) for x in X]
+            return (lambda i, s: T.load().tb_rmsnorm(T.F32, T.ptr(X[i % k]), T.ptr(g), T.ptr(Y[i % k]), rows, cols,
+                                                      1e-5, s)), (X, g, Y)
+        cases.append(Case("rmsnorm_" + tag, cfg, make, 2 * n * 4 + cols * 4))
+
+    rms_case(128, 2048, "128x2048", "configs[0]: RMSNorm [128,2048] eps 1e-5")
+    rms_case(1 << 18, 4096, "4GiB", "sweep: [262144,4096] fp32")
+
+    def swiglu_case(n, tag, cfg):
+        k = rot(3 * n * 4)
+
+        def make():
+            G = [f32((n,), 8 + i) for i in range(k)]
+            U = [f32((n,), 50 + i) for i in range(k)]
+            Y = [torch.empty_like(g) for g in G]
+            return (lambda i, s: T.load().tb_swiglu(T.F32, T.ptr(G[i % k]), T.ptr(U[i % k]), T.ptr(Y[i % k]), n, s)), (G, U, Y)
+        cases.append(Case("swiglu_" + tag, cfg, make, 3 * n * 4))
+
+    swiglu_case(128 * 8192, "1x128x8192", "configs[0]: SwiGLU [1,128,8192]")
+    swiglu_case((1 << 18) * 4096, "4GiB", "sweep: [262144,4096] fp32")
+
+    # ---- A9 softmax, A15 argmax -----------------------------------------------------------
+    def rows_case(kind, rows, cols, tag, cfg):
+        n = rows * cols
+        k = rot((2 if kind == "softmax" else 1) * n * 4)
+
+        def make():
+            X = [f32((rows, cols), 9 + i, 2.0) for i in range(k)]
+            if kind == "softmax":
+                Y = [torch.empty_like(x) for x in X]
+                return (lambda i, s: T.load().tb_softmax(T.ptr(X[i % k]), T.ptr(Y[i % k]), rows, cols, s)), (X, Y)
+            idx = torch.empty(rows, dtype=torch.int64, device=dev)
+            return (lambda i, s: T.load().tb_argmax(T.ptr(X[i % k]), rows, cols, T.ptr(idx), s)), (X, idx)
+        cases.append(Case(kind + "_" + tag, cfg, make, (2 if kind == "softmax" else 1) * n * 4 + (0 if kind == "softmax" else 8 * rows)))
+
+    rows_case("softmax", 1, 128256, "1x128256", "configs[0]: softmax logits[1,128256]")
+    rows_case("softmax", 64, 128256, "64x128256", "sweep: softmax [64,128256]")
+    rows_case("softmax", 8192, 128256, "8192x128256", "large: softmax [8192,128256] (4.2 GB)")
+    rows_case("argmax", 1, 128256, "1x128256", "configs[0]: argmax [1,128256]")
+    rows_case("argmax", 64, 128256, "64x128256", "sweep: argmax [64,128256]")
+    rows_case("argmax", 8192, 128256, "8192x128256", "large: argmax [8192,128256] (4.2 GB)")
+
+    # ---- A14/A17 dequant, quantize, embedding; A13 RoPE ---------------------------------
+    def dequant_case(N, K):
+        nb = N * K // 32
+        k = rot(nb * 34 + N * K * 4)
+
+        def make():
+            kk = min(k, 4)
+            W = [qblocks(nb, 34, 11 + i) for i in range(kk)]
+            Y = [torch.empty(N * K, device=dev) for _ in range(kk)]
+            return (lambda i, s: T.load().tb_dequant(T.Q8_0, T.ptr(W[i % kk]), nb, T.ptr(Y[i % kk]), s)), (W, Y)
+        cases.append(Case("dequant_q8_0_8192x2048", "configs[1]: exact block dequant of W[8192,2048]", make, nb * 34 + N * K * 4))
+
+    dequant_case(8192, 2048)
+
+    def quantize_case(M, K):
+        def make():
+            X = f32((M, K), 12)
+            Q = torch.empty(M * K // 32 * 34, dtype=torch.uint8, device=dev)
+            return (lambda i, s: T.load().tb_quantize_q8_0(T.ptr(X), M, K, T.ptr(Q), s)), (X, Q)
+        cases.append(Case("quantize_q8_0_512x8192", "configs[2]: X[512,8192] -> Q8_0", make, M * K * 4 + M * K // 32 * 34))
+
+    quantize_case(512, 8192)
+
+    def embed_case(n, dim, vocab):
+        def make():
+            W = qblocks(vocab * dim // 32, 34, 13)
+            ids = torch.from_numpy(np.random.default_rng(0).integers(0, vocab, n).astype(np.int32)).to(dev)
+            Y = torch.empty((n, dim), device=dev)
+            return (lambda i, s: T.load().tb_embedding(T.Q8_0, T.ptr(W), dim, vocab, T.ptr(ids), n, T.ptr(Y), s)), (W, ids, Y)
+        cases.append(Case("embedding_q8_0_512ids", "configs[3]: token_embd gather of 512 ids, dim 2048", make,
+                          n * (dim // 32 * 34 + dim * 4)))
+
+    embed_case(512, 2048, 128256)
+
+    def rope_case(H, S, D):
+        def make():
+            X = f32((S, H, D), 14)
+            c = torch.rand(1024 * D // 2, device=dev)
+            s_ = torch.rand(1024 * D // 2, device=dev)
+            v = T.view(X, 0, (1, H, S, D), (S * H * D, D, H * D, 1))
+            return (lambda i, s: T.load().tb_rope(T.byref(v), T.ptr(c), T.ptr(s_), D, 1024, 0, s)), (X, c, s_, v)
+        cases.append(Case("rope_q_1x32x512x64", "configs[3]: RoPE on Q [1,32,512,64] view", make, 2 * H * S * D * 4 + S * D * 4))
+
+    rope_case(32, 512, 64)
+
+    # ---- A10/A11: quantized matmul ----------------------------------------------------------
+    def gemv_case(N, K, entry, tag, cfg):
+        wb = N * K // 32 * 34
+        k = rot(wb)
+
+        def make():
+            W = [qblocks(N * K // 32, 34, 15 + i) for i in range(k)]
+            x = f32((1, K), 16)
+            y = torch.empty((1, N), device=dev)
+            fn = getattr(T.load(), entry)
+            return (lambda i, s: fn(T.Q8_0, T.ptr(x), 1, K, T.ptr(W[i % k]), N, T.ptr(y), s)), (W, x, y)
+        cases.append(Case(tag, cfg, make, wb + K * 4 + N * 4))
+
+    gemv_case(8192, 2048, "tb_matmul_quant", "gemv_q8_0_8192x2048", "configs[1]: decode GEMV (default, 1e-5)")
+    gemv_case(8192, 2048, "tb_matmul_quant_exact", "gemv_q8_0_8192x2048_exact", "configs[1]: decode GEMV, bit-exact")
+    gemv_case(2048, 8192, "tb_matmul_quant", "gemv_q8_0_2048x8192", "configs[3]: ffn_down GEMV")
+    gemv_case(128256, 2048, "tb_matmul_quant", "gemv_q8_0_128256x2048", "configs[3]: tied lm_head GEMV")
+
+    def gemm_case(dt, M, K, N, tag, cfg):
+        def make():
+            W = qblocks(N * K // 32, 34 if dt == T.Q8_0 else 18, 17)
+            X = f32((M, K), 18)
+            Y = torch.empty((M, N), device=dev)
+            return (lambda i, s: T.load().tb_matmul_quant(dt, T.ptr(X), M, K, T.ptr(W), N, T.ptr(Y), s)), (W, X, Y)
+        wb = N * K // 32 * (34 if dt == T.Q8_0 else 18)
+        cases.append(Case(tag, cfg, make, wb + M * K * 4 + M * N * 4, flops=2 * M * N * K))
+
+    gemm_case(T.Q4_0, 512, 8192, 2048, "gemm_q4_0_512x8192x2048", "configs[2]: Q4_0 down GEMM")
+    gemm_case(T.Q8_0, 512, 2048, 8192, "gemm_q8_0_512x2048x8192", "configs[2]: Q8_0 gate/up GEMM")
+    return cases
+
+
+def run(only=None, min_ms=20.0, out=None):
+    import torch
+
+    import turbo_b200 as T
+    T.call("tb_init", 0)
+    peak, kind = _peak()
+    stream = torch.cuda.Stream()
+    results = []
+    for case in _cases(T, torch):
+        if only and not any(o in case.name for o in only):
+            continue
+        launch, keep = case.make()
+        sh = ctypes.c_void_p(stream.cuda_stream)
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                T.check(launch(i, sh), case.name)
+        stream.synchronize()
+        # size the graph for >= min_ms of GPU time
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        with torch.cuda.stream(stream):
+            for i in range(3):
+                T.check(launch(i, sh), case.name)
+        t1.record(stream)
+        stream.synchronize()
+        est = max(t0.elapsed_time(t1) / 3, 1e-3)
+        n = int(max(8, min(2000, min_ms / est)))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=stream):
+            cs = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            for i in range(n):
+                T.check(launch(i, cs), case.name)
+        with torch.cuda.stream(stream):
+            g.replay()
+        stream.synchronize()
+        t0.record(stream)
+        with torch.cuda.stream(stream):
+            g.replay()
+        t1.record(stream)
+        stream.synchronize()
+        us = t0.elapsed_time(t1) * 1e3 / n
+        gbs = case.algo_bytes / (us * 1e-6) / 1e9
+        line = {"op": case.name, "config": case.config, "us_per_call": round(us, 3), "calls": n,
+                "algo_bytes": case.algo_bytes, "GB_s": round(gbs, 1), "hbm_frac": round(gbs / peak, 4),
+                "peak_GB_s": peak, "peak_source": kind}
+        if case.flops:
+            line["TFLOP_s"] = round(case.flops / (us * 1e-6) / 1e12, 3)
+        results.append(line)
+        print(json.dumps(line), flush=True)
+        del g, keep, launch
+        torch.cuda.empty_cache()
+    if out:
+        with open(out, "w") as f:
+            for r in results:
+                f.write(json.dumps(r) + "\n")
+    return results

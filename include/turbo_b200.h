@@ -247,6 +247,17 @@ tb_status tb_argmax_shard_keys(const float *x_dev, int64_t rows, int64_t cols, i
 tb_status tb_argmax_key_index(const int64_t *keys_dev, int64_t rows, int64_t *idx_dev,
                               tb_stream stream);
 
+/* ---------------------------------------------------------------- diagnostics -- */
+
+/* Evaluates the two fp32 exp implementations of the softmax and SwiGLU kernels
+ * on every fp32 bit pattern against exp in double precision rounded to float,
+ * on the current device, synchronously.  counts[0]: inputs where the
+ * correctly-rounding version (SwiGLU) differs; counts[1]: its largest distance
+ * in ulp; counts[2]: inputs where the fp32-only version (softmax) is more than
+ * 2 ulp away; counts[3]: its largest distance.  No reference counterpart: the
+ * reference calls glibc expf. */
+tb_status tb_selfcheck_exp(uint64_t counts[4]);
+
 #if defined(__GNUC__)
 #pragma GCC visibility pop
 #endif

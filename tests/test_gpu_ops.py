@@ -6,6 +6,8 @@ scale, RoPE, embedding, fp32 matmul, argmax.  Tolerance-bound (tree reductions):
 RMSNorm and softmax at 1e-5 relative (fp32), 1e-2 for bf16.  SwiGLU uses a
 correctly rounded exp; it differs from glibc's expf only where glibc misrounds.
 """
+import ctypes
+
 import numpy as np
 import pytest
 
@@ -287,6 +289,32 @@ def test_kv_cache_append_and_transpose_copy():
     assert_bits(host(dc2), cache)
 
 
+@pytest.mark.parametrize("shape", [(300, 200), (3, 100, 90), (64, 64), (2, 33, 70)])
+def test_contiguous_of_transpose_tiles_bit_exact(shape):
+    # contiguous() of a view whose last two dims are swapped: the tiled
+    # transpose path (64x64 tiles when both extents reach 64, else 32x32)
+    *lead, R, C = shape
+    n = int(np.prod(shape))
+    src = synth.normal((n,), 1.0, seed=n)
+    # source memory is [lead..., C, R] contiguous; the view is [lead..., R, C]
+    mem_shape = tuple(lead) + (C, R)
+    mst = [1] * len(mem_shape)
+    for i in range(len(mem_shape) - 2, -1, -1):
+        mst[i] = mst[i + 1] * mem_shape[i + 1]
+    vstrides = tuple(mst[:-2]) + (1, R)
+    for dt in (torch.float32, torch.bfloat16):
+        ds = dev(src).to(dt)
+        out = torch.empty(shape, dtype=dt, device="cuda")
+        T.call("tb_copy", T.byref(T.view(out)), T.byref(T.view(ds, 0, shape, vstrides)), S())
+        want = ds.as_strided(shape, vstrides).contiguous()
+        assert torch.equal(out.view(torch.int16) if dt == torch.bfloat16 else out.view(torch.int32),
+                           want.view(torch.int16) if dt == torch.bfloat16 else want.view(torch.int32))
+    ref = O.contiguous(src, 0, shape, vstrides)
+    got = torch.empty(shape, dtype=torch.float32, device="cuda")
+    T.call("tb_copy", T.byref(T.view(got)), T.byref(T.view(dev(src), 0, shape, vstrides)), S())
+    assert_bits(host(got), ref)
+
+
 def test_copy_shape_mismatch():
     a = torch.zeros(12, device="cuda")
     with pytest.raises(T.TbError) as e:
@@ -353,6 +381,42 @@ def test_softmax(rows, cols):
     y = torch.empty((rows, cols), dtype=torch.float32, device="cuda")
     T.call("tb_softmax", T.ptr(dev(x)), T.ptr(y), rows, cols, S())
     assert_softmax(host(y), x)
+
+
+def test_softmax_many_short_rows():
+    # more clusters than SMs: the 256-thread CTA variant
+    x = synth.normal((160, 4099), 2.0, seed=5)
+    y = torch.empty((160, 4099), dtype=torch.float32, device="cuda")
+    T.call("tb_softmax", T.ptr(dev(x)), T.ptr(y), 160, 4099, S())
+    assert_softmax(host(y), x)
+
+
+@pytest.mark.parametrize("cols", [9, 128256])
+def test_softmax_special_values_match_reference(cols):
+    # -inf entries give 0; a NaN, an all -inf row or a +inf make the row NaN
+    from oracle import refbind as R
+    x = synth.normal((4, cols), 2.0, seed=cols)
+    x[0, 3] = -np.inf
+    x[1, cols // 2] = np.nan
+    x[2, :] = -np.inf
+    x[3, cols - 1] = np.inf
+    y = torch.empty((4, cols), dtype=torch.float32, device="cuda")
+    T.call("tb_softmax", T.ptr(dev(x)), T.ptr(y), 4, cols, S())
+    got = host(y)
+    ref = R.softmax(x) if R.available() else O.softmax(x)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    assert got[0, 3] == 0.0
+    assert_softmax(got[:1], x[:1])
+
+
+def test_exp_selfcheck_every_float():
+    counts = (ctypes.c_uint64 * 4)()
+    T.call("tb_selfcheck_exp", ctypes.cast(counts, ctypes.c_void_p))
+    n_cr, max_cr, n_fast, max_fast = list(counts)
+    print("exp_cr: %d of 2^32 inputs differ from the double-precision exp (max %d ulp); "
+          "exp_fast: %d beyond 2 ulp (max %d ulp)" % (n_cr, max_cr, n_fast, max_fast))
+    assert max_cr <= 1 and n_cr <= 1024
+    assert n_fast == 0 and max_fast <= 2
 
 
 def test_softmax_kat():

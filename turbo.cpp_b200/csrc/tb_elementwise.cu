@@ -255,37 +255,53 @@ __global__ void __launch_bounds__(kThreads) copy_strided_kernel(const T *__restr
 // the destination's, so both sides stay coalesced.  Used when the source's
 // unit-stride dim is not the destination's (e.g. contiguous() of a transposed
 // view, attention.cpp:144-145).
-template <typename T>
+template <typename T, int TILE>
 __global__ void __launch_bounds__(256) copy_transpose_kernel(const T *__restrict__ src,
                                                              T *__restrict__ dst, int64_t outer,
                                                              int64_t R, int64_t C, Walk3 w) {
   // Logical element (o, r, c): dst at w.o0 + o..., r*w.s0[R] + c*w.s0[C]; the
   // source has unit stride along r (dim rank-2) and the dst along c (rank-1).
-  __shared__ T tile[32][33];
+  // TILE x TILE tiles; TILE consecutive threads run along the unit-stride axis
+  // of each side, and every thread has TILE*TILE/256 loads in flight before
+  // the tile is turned around in shared memory.
+  constexpr int TY = 256 / TILE, PER = TILE / TY;
+  __shared__ T tile[TILE][TILE + 1];
   const int rd = w.rank - 2, cd = w.rank - 1;
-  int64_t tiles_c = (C + 31) / 32, tiles_r = (R + 31) / 32;
-  int64_t tiles = outer * tiles_r * tiles_c;
+  const int tx = threadIdx.x % TILE, ty = threadIdx.x / TILE;
+  const int64_t sc = w.s1[cd], dr = w.s0[rd];
+  const int64_t tiles_c = (C + TILE - 1) / TILE, tiles_r = (R + TILE - 1) / TILE;
+  const int64_t per_outer = tiles_r * tiles_c, tiles = outer * per_outer;
   for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
-    int64_t o = t / (tiles_r * tiles_c);
-    int64_t rem = t % (tiles_r * tiles_c);
-    int64_t r0 = (rem / tiles_c) * 32, c0 = (rem % tiles_c) * 32;
+    const int64_t o = t / per_outer, rem = t - o * per_outer;
+    const int64_t r0 = (rem / tiles_c) * TILE, c0 = (rem % tiles_c) * TILE;
     int64_t od = w.o0, os = w.o1, ro = o;
     for (int d = w.rank - 3; d >= 0; --d) {
-      int64_t idx = ro % w.shape[d];
+      const int64_t idx = ro % w.shape[d];
       ro /= w.shape[d];
       od += idx * w.s0[d];
       os += idx * w.s1[d];
     }
-    // read: threads along r (unit stride in src)
-    for (int k = threadIdx.x / 32; k < 32; k += blockDim.x / 32) {
-      int64_t c = c0 + k, r = r0 + (threadIdx.x & 31);
-      if (c < C && r < R) tile[k][threadIdx.x & 31] = src[os + r * w.s1[rd] + c * w.s1[cd]];
+    T v[PER];
+    {
+      const int64_t r = r0 + tx;
+      const T *sp = src + os + r;  // src unit stride along r
+#pragma unroll
+      for (int k = 0; k < PER; ++k) {
+        const int64_t c = c0 + ty + k * TY;
+        v[k] = (r < R && c < C) ? sp[c * sc] : T(0);
+      }
     }
+#pragma unroll
+    for (int k = 0; k < PER; ++k) tile[ty + k * TY][tx] = v[k];
     __syncthreads();
-    // write: threads along c (unit stride in dst)
-    for (int k = threadIdx.x / 32; k < 32; k += blockDim.x / 32) {
-      int64_t r = r0 + k, c = c0 + (threadIdx.x & 31);
-      if (c < C && r < R) dst[od + r * w.s0[rd] + c * w.s0[cd]] = tile[threadIdx.x & 31][k];
+    {
+      const int64_t c = c0 + tx;
+      T *dp = dst + od + c;  // dst unit stride along c
+#pragma unroll
+      for (int k = 0; k < PER; ++k) {
+        const int64_t r = r0 + ty + k * TY;
+        if (r < R && c < C) dp[r * dr] = tile[tx][ty + k * TY];
+      }
     }
     __syncthreads();
   }
@@ -293,16 +309,31 @@ __global__ void __launch_bounds__(256) copy_transpose_kernel(const T *__restrict
 
 // ---- SwiGLU -----------------------------------------------------------------
 // silu(g) * u with silu(g) = g / (1 + exp(-g)) (src/nn/swiglu.cpp:25-31): the
-// division and products are IEEE-rounded as in the reference; exp follows the
-// reference's libm (exp_ref).
+// division and products are IEEE-rounded as in the reference; exp is the
+// correctly rounding exp_cr (the reference's glibc expf is too, but on ~0.03%
+// of inputs).
 __device__ __forceinline__ float swiglu1(float g, float u) {
-  float e = exp_ref(-g);
+  float e = exp_cr(-g);
   float s = __fdiv_rn(g, __fadd_rn(1.0f, e));
   return __fmul_rn(s, u);
 }
 __device__ __forceinline__ float swiglu1_bf16(float g, float u) {
   float e = __expf(-g);  // bf16 results: fp32 exp is far below the output rounding
   return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), u);
+}
+
+template <typename T>
+__device__ __forceinline__ uint4 swiglu_vec(const uint4 a, const uint4 b) {
+  constexpr int V = Vec<T>::N;
+  const T *ga = reinterpret_cast<const T *>(&a), *ub = reinterpret_cast<const T *>(&b);
+  uint4 r;
+  T *rr = reinterpret_cast<T *>(&r);
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    const float gf = to_f(ga[k]), uf = to_f(ub[k]);
+    rr[k] = from_f<T>(sizeof(T) == 4 ? swiglu1(gf, uf) : swiglu1_bf16(gf, uf));
+  }
+  return r;
 }
 
 template <typename T>
@@ -318,18 +349,15 @@ __global__ void __launch_bounds__(kThreads) swiglu_kernel(const T *__restrict__ 
     const uint4 *gv = reinterpret_cast<const uint4 *>(g);
     const uint4 *uv = reinterpret_cast<const uint4 *>(u);
     uint4 *yv = reinterpret_cast<uint4 *>(y);
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += stride) {
-      uint4 a = __ldcs(gv + i), b = __ldcs(uv + i);
-      const T *ga = reinterpret_cast<const T *>(&a), *ub = reinterpret_cast<const T *>(&b);
-      uint4 r;
-      T *rr = reinterpret_cast<T *>(&r);
-#pragma unroll
-      for (int k = 0; k < V; ++k) {
-        float gf = to_f(ga[k]), uf = to_f(ub[k]);
-        rr[k] = from_f<T>(sizeof(T) == 4 ? swiglu1(gf, uf) : swiglu1_bf16(gf, uf));
-      }
-      __stcs(yv + i, r);
+    // two vectors per thread per step: four 16-byte loads in flight
+    int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    for (; i + stride < nvec; i += 2 * stride) {
+      const uint4 a0 = __ldcs(gv + i), b0 = __ldcs(uv + i);
+      const uint4 a1 = __ldcs(gv + i + stride), b1 = __ldcs(uv + i + stride);
+      __stcs(yv + i, swiglu_vec<T>(a0, b0));
+      __stcs(yv + i + stride, swiglu_vec<T>(a1, b1));
     }
+    if (i < nvec) __stcs(yv + i, swiglu_vec<T>(__ldcs(gv + i), __ldcs(uv + i)));
     base = nvec * V;
   }
   for (int64_t i = base + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
@@ -339,14 +367,6 @@ __global__ void __launch_bounds__(kThreads) swiglu_kernel(const T *__restrict__ 
 }
 
 // ---- host helpers --------------------------------------------------------------
-
-int grid_for(int64_t work_items, const DeviceState *st, int per_sm = 8) {
-  int64_t want = (work_items + kThreads - 1) / kThreads;
-  int64_t cap = (int64_t)st->sm_count * per_sm;
-  if (want > cap) want = cap;
-  if (want < 1) want = 1;
-  return (int)want;
-}
 
 bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
 
@@ -395,7 +415,7 @@ tb_status launch_binary(const tb_view *a, const tb_view *b, const tb_view *out, 
   merge_dims(w, 3);
   bool out_c = w.rank == 1 && w.s0[0] == 1;
   if (out_c && w.s1[0] == 1 && w.s2[0] == 1 && aligned16(pa) && aligned16(pb) && aligned16(po)) {
-    binary_flat_kernel<T, OP><<<grid_for(n / V / 2 + 1, st), kThreads, 0, s>>>(pa, pb, po, n);
+    binary_flat_kernel<T, OP><<<wave_grid(binary_flat_kernel<T, OP>, kThreads, n / V / 2 + 1, st->sm_count), kThreads, 0, s>>>(pa, pb, po, n);
     return check_launch("tb_binary");
   }
   // row-vector broadcast: [rows, inner] with one side stride-0 over rows
@@ -406,15 +426,15 @@ tb_status launch_binary(const tb_view *a, const tb_view *b, const tb_view *out, 
     bool a_row = w.s1[0] == 0 && w.s1[1] == 1;
     bool b_row = w.s2[0] == 0 && w.s2[1] == 1;
     if (a_full && b_row) {
-      binary_rowvec_kernel<T, OP><<<grid_for(n / V, st), kThreads, 0, s>>>(pa, pb, po, n, w.shape[1], 0);
+      binary_rowvec_kernel<T, OP><<<wave_grid(binary_rowvec_kernel<T, OP>, kThreads, n / V, st->sm_count), kThreads, 0, s>>>(pa, pb, po, n, w.shape[1], 0);
       return check_launch("tb_binary");
     }
     if (b_full && a_row) {
-      binary_rowvec_kernel<T, OP><<<grid_for(n / V, st), kThreads, 0, s>>>(pb, pa, po, n, w.shape[1], 1);
+      binary_rowvec_kernel<T, OP><<<wave_grid(binary_rowvec_kernel<T, OP>, kThreads, n / V, st->sm_count), kThreads, 0, s>>>(pb, pa, po, n, w.shape[1], 1);
       return check_launch("tb_binary");
     }
   }
-  binary_strided_kernel<T, OP><<<grid_for(n, st), kThreads, 0, s>>>(pa, pb, po, n, w);
+  binary_strided_kernel<T, OP><<<wave_grid(binary_strided_kernel<T, OP>, kThreads, n, st->sm_count), kThreads, 0, s>>>(pa, pb, po, n, w);
   return check_launch("tb_binary");
 }
 
@@ -466,7 +486,7 @@ tb_status tb_scale(const tb_view *x, float sc, const tb_view *out, tb_stream str
   const float *px = static_cast<const float *>(x->data) + x->offset;
   float *po = static_cast<float *>(out->data) + out->offset;
   if (is_contiguous(x) && aligned16(px) && aligned16(po)) {
-    scale_flat_kernel<<<grid_for(n / 4 + 1, st), kThreads, 0, s>>>(px, po, n, sc);
+    scale_flat_kernel<<<wave_grid(scale_flat_kernel, kThreads, n / 4 + 1, st->sm_count), kThreads, 0, s>>>(px, po, n, sc);
     return check_launch("tb_scale");
   }
   Walk3 w;
@@ -479,7 +499,7 @@ tb_status tb_scale(const tb_view *x, float sc, const tb_view *out, tb_stream str
   }
   w.o0 = w.o1 = w.o2 = 0;
   merge_dims(w, 2);
-  scale_strided_kernel<<<grid_for(n, st), kThreads, 0, s>>>(px, po, n, sc, w);
+  scale_strided_kernel<<<wave_grid(scale_strided_kernel, kThreads, n, st->sm_count), kThreads, 0, s>>>(px, po, n, sc, w);
   return check_launch("tb_scale");
 }
 
@@ -515,7 +535,7 @@ tb_status tb_copy(const tb_view *dst, const tb_view *src, tb_stream stream) {
   if (w.rank == 1 && w.s0[0] == 1 && w.s1[0] == 1) {
     int64_t bytes = n * es;
     if (aligned16(ps) && aligned16(pd) && bytes % 16 == 0) {
-      copy_flat16_kernel<<<grid_for(bytes / 32 + 1, st), kThreads, 0, s>>>(
+      copy_flat16_kernel<<<wave_grid(copy_flat16_kernel, kThreads, bytes / 32 + 1, st->sm_count), kThreads, 0, s>>>(
           reinterpret_cast<const uint4 *>(ps), reinterpret_cast<uint4 *>(pd), bytes / 16);
       return check_launch("tb_copy");
     }
@@ -528,18 +548,25 @@ tb_status tb_copy(const tb_view *dst, const tb_view *src, tb_stream stream) {
   if (w.rank >= 2 && w.s0[w.rank - 1] == 1 && w.s1[w.rank - 2] == 1 && w.s1[w.rank - 1] != 1) {
     int64_t R = w.shape[w.rank - 2], C = w.shape[w.rank - 1];
     int64_t outer = n / (R * C);
-    int64_t tiles = outer * ((R + 31) / 32) * ((C + 31) / 32);
+    const bool big = R >= 64 && C >= 64;
+    const int T_ = big ? 64 : 32;
+    int64_t tiles = outer * ((R + T_ - 1) / T_) * ((C + T_ - 1) / T_);
     int grid = (int)std::min<int64_t>(tiles, (int64_t)st->sm_count * 8);
-    if (es == 4)
-      copy_transpose_kernel<float><<<grid, 256, 0, s>>>((const float *)ps, (float *)pd, outer, R, C, w);
-    else
-      copy_transpose_kernel<uint16_t><<<grid, 256, 0, s>>>((const uint16_t *)ps, (uint16_t *)pd, outer, R, C, w);
+    if (es == 4) {
+      if (big) copy_transpose_kernel<float, 64><<<grid, 256, 0, s>>>((const float *)ps, (float *)pd, outer, R, C, w);
+      else copy_transpose_kernel<float, 32><<<grid, 256, 0, s>>>((const float *)ps, (float *)pd, outer, R, C, w);
+    } else {
+      if (big)
+        copy_transpose_kernel<uint16_t, 64><<<grid, 256, 0, s>>>((const uint16_t *)ps, (uint16_t *)pd, outer, R, C, w);
+      else
+        copy_transpose_kernel<uint16_t, 32><<<grid, 256, 0, s>>>((const uint16_t *)ps, (uint16_t *)pd, outer, R, C, w);
+    }
     return check_launch("tb_copy");
   }
   if (es == 4)
-    copy_strided_kernel<float><<<grid_for(n, st), kThreads, 0, s>>>((const float *)ps, (float *)pd, n, w);
+    copy_strided_kernel<float><<<wave_grid(copy_strided_kernel<float>, kThreads, n, st->sm_count), kThreads, 0, s>>>((const float *)ps, (float *)pd, n, w);
   else
-    copy_strided_kernel<uint16_t><<<grid_for(n, st), kThreads, 0, s>>>((const uint16_t *)ps, (uint16_t *)pd, n, w);
+    copy_strided_kernel<uint16_t><<<wave_grid(copy_strided_kernel<uint16_t>, kThreads, n, st->sm_count), kThreads, 0, s>>>((const uint16_t *)ps, (uint16_t *)pd, n, w);
   return check_launch("tb_copy");
 }
 
@@ -552,10 +579,10 @@ tb_status tb_swiglu(int dtype, const void *g, const void *u, void *y, int64_t n,
   cudaStream_t s = as_stream(stream);
   int vec_ok = aligned16(g) && aligned16(u) && aligned16(y);
   if (dtype == TB_F32) {
-    swiglu_kernel<float><<<grid_for(n / 4 + 1, st), kThreads, 0, s>>>(
+    swiglu_kernel<float><<<wave_grid(swiglu_kernel<float>, kThreads, n / 4 + 1, st->sm_count), kThreads, 0, s>>>(
         (const float *)g, (const float *)u, (float *)y, n, vec_ok);
   } else if (dtype == TB_BF16) {
-    swiglu_kernel<__nv_bfloat16><<<grid_for(n / 8 + 1, st), kThreads, 0, s>>>(
+    swiglu_kernel<__nv_bfloat16><<<wave_grid(swiglu_kernel<__nv_bfloat16>, kThreads, n / 8 + 1, st->sm_count), kThreads, 0, s>>>(
         (const __nv_bfloat16 *)g, (const __nv_bfloat16 *)u, (__nv_bfloat16 *)y, n, vec_ok);
   } else {
     return fail(TB_EINVAL, "tb_swiglu: dtype must be TB_F32 or TB_BF16");

@@ -83,6 +83,18 @@ template <typename F> inline tb_status ensure_smem_for(F *func, size_t bytes) {
   return ensure_smem(reinterpret_cast<const void *>(func), bytes);
 }
 
+// CTAs of `func` (launched with `threads` threads and `smem` dynamic shared
+// memory) that fit on one SM at once, cached per (function, device, shape).
+// Grid-stride kernels launch SMs x this many CTAs: one full wave, no tail.
+int resident_ctas(const void *func, int threads, size_t smem);
+template <typename F> inline int wave_grid(F *func, int threads, int64_t work_items, int sm_count,
+                                           size_t smem = 0) {
+  const int64_t cap = (int64_t)sm_count * resident_ctas(reinterpret_cast<const void *>(func), threads, smem);
+  int64_t want = (work_items + threads - 1) / threads;
+  if (want > cap) want = cap;
+  return (int)(want < 1 ? 1 : want);
+}
+
 // ----------------------------------------------------------------- device side
 
 constexpr uint32_t ERR_TIMEOUT = 1u;
@@ -191,11 +203,71 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
 }
 
 // ---- exp for the softmax / SiLU paths -----------------------------------------
-// exp evaluated in double precision and rounded once to float: the correctly
-// rounded result unless exp(x) lies within about one double ulp of a float
-// rounding boundary.  The reference calls glibc expf, whose documented error
-// bound is 0.502 ulp, i.e. it is correctly rounded except on ~0.03% of inputs;
-// there the two differ by one ulp of exp.
+// The reference calls glibc expf, whose documented error bound is 0.502 ulp: it
+// is correctly rounded except on ~0.03% of inputs.  Two implementations here,
+// both written from the textbook method (argument reduction x = k ln2 + r,
+// |r| <= ln2/2, exp(r) from its Taylor series, scaling by 2^k in the exponent
+// field):
+//
+// exp_cr    reduction and series in double precision (series to degree 12: the
+//           truncation error is below 2^-51 on |r| <= ln2/2), rounded once to
+//           float.  Correctly rounded unless exp(x) lies within ~2^-50
+//           (relative) of a float rounding boundary.  Used where the reference's
+//           result is matched bit for bit (SwiGLU).
+// exp_fast  fp32 arithmetic only: ln2 split in a 16-bit head and a tail
+//           (Cody and Waite) so k*ln2_hi is exact, series to degree 7 (truncation
+//           below 2^-27), 2^k applied as two power-of-two factors so results in
+//           the subnormal range round once.  Within 2 ulp.  Used where the
+//           reference's result is matched within a tolerance (softmax).
+// exp_ref   double-precision libdevice exp rounded to float: the self-check's
+//           yardstick for the two above, not used on a product path.
 __device__ __forceinline__ float exp_ref(float x) { return __double2float_rn(exp((double)x)); }
+
+__device__ __forceinline__ float exp_cr(float xf) {
+  if (xf != xf) return xf;
+  // exp(-110) rounds to +0 and exp(100) to +inf, so clamping changes no result
+  const double x = (double)fminf(fmaxf(xf, -110.0f), 100.0f);
+  const double kRound = 6755399441055744.0;  // 1.5 * 2^52: t's low word holds rint(x / ln2)
+  const double t = fma(x, 1.4426950408889634, kRound);
+  const int k = __double2loint(t);
+  const double kd = t - kRound;
+  const double r = fma(kd, -0.6931471805599453, x);  // |k| <= 159: error ~1e-17, far below 2^-50
+  double p = 1.0 / 479001600.0;                      // 1/12!
+  p = fma(p, r, 1.0 / 39916800.0);
+  p = fma(p, r, 1.0 / 3628800.0);
+  p = fma(p, r, 1.0 / 362880.0);
+  p = fma(p, r, 1.0 / 40320.0);
+  p = fma(p, r, 1.0 / 5040.0);
+  p = fma(p, r, 1.0 / 720.0);
+  p = fma(p, r, 1.0 / 120.0);
+  p = fma(p, r, 1.0 / 24.0);
+  p = fma(p, r, 1.0 / 6.0);
+  p = fma(p, r, 0.5);
+  p = fma(p, r, 1.0);
+  p = fma(p, r, 1.0);
+  // p is in [0.70, 1.42]; 2^k (k in [-159, 145]) keeps the double normal
+  return __double2float_rn(__hiloint2double(__double2hiint(p) + (int)((unsigned)k << 20), __double2loint(p)));
+}
+
+__device__ __forceinline__ float exp_fast(float x) {
+  if (x != x) return x;
+  x = fminf(fmaxf(x, -104.0f), 89.0f);  // exp(-104) rounds to +0, exp(89) to +inf
+  const float kRound = 12582912.0f;     // 1.5 * 2^23
+  const float t = fmaf(x, 1.44269504f, kRound);
+  const int k = __float_as_int(t) - 0x4B400000;
+  const float kf = t - kRound;
+  float r = fmaf(kf, -0.693145751953125f, x);  // ln2 head: 16 significant bits
+  r = fmaf(kf, -1.4286068203094173e-6f, r);    // ln2 - head
+  float p = 1.0f / 5040.0f;
+  p = fmaf(p, r, 1.0f / 720.0f);
+  p = fmaf(p, r, 1.0f / 120.0f);
+  p = fmaf(p, r, 1.0f / 24.0f);
+  p = fmaf(p, r, 1.0f / 6.0f);
+  p = fmaf(p, r, 0.5f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  const int k1 = k >> 1, k2 = k - k1;  // each in [-75, 64]
+  return __fmul_rn(__fmul_rn(p, __int_as_float((k1 + 127) << 23)), __int_as_float((k2 + 127) << 23));
+}
 
 }  // namespace tb

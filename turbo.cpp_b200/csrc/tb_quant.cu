@@ -123,37 +123,72 @@ __global__ void embedding_f32_kernel(const float *__restrict__ w, int64_t dim, i
   }
 }
 
-// Q8_0 quantisation, one warp per block of 32 (quant_math.hpp:68-90):
-// amax with NaN ignored (std::max keeps the running max), d = amax / 127,
-// stored as half (round to nearest even), id = 1/d from the fp32 d,
-// q = roundf(x * id) (half away from zero).
-__global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float *__restrict__ x,
-                                                            int64_t rows, int64_t k,
-                                                            uint8_t *__restrict__ out) {
-  const int lane = threadIdx.x & 31;
-  const int64_t nb_row = k / 32;
-  const int64_t total = rows * nb_row;
-  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
-  for (int64_t blk = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); blk < total;
-       blk += warps) {
-    int64_t r = blk / nb_row, b = blk % nb_row;
-    float v = x[r * k + b * 32 + lane];
-    float a = fabsf(v);
-    a = (a == a) ? a : 0.f;  // a NaN never replaces the running max
+// Q8_0 quantisation (quant_math.hpp:68-90): amax with NaN ignored (std::max
+// keeps the running max), d = amax / 127, stored as half (round to nearest
+// even), id = 1/d from the fp32 d, q = roundf(x * id) (half away from zero).
+// With k a multiple of 32 the blocks of consecutive rows are consecutive, so
+// block i reads x[32 i, 32 i + 32).  One warp takes 32 consecutive blocks:
+// 8 coalesced 16-byte loads per lane (8 lanes per block), the amax over each
+// group of 8 lanes, the 1088 output bytes assembled in shared memory and
+// written as 68 16-byte stores.
+constexpr int kQuantWarps = 8;
+
+__device__ __forceinline__ void st_shared_u16(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(kQuantWarps * 32) quantize_q8_0_kernel(const float *__restrict__ x,
+                                                                         int64_t nblocks,
+                                                                         uint8_t *__restrict__ out) {
+  __shared__ __align__(16) uint8_t stage[kQuantWarps][32 * 34];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int sub = lane & 7;  // this lane's 4 values of its block
+  const bool vin = (reinterpret_cast<uintptr_t>(x) & 15) == 0;
+  const bool vout = (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+  const uint32_t sbase = (uint32_t)__cvta_generic_to_shared(&stage[warp][0]);
+  const int64_t nwarps = (int64_t)gridDim.x * kQuantWarps;
+  for (int64_t g = (int64_t)blockIdx.x * kQuantWarps + warp; g * 32 < nblocks; g += nwarps) {
+    const int64_t b0 = g * 32;
+    const int nb = (nblocks - b0 < 32) ? (int)(nblocks - b0) : 32;
+    float4 v[8];
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-    float d = __fdiv_rn(a, 127.0f);
-    float id = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
-    uint8_t *ob = out + blk * 34;
-    int q = (int)roundf(__fmul_rn(v, id));
-    ob[2 + lane] = (uint8_t)(int8_t)q;
-    if (lane == 0) {
-      // Explicit byte stores: nvcc 12.9 was seen to drop the low byte when the
-      // two halves of a 16-bit value were stored as `h & 0xFF` / `h >> 8`.
-      const uint32_t h = __half_as_ushort(__float2half_rn(d));
-      asm volatile("st.u8 [%0], %1;" ::"l"(ob), "r"(h & 0xFFu) : "memory");
-      asm volatile("st.u8 [%0], %1;" ::"l"(ob + 1), "r"(h >> 8) : "memory");
+    for (int j = 0; j < 8; ++j) {
+      const int bl = j * 4 + (lane >> 3);
+      v[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (bl < nb) {
+        const float *p = x + (b0 + bl) * 32 + sub * 4;
+        v[j] = vin ? __ldcs(reinterpret_cast<const float4 *>(p)) : make_float4(p[0], p[1], p[2], p[3]);
+      }
     }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int bl = j * 4 + (lane >> 3);
+      float a = fmaxf(fmaxf(fabsf(v[j].x), fabsf(v[j].y)), fmaxf(fabsf(v[j].z), fabsf(v[j].w)));
+      a = (a == a) ? a : 0.f;  // fmaxf already skips a NaN operand; all four NaN gives 0
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 1));
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 2));
+      a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, 4));
+      const float d = __fdiv_rn(a, 127.0f);
+      const float id = d != 0.f ? __fdiv_rn(1.0f, d) : 0.f;
+      const uint32_t q0 = (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[j].x, id));
+      const uint32_t q1 = (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[j].y, id));
+      const uint32_t q2 = (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[j].z, id));
+      const uint32_t q3 = (uint32_t)(uint8_t)(int8_t)(int)roundf(__fmul_rn(v[j].w, id));
+      // block bl occupies stage bytes [34 bl, 34 bl + 34): half d, then 32 quants
+      const uint32_t at = sbase + (uint32_t)(bl * 34);
+      st_shared_u16(at + 2 + sub * 4, q0 | (q1 << 8));
+      st_shared_u16(at + 4 + sub * 4, q2 | (q3 << 8));
+      if (sub == 0) st_shared_u16(at, __half_as_ushort(__float2half_rn(d)));
+    }
+    __syncwarp();
+    uint8_t *ob = out + b0 * 34;
+    if (nb == 32 && vout) {
+      const uint4 *src = reinterpret_cast<const uint4 *>(&stage[warp][0]);
+      for (int i = lane; i < 68; i += 32) reinterpret_cast<uint4 *>(ob)[i] = src[i];
+    } else {
+      for (int i = lane; i < nb * 34; i += 32) ob[i] = stage[warp][i];
+    }
+    __syncwarp();
   }
 }
 
@@ -163,10 +198,11 @@ __global__ void __launch_bounds__(256) quantize_q8_0_kernel(const float *__restr
 // lookup), for entry points that must not allocate.
 tb_status launch_quantize_q8_0(const float *x, int64_t rows, int64_t k, void *blocks, cudaStream_t s,
                                int sm_count) {
-  int64_t total = rows * (k / 32);
-  int grid = (int)std::min<int64_t>((total + 7) / 8, (int64_t)sm_count * 16);
+  const int64_t total = rows * (k / 32);
+  const int64_t groups = (total + 31) / 32;
+  int grid = (int)std::min<int64_t>((groups + kQuantWarps - 1) / kQuantWarps, (int64_t)sm_count * 8);
   if (grid < 1) grid = 1;
-  quantize_q8_0_kernel<<<grid, 256, 0, s>>>(x, rows, k, (uint8_t *)blocks);
+  quantize_q8_0_kernel<<<grid, kQuantWarps * 32, 0, s>>>(x, total, (uint8_t *)blocks);
   return check_launch("quantize_q8_0");
 }
 
@@ -200,10 +236,7 @@ tb_status tb_quantize_q8_0(const float *x, int64_t rows, int64_t k, void *blocks
   if (!x || !blocks) return fail(TB_EINVAL, "tb_quantize_q8_0: null pointer");
   DeviceState *st;
   TB_TRY(device_state(&st));
-  int64_t total = rows * (k / 32);
-  int grid = (int)std::min<int64_t>((total + 7) / 8, (int64_t)st->sm_count * 16);
-  quantize_q8_0_kernel<<<grid, 256, 0, as_stream(stream)>>>(x, rows, k, (uint8_t *)blocks);
-  return check_launch("tb_quantize_q8_0");
+  return launch_quantize_q8_0(x, rows, k, blocks, as_stream(stream), st->sm_count);
 }
 
 tb_status tb_embedding(int dtype, const void *w, int64_t dim, int64_t vocab, const int32_t *ids,

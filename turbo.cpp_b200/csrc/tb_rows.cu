@@ -156,17 +156,27 @@ __global__ void __launch_bounds__(kRowThreads) rmsnorm_any_kernel(const T *__res
 }
 
 // ---------------------------------------------------------------- softmax ----
-// MODE 0: full softmax of each row (src/nn/softmax.cpp:30-50):
-//   M = max, e = exp(x - M) stored, S = sum e, y = e / S.
+// MODE 0: softmax of each row (src/nn/softmax.cpp:30-50): M = max (strict '>',
+//   so NaN never becomes the maximum), e = exp(x - M) stored, S = sum of e,
+//   y = e / S, here e * (1/S) (within 1.5 ulp of the quotient; the reference's
+//   own S is a sequential fp32 sum, which a parallel sum matches only within a
+//   tolerance anyway).
 // MODE 1: shard statistics only: row max and sum of exp(x - max) of this slice.
-// The cluster's CTAs split the row's columns; CTA rank c owns [c*span, ...).
-template <int MODE>
-__global__ void __launch_bounds__(kRowThreads) softmax_cluster_kernel(
+// The cluster's CTAs split the row's columns: CTA c owns [c*span, (c+1)*span),
+// span a multiple of 4 so a slice is 16-byte aligned whenever its row is.  Each
+// CTA stages its slice in shared memory, so the row is read once and written
+// once; the CTAs exchange their maxima, then their sums, through distributed
+// shared memory.
+template <int MODE, int NT>
+__global__ void __launch_bounds__(NT) softmax_cluster_kernel(
     const float *__restrict__ x, float *__restrict__ y, int64_t rows, int64_t cols, int64_t ldx,
-    int64_t ldy, int span, float *__restrict__ out_max, float *__restrict__ out_sum) {
-  extern __shared__ float slice[];  // span floats
+    int64_t ldy, int span, float *__restrict__ out_max, float *__restrict__ out_sum,
+    uint32_t *__restrict__ err) {
+  extern __shared__ float4 slice4[];  // span floats
+  float *slice = reinterpret_cast<float *>(slice4);
   __shared__ float scratch[32];
   __shared__ float part[2];  // this CTA's [max, sum] for the cluster exchange
+  __shared__ __align__(8) uint64_t bar;
   cg::cluster_group cluster = cg::this_cluster();
   const int crank = (int)cluster.block_rank();
   const int csize = (int)cluster.num_blocks();
@@ -175,26 +185,58 @@ __global__ void __launch_bounds__(kRowThreads) softmax_cluster_kernel(
   const int64_t c0 = (int64_t)crank * span;
   const int64_t c1 = (c0 + span < cols) ? c0 + span : cols;
   const int n = c1 > c0 ? (int)(c1 - c0) : 0;
+  const int n4 = n >> 2;
   const float *xr = x + row * ldx + c0;
 
-  float m = -INFINITY;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    float v = xr[i];
-    slice[i] = v;
-    m = (v > m) ? v : m;  // NaN never becomes the max (strict '>')
+  // Stage the slice: one bulk copy of its 16-byte part when the slice is
+  // aligned (plain loads for the last n % 4 floats), else plain loads.
+  const bool bulk = n4 > 0 && (reinterpret_cast<uintptr_t>(xr) & 15) == 0;
+  if (bulk) {
+    if (threadIdx.x == 0) {
+      mbar_init(&bar, 1);
+      fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      mbar_arrive_expect_tx(&bar, (uint32_t)n4 * 16u);
+      bulk_g2s(slice4, xr, (uint32_t)n4 * 16u, &bar);
+    }
+    for (int i = 4 * n4 + threadIdx.x; i < n; i += NT) slice[i] = xr[i];
+    if (!mbar_wait_bounded(&bar, 0, err)) mbar_wait_bounded(&bar, 0, err);  // second, bounded wait for the copy
+  } else {
+    for (int i = threadIdx.x; i < n; i += NT) slice[i] = xr[i];
   }
+  __syncthreads();
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < n4; i += NT) {
+    const float4 v = slice4[i];
+    m = v.x > m ? v.x : m;
+    m = v.y > m ? v.y : m;
+    m = v.z > m ? v.z : m;
+    m = v.w > m ? v.w : m;
+  }
+  for (int i = 4 * n4 + threadIdx.x; i < n; i += NT) m = slice[i] > m ? slice[i] : m;
   m = block_max(m, scratch);
   if (threadIdx.x == 0) part[0] = m;
   cluster.sync();
   float M = -INFINITY;
   for (int c = 0; c < csize; ++c) {
-    float pm = *cluster.map_shared_rank(&part[0], c);
-    M = (pm > M) ? pm : M;
+    const float pm = *cluster.map_shared_rank(&part[0], c);
+    M = pm > M ? pm : M;
   }
   float s = 0.f;
-  for (int i = threadIdx.x; i < n; i += blockDim.x) {
-    float e = exp_ref(__fsub_rn(slice[i], M));
-    slice[i] = e;
+  for (int i = threadIdx.x; i < n4; i += NT) {
+    float4 v = slice4[i];
+    v.x = exp_fast(__fsub_rn(v.x, M));
+    v.y = exp_fast(__fsub_rn(v.y, M));
+    v.z = exp_fast(__fsub_rn(v.z, M));
+    v.w = exp_fast(__fsub_rn(v.w, M));
+    if (MODE == 0) slice4[i] = v;
+    s = __fadd_rn(s, __fadd_rn(__fadd_rn(v.x, v.y), __fadd_rn(v.z, v.w)));
+  }
+  for (int i = 4 * n4 + threadIdx.x; i < n; i += NT) {
+    const float e = exp_fast(__fsub_rn(slice[i], M));
+    if (MODE == 0) slice[i] = e;
     s = __fadd_rn(s, e);
   }
   s = block_sum(s, scratch);
@@ -208,14 +250,27 @@ __global__ void __launch_bounds__(kRowThreads) softmax_cluster_kernel(
       out_sum[row] = S;
     }
   } else {
+    const float inv = __frcp_rn(S);
     float *yr = y + row * ldy + c0;
-    for (int i = threadIdx.x; i < n; i += blockDim.x) yr[i] = __fdiv_rn(slice[i], S);
+    if ((reinterpret_cast<uintptr_t>(yr) & 15) == 0) {
+      for (int i = threadIdx.x; i < n4; i += NT) {
+        float4 v = slice4[i];
+        v.x = __fmul_rn(v.x, inv);
+        v.y = __fmul_rn(v.y, inv);
+        v.z = __fmul_rn(v.z, inv);
+        v.w = __fmul_rn(v.w, inv);
+        __stcs(reinterpret_cast<float4 *>(yr) + i, v);
+      }
+      for (int i = 4 * n4 + threadIdx.x; i < n; i += NT) yr[i] = __fmul_rn(slice[i], inv);
+    } else {
+      for (int i = threadIdx.x; i < n; i += NT) yr[i] = __fmul_rn(slice[i], inv);
+    }
   }
   cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
 }
 
-// Rows too long for the cluster's shared memory: online max/sum, then a
-// second read for the output.
+// Rows too long for the cluster's shared memory: max, then sum, then the
+// output, each a pass over the row (the later passes mostly hit L2).
 __global__ void __launch_bounds__(kRowThreads) softmax_long_kernel(const float *__restrict__ x,
                                                                    float *__restrict__ y,
                                                                    int64_t rows, int64_t cols) {
@@ -226,30 +281,33 @@ __global__ void __launch_bounds__(kRowThreads) softmax_long_kernel(const float *
     for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) m = xr[i] > m ? xr[i] : m;
     m = block_max(m, scratch);
     float s = 0.f;
-    for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) s = __fadd_rn(s, exp_ref(__fsub_rn(xr[i], m)));
+    for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) s = __fadd_rn(s, exp_fast(__fsub_rn(xr[i], m)));
     s = block_sum(s, scratch);
+    const float inv = __frcp_rn(s);
     for (int64_t i = threadIdx.x; i < cols; i += blockDim.x)
-      y[r * cols + i] = __fdiv_rn(exp_ref(__fsub_rn(xr[i], m)), s);
+      y[r * cols + i] = __fmul_rn(exp_fast(__fsub_rn(xr[i], m)), inv);
   }
 }
 
-// Shard finish: y = exp(x - M) / S for this shard's columns.
+// Shard finish: y = exp(x - M) * (1/S) for this shard's columns.
 __global__ void __launch_bounds__(kRowThreads) softmax_finish_kernel(
     const float *__restrict__ x, int64_t rows, int64_t cols, int64_t ldx,
     const float *__restrict__ gmax, const float *__restrict__ gsum, float *__restrict__ y,
     int64_t ldy) {
-  int64_t total = rows * cols;
-  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
-       t += (int64_t)gridDim.x * blockDim.x) {
-    int64_t r = t / cols, c = t % cols;
-    y[r * ldy + c] = __fdiv_rn(exp_ref(__fsub_rn(x[r * ldx + c], gmax[r])), gsum[r]);
+  for (int64_t r = blockIdx.y; r < rows; r += gridDim.y) {
+    const float M = gmax[r], inv = __frcp_rn(gsum[r]);
+    const float *xr = x + r * ldx;
+    float *yr = y + r * ldy;
+    for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < cols;
+         c += (int64_t)gridDim.x * blockDim.x)
+      yr[c] = __fmul_rn(exp_fast(__fsub_rn(xr[c], M)), inv);
   }
 }
 
 __global__ void softmax_rescale_kernel(const float *__restrict__ lmax, const float *__restrict__ gmax,
                                        float *__restrict__ sum, int64_t rows) {
   int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (r < rows) sum[r] = __fmul_rn(sum[r], exp_ref(__fsub_rn(lmax[r], gmax[r])));
+  if (r < rows) sum[r] = __fmul_rn(sum[r], exp_fast(__fsub_rn(lmax[r], gmax[r])));
 }
 
 // ----------------------------------------------------------------- argmax ----
@@ -286,30 +344,45 @@ __global__ void __launch_bounds__(kRowThreads) argmax_cluster_kernel(
   const int64_t c0 = (int64_t)crank * span;
   const int64_t c1 = (c0 + span < cols) ? c0 + span : cols;
   const float *xr = x + row * ldx;
-  uint64_t best = 0;
+  // Each thread scans its columns in increasing order keeping the first
+  // strict maximum (greedy_sample's rule: NaN and -inf never win, a tie keeps
+  // the earlier column); the key is formed once, for the block reduction.
+  float bv = -INFINITY;
+  int64_t bi = -1;
   const bool vec = ((reinterpret_cast<uintptr_t>(xr + c0) & 15) == 0);
-  int64_t i = c0 + threadIdx.x * 4;
+  int64_t tail = c0;
   if (vec) {
-    for (; i + 3 < c1; i += (int64_t)blockDim.x * 4) {
-      float4 v = __ldcs(reinterpret_cast<const float4 *>(xr + i));
-      uint64_t k0 = argmax_key(v.x, col_base + i), k1 = argmax_key(v.y, col_base + i + 1);
-      uint64_t k2 = argmax_key(v.z, col_base + i + 2), k3 = argmax_key(v.w, col_base + i + 3);
-      k0 = k1 > k0 ? k1 : k0;
-      k2 = k3 > k2 ? k3 : k2;
-      k0 = k2 > k0 ? k2 : k0;
-      best = k0 > best ? k0 : best;
+    const int64_t nv = (c1 - c0) / 4;
+    const float4 *x4 = reinterpret_cast<const float4 *>(xr + c0);
+    int64_t j = threadIdx.x;
+    for (; j + 3 * (int64_t)blockDim.x < nv; j += 4 * (int64_t)blockDim.x) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldcs(x4 + j + u * (int64_t)blockDim.x);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t col = c0 + 4 * (j + u * (int64_t)blockDim.x);
+        if (v[u].x > bv) { bv = v[u].x; bi = col; }
+        if (v[u].y > bv) { bv = v[u].y; bi = col + 1; }
+        if (v[u].z > bv) { bv = v[u].z; bi = col + 2; }
+        if (v[u].w > bv) { bv = v[u].w; bi = col + 3; }
+      }
     }
-    // remaining columns of this slice
-    for (int64_t j = c0 + ((c1 - c0) / 4) * 4 + threadIdx.x; j < c1; j += blockDim.x) {
-      uint64_t k = argmax_key(xr[j], col_base + j);
-      best = k > best ? k : best;
+    for (; j < nv; j += blockDim.x) {
+      const float4 v = __ldcs(x4 + j);
+      const int64_t col = c0 + 4 * j;
+      if (v.x > bv) { bv = v.x; bi = col; }
+      if (v.y > bv) { bv = v.y; bi = col + 1; }
+      if (v.z > bv) { bv = v.z; bi = col + 2; }
+      if (v.w > bv) { bv = v.w; bi = col + 3; }
     }
-  } else {
-    for (int64_t j = c0 + threadIdx.x; j < c1; j += blockDim.x) {
-      uint64_t k = argmax_key(xr[j], col_base + j);
-      best = k > best ? k : best;
-    }
+    tail = c0 + 4 * nv;
   }
+  for (int64_t k = tail + threadIdx.x; k < c1; k += blockDim.x) {
+    const float v = xr[k];
+    if (v > bv) { bv = v; bi = k; }
+  }
+  uint64_t best = bi >= 0 ? argmax_key(bv, col_base + bi) : 0ull;
   best = block_max_u64(best, scratch);
   if (threadIdx.x == 0) part = best;
   cluster.sync();
@@ -346,12 +419,12 @@ int cluster_for(int64_t cols, int64_t smem_budget_floats) {
   return c;
 }
 
-template <typename Kern, typename... Args>
-tb_status launch_cluster(Kern k, int64_t rows, int csize, size_t smem, cudaStream_t s,
-                         Args... args) {
+template <int NT, typename Kern, typename... Args>
+tb_status launch_cluster_nt(Kern k, int64_t rows, int csize, size_t smem, cudaStream_t s,
+                            Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)(rows * csize), 1, 1);
-  cfg.blockDim = dim3(kRowThreads, 1, 1);
+  cfg.blockDim = dim3(NT, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -375,7 +448,19 @@ tb_status launch_cluster(Kern k, int64_t rows, int csize, size_t smem, cudaStrea
   return TB_OK;
 }
 
+template <typename Kern, typename... Args>
+tb_status launch_cluster(Kern k, int64_t rows, int csize, size_t smem, cudaStream_t s, Args... args) {
+  return launch_cluster_nt<kRowThreads>(k, rows, csize, smem, s, args...);
+}
+
 constexpr int64_t kSliceFloats = (96 * 1024) / 4;  // dynamic smem per CTA for a slice
+
+// Columns per CTA of a cluster of `cs`: a multiple of 4, so that each slice
+// starts 16-byte aligned when its row does.
+int softmax_span(int64_t cols, int cs) {
+  int64_t span = (cols + cs - 1) / cs;
+  return (int)((span + 3) / 4 * 4);
+}
 
 }  // namespace
 }  // namespace tb
@@ -434,9 +519,13 @@ tb_status tb_softmax(const float *x, float *y, int64_t rows, int64_t cols, tb_st
     softmax_long_kernel<<<(int)grid, kRowThreads, 0, s>>>(x, y, rows, cols);
     return check_launch("tb_softmax");
   }
-  int span = (int)((cols + cs - 1) / cs);
-  return launch_cluster(softmax_cluster_kernel<0>, rows, cs, (size_t)span * 4, s, x, y, rows, cols,
-                        cols, cols, span, (float *)nullptr, (float *)nullptr);
+  const int span = softmax_span(cols, cs);
+  if (rows * cs <= st->sm_count)  // few rows: wide CTAs shorten each row's critical path
+    return launch_cluster_nt<1024>(softmax_cluster_kernel<0, 1024>, rows, cs, (size_t)span * 4, s, x, y,
+                                   rows, cols, cols, cols, span, (float *)nullptr, (float *)nullptr,
+                                   st->err_word);
+  return launch_cluster_nt<512>(softmax_cluster_kernel<0, 512>, rows, cs, (size_t)span * 4, s, x, y, rows,
+                                cols, cols, cols, span, (float *)nullptr, (float *)nullptr, st->err_word);
 }
 
 tb_status tb_argmax(const float *x, int64_t rows, int64_t cols, int64_t *idx, tb_stream stream) {
@@ -464,9 +553,14 @@ tb_status tb_softmax_shard_stats(const float *x, int64_t rows, int64_t cols, int
   TB_TRY(device_state(&st));
   int cs = cluster_for(cols, kSliceFloats);
   if (cs == 0) return fail(TB_EINVAL, "tb_softmax_shard_stats: shard too wide (%lld columns)", (long long)cols);
-  int span = (int)((cols + cs - 1) / cs);
-  return launch_cluster(softmax_cluster_kernel<1>, rows, cs, (size_t)span * 4, as_stream(stream), x,
-                        (float *)nullptr, rows, cols, ld, (int64_t)0, span, row_max, row_sum);
+  const int span = softmax_span(cols, cs);
+  if (rows * cs <= st->sm_count)
+    return launch_cluster_nt<1024>(softmax_cluster_kernel<1, 1024>, rows, cs, (size_t)span * 4, as_stream(stream),
+                                   x, (float *)nullptr, rows, cols, ld, (int64_t)0, span, row_max, row_sum,
+                                   st->err_word);
+  return launch_cluster_nt<512>(softmax_cluster_kernel<1, 512>, rows, cs, (size_t)span * 4, as_stream(stream), x,
+                                (float *)nullptr, rows, cols, ld, (int64_t)0, span, row_max, row_sum,
+                                st->err_word);
 }
 
 tb_status tb_softmax_shard_rescale(const float *lmax, const float *gmax, float *sum, int64_t rows,
@@ -486,9 +580,12 @@ tb_status tb_softmax_shard_finish(const float *x, int64_t rows, int64_t cols, in
   if (!x || !gmax || !gsum || !y) return fail(TB_EINVAL, "tb_softmax_shard_finish: null pointer");
   DeviceState *st;
   TB_TRY(device_state(&st));
-  int64_t total = rows * cols;
-  int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)st->sm_count * 8);
-  softmax_finish_kernel<<<grid, 256, 0, as_stream(stream)>>>(x, rows, cols, ld, gmax, gsum, y, ld_y);
+  // columns across blockIdx.x, rows across blockIdx.y: about 8 CTAs per SM in all
+  const int64_t per_row = (cols + kRowThreads - 1) / kRowThreads;
+  const int64_t gy = std::min<int64_t>(rows, 65535);
+  const int64_t gx = std::max<int64_t>(1, std::min<int64_t>(per_row, ((int64_t)st->sm_count * 8 + gy - 1) / gy));
+  softmax_finish_kernel<<<dim3((unsigned)gx, (unsigned)gy), kRowThreads, 0, as_stream(stream)>>>(
+      x, rows, cols, ld, gmax, gsum, y, ld_y);
   return check_launch("tb_softmax_shard_finish");
 }
 

@@ -4,6 +4,7 @@
 #include <cstdio>
 #include <cstring>
 #include <map>
+#include <tuple>
 #include <mutex>
 #include <vector>
 
@@ -93,6 +94,20 @@ tb_status ensure_smem(const void *func, size_t bytes) {
   if (e != cudaSuccess) return fail(TB_ECUDA, "smem carveout: %s", cudaGetErrorString(e));
   cur = bytes;
   return TB_OK;
+}
+
+int resident_ctas(const void *func, int threads, size_t smem) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 1;
+  static std::map<std::tuple<const void *, int, int, size_t>, int> cache;
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto key = std::make_tuple(func, dev, threads, smem);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, func, threads, smem) != cudaSuccess || n < 1) n = 1;
+  cache[key] = n;
+  return n;
 }
 
 tb_status validate_view(const tb_view *v, const char *name) {

@@ -1,0 +1,75 @@
+// tb_selfcheck.cu -- device self-check of the exp implementations used by the
+// softmax and SwiGLU kernels, over every fp32 bit pattern.
+#include "tb_internal.cuh"
+
+namespace tb {
+namespace {
+
+// Distance in units in the last place between two floats (NaN == NaN; a NaN
+// against a number counts as 2^32).
+__device__ __forceinline__ unsigned long long ulp_dist(float a, float b) {
+  const bool na = a != a, nb = b != b;
+  if (na || nb) return (na && nb) ? 0ull : (1ull << 32);
+  int32_t ia = __float_as_int(a), ib = __float_as_int(b);
+  ia = ia < 0 ? (int32_t)(0x80000000u - (uint32_t)ia) : ia;  // -0.0 -> 0
+  ib = ib < 0 ? (int32_t)(0x80000000u - (uint32_t)ib) : ib;
+  const long long d = (long long)ia - (long long)ib;
+  return (unsigned long long)(d < 0 ? -d : d);
+}
+
+// out[0]: inputs where exp_cr differs from exp_ref; out[1]: largest such
+// distance (ulp); out[2]: inputs where exp_fast differs by more than 2 ulp;
+// out[3]: largest exp_fast distance.
+__global__ void exp_check_kernel(unsigned long long *out) {
+  unsigned long long n_cr = 0, max_cr = 0, n_fast = 0, max_fast = 0;
+  const unsigned long long stride = (unsigned long long)gridDim.x * blockDim.x;
+  for (unsigned long long i = (unsigned long long)blockIdx.x * blockDim.x + threadIdx.x; i < (1ull << 32);
+       i += stride) {
+    const float x = __uint_as_float((uint32_t)i);
+    const float ref = exp_ref(x);
+    const unsigned long long dc = ulp_dist(exp_cr(x), ref);
+    const unsigned long long df = ulp_dist(exp_fast(x), ref);
+    n_cr += dc != 0;
+    max_cr = dc > max_cr ? dc : max_cr;
+    n_fast += df > 2;
+    max_fast = df > max_fast ? df : max_fast;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    n_cr += __shfl_xor_sync(0xffffffffu, n_cr, o);
+    n_fast += __shfl_xor_sync(0xffffffffu, n_fast, o);
+    const unsigned long long a = __shfl_xor_sync(0xffffffffu, max_cr, o);
+    const unsigned long long b = __shfl_xor_sync(0xffffffffu, max_fast, o);
+    max_cr = a > max_cr ? a : max_cr;
+    max_fast = b > max_fast ? b : max_fast;
+  }
+  if ((threadIdx.x & 31) == 0) {
+    atomicAdd(out + 0, n_cr);
+    atomicMax(out + 1, max_cr);
+    atomicAdd(out + 2, n_fast);
+    atomicMax(out + 3, max_fast);
+  }
+}
+
+}  // namespace
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" tb_status tb_selfcheck_exp(uint64_t *counts) {
+  if (!counts) return fail(TB_EINVAL, "tb_selfcheck_exp: null pointer");
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  unsigned long long *d = nullptr;
+  cudaError_t e = cudaMalloc(&d, 4 * sizeof(unsigned long long));
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_selfcheck_exp: %s", cudaGetErrorString(e));
+  e = cudaMemset(d, 0, 4 * sizeof(unsigned long long));
+  if (e == cudaSuccess) {
+    exp_check_kernel<<<st->sm_count * 8, 256>>>(d);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) e = cudaMemcpy(counts, d, 4 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
+  cudaFree(d);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_selfcheck_exp: %s", cudaGetErrorString(e));
+  return TB_OK;
+}

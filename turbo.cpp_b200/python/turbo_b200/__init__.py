@@ -76,6 +76,7 @@ SIGNATURES = {
     "tb_softmax_shard_finish": [_P, _I64, _I64, _I64, _P, _P, _P, _I64, _P],
     "tb_argmax_shard_keys": [_P, _I64, _I64, _I64, _I64, _P, _P],
     "tb_argmax_key_index": [_P, _I64, _P, _P],
+    "tb_selfcheck_exp": [_P],
 }
 
 _lib = None

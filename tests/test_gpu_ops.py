@@ -179,6 +179,50 @@ def test_matmul_q4_0_bit_exact(M, K, N):
     assert_bits(run_matmul(T.Q4_0, x, wq, N), O.matmul_q4_0(x, wq, N))
 
 
+def assert_gemm_tol(got, xd, wd, tol=F32_REL):
+    """|y - y_exact| <= tol * sum_k |w_k x_k| per output, y_exact in float64
+    from the exactly dequantised operands (the reference is itself within
+    ~1e-7 of it)."""
+    x64, w64 = xd.astype(np.float64), wd.astype(np.float64)
+    ref = x64 @ w64.T
+    scale = np.abs(x64) @ np.abs(w64).T
+    err = np.abs(got.astype(np.float64) - ref) / np.maximum(scale, 1e-30)
+    assert err.max() <= tol, "max scaled err %g" % err.max()
+    return err.max()
+
+
+# prefill shapes on the tcgen05 path (M >= 32, K % 256 == 0): the benchmark's
+# gate/up and down GEMMs, ragged M and N, a K range split over several CTAs
+TC_SHAPES = [(512, 2048, 8192), (32, 256, 128), (130, 512, 300), (64, 2048, 1000), (200, 8192, 256),
+             (33, 4096, 2049)]
+
+
+@pytest.mark.parametrize("M,K,N", TC_SHAPES)
+def test_matmul_q8_0_tensor_cores_within_tolerance(M, K, N):
+    w = synth.normal((N, K), 0.02, seed=K + N)
+    wq = synth.quantize_q8_0(w)
+    x = synth.normal((M, K), 1.0, seed=M)
+    got = run_matmul(T.Q8_0, x, wq, N, "tb_matmul_quant")
+    err = assert_gemm_tol(got, x, synth.dequantize_q8_0(wq, K))
+    print("Q8_0 %dx%dx%d: max scaled error %.3g" % (M, K, N, err))
+    if M * N * K <= 64 * 2048 * 1000:  # and against the oracle's own result
+        assert_dot_tol(got, x, wq, K)
+
+
+@pytest.mark.parametrize("M,K,N", [(512, 8192, 2048), (64, 256, 130), (96, 1024, 640)])
+def test_matmul_q4_0_tensor_cores_within_tolerance(M, K, N):
+    wq = synth.quantize_q4_0(synth.normal((N, K), 0.02, seed=K + N))
+    x = synth.normal((M, K), 1.0, seed=M + 1)
+    got = run_matmul(T.Q4_0, x, wq, N, "tb_matmul_quant")
+    xd = synth.dequantize_q8_0(synth.quantize_q8_0(x), K)  # the reference quantises X rows
+    err = assert_gemm_tol(got, xd, synth.dequantize_q4_0(wq, K))
+    print("Q4_0 %dx%dx%d: max scaled error %.3g" % (M, K, N, err))
+    if M <= 96:
+        ref = O.matmul_q4_0(x, wq, N)
+        scale = np.abs(xd.astype(np.float64)) @ np.abs(synth.dequantize_q4_0(wq, K).astype(np.float64)).T
+        assert (np.abs(got - ref) / scale).max() <= F32_REL
+
+
 def test_matmul_quant_rejects_bad_k():
     x = torch.zeros((1, 40), device="cuda")
     with pytest.raises(T.TbError) as e:

@@ -203,7 +203,9 @@ tb_status tb_matmul_quant_exact(int dtype, const float *x_dev, int64_t M, int64_
  * or fail).  No counterpart in the reference, which runs on the CPU.
  * The quantized copy of X goes to a fixed 8 MiB buffer compiled into the
  * library (held on every GPU that loads it until the process exits) instead
- * of allocated scratch; results are identical to tb_matmul_quant(TB_Q4_0).
+ * of allocated scratch; results are identical to tb_matmul_quant_exact(TB_Q4_0)
+ * (the reference's summation order), and so to tb_matmul_quant(TB_Q4_0) on
+ * every shape that entry does not send to the tensor cores (M < 32). 
  * Requires M * (K/32) * 34 <= 8 MiB (e.g. M = 512 at K = 8192), else TB_EINVAL.
  * Calls no cudaMalloc/cudaFree.  The first call on a device looks up the
  * buffer's address (cudaGetSymbolAddress); make it before any stream capture.

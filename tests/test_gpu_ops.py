@@ -203,7 +203,8 @@ def test_matmul_q8_0_tensor_cores_within_tolerance(M, K, N):
     wq = synth.quantize_q8_0(w)
     x = synth.normal((M, K), 1.0, seed=M)
     got = run_matmul(T.Q8_0, x, wq, N, "tb_matmul_quant")
-    err = assert_gemm_tol(got, x, synth.dequantize_q8_0(wq, K))
+    # 1e-5 is the bar; the split accumulators keep the tensor-core path near 3e-7
+    err = assert_gemm_tol(got, x, synth.dequantize_q8_0(wq, K), tol=1e-6)
     print("Q8_0 %dx%dx%d: max scaled error %.3g" % (M, K, N, err))
     if M * N * K <= 64 * 2048 * 1000:  # and against the oracle's own result
         assert_dot_tol(got, x, wq, K)
@@ -215,7 +216,7 @@ def test_matmul_q4_0_tensor_cores_within_tolerance(M, K, N):
     x = synth.normal((M, K), 1.0, seed=M + 1)
     got = run_matmul(T.Q4_0, x, wq, N, "tb_matmul_quant")
     xd = synth.dequantize_q8_0(synth.quantize_q8_0(x), K)  # the reference quantises X rows
-    err = assert_gemm_tol(got, xd, synth.dequantize_q4_0(wq, K))
+    err = assert_gemm_tol(got, xd, synth.dequantize_q4_0(wq, K), tol=1e-6)
     print("Q4_0 %dx%dx%d: max scaled error %.3g" % (M, K, N, err))
     if M <= 96:
         ref = O.matmul_q4_0(x, wq, N)

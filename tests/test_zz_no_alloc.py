@@ -3,10 +3,12 @@ allocate device memory during a call.
 
 It keeps the quantized copy of X in a fixed buffer compiled into the library
 instead of scratch from the allocator.  Its output must equal the regular
-entry point's (tb_matmul_quant, TB_Q4_0) bit for bit -- the tolerance the Q4_0
-tests use -- on two calls in a row, so that whatever the first call left in
-the shared buffer cannot leak into the second.  This file is named to be
-collected last; it passes alone in a fresh process as well.
+bit-exact entry point's (tb_matmul_quant_exact, TB_Q4_0) bit for bit -- the
+tolerance the Q4_0 tests use -- on two calls in a row, so that whatever the
+first call left in the shared buffer cannot leak into the second; below 32 rows
+it also equals tb_matmul_quant (which takes the tensor cores from 32 rows on).
+This file is named to be collected last; it passes alone in a fresh process as
+well.
 """
 import numpy as np
 import pytest
@@ -36,12 +38,17 @@ def test_static_scratch_matches_regular_entry_two_calls():
         dx, dw = _dev(x, keep), _dev(wq, keep)
         y_reg = torch.empty((M, N), dtype=torch.float32, device="cuda")
         y_fix = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
-        T.call("tb_matmul_quant", T.Q4_0, T.ptr(dx), M, K, T.ptr(dw), N, T.ptr(y_reg), s)
+        T.call("tb_matmul_quant_exact", T.Q4_0, T.ptr(dx), M, K, T.ptr(dw), N, T.ptr(y_reg), s)
         T.call("tb_matmul_q4_0_static_scratch", T.ptr(dx), M, K, T.ptr(dw), N, T.ptr(y_fix), s)
         torch.cuda.synchronize()
         a = y_reg.cpu().numpy()
         b = y_fix.cpu().numpy()
         assert np.array_equal(a.view(np.uint32), b.view(np.uint32)), (M, K, N)
+        if M < 32:
+            y_def = torch.empty((M, N), dtype=torch.float32, device="cuda")
+            T.call("tb_matmul_quant", T.Q4_0, T.ptr(dx), M, K, T.ptr(dw), N, T.ptr(y_def), s)
+            torch.cuda.synchronize()
+            assert np.array_equal(y_def.cpu().numpy().view(np.uint32), b.view(np.uint32)), (M, K, N)
 
 
 def test_static_scratch_rejects_oversize():

@@ -31,8 +31,8 @@
 // core matrices, 128 B apart along K (leading byte offset) and 1024 B apart
 // along rows (stride byte offset).  The activations are written in exactly
 // this layout by split_x_kernel, block-column by block-column, so a stage's
-// 128 x 32 tile is one contiguous 16 KiB bulk copy.  The accumulator
-// (128 lanes x 128 fp32 columns) lives in tensor memory.
+// 128 x 32 tile is one contiguous 16 KiB bulk copy.  The accumulators
+// (128 lanes x 128 fp32 columns each) live in tensor memory.
 // No TMA multicast anywhere: every load reads this GPU's own memory.
 #include <algorithm>
 
@@ -44,6 +44,14 @@ namespace {
 constexpr int kTileRows = 128;  // weight rows per CTA (UMMA M)
 constexpr int kTileTok = 128;   // tokens per CTA (UMMA N)
 constexpr int kStages = 3;
+// Tensor-memory accumulators: the tensor core's fp32 accumulation truncates
+// each MMA's sum, so the error grows with the number of MMAs folded into one
+// accumulator and with its magnitude.  The hi*hi products rotate over three
+// accumulators (k-block i into i % 3) and the two small correction products
+// (hi*lo, lo*hi, ~2^-11 of the main term) go to a fourth; the epilogue adds
+// the four with round-to-nearest.  4 x 128 columns = all 512 of tensor memory.
+constexpr int kMainAcc = 3;
+constexpr int kTmemCols = 512;
 constexpr int kOpBytes = 128 * 32 * 4;    // one 128 x 32 tf32 operand tile
 constexpr int kStageBytes = 4 * kOpBytes;  // A hi, A lo, B hi, B lo
 constexpr int kGemmThreads = 256;
@@ -199,7 +207,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(
   }
   if (warp == 1) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
-                 "r"(kTileTok));
+                 "r"(kTmemCols));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -230,12 +238,14 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(
         tc_fence_after();
         const uint32_t st = sbase + (uint32_t)(s * kStageBytes);
 #pragma unroll
+        const uint32_t dmain = tmem + (uint32_t)((i % kMainAcc) * kTileTok);
+        const uint32_t dcorr = tmem + (uint32_t)(kMainAcc * kTileTok);
         for (int j = 0; j < 4; ++j) {  // four k-steps of 8 tf32 (32 bytes) per block
           const uint64_t ah = op_desc(st + j * 256), al = op_desc(st + kOpBytes + j * 256);
           const uint64_t bh = op_desc(st + 2 * kOpBytes + j * 256), bl = op_desc(st + 3 * kOpBytes + j * 256);
-          mma_tf32(tmem, ah, bh, (i | j) != 0);
-          mma_tf32(tmem, ah, bl, 1);
-          mma_tf32(tmem, al, bh, 1);
+          mma_tf32(dmain, ah, bh, (i >= kMainAcc || j != 0) ? 1u : 0u);
+          mma_tf32(dcorr, ah, bl, (i | j) != 0);
+          mma_tf32(dcorr, al, bh, 1);
         }
         mma_commit(&s_empty[s]);
       }
@@ -336,15 +346,30 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(
       tc_fence_after();
       const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
       float *o = out + (int64_t)blockIdx.z * split_stride;
+      const int nmain = iters < kMainAcc ? iters : kMainAcc;
 #pragma unroll 1
       for (int cb = 0; cb < kTileTok / 32; ++cb) {
+        // (main 0 + main 1 + main 2) + corrections, each add rounded to nearest
+        float acc[32];
         uint32_t r[32];
+        tmem_ld32(tmem + lane_base + (uint32_t)(kMainAcc * kTileTok + cb * 32), r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(r[j]);
+        float sum[32];
         tmem_ld32(tmem + lane_base + (uint32_t)(cb * 32), r);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) sum[j] = __uint_as_float(r[j]);
+#pragma unroll 1
+        for (int p = 1; p < nmain; ++p) {
+          tmem_ld32(tmem + lane_base + (uint32_t)(p * kTileTok + cb * 32), r);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) sum[j] = __fadd_rn(sum[j], __uint_as_float(r[j]));
+        }
         if (live) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             const int m = m0 + cb * 32 + j;
-            if (m < M) o[(int64_t)m * N + n] = __uint_as_float(r[j]);
+            if (m < M) o[(int64_t)m * N + n] = __fadd_rn(sum[j], acc[j]);
           }
         }
       }
@@ -356,7 +381,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_tc_kernel(
     tc_fence_after();
     if (lane == 0) mbar_wait_bounded(&acc_full, 0, err);  // no MMA may still write the accumulator
     __syncwarp();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTileTok));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
 }
 

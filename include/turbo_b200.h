@@ -249,6 +249,44 @@ tb_status tb_argmax_shard_keys(const float *x_dev, int64_t rows, int64_t cols, i
 tb_status tb_argmax_key_index(const int64_t *keys_dev, int64_t rows, int64_t *idx_dev,
                               tb_stream stream);
 
+/* ------------------------------------------- decode step with a device position -- */
+
+/* tb_rope with the position offset read from device memory (*pos_dev) when
+ * the kernel runs, so a decode step can be captured once and replayed.  A
+ * position outside the table sets bit 1 of the device error word and leaves x
+ * unchanged (tb_rope itself returns TB_ERANGE, rope.cpp:58-61). */
+tb_status tb_rope_at(const tb_view *x, const float *cos_dev, const float *sin_dev, int64_t head_dim,
+                     int64_t max_seq, const int32_t *pos_dev, tb_stream stream);
+/* One token's K and V rows into the layer caches [max_seq, row_elems] at row
+ * *pos_dev: the cache writes of src/nn/attention.cpp:66-84 for S = 1. */
+tb_status tb_kv_append(float *k_cache_dev, float *v_cache_dev, const float *k_dev, const float *v_dev,
+                       int64_t row_elems, int64_t max_seq, const int32_t *pos_dev, tb_stream stream);
+/* All query heads of one token against the caches' first *pos_dev + 1 rows
+ * (src/nn/attention.cpp:104-141 with S = 1; no mask applies): per head, scores
+ * as the fp32 matmul computes them (fma chain over head_dim) times scale,
+ * softmax as tb_softmax, then probabilities x V.  q [heads, head_dim], caches
+ * [max_seq, kv_heads, head_dim], out [heads, head_dim]; head_dim 64. */
+tb_status tb_attention_decode(const float *q_dev, const float *k_cache_dev, const float *v_cache_dev,
+                              int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t max_seq, float scale,
+                              const int32_t *pos_dev, float *out_dev, tb_stream stream);
+/* margins[*pos_dev] = logits[*idx_dev] - the largest other logit. */
+tb_status tb_decode_margin(const float *logits_dev, int64_t vocab, const int64_t *idx_dev,
+                           const int32_t *pos_dev, int64_t max_seq, float *margins_dev, tb_stream stream);
+/* End of a decode step: ids[0] = *idx (the next step's input token),
+ * history[*pos] = *idx, *pos += 1. */
+tb_status tb_decode_advance(const int64_t *idx_dev, int32_t *ids_dev, int32_t *pos_dev, int32_t *history_dev,
+                            int64_t max_seq, tb_stream stream);
+
+/* Streams and CUDA graphs for callers without the CUDA runtime: capture a
+ * sequence of calls on a created stream once, replay it many times. */
+typedef struct tb_graph_s *tb_graph;
+tb_status tb_stream_create(tb_stream *out);
+tb_status tb_stream_destroy(tb_stream stream);
+tb_status tb_capture_begin(tb_stream stream);
+tb_status tb_capture_end(tb_stream stream, tb_graph *out);
+tb_status tb_graph_launch(tb_graph graph, tb_stream stream);
+tb_status tb_graph_destroy(tb_graph graph);
+
 /* ---------------------------------------------------------------- diagnostics -- */
 
 /* Evaluates the two fp32 exp implementations of the softmax and SwiGLU kernels

@@ -600,3 +600,115 @@ def test_sharded_softmax_and_argmax_emulated(shards):
     got = host(idx)
     for r in range(rows):
         assert got[r] == O.argmax(x[r]), r
+
+
+# ------------------------------------------------ decode step (device position) ----
+
+def _pos(p):
+    return dev(np.array([p], np.int32))
+
+
+def test_rope_at_matches_rope_and_checks_range():
+    H, D, max_seq = 32, 64, 1024
+    c, s_ = O.rope_tables(D, max_seq, 500000.0)
+    dc, ds = dev(c), dev(s_)
+    x = synth.normal((H * D,), 1.0, seed=40)
+    a, b = dev(x), dev(x)
+    va = T.view(a, 0, (1, H, 1, D), (H * D, D, H * D, 1))
+    vb = T.view(b, 0, (1, H, 1, D), (H * D, D, H * D, 1))
+    T.call("tb_rope", T.byref(va), T.ptr(dc), T.ptr(ds), D, max_seq, 517, S())
+    T.call("tb_rope_at", T.byref(vb), T.ptr(dc), T.ptr(ds), D, max_seq, T.ptr(_pos(517)), S())
+    assert_bits(host(b), host(a))
+    assert T.take_device_errors() == 0
+    c2 = dev(x)
+    vc = T.view(c2, 0, (1, H, 1, D), (H * D, D, H * D, 1))
+    T.call("tb_rope_at", T.byref(vc), T.ptr(dc), T.ptr(ds), D, max_seq, T.ptr(_pos(max_seq)), S())
+    torch.cuda.synchronize()
+    assert T.take_device_errors() & 2
+    assert_bits(host(c2), x)  # left unchanged
+
+
+def test_kv_append_and_range():
+    row, max_seq = 8 * 64, 40
+    kc = torch.zeros(max_seq * row, device="cuda")
+    vc = torch.zeros(max_seq * row, device="cuda")
+    k = synth.normal((row,), 1.0, seed=41)
+    v = synth.normal((row,), 1.0, seed=42)
+    T.call("tb_kv_append", T.ptr(kc), T.ptr(vc), T.ptr(dev(k)), T.ptr(dev(v)), row, max_seq, T.ptr(_pos(7)), S())
+    hk, hv = host(kc).reshape(max_seq, row), host(vc).reshape(max_seq, row)
+    assert_bits(hk[7], k)
+    assert_bits(hv[7], v)
+    assert not hk[:7].any() and not hk[8:].any()
+    T.call("tb_kv_append", T.ptr(kc), T.ptr(vc), T.ptr(dev(k)), T.ptr(dev(v)), row, max_seq, T.ptr(_pos(max_seq)), S())
+    torch.cuda.synchronize()
+    assert T.take_device_errors() & 2
+    assert np.count_nonzero(host(kc)) == np.count_nonzero(hk)
+
+
+@pytest.mark.parametrize("pos", [0, 1, 255, 640, 1023])
+def test_attention_decode_against_float64(pos):
+    H, KVH, D, max_seq = 32, 8, 64, 1024
+    q = synth.normal((H, D), 1.0, seed=pos)
+    kc = synth.normal((max_seq, KVH, D), 1.0, seed=pos + 1)
+    vc = synth.normal((max_seq, KVH, D), 1.0, seed=pos + 2)
+    out = torch.empty((H, D), device="cuda")
+    scale = np.float32(1.0) / np.sqrt(np.float32(D))
+    T.call("tb_attention_decode", T.ptr(dev(q)), T.ptr(dev(kc)), T.ptr(dev(vc)), H, KVH, D, max_seq,
+           float(scale), T.ptr(_pos(pos)), T.ptr(out), S())
+    got = host(out)
+    ctx = pos + 1
+    want = np.empty((H, D))
+    for h in range(H):
+        kh = kc[:ctx, h // (H // KVH)].astype(np.float64)
+        vh = vc[:ctx, h // (H // KVH)].astype(np.float64)
+        s = (kh @ q[h].astype(np.float64)) * float(scale)
+        p = np.exp(s - s.max())
+        p /= p.sum()
+        want[h] = p @ vh
+    # per output: |err| <= 1e-5 * sum_c p_c |v_c| (the conditioning of p . V)
+    cond = np.empty((H, D))
+    for h in range(H):
+        kh = kc[:ctx, h // (H // KVH)].astype(np.float64)
+        s = (kh @ q[h].astype(np.float64)) * float(scale)
+        p = np.exp(s - s.max())
+        p /= p.sum()
+        cond[h] = p @ np.abs(vc[:ctx, h // (H // KVH)].astype(np.float64))
+    assert (np.abs(got - want) / cond).max() <= F32_REL
+
+
+def test_decode_margin_and_advance():
+    V, max_seq = 1000, 16
+    logits = synth.normal((V,), 1.0, seed=43)
+    logits[123] = 9.0
+    logits[7] = 8.5
+    dl = dev(logits)
+    idx = torch.empty(1, dtype=torch.int64, device="cuda")
+    T.call("tb_argmax", T.ptr(dl), 1, V, T.ptr(idx), S())
+    pos = _pos(5)
+    margins = torch.zeros(max_seq, device="cuda")
+    ids = torch.zeros(1, dtype=torch.int32, device="cuda")
+    hist = torch.zeros(max_seq, dtype=torch.int32, device="cuda")
+    T.call("tb_decode_margin", T.ptr(dl), V, T.ptr(idx), T.ptr(pos), max_seq, T.ptr(margins), S())
+    T.call("tb_decode_advance", T.ptr(idx), T.ptr(ids), T.ptr(pos), T.ptr(hist), max_seq, S())
+    assert host(margins)[5] == np.float32(9.0) - np.float32(8.5)
+    assert host(ids)[0] == 123 and host(hist)[5] == 123 and host(pos)[0] == 6
+
+
+def test_graph_capture_and_replay():
+    st = ctypes.c_void_p()
+    T.call("tb_stream_create", ctypes.byref(st))
+    x = dev(synth.normal((4096,), 1.0, seed=44))
+    y = torch.empty(4096, device="cuda")
+    vx, vy = T.view(x), T.view(y)
+    g = ctypes.c_void_p()
+    T.call("tb_capture_begin", st)
+    T.call("tb_scale", T.byref(vx), 2.0, T.byref(vy), st)
+    T.call("tb_binary", 0, T.byref(vy), T.byref(vx), T.byref(vy), st)
+    T.call("tb_capture_end", st, ctypes.byref(g))
+    for _ in range(3):
+        T.call("tb_graph_launch", g, st)
+    T.call("tb_sync", st)
+    xs = host(x)
+    assert_bits(host(y), xs * np.float32(2.0) + xs)
+    T.call("tb_graph_destroy", g)
+    T.call("tb_stream_destroy", st)

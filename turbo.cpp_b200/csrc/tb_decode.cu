@@ -1,0 +1,265 @@
+// tb_decode.cu -- the pieces of a one-token decode step whose arguments depend
+// on the position, with the position held in device memory so that one step
+// can be captured once in a CUDA graph and replayed for every token:
+//   tb_kv_append         cache rows [pos] <- this token's K and V
+//                        (attention.cpp:66-84 with S = 1: Kc.slice(pos).copy_(K))
+//   tb_attention_decode  all query heads of one token against the cache
+//                        (attention.cpp:104-141 with S = 1, fused per head)
+//   tb_decode_margin     top-1 minus top-2 logit (a diagnostic for callers)
+//   tb_decode_advance    next token id, history, pos += 1
+// plus stream and graph handles for callers without the CUDA runtime.
+// Every kernel checks pos against the cache length: a position outside it
+// sets bit 1 of the device error word and writes nothing.
+#include <algorithm>
+
+#include "tb_internal.cuh"
+
+namespace tb {
+namespace {
+
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+__global__ void kv_append_kernel(float *__restrict__ kc, float *__restrict__ vc, const float *__restrict__ k,
+                                 const float *__restrict__ v, int row, int max_seq,
+                                 const int32_t *__restrict__ pos_dev, uint32_t *__restrict__ err) {
+  const int pos = *pos_dev;
+  if (pos < 0 || pos >= max_seq) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(err, ERR_INDEX);
+    return;
+  }
+  const int64_t base = (int64_t)pos * row;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < row; i += gridDim.x * blockDim.x) {
+    kc[base + i] = k[i];
+    vc[base + i] = v[i];
+  }
+}
+
+// One CTA per query head h (key/value head h / (H / KVH)), ctx = pos + 1 keys:
+//   score[c] = (fma chain over d of q[d] * K[c][d]) * scale   -- the fp32
+//              matmul's order (tb_matmul_f32), then Tensor::operator*(float)
+//   p[c]     = exp(score[c] - max) * (1 / sum)                 -- tb_softmax
+//   out[d]   = sum over c of p[c] * V[c][d]: four consecutive ranges of c,
+//              each an fma chain, added in range order
+// The scores stay in shared memory (ctx floats).
+template <int D>
+__global__ void __launch_bounds__(256) attention_decode_kernel(
+    const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc, int H, int KVH,
+    int max_seq, float scale, const int32_t *__restrict__ pos_dev, float *__restrict__ out,
+    uint32_t *__restrict__ err) {
+  extern __shared__ float sc[];
+  __shared__ float qs[D];
+  __shared__ float red[8];
+  __shared__ float part[256 / D][D];
+  const int h = blockIdx.x;
+  const int kvh = h / (H / KVH);
+  const int pos = *pos_dev;
+  if (pos < 0 || pos >= max_seq) {
+    if (h == 0 && threadIdx.x == 0) atomicOr(err, ERR_INDEX);
+    return;
+  }
+  const int ctx = pos + 1;
+  const int rs = KVH * D;  // cache row stride (floats)
+  if (threadIdx.x < D) qs[threadIdx.x] = q[h * D + threadIdx.x];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  float m = -INFINITY;
+  for (int c = threadIdx.x; c < ctx; c += 256) {
+    const float4 *kr = reinterpret_cast<const float4 *>(kc + (int64_t)c * rs + kvh * D);
+    float acc = 0.f;
+#pragma unroll
+    for (int d4 = 0; d4 < D / 4; ++d4) {
+      const float4 kv = __ldg(kr + d4);
+      acc = __fmaf_rn(qs[4 * d4 + 0], kv.x, acc);
+      acc = __fmaf_rn(qs[4 * d4 + 1], kv.y, acc);
+      acc = __fmaf_rn(qs[4 * d4 + 2], kv.z, acc);
+      acc = __fmaf_rn(qs[4 * d4 + 3], kv.w, acc);
+    }
+    const float s = __fmul_rn(acc, scale);
+    sc[c] = s;
+    m = s > m ? s : m;
+  }
+  m = warp_max_f(m);
+  if (lane == 0) red[warp] = m;
+  __syncthreads();
+  float M = red[0];
+  for (int w = 1; w < 8; ++w) M = fmaxf(M, red[w]);
+  __syncthreads();
+  float s = 0.f;
+  for (int c = threadIdx.x; c < ctx; c += 256) {
+    const float e = exp_fast(__fsub_rn(sc[c], M));
+    sc[c] = e;
+    s = __fadd_rn(s, e);
+  }
+  s = warp_sum_f(s);
+  if (lane == 0) red[warp] = s;
+  __syncthreads();
+  float S = 0.f;
+  for (int w = 0; w < 8; ++w) S = __fadd_rn(S, red[w]);
+  const float inv = __frcp_rn(S);
+
+  constexpr int NCH = 256 / D;
+  const int d = threadIdx.x % D, ch = threadIdx.x / D;
+  const int len = (ctx + NCH - 1) / NCH;
+  const int c0 = ch * len, c1 = min(ctx, c0 + len);
+  const float *vcol = vc + kvh * D + d;
+  float acc = 0.f;
+  for (int c = c0; c < c1; ++c) acc = __fmaf_rn(__fmul_rn(sc[c], inv), __ldg(vcol + (int64_t)c * rs), acc);
+  part[ch][d] = acc;
+  __syncthreads();
+  if (threadIdx.x < D) {
+    float o = part[0][threadIdx.x];
+    for (int k = 1; k < NCH; ++k) o = __fadd_rn(o, part[k][threadIdx.x]);
+    out[h * D + threadIdx.x] = o;
+  }
+}
+
+// margins[pos] = logits[idx] - (largest other logit; NaN never counts)
+__global__ void __launch_bounds__(1024) margin_kernel(const float *__restrict__ logits, int64_t V,
+                                                      const int64_t *__restrict__ idx,
+                                                      const int32_t *__restrict__ pos_dev, int max_seq,
+                                                      float *__restrict__ margins) {
+  __shared__ float red[32];
+  const int64_t id = *idx;
+  float t = -INFINITY;
+  for (int64_t i = threadIdx.x; i < V; i += blockDim.x)
+    if (i != id) t = fmaxf(t, logits[i]);
+  t = warp_max_f(t);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = t;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float top2 = red[0];
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) top2 = fmaxf(top2, red[w]);
+    const int pos = *pos_dev;
+    if (pos >= 0 && pos < max_seq) margins[pos] = logits[id] - top2;
+  }
+}
+
+__global__ void advance_kernel(const int64_t *__restrict__ idx, int32_t *__restrict__ ids,
+                               int32_t *__restrict__ pos_dev, int32_t *__restrict__ history, int max_seq) {
+  const int pos = *pos_dev;
+  const int tok = (int)*idx;
+  ids[0] = tok;
+  if (pos >= 0 && pos < max_seq) history[pos] = tok;
+  *pos_dev = pos + 1;
+}
+
+}  // namespace
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" {
+
+tb_status tb_kv_append(float *k_cache, float *v_cache, const float *k, const float *v, int64_t row_elems,
+                       int64_t max_seq, const int32_t *pos_dev, tb_stream stream) {
+  if (row_elems <= 0 || max_seq <= 0 || row_elems > 0x7FFFFFFF || max_seq > 0x7FFFFFFF)
+    return fail(TB_EINVAL, "tb_kv_append: bad extents");
+  if (!k_cache || !v_cache || !k || !v || !pos_dev) return fail(TB_EINVAL, "tb_kv_append: null pointer");
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  const int grid = (int)std::min<int64_t>((row_elems + 255) / 256, 64);
+  kv_append_kernel<<<grid, 256, 0, as_stream(stream)>>>(k_cache, v_cache, k, v, (int)row_elems, (int)max_seq,
+                                                         pos_dev, st->err_word);
+  return check_launch("tb_kv_append");
+}
+
+tb_status tb_attention_decode(const float *q, const float *k_cache, const float *v_cache, int64_t heads,
+                              int64_t kv_heads, int64_t head_dim, int64_t max_seq, float scale,
+                              const int32_t *pos_dev, float *out, tb_stream stream) {
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 || max_seq <= 0)
+    return fail(TB_EINVAL, "tb_attention_decode: heads must be a positive multiple of kv_heads");
+  if (head_dim != 64) return fail(TB_EINVAL, "tb_attention_decode: head_dim %lld (64 supported)", (long long)head_dim);
+  if (!q || !k_cache || !v_cache || !pos_dev || !out) return fail(TB_EINVAL, "tb_attention_decode: null pointer");
+  if ((reinterpret_cast<uintptr_t>(k_cache) & 15) != 0)
+    return fail(TB_EINVAL, "tb_attention_decode: the key cache must be 16-byte aligned");
+  const size_t smem = (size_t)max_seq * sizeof(float);
+  if (smem > 200 * 1024) return fail(TB_EINVAL, "tb_attention_decode: cache of %lld rows too long", (long long)max_seq);
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  TB_TRY(ensure_smem_for(attention_decode_kernel<64>, smem));
+  attention_decode_kernel<64><<<(unsigned)heads, 256, smem, as_stream(stream)>>>(
+      q, k_cache, v_cache, (int)heads, (int)kv_heads, (int)max_seq, scale, pos_dev, out, st->err_word);
+  return check_launch("tb_attention_decode");
+}
+
+tb_status tb_decode_margin(const float *logits, int64_t vocab, const int64_t *idx_dev, const int32_t *pos_dev,
+                           int64_t max_seq, float *margins_dev, tb_stream stream) {
+  if (vocab <= 0 || max_seq <= 0) return fail(TB_EINVAL, "tb_decode_margin: bad extents");
+  if (!logits || !idx_dev || !pos_dev || !margins_dev) return fail(TB_EINVAL, "tb_decode_margin: null pointer");
+  margin_kernel<<<1, 1024, 0, as_stream(stream)>>>(logits, vocab, idx_dev, pos_dev, (int)max_seq, margins_dev);
+  return check_launch("tb_decode_margin");
+}
+
+tb_status tb_decode_advance(const int64_t *idx_dev, int32_t *ids_dev, int32_t *pos_dev, int32_t *history_dev,
+                            int64_t max_seq, tb_stream stream) {
+  if (max_seq <= 0) return fail(TB_EINVAL, "tb_decode_advance: bad extents");
+  if (!idx_dev || !ids_dev || !pos_dev || !history_dev) return fail(TB_EINVAL, "tb_decode_advance: null pointer");
+  advance_kernel<<<1, 1, 0, as_stream(stream)>>>(idx_dev, ids_dev, pos_dev, history_dev, (int)max_seq);
+  return check_launch("tb_decode_advance");
+}
+
+// ---- streams and graphs ------------------------------------------------------------
+
+tb_status tb_stream_create(tb_stream *out) {
+  if (!out) return fail(TB_EINVAL, "tb_stream_create: null pointer");
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  cudaStream_t s = nullptr;
+  cudaError_t e = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_stream_create: %s", cudaGetErrorString(e));
+  *out = reinterpret_cast<tb_stream>(s);
+  return TB_OK;
+}
+
+tb_status tb_stream_destroy(tb_stream s) {
+  if (!s) return TB_OK;
+  cudaError_t e = cudaStreamDestroy(as_stream(s));
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_stream_destroy: %s", cudaGetErrorString(e));
+  return TB_OK;
+}
+
+tb_status tb_capture_begin(tb_stream s) {
+  if (!s) return fail(TB_EINVAL, "tb_capture_begin: capture needs a created stream, not the default stream");
+  cudaError_t e = cudaStreamBeginCapture(as_stream(s), cudaStreamCaptureModeRelaxed);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_capture_begin: %s", cudaGetErrorString(e));
+  return TB_OK;
+}
+
+tb_status tb_capture_end(tb_stream s, tb_graph *out) {
+  if (!s || !out) return fail(TB_EINVAL, "tb_capture_end: null argument");
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(as_stream(s), &g);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_capture_end: %s", cudaGetErrorString(e));
+  cudaGraphExec_t x = nullptr;
+  e = cudaGraphInstantiate(&x, g, 0);
+  cudaGraphDestroy(g);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_capture_end: instantiate: %s", cudaGetErrorString(e));
+  *out = reinterpret_cast<tb_graph>(x);
+  return TB_OK;
+}
+
+tb_status tb_graph_launch(tb_graph g, tb_stream s) {
+  if (!g) return fail(TB_EINVAL, "tb_graph_launch: null graph");
+  cudaError_t e = cudaGraphLaunch(reinterpret_cast<cudaGraphExec_t>(g), as_stream(s));
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_graph_launch: %s", cudaGetErrorString(e));
+  return TB_OK;
+}
+
+tb_status tb_graph_destroy(tb_graph g) {
+  if (!g) return TB_OK;
+  cudaError_t e = cudaGraphExecDestroy(reinterpret_cast<cudaGraphExec_t>(g));
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_graph_destroy: %s", cudaGetErrorString(e));
+  return TB_OK;
+}
+
+}  // extern "C"

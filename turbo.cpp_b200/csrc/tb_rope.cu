@@ -20,7 +20,15 @@ struct RopeView {
 __global__ void __launch_bounds__(256) rope_kernel(float *__restrict__ x, RopeView v,
                                                    const float *__restrict__ cos_t,
                                                    const float *__restrict__ sin_t,
-                                                   int64_t pos_offset) {
+                                                   int64_t pos_offset, const int32_t *__restrict__ pos_dev,
+                                                   int64_t max_seq, uint32_t *__restrict__ err) {
+  if (pos_dev) {  // position held in device memory (a captured decode step)
+    pos_offset = *pos_dev;
+    if (pos_offset < 0 || pos_offset + v.S > max_seq) {
+      if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(err, ERR_INDEX);
+      return;
+    }
+  }
   const int64_t total = v.B * v.H * v.S * v.half;
   for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total;
        t += (int64_t)gridDim.x * blockDim.x) {
@@ -69,9 +77,9 @@ extern "C" tb_status tb_fill_upper(float *x, int64_t rows, int64_t cols, int64_t
   return check_launch("tb_fill_upper");
 }
 
-extern "C" tb_status tb_rope(const tb_view *x, const float *cos_t, const float *sin_t,
-                             int64_t head_dim, int64_t max_seq, int64_t pos_offset,
-                             tb_stream stream) {
+namespace {
+tb_status rope_launch(const tb_view *x, const float *cos_t, const float *sin_t, int64_t head_dim,
+                      int64_t max_seq, int64_t pos_offset, const int32_t *pos_dev, tb_stream stream) {
   TB_TRY(validate_view(x, "tb_rope x"));
   if (x->dtype != TB_F32) return fail(TB_EINVAL, "tb_rope: fp32 only");
   if (head_dim <= 0 || head_dim % 2 != 0) return fail(TB_EINVAL, "RoPE requires an even head dimension.");
@@ -90,8 +98,9 @@ extern "C" tb_status tb_rope(const tb_view *x, const float *cos_t, const float *
     v.sb = 0; v.sh = 0; v.ss = x->strides[0]; v.sd = x->strides[1];
   }
   v.off = x->offset;
-  // rope.cpp:58-61 / 81-84: a position at or past the table raises out_of_range.
-  if (v.B > 0 && v.S > 0 && pos_offset + v.S > max_seq)
+  // rope.cpp:58-61 / 81-84: a position at or past the table raises out_of_range
+  // (checked on the device when the position lives there).
+  if (!pos_dev && v.B > 0 && v.S > 0 && pos_offset + v.S > max_seq)
     return fail(TB_ERANGE, "Sequence position exceeds RoPE cache size.");
   int64_t total = v.B * v.H * v.S * v.half;
   if (total == 0) return TB_OK;
@@ -99,6 +108,20 @@ extern "C" tb_status tb_rope(const tb_view *x, const float *cos_t, const float *
   DeviceState *st;
   TB_TRY(device_state(&st));
   int grid = (int)std::min<int64_t>((total + 255) / 256, (int64_t)st->sm_count * 8);
-  rope_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<float *>(x->data), v, cos_t, sin_t, pos_offset);
+  rope_kernel<<<grid, 256, 0, as_stream(stream)>>>(static_cast<float *>(x->data), v, cos_t, sin_t, pos_offset,
+                                                   pos_dev, max_seq, st->err_word);
   return check_launch("tb_rope");
+}
+}  // namespace
+
+extern "C" tb_status tb_rope(const tb_view *x, const float *cos_t, const float *sin_t,
+                             int64_t head_dim, int64_t max_seq, int64_t pos_offset,
+                             tb_stream stream) {
+  return rope_launch(x, cos_t, sin_t, head_dim, max_seq, pos_offset, nullptr, stream);
+}
+
+extern "C" tb_status tb_rope_at(const tb_view *x, const float *cos_t, const float *sin_t, int64_t head_dim,
+                                int64_t max_seq, const int32_t *pos_dev, tb_stream stream) {
+  if (!pos_dev) return fail(TB_EINVAL, "tb_rope_at: null position");
+  return rope_launch(x, cos_t, sin_t, head_dim, max_seq, 0, pos_dev, stream);
 }

@@ -1,0 +1,55 @@
+// decode_graph.hpp -- greedy decode of MiniGPT as one CUDA graph per token.
+// No reference counterpart: the reference loop (src/core/generate.cpp:30-63)
+// calls MiniGPT::forward once per token.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+
+#include "turbo_b200.h"
+
+namespace turbo {
+class MiniGPT;
+class KVCache;
+
+// One decode step -- embedding, the transformer blocks, final norm, LM head,
+// argmax -- recorded once as a CUDA graph.  The position, the input token and
+// the chosen tokens live in device memory, so the same graph is replayed for
+// every token with no host work in between.  The step runs the kernels
+// MiniGPT::forward runs for one token, except that each layer's attention is a
+// single fused kernel (tb_attention_decode) instead of the per-head loop of
+// attention.cpp:104-141; its softmax sum and probability-times-V order differ
+// within the fp32 tolerance.
+class DecodeGraph {
+ public:
+  // `kv` holds the prompt's keys/values (kv.get_current_seq_len() rows).
+  DecodeGraph(MiniGPT &model, KVCache &kv, bool want_margins);
+  ~DecodeGraph();
+  DecodeGraph(const DecodeGraph &) = delete;
+  DecodeGraph &operator=(const DecodeGraph &) = delete;
+
+  // Feeds `first` at the cache's current position and the chosen token after
+  // it, `steps` times: out_ids[s] is the token chosen at step s; margins[s]
+  // (optional) its top-1 minus top-2 logit.  Advances the cache by `steps`.
+  void generate(int first, size_t steps, int *out_ids, float *margins);
+
+ private:
+  void enqueue_step();
+  void *buf(size_t bytes);
+
+  MiniGPT &m_;
+  KVCache &kv_;
+  bool margins_on_;
+  tb_stream stream_ = nullptr;
+  tb_graph graph_ = nullptr;
+  size_t E_, H_, KVH_, D_, F_, V_;
+  int max_seq_;
+  float scale_;
+  // device buffers
+  void *arena_[32] = {};
+  int n_arena_ = 0;
+  int32_t *ids_, *pos_, *hist_;
+  int64_t *idx_;
+  float *margins_, *x_, *xn_, *h_, *q_, *k_, *v_, *ctx_, *ao_, *g_, *u_, *sw_, *fo_, *logits_;
+};
+
+}  // namespace turbo

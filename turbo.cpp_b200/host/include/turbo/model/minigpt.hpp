@@ -9,6 +9,7 @@
 #include "../tensor/tensor.hpp"
 
 namespace turbo {
+class DecodeGraph;
 class KVCache;
 class GGUFLoader;
 
@@ -16,6 +17,7 @@ class GGUFLoader;
 // output norm -> LM head on the last token (tied to token_embd if no output.weight).
 class MiniGPT {
  private:
+  friend class ::turbo::DecodeGraph;
   nn::Embedding tok_emb;
   std::vector<nn::TransformerBlock> blocks;
   nn::RMSNorm norm;

@@ -5,11 +5,13 @@
 #include "softmax.hpp"
 
 namespace turbo {
+class DecodeGraph;
 class KVCache;
 namespace nn {
 // nn::MultiHeadAttention with grouped KV heads (reference include/turbo/nn/attention.hpp).
 class MultiHeadAttention : public Layer {
  private:
+  friend class ::turbo::DecodeGraph;
   size_t embed_dim;
   size_t num_heads;
   size_t num_kv_heads;

@@ -4,10 +4,12 @@
 #include "swiglu.hpp"
 
 namespace turbo {
+class DecodeGraph;
 namespace nn {
 // nn::FeedForward (reference include/turbo/nn/ffn.hpp).
 class FeedForward : public Layer {
  private:
+  friend class ::turbo::DecodeGraph;
   Linear gate_proj;
   Linear up_proj;
   SwiGLU swiglu;

@@ -2,10 +2,12 @@
 #include "layer.hpp"
 
 namespace turbo {
+class DecodeGraph;
 namespace nn {
 // nn::RMSNorm (reference include/turbo/nn/rmsnorm.hpp).
 class RMSNorm : public Layer {
  private:
+  friend class ::turbo::DecodeGraph;
   Tensor weight;
   float epsilon = 1e-5f;
   size_t hidden_size = 0;

@@ -5,11 +5,13 @@
 #include "../tensor/tensor.hpp"
 
 namespace turbo {
+class DecodeGraph;
 namespace nn {
 // nn::RoPE (reference include/turbo/nn/rope.hpp).  The cos/sin tables are
 // computed on the host as the reference constructor does and uploaded once.
 class RoPE {
  private:
+  friend class ::turbo::DecodeGraph;
   size_t head_dim;
   size_t max_seq_len;
   float theta_base;

@@ -5,12 +5,14 @@
 #include "rmsnorm.hpp"
 
 namespace turbo {
+class DecodeGraph;
 class KVCache;
 class GGUFLoader;
 namespace nn {
 // nn::TransformerBlock (reference include/turbo/nn/transformer_block.hpp).
 class TransformerBlock : public Layer {
  private:
+  friend class ::turbo::DecodeGraph;
   RMSNorm attention_norm;
   MultiHeadAttention attention;
   RMSNorm ffn_norm;

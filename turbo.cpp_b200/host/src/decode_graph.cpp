@@ -1,0 +1,200 @@
+// decode_graph.cpp -- DecodeGraph: one greedy decode step of MiniGPT captured
+// as a CUDA graph (see turbo/core/decode_graph.hpp).
+#include "turbo/core/decode_graph.hpp"
+
+#include <cmath>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "host_util.hpp"
+#include "turbo/core/kv_cache.hpp"
+#include "turbo/model/minigpt.hpp"
+
+using turbo::detail::tb_check;
+using turbo::detail::tb_dtype_of;
+
+namespace turbo {
+
+void *DecodeGraph::buf(size_t bytes) {
+  void *p = nullptr;
+  tb_check(tb_alloc(&p, bytes));
+  arena_[n_arena_++] = p;
+  return p;
+}
+
+DecodeGraph::DecodeGraph(MiniGPT &model, KVCache &kv, bool want_margins)
+    : m_(model), kv_(kv), margins_on_(want_margins) {
+  if (m_.blocks.empty()) throw std::invalid_argument("DecodeGraph: the model has no blocks");
+  const Tensor &emb = m_.tok_emb.get_weight();
+  E_ = emb.get_shape()[0];
+  V_ = emb.get_shape()[1];
+  H_ = m_.num_heads_;
+  KVH_ = m_.num_kv_heads_;
+  D_ = m_.head_dim_;
+  F_ = m_.blocks[0].ffn.gate_proj.get_weight().get_shape()[1];
+  max_seq_ = kv.get_max_seq_len();
+  scale_ = 1.0f / std::sqrt(static_cast<float>(D_));
+  if (H_ * D_ != E_ || H_ % KVH_ != 0) throw std::invalid_argument("DecodeGraph: inconsistent head layout");
+  if (m_.lm_head.get_weight().get_shape()[1] != V_) throw std::invalid_argument("DecodeGraph: LM head width");
+  for (auto &b : m_.blocks)
+    for (nn::Linear *l : {&b.attention.q_proj, &b.attention.k_proj, &b.attention.v_proj, &b.attention.o_proj,
+                          &b.ffn.gate_proj, &b.ffn.up_proj, &b.ffn.down_proj})
+      if (!l->get_bias().is_empty()) throw std::invalid_argument("DecodeGraph: biased projections unsupported");
+  tb_check(tb_stream_create(&stream_));
+  ids_ = static_cast<int32_t *>(buf(16));
+  pos_ = static_cast<int32_t *>(buf(16));
+  idx_ = static_cast<int64_t *>(buf(16));
+  hist_ = static_cast<int32_t *>(buf(sizeof(int32_t) * (size_t)max_seq_));
+  margins_ = static_cast<float *>(buf(sizeof(float) * (size_t)max_seq_));
+  const size_t f = sizeof(float);
+  x_ = static_cast<float *>(buf(f * E_));
+  xn_ = static_cast<float *>(buf(f * E_));
+  h_ = static_cast<float *>(buf(f * E_));
+  q_ = static_cast<float *>(buf(f * E_));
+  k_ = static_cast<float *>(buf(f * KVH_ * D_));
+  v_ = static_cast<float *>(buf(f * KVH_ * D_));
+  ctx_ = static_cast<float *>(buf(f * E_));
+  ao_ = static_cast<float *>(buf(f * E_));
+  g_ = static_cast<float *>(buf(f * F_));
+  u_ = static_cast<float *>(buf(f * F_));
+  sw_ = static_cast<float *>(buf(f * F_));
+  fo_ = static_cast<float *>(buf(f * E_));
+  logits_ = static_cast<float *>(buf(f * V_));
+}
+
+DecodeGraph::~DecodeGraph() {
+  if (graph_) tb_graph_destroy(graph_);
+  if (stream_) {
+    tb_sync(stream_);
+    tb_stream_destroy(stream_);
+  }
+  for (int i = 0; i < n_arena_; ++i) tb_free(arena_[i]);
+}
+
+namespace {
+// y[1, N] = x[1, K] . W for the projection's quantized (or fp32) weight.
+void linear(nn::Linear &l, const float *x, float *y, tb_stream s) {
+  const Tensor &w = l.get_weight();
+  const int64_t K = (int64_t)w.get_shape()[0], N = (int64_t)w.get_shape()[1];
+  const int dt = tb_dtype_of(w.dtype());
+  if (dt != TB_Q8_0 && dt != TB_Q4_0) throw std::invalid_argument("DecodeGraph: projection weights must be Q8_0/Q4_0");
+  if (exact_matmul())
+    tb_check(tb_matmul_quant_exact(dt, x, 1, K, w.get_storage()->device_data(), N, y, s));
+  else
+    tb_check(tb_matmul_quant(dt, x, 1, K, w.get_storage()->device_data(), N, y, s));
+}
+
+tb_view vec_view(const float *p, int64_t n) {
+  tb_view v{};
+  v.data = const_cast<float *>(p);
+  v.dtype = TB_F32;
+  v.rank = 2;
+  v.shape[0] = 1;
+  v.shape[1] = n;
+  v.strides[0] = n;
+  v.strides[1] = 1;
+  return v;
+}
+
+// [1, heads, 1, D] over a contiguous [heads * D] vector: the B, H, S, D view
+// RoPE::apply_in_place receives from attention.cpp for one token.
+tb_view head_view(float *p, int64_t heads, int64_t D) {
+  tb_view v{};
+  v.data = p;
+  v.dtype = TB_F32;
+  v.rank = 4;
+  v.shape[0] = 1;
+  v.shape[1] = heads;
+  v.shape[2] = 1;
+  v.shape[3] = D;
+  v.strides[0] = heads * D;
+  v.strides[1] = D;
+  v.strides[2] = heads * D;
+  v.strides[3] = 1;
+  return v;
+}
+}  // namespace
+
+void DecodeGraph::enqueue_step() {
+  tb_stream s = stream_;
+  const int64_t E = (int64_t)E_, F = (int64_t)F_, V = (int64_t)V_;
+  const Tensor &emb = m_.tok_emb.get_weight();
+  tb_check(tb_embedding(tb_dtype_of(emb.dtype()), emb.get_storage()->device_data(), E, V, ids_, 1, x_, s));
+  for (size_t l = 0; l < m_.blocks.size(); ++l) {
+    nn::TransformerBlock &b = m_.blocks[l];
+    nn::MultiHeadAttention &a = b.attention;
+    tb_check(tb_rmsnorm(TB_F32, x_, static_cast<const float *>(b.attention_norm.get_weight().device_ptr()), xn_, 1,
+                        E, b.attention_norm.epsilon, s));
+    linear(a.q_proj, xn_, q_, s);
+    linear(a.k_proj, xn_, k_, s);
+    linear(a.v_proj, xn_, v_, s);
+    const float *cs = static_cast<const float *>(a.rope.dev_cos->device_ptr());
+    const float *sn = static_cast<const float *>(a.rope.dev_sin->device_ptr());
+    tb_view vq = head_view(q_, (int64_t)H_, (int64_t)D_), vk = head_view(k_, (int64_t)KVH_, (int64_t)D_);
+    tb_check(tb_rope_at(&vq, cs, sn, (int64_t)D_, (int64_t)a.rope.max_seq_len, pos_, s));
+    tb_check(tb_rope_at(&vk, cs, sn, (int64_t)D_, (int64_t)a.rope.max_seq_len, pos_, s));
+    float *kc = static_cast<float *>(kv_.get_k_cache((int)l).device_ptr());
+    float *vc = static_cast<float *>(kv_.get_v_cache((int)l).device_ptr());
+    tb_check(tb_kv_append(kc, vc, k_, v_, (int64_t)(KVH_ * D_), max_seq_, pos_, s));
+    tb_check(tb_attention_decode(q_, kc, vc, (int64_t)H_, (int64_t)KVH_, (int64_t)D_, max_seq_, scale_, pos_, ctx_, s));
+    linear(a.o_proj, ctx_, ao_, s);
+    tb_view vx = vec_view(x_, E), va = vec_view(ao_, E), vh = vec_view(h_, E);
+    tb_check(tb_binary(0, &vx, &va, &vh, s));
+    tb_check(tb_rmsnorm(TB_F32, h_, static_cast<const float *>(b.ffn_norm.get_weight().device_ptr()), xn_, 1, E,
+                        b.ffn_norm.epsilon, s));
+    linear(b.ffn.gate_proj, xn_, g_, s);
+    linear(b.ffn.up_proj, xn_, u_, s);
+    tb_check(tb_swiglu(TB_F32, g_, u_, sw_, F, s));
+    linear(b.ffn.down_proj, sw_, fo_, s);
+    tb_view vf = vec_view(fo_, E);
+    tb_check(tb_binary(0, &vh, &vf, &vx, s));
+  }
+  tb_check(tb_rmsnorm(TB_F32, x_, static_cast<const float *>(m_.norm.get_weight().device_ptr()), xn_, 1, E,
+                      m_.norm.epsilon, s));
+  linear(m_.lm_head, xn_, logits_, s);
+  tb_check(tb_argmax(logits_, 1, V, idx_, s));
+  if (margins_on_) tb_check(tb_decode_margin(logits_, V, idx_, pos_, max_seq_, margins_, s));
+  tb_check(tb_decode_advance(idx_, ids_, pos_, hist_, max_seq_, s));
+}
+
+void DecodeGraph::generate(int first, size_t steps, int *out_ids, float *margins) {
+  if (steps == 0) return;
+  const int pos0 = kv_.get_current_seq_len();
+  if (first < 0 || (size_t)first >= V_)
+    throw std::out_of_range("Token ID " + std::to_string(first) + " exceeds vocabulary size " + std::to_string(V_));
+  if ((size_t)pos0 + steps > (size_t)max_seq_) throw std::out_of_range("KV cache is full.");
+  uint32_t flags = 0;
+  tb_check(tb_take_device_errors(&flags));  // start from a clean error word
+  const int32_t init[2] = {first, pos0};
+  tb_check(tb_upload(ids_, &init[0], sizeof(int32_t), stream_));
+  tb_check(tb_upload(pos_, &init[1], sizeof(int32_t), stream_));
+  // the first step runs eagerly: it sets every kernel's attributes before capture
+  enqueue_step();
+  if (steps > 1) {
+    if (!graph_) {
+      tb_check(tb_capture_begin(stream_));
+      try {
+        enqueue_step();
+      } catch (...) {
+        tb_graph g = nullptr;
+        tb_capture_end(stream_, &g);
+        if (g) tb_graph_destroy(g);
+        throw;
+      }
+      tb_check(tb_capture_end(stream_, &graph_));
+    }
+    for (size_t i = 1; i < steps; ++i) tb_check(tb_graph_launch(graph_, stream_));
+  }
+  std::vector<int32_t> hist(steps);
+  tb_check(tb_download(hist.data(), hist_ + pos0, sizeof(int32_t) * steps, stream_));
+  if (margins) tb_check(tb_download(margins, margins_ + pos0, sizeof(float) * steps, stream_));
+  tb_check(tb_sync(stream_));
+  tb_check(tb_take_device_errors(&flags));
+  if (flags & 2u) throw std::out_of_range("Sequence position exceeds RoPE cache size.");
+  if (flags) throw std::runtime_error("DecodeGraph: device error flags " + std::to_string(flags));
+  for (size_t i = 0; i < steps; ++i) out_ids[i] = hist[i];
+  kv_.increment_seq_len((int)steps);
+}
+
+}  // namespace turbo

@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "host_util.hpp"
+#include "turbo/core/decode_graph.hpp"
 #include "turbo/core/kv_cache.hpp"
 #include "turbo/core/sampler.hpp"
 #include "turbo/loader/gguf_loader.hpp"
@@ -23,6 +24,7 @@ thread_local std::string g_err;
 struct Model {
   std::unique_ptr<turbo::GGUFLoader> loader;
   std::unique_ptr<turbo::MiniGPT> model;
+  bool exact = false;
 };
 
 template <class F> int guarded(F &&f) {
@@ -45,7 +47,9 @@ template <class F> int guarded(F &&f) {
 TBM_API const char *tbm_last_error() { return g_err.c_str(); }
 
 // Loads a GGUF model onto the current device.  exact != 0 selects the
-// bit-identical quantized matmul kernels for this process.
+// bit-identical quantized matmul kernels for this process and the reference's
+// op-by-op decode; otherwise decode steps replay one CUDA graph per token
+// (turbo::DecodeGraph).
 TBM_API void *tbm_model_load(const char *path, int exact) {
   Model *m = nullptr;
   int st = guarded([&] {
@@ -54,6 +58,7 @@ TBM_API void *tbm_model_load(const char *path, int exact) {
     mm->loader = std::make_unique<turbo::GGUFLoader>(path);
     mm->loader->parse();
     mm->model = std::make_unique<turbo::MiniGPT>(*mm->loader);
+    mm->exact = exact != 0;
     turbo::device_synchronize();
     m = mm.release();
   });
@@ -97,10 +102,16 @@ TBM_API int tbm_model_generate(void *h, const int *prompt, size_t n_prompt, size
     kv.increment_seq_len((int)n_prompt);
     int next = pick(logits, 0);
     auto t1 = std::chrono::steady_clock::now();
-    for (size_t s = 0; s < steps; ++s) {
-      logits = model.forward(std::vector<int>{next}, &kv);
-      kv.increment_seq_len(1);
-      next = pick(logits, s + 1);
+    if (!m->exact && steps > 0 && !last_logits) {
+      turbo::device_synchronize();  // the prefill's cache writes, before the decode stream starts
+      turbo::DecodeGraph dg(model, kv, margins != nullptr);
+      dg.generate(next, steps, out_ids + 1, margins ? margins + 1 : nullptr);
+    } else {
+      for (size_t s = 0; s < steps; ++s) {
+        logits = model.forward(std::vector<int>{next}, &kv);
+        kv.increment_seq_len(1);
+        next = pick(logits, s + 1);
+      }
     }
     turbo::device_synchronize();
     auto t2 = std::chrono::steady_clock::now();

@@ -77,6 +77,17 @@ SIGNATURES = {
     "tb_argmax_shard_keys": [_P, _I64, _I64, _I64, _I64, _P, _P],
     "tb_argmax_key_index": [_P, _I64, _P, _P],
     "tb_selfcheck_exp": [_P],
+    "tb_rope_at": [_VP, _P, _P, _I64, _I64, _P, _P],
+    "tb_kv_append": [_P, _P, _P, _P, _I64, _I64, _P, _P],
+    "tb_attention_decode": [_P, _P, _P, _I64, _I64, _I64, _I64, _F, _P, _P, _P],
+    "tb_decode_margin": [_P, _I64, _P, _P, _I64, _P, _P],
+    "tb_decode_advance": [_P, _P, _P, _P, _I64, _P],
+    "tb_stream_create": [ctypes.POINTER(_P)],
+    "tb_stream_destroy": [_P],
+    "tb_capture_begin": [_P],
+    "tb_capture_end": [_P, ctypes.POINTER(_P)],
+    "tb_graph_launch": [_P, _P],
+    "tb_graph_destroy": [_P],
 }
 
 _lib = None

@@ -701,6 +701,198 @@ tb_status launch_span(const float *x, int64_t K, const void *w, int64_t N, float
 }
 
 // ---------------------------------------------------------------------------
+// Ring GEMV (M == 1, default tolerance), the decode path.
+//
+// One CTA per SM owns a contiguous range of rows, cut into spans of NW rows
+// (one row per warp).  Spans stream through a ring of `slots` shared-memory
+// buffers, one bulk copy and one mbarrier per span; the last warp to finish a
+// span refills its slot with the span `slots` ahead.  The ring keeps the
+// CTA's shared memory small (NW * slots rows), so that under programmatic
+// dependent launch the next GEMV's CTA fits on the SM beside this one and
+// starts streaming its weights while this one drains: back-to-back GEMVs of a
+// decode step become one continuous weight stream.
+template <int NW>
+__global__ void __launch_bounds__(NW * 32) gemv_q8_0_ring_kernel(const uint8_t *__restrict__ W,
+                                                                 const float *__restrict__ X,
+                                                                 float *__restrict__ Y, int N, int K, int slots,
+                                                                 uint32_t *__restrict__ err) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  __shared__ int done[8];
+  __shared__ int abort_flag;
+  const int nb = K / 32;
+  const int rb = nb * 34;
+  const int XS = (nb & 1) ? nb + 2 : nb + 1;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem);  // [slots], slots <= 8
+  float *xs = reinterpret_cast<float *>(smem + 128);
+  uint8_t *ring = reinterpret_cast<uint8_t *>(xs + 32 * XS);
+  ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(ring) + 127) & ~uintptr_t(127));
+  const size_t slot_bytes = (size_t)NW * rb;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+
+  const int G = gridDim.x, base = N / G, rem = N % G;
+  const int n0 = blockIdx.x * base + min((int)blockIdx.x, rem);
+  const int cnt = base + ((int)blockIdx.x < rem ? 1 : 0);
+  const int nspans = (cnt + NW - 1) / NW;
+
+  auto issue = [&](int k) {  // span k -> slot k % slots (one thread)
+    const int slot = k % slots;
+    const int nr = min(NW, cnt - k * NW);
+    const uint32_t bytes = (uint32_t)(nr * rb);
+    mbar_arrive_expect_tx(full + slot, bytes);
+    bulk_g2s(ring + slot * slot_bytes, W + ((int64_t)n0 + (int64_t)k * NW) * rb, bytes, full + slot);
+  };
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < slots; ++i) {
+      mbar_init(full + i, 1);
+      done[i] = 0;
+    }
+    abort_flag = 0;
+    fence_mbar_init();
+    for (int k = 0; k < slots && k < nspans; ++k) issue(k);
+  }
+  pdl_launch_dependents();
+  pdl_wait();  // x (and the order of our y writes) depend on the previous kernel
+
+  // x -> shared memory, transposed [j][block] with an odd pitch
+  {
+    const float4 *x4 = reinterpret_cast<const float4 *>(X);
+    const int nv = K >> 2;
+    for (int b4 = threadIdx.x; b4 < nv; b4 += NW * 32) {
+      const float4 v = __ldg(x4 + b4);
+      const int i = b4 * 4;
+      xs[((i + 0) & 31) * XS + ((i + 0) >> 5)] = v.x;
+      xs[((i + 1) & 31) * XS + ((i + 1) >> 5)] = v.y;
+      xs[((i + 2) & 31) * XS + ((i + 2) >> 5)] = v.z;
+      xs[((i + 3) & 31) * XS + ((i + 3) >> 5)] = v.w;
+    }
+  }
+  __syncthreads();
+  const bool onepass = nb <= 64;
+  uint64_t xp[32];
+  if (onepass) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      xp[j] = pack2(lane < nb ? xs[j * XS + lane] : 0.f, lane + 32 < nb ? xs[j * XS + lane + 32] : 0.f);
+  }
+  const uint64_t off2 = pack2(-(kMagic + 128.0f), -(kMagic + 128.0f));
+
+  for (int k = 0; k < nspans; ++k) {
+    const int slot = k % slots;
+    const int nr = min(NW, cnt - k * NW);
+    if (warp < nr) {
+      bool ok = !*(volatile int *)&abort_flag && mbar_wait_bounded(full + slot, (uint32_t)((k / slots) & 1), err);
+      if (!__all_sync(0xffffffffu, ok)) {
+        if (lane == 0) abort_flag = 1;
+        return;
+      }
+      const uint8_t *wrow = ring + slot * slot_bytes + (size_t)warp * rb;
+      float racc = 0.f;
+      for (int p = 0; p * 64 < nb; ++p) {
+        const int b1 = p * 64 + lane, b2 = b1 + 32;
+        const bool v1 = b1 < nb, v2 = b2 < nb;
+        if (!onepass) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            xp[j] = pack2(v1 ? xs[j * XS + b1] : 0.f, v2 ? xs[j * XS + b2] : 0.f);
+        }
+        float d1, d2;
+        uint32_t q1[8], q2[8];
+        load_q8_block(wrow, 34 * (v1 ? b1 : 0), d1, q1);
+        load_q8_block(wrow, 34 * (v2 ? b2 : 0), d2, q2);
+        // two independent packed chains (elements 0-15 and 16-31 of each block)
+        uint64_t acc0 = pack2(0.f, 0.f), acc1 = pack2(0.f, 0.f);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          const uint32_t u1 = q1[kk] ^ 0x80808080u, u2 = q2[kk] ^ 0x80808080u;
+          const uint32_t w1 = q1[kk + 4] ^ 0x80808080u, w2 = q2[kk + 4] ^ 0x80808080u;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const uint32_t sel = 0x7650u | (uint32_t)e;
+            const uint64_t m = pack2(__uint_as_float(__byte_perm(u1, kMagicHi, sel)),
+                                     __uint_as_float(__byte_perm(u2, kMagicHi, sel)));
+            const uint64_t n = pack2(__uint_as_float(__byte_perm(w1, kMagicHi, sel)),
+                                     __uint_as_float(__byte_perm(w2, kMagicHi, sel)));
+            acc0 = fma2(add2(m, off2), xp[4 * kk + e], acc0);
+            acc1 = fma2(add2(n, off2), xp[4 * kk + 16 + e], acc1);
+          }
+        }
+        float s1, s2;
+        unpack2(add2(acc0, acc1), s1, s2);
+        if (v1) racc = fmaf(s1, d1, racc);
+        if (v2) racc = fmaf(s2, d2, racc);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) racc += __shfl_xor_sync(0xffffffffu, racc, o);
+      if (lane == 0) Y[n0 + k * NW + warp] = racc;
+      // The last of the span's nr warps refills the slot with span k + slots.
+      // Only warps that waited for this span count: a warp without a row (only
+      // in the last, partial span) must not touch a counter, or it could run
+      // ahead and count toward a span that is still being read.
+      if (lane == 0) {
+        __threadfence_block();
+        if (atomicAdd(&done[slot], 1) == nr - 1) {
+          done[slot] = 0;
+          if (k + slots < nspans) {
+            fence_proxy_async_smem();
+            issue(k + slots);
+          }
+        }
+      }
+      __syncwarp();
+    }
+  }
+}
+
+size_t ring_smem_bytes(int K, int NW, int slots) {
+  const int nb = K / 32;
+  const int XS = (nb & 1) ? nb + 2 : nb + 1;
+  size_t s = 128 + (size_t)32 * XS * 4;
+  s = (s + 127) & ~size_t(127);
+  // + slack: the last block's 9-word read may run 2 bytes past the ring
+  return s + (size_t)slots * NW * nb * 34 + 128;
+}
+
+template <int NW>
+tb_status launch_ring(const float *x, int64_t K, const void *w, int64_t N, float *y, int slots, cudaStream_t s,
+                      const DeviceState *st, int ctas_per_sm = 1) {
+  const int grid = (int)std::min<int64_t>(N, (int64_t)st->sm_count * ctas_per_sm);
+  const size_t smem = ring_smem_bytes((int)K, NW, slots);
+  if (smem > (size_t)st->smem_optin) return fail(TB_EINVAL, "tb_matmul_quant: K=%lld too large", (long long)K);
+  auto kern = gemv_q8_0_ring_kernel<NW>;
+  TB_TRY(ensure_smem_for(kern, smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3(NW * 32, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, (const uint8_t *)w, x, y, (int)N, (int)K, slots, st->err_word);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_matmul_quant(Q8_0 ring): %s", cudaGetErrorString(e));
+  return TB_OK;
+}
+
+// Ring shape: 8 rows (warps) per span, two slots, two CTAs per SM when two fit
+// in shared memory (K <= 4096); measured on the 8192 x 2048 decode GEMV and a
+// 16-layer mix of the 1B decoder's projections against deeper rings, 4 and 16
+// warps and one or three CTAs per SM.
+constexpr int kRingSlots = 2;
+int ring_ctas_per_sm(int64_t K, const DeviceState *st) {
+  return 2 * ring_smem_bytes((int)K, 8, kRingSlots) <= (size_t)st->smem_optin ? 2 : 1;
+}
+
+tb_status launch_ring_cfg(const float *x, int64_t K, const void *w, int64_t N, float *y, int nw, int slots,
+                          cudaStream_t s, const DeviceState *st, int ctas_per_sm) {
+  if (nw == 4) return launch_ring<4>(x, K, w, N, y, slots, s, st, ctas_per_sm);
+  if (nw == 16) return launch_ring<16>(x, K, w, N, y, slots, s, st, ctas_per_sm);
+  if (nw == 32) return launch_ring<32>(x, K, w, N, y, slots, s, st, ctas_per_sm);
+  return launch_ring<8>(x, K, w, N, y, slots, s, st, ctas_per_sm);
+}
+
+// ---------------------------------------------------------------------------
 // Q4_0 weights times Q8_0-quantized activations, in the order of
 // vec_dot_q4_0_q8_0_avx2 (quant_math.hpp:184-248): eight fp32 lanes, lane l
 // accumulating, block after block, fma(p0, d, acc) then fma(p1, d, acc) where
@@ -797,7 +989,8 @@ tb_status launch_q8_0(const float *x, int64_t M, int64_t K, const void *w, int64
   const int64_t rbytes = K / 32 * 34;
   if (M == 1 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 && rbytes % 16 == 0 &&
       (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
-    return exact ? launch_span<1>(x, K, w, N, y, s, st) : launch_span<0>(x, K, w, N, y, s, st);
+    if (exact) return launch_span<1>(x, K, w, N, y, s, st);
+    return launch_ring<8>(x, K, w, N, y, kRingSlots, s, st, ring_ctas_per_sm(K, st));
   }
   if (false) {
     constexpr int NC = 8;

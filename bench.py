@@ -393,6 +393,47 @@ def run_ops_suite(args):
     return 0
 
 
+DECODE_MODEL = "/tmp/turbo_b200_llama1b_q8_0_seed0.gguf"
+
+
+def run_decode_suite(args):
+    """The 1B-shaped Q8_0 greedy decode (prefill 512 ids, then 128 steps) through
+    the C++ host layer, both paths; token ids checked against the reference's
+    run (tests/golden/decode_1b.npz, made by tests/golden/make_decode_golden.py
+    on the reference library)."""
+    import numpy as np
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    from turbo_b200 import gguf_synth
+    from turbo_b200.model import Model
+    golden = np.load(os.path.join(ROOT, "tests", "golden", "decode_1b.npz"))
+    if not os.path.exists(DECODE_MODEL):
+        gguf_synth.write_model(DECODE_MODEL + ".part")
+        os.replace(DECODE_MODEL + ".part", DECODE_MODEL)
+    steps = int(golden["steps"])
+    for exact in ([False] if args.only != "both" else [False, True]):
+        m = Model(DECODE_MODEL, exact=exact)
+        m.generate(golden["prompt"], 4, max_seq=int(golden["max_seq"]), want_margins=False)  # warm-up
+        runs = [m.generate(golden["prompt"], steps, max_seq=int(golden["max_seq"]), want_margins=False)
+                for _ in range(max(1, args.reps))]
+        m.close()
+        best = min(runs, key=lambda r: r["decode_ms"])
+        same = all(bool(np.array_equal(r["ids"], golden["ids"])) for r in runs)
+        line = {"suite": "decode", "metric": "Q8_0 1B-shape greedy decode tokens/sec",
+                "value": round(steps / (best["decode_ms"] / 1e3), 1), "unit": "tok/s",
+                "path": "exact op-by-op" if exact else "CUDA graph per token, fused layer",
+                "prefill_ms": round(best["prefill_ms"], 1), "decode_ms": round(best["decode_ms"], 1),
+                "steps": steps, "prompt": int(golden["prompt"].size), "runs": len(runs),
+                "ids_identical_to_reference": same,
+                "reference_cpu": {"decode_tok_s": round(steps / (float(golden["decode_ms"]) / 1e3), 2),
+                                  "prefill_ms": round(float(golden["prefill_ms"]), 1),
+                                  "threads": int(golden["threads"]),
+                                  "note": "the reference library on this repository's build host (golden file)"}}
+        print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -402,12 +443,16 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exact", action="store_true",
                     help="time tb_matmul_quant_exact (bit-identical to the reference) instead")
-    ap.add_argument("--suite", default="headline", choices=["headline", "ops"],
-                    help="ops: per-op throughput of every hot-path kernel (one JSON line per op)")
+    ap.add_argument("--suite", default="headline", choices=["headline", "ops", "decode"],
+                    help="ops: per-op throughput of every hot-path kernel (one JSON line per op); "
+                         "decode: the 1B-shaped greedy decode in tokens/sec")
+    ap.add_argument("--reps", type=int, default=3, help="with --suite decode: timed generate calls")
     ap.add_argument("--only", default="", help="with --suite ops: comma-separated op name filters")
     args = ap.parse_args()
     if args.suite == "ops":
         return run_ops_suite(args)
+    if args.suite == "decode":
+        return run_decode_suite(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -277,6 +277,38 @@ tb_status tb_decode_margin(const float *logits_dev, int64_t vocab, const int64_t
 tb_status tb_decode_advance(const int64_t *idx_dev, int32_t *ids_dev, int32_t *pos_dev, int32_t *history_dev,
                             int64_t max_seq, tb_stream stream);
 
+/* Fused decode-step GEMVs (Q8_0 weights, one input row x[K], K a multiple of
+ * 256; x, gamma and weights 16-byte aligned).  When gamma is non-NULL the input
+ * is first RMS-normalised as tb_rmsnorm does (x / sqrt(mean(x^2) + eps) *
+ * gamma; the sum of squares is taken in a different order, so results agree
+ * with the unfused pair within 1e-5).  The dot products are those of
+ * tb_matmul_quant for M = 1. */
+typedef struct {
+  const void *w;          /* n rows of K/32 Q8_0 blocks (GGUF logical {K, n}) */
+  int64_t n;              /* rows */
+  float *y;               /* out [n] */
+  const float *residual;  /* optional [n]: y = residual + W.x, added as tb_binary(add) */
+} tb_gemv_segment;
+/* Up to three matrices over the same input in one launch (e.g. the Q, K and V
+ * projections of attention.cpp:44-46, or the O projection plus the residual
+ * of transformer_block.cpp). */
+tb_status tb_gemv_q8_0_multi(const float *x_dev, int64_t K, const float *gamma_dev, float eps,
+                             const tb_gemv_segment *segs, int nseg, tb_stream stream);
+/* y[i] = silu(G x)[i] * (U x)[i] for gate and up weights of n rows each: the
+ * FeedForward's gate_proj, up_proj and SwiGLU (src/nn/ffn.cpp,
+ * src/nn/swiglu.cpp:25-31) in one launch, with tb_swiglu's rounding. */
+tb_status tb_gemv_q8_0_swiglu(const float *x_dev, int64_t K, const float *gamma_dev, float eps,
+                              const void *w_gate_dev, const void *w_up_dev, int64_t n, float *y_dev,
+                              tb_stream stream);
+/* RoPE of q [heads, head_dim] and k [kv_heads, head_dim] at position *pos_dev
+ * (tb_rope_at's arithmetic) and the cache append of k and v at row *pos_dev
+ * (tb_kv_append), in one launch.  A position outside the table or the cache
+ * sets bit 1 of the device error word and writes nothing. */
+tb_status tb_rope_kv_append(float *q_dev, float *k_dev, const float *v_dev, int64_t heads, int64_t kv_heads,
+                            int64_t head_dim, const float *cos_dev, const float *sin_dev, int64_t rope_max_seq,
+                            float *k_cache_dev, float *v_cache_dev, int64_t max_seq, const int32_t *pos_dev,
+                            tb_stream stream);
+
 /* Streams and CUDA graphs for callers without the CUDA runtime: capture a
  * sequence of calls on a created stream once, replay it many times. */
 typedef struct tb_graph_s *tb_graph;

@@ -712,3 +712,100 @@ def test_graph_capture_and_replay():
     assert_bits(host(y), xs * np.float32(2.0) + xs)
     T.call("tb_graph_destroy", g)
     T.call("tb_stream_destroy", st)
+
+
+# --------------------------------------------------- fused decode-step GEMVs ----
+
+def _q8_dev(N, K, seed):
+    wq = synth.quantize_q8_0(synth.normal((N, K), 0.02, seed=seed))
+    return wq, dev(wq)
+
+
+@pytest.mark.parametrize("sizes,K", [((2048, 512, 512), 2048), ((37, 100, 5), 256), ((300,), 8192)])
+def test_gemv_multi_equals_separate_gemvs_bit_exact(sizes, K):
+    x = dev(synth.normal((K,), 1.0, seed=K))
+    segs, outs, refs, ress = [], [], [], []
+    for i, n in enumerate(sizes):
+        wq, dw = _q8_dev(n, K, seed=n + i)
+        y = torch.empty(n, device="cuda")
+        r = dev(synth.normal((n,), 1.0, seed=i)) if i == 0 else None
+        ref = torch.empty(n, device="cuda")
+        T.call("tb_matmul_quant", T.Q8_0, T.ptr(x), 1, K, T.ptr(dw), n, T.ptr(ref), S())
+        if r is not None:  # ref = r + W x as tb_binary(add)
+            out = torch.empty(n, device="cuda")
+            T.call("tb_binary", 0, T.byref(T.view(r)), T.byref(T.view(ref)), T.byref(T.view(out)), S())
+            ref = out
+        segs.append(T.GemvSegment(dw.data_ptr(), n, y.data_ptr(), r.data_ptr() if r is not None else None))
+        outs.append(y)
+        refs.append(ref)
+        ress.append(r)
+    arr = (T.GemvSegment * len(segs))(*segs)
+    T.call("tb_gemv_q8_0_multi", T.ptr(x), K, None, 0.0, ctypes.cast(arr, ctypes.c_void_p), len(segs), S())
+    for y, ref in zip(outs, refs):
+        assert_bits(host(y), host(ref))
+
+
+def test_gemv_multi_with_rmsnorm_within_tolerance():
+    K, N = 2048, 3072
+    xh = synth.normal((K,), 1.0, seed=50)
+    g = synth.uniform((K,), 0.5, 1.5, seed=51)
+    wq, dw = _q8_dev(N, K, seed=52)
+    x, dg = dev(xh), dev(g)
+    y = torch.empty(N, device="cuda")
+    seg = (T.GemvSegment * 1)(T.GemvSegment(dw.data_ptr(), N, y.data_ptr(), None))
+    T.call("tb_gemv_q8_0_multi", T.ptr(x), K, T.ptr(dg), 1e-5, ctypes.cast(seg, ctypes.c_void_p), 1, S())
+    xn = O.rmsnorm(xh.reshape(1, K), g)
+    assert_dot_tol(host(y).reshape(1, N), xn, wq, K)
+
+
+def test_gemv_swiglu_equals_separate_ops_bit_exact_and_with_norm():
+    K, N = 2048, 8192
+    xh = synth.normal((K,), 1.0, seed=53)
+    x = dev(xh)
+    wg, dg = _q8_dev(N, K, seed=54)
+    wu, du = _q8_dev(N, K, seed=55)
+    y = torch.empty(N, device="cuda")
+    T.call("tb_gemv_q8_0_swiglu", T.ptr(x), K, None, 0.0, T.ptr(dg), T.ptr(du), N, T.ptr(y), S())
+    gg, uu, ref = (torch.empty(N, device="cuda") for _ in range(3))
+    T.call("tb_matmul_quant", T.Q8_0, T.ptr(x), 1, K, T.ptr(dg), N, T.ptr(gg), S())
+    T.call("tb_matmul_quant", T.Q8_0, T.ptr(x), 1, K, T.ptr(du), N, T.ptr(uu), S())
+    T.call("tb_swiglu", T.F32, T.ptr(gg), T.ptr(uu), T.ptr(ref), N, S())
+    assert_bits(host(y), host(ref))
+    # with the RMSNorm prologue: against the oracle chain within tolerance
+    gam = synth.uniform((K,), 0.5, 1.5, seed=56)
+    T.call("tb_gemv_q8_0_swiglu", T.ptr(x), K, T.ptr(dev(gam)), 1e-5, T.ptr(dg), T.ptr(du), N, T.ptr(y), S())
+    xn = O.rmsnorm(xh.reshape(1, K), gam)
+    g_ref, u_ref = O.matmul_q8_0(xn, wg, N)[0], O.matmul_q8_0(xn, wu, N)[0]
+    want = O.swiglu(g_ref, u_ref)
+    # g and u are each within 1e-5 of their sum |w x|; propagate through
+    # y = silu(g) * u (|d silu / dg| <= 1.1)
+    xa = np.abs(xn[0].astype(np.float64))
+    sg = np.abs(synth.dequantize_q8_0(wg, K)).astype(np.float64) @ xa
+    su = np.abs(synth.dequantize_q8_0(wu, K)).astype(np.float64) @ xa
+    silu = np.abs(g_ref.astype(np.float64)) / (1 + np.exp(-g_ref.astype(np.float64)))
+    bound = F32_REL * (1.1 * np.abs(u_ref) * sg + silu * su) + 1e-30
+    assert (np.abs(host(y).astype(np.float64) - want) / bound).max() <= 1.0
+
+
+def test_rope_kv_append_equals_separate_ops():
+    H, KVH, D, max_seq = 32, 8, 64, 1024
+    c, s_ = O.rope_tables(D, max_seq, 500000.0)
+    dc, ds = dev(c), dev(s_)
+    qh = synth.normal((H * D,), 1.0, seed=57)
+    kh = synth.normal((KVH * D,), 1.0, seed=58)
+    vh = synth.normal((KVH * D,), 1.0, seed=59)
+    pos = _pos(300)
+    q1, k1, v1 = dev(qh), dev(kh), dev(vh)
+    kc1, vc1 = torch.zeros(max_seq * KVH * D, device="cuda"), torch.zeros(max_seq * KVH * D, device="cuda")
+    T.call("tb_rope_kv_append", T.ptr(q1), T.ptr(k1), T.ptr(v1), H, KVH, D, T.ptr(dc), T.ptr(ds), max_seq,
+           T.ptr(kc1), T.ptr(vc1), max_seq, T.ptr(pos), S())
+    q2, k2, v2 = dev(qh), dev(kh), dev(vh)
+    kc2, vc2 = torch.zeros_like(kc1), torch.zeros_like(vc1)
+    vq = T.view(q2, 0, (1, H, 1, D), (H * D, D, H * D, 1))
+    vk = T.view(k2, 0, (1, KVH, 1, D), (KVH * D, D, KVH * D, 1))
+    T.call("tb_rope_at", T.byref(vq), T.ptr(dc), T.ptr(ds), D, max_seq, T.ptr(pos), S())
+    T.call("tb_rope_at", T.byref(vk), T.ptr(dc), T.ptr(ds), D, max_seq, T.ptr(pos), S())
+    T.call("tb_kv_append", T.ptr(kc2), T.ptr(vc2), T.ptr(k2), T.ptr(v2), KVH * D, max_seq, T.ptr(pos), S())
+    for a, b in ((q1, q2), (k1, k2), (kc1, kc2), (vc1, vc2)):
+        assert_bits(host(a), host(b))
+    assert T.take_device_errors() == 0

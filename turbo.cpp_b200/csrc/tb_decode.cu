@@ -10,9 +10,13 @@
 // plus stream and graph handles for callers without the CUDA runtime.
 // Every kernel checks pos against the cache length: a position outside it
 // sets bit 1 of the device error word and writes nothing.
+#include <cooperative_groups.h>
+
 #include <algorithm>
 
 #include "tb_internal.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace tb {
 namespace {
@@ -43,37 +47,46 @@ __global__ void kv_append_kernel(float *__restrict__ kc, float *__restrict__ vc,
   }
 }
 
-// One CTA per query head h (key/value head h / (H / KVH)), ctx = pos + 1 keys:
+// One thread-block cluster of NC CTAs per query head h (key/value head
+// h / (H / KVH)); ctx = pos + 1 keys, CTA r of the cluster owns keys
+// [r * chunk, (r + 1) * chunk):
 //   score[c] = (fma chain over d of q[d] * K[c][d]) * scale   -- the fp32
 //              matmul's order (tb_matmul_f32), then Tensor::operator*(float)
-//   p[c]     = exp(score[c] - max) * (1 / sum)                 -- tb_softmax
-//   out[d]   = sum over c of p[c] * V[c][d]: four consecutive ranges of c,
-//              each an fma chain, added in range order
-// The scores stay in shared memory (ctx floats).
-template <int D>
+//   p[c]     = exp(score[c] - max) * (1 / sum)                 -- tb_softmax;
+//              max and sum exchanged through distributed shared memory
+//   out[d]   = sum over c of p[c] * V[c][d]: per CTA four consecutive ranges
+//              of its keys, each an fma chain, then the CTAs' partials added
+//              in cluster-rank order by rank 0
+template <int D, int NC>
 __global__ void __launch_bounds__(256) attention_decode_kernel(
     const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc, int H, int KVH,
     int max_seq, float scale, const int32_t *__restrict__ pos_dev, float *__restrict__ out,
     uint32_t *__restrict__ err) {
-  extern __shared__ float sc[];
+  extern __shared__ float sc[];  // this CTA's scores, ceil(max_seq / NC) floats
   __shared__ float qs[D];
   __shared__ float red[8];
-  __shared__ float part[256 / D][D];
-  const int h = blockIdx.x;
+  __shared__ float part[2];           // this CTA's [max, sum]
+  __shared__ float pv[256 / D][D];    // partial outputs of the four key ranges
+  __shared__ float octa[D];           // this CTA's partial output
+  cg::cluster_group cluster = cg::this_cluster();
+  const int cr = (int)cluster.block_rank();
+  const int h = blockIdx.x / NC;
   const int kvh = h / (H / KVH);
   const int pos = *pos_dev;
-  if (pos < 0 || pos >= max_seq) {
-    if (h == 0 && threadIdx.x == 0) atomicOr(err, ERR_INDEX);
+  if (pos < 0 || pos >= max_seq) {  // every CTA of the cluster leaves here together
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(err, ERR_INDEX);
     return;
   }
   const int ctx = pos + 1;
+  const int chunk = (ctx + NC - 1) / NC;
+  const int c0 = min(ctx, cr * chunk), c1 = min(ctx, c0 + chunk);
   const int rs = KVH * D;  // cache row stride (floats)
   if (threadIdx.x < D) qs[threadIdx.x] = q[h * D + threadIdx.x];
   __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   float m = -INFINITY;
-  for (int c = threadIdx.x; c < ctx; c += 256) {
+  for (int c = c0 + threadIdx.x; c < c1; c += 256) {
     const float4 *kr = reinterpret_cast<const float4 *>(kc + (int64_t)c * rs + kvh * D);
     float acc = 0.f;
 #pragma unroll
@@ -85,42 +98,61 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(
       acc = __fmaf_rn(qs[4 * d4 + 3], kv.w, acc);
     }
     const float s = __fmul_rn(acc, scale);
-    sc[c] = s;
+    sc[c - c0] = s;
     m = s > m ? s : m;
   }
   m = warp_max_f(m);
   if (lane == 0) red[warp] = m;
   __syncthreads();
-  float M = red[0];
-  for (int w = 1; w < 8; ++w) M = fmaxf(M, red[w]);
-  __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = red[0];
+    for (int w = 1; w < 8; ++w) t = fmaxf(t, red[w]);
+    part[0] = t;
+  }
+  cluster.sync();
+  float M = -INFINITY;
+  for (int r = 0; r < NC; ++r) M = fmaxf(M, *cluster.map_shared_rank(&part[0], r));
   float s = 0.f;
-  for (int c = threadIdx.x; c < ctx; c += 256) {
-    const float e = exp_fast(__fsub_rn(sc[c], M));
-    sc[c] = e;
+  for (int c = c0 + threadIdx.x; c < c1; c += 256) {
+    const float e = exp_fast(__fsub_rn(sc[c - c0], M));
+    sc[c - c0] = e;
     s = __fadd_rn(s, e);
   }
   s = warp_sum_f(s);
+  __syncthreads();  // the max's red[] reads are done
   if (lane == 0) red[warp] = s;
   __syncthreads();
+  if (threadIdx.x == 0) {
+    float t = 0.f;
+    for (int w = 0; w < 8; ++w) t = __fadd_rn(t, red[w]);
+    part[1] = t;
+  }
+  cluster.sync();
   float S = 0.f;
-  for (int w = 0; w < 8; ++w) S = __fadd_rn(S, red[w]);
+  for (int r = 0; r < NC; ++r) S = __fadd_rn(S, *cluster.map_shared_rank(&part[1], r));
   const float inv = __frcp_rn(S);
 
   constexpr int NCH = 256 / D;
   const int d = threadIdx.x % D, ch = threadIdx.x / D;
-  const int len = (ctx + NCH - 1) / NCH;
-  const int c0 = ch * len, c1 = min(ctx, c0 + len);
+  const int n = c1 - c0, len = (n + NCH - 1) / NCH;
+  const int a0 = c0 + ch * len, a1 = min(c1, a0 + len);
   const float *vcol = vc + kvh * D + d;
   float acc = 0.f;
-  for (int c = c0; c < c1; ++c) acc = __fmaf_rn(__fmul_rn(sc[c], inv), __ldg(vcol + (int64_t)c * rs), acc);
-  part[ch][d] = acc;
+  for (int c = a0; c < a1; ++c) acc = __fmaf_rn(__fmul_rn(sc[c - c0], inv), __ldg(vcol + (int64_t)c * rs), acc);
+  pv[ch][d] = acc;
   __syncthreads();
   if (threadIdx.x < D) {
-    float o = part[0][threadIdx.x];
-    for (int k = 1; k < NCH; ++k) o = __fadd_rn(o, part[k][threadIdx.x]);
+    float o = pv[0][threadIdx.x];
+    for (int k = 1; k < NCH; ++k) o = __fadd_rn(o, pv[k][threadIdx.x]);
+    octa[threadIdx.x] = o;
+  }
+  cluster.sync();
+  if (cr == 0 && threadIdx.x < D) {
+    float o = octa[threadIdx.x];
+    for (int r = 1; r < NC; ++r) o = __fadd_rn(o, *cluster.map_shared_rank(&octa[threadIdx.x], r));
     out[h * D + threadIdx.x] = o;
   }
+  cluster.sync();  // peers' shared memory stays alive until rank 0 has read it
 }
 
 // margins[pos] = logits[idx] - (largest other logit; NaN never counts)
@@ -182,13 +214,28 @@ tb_status tb_attention_decode(const float *q, const float *k_cache, const float 
   if (!q || !k_cache || !v_cache || !pos_dev || !out) return fail(TB_EINVAL, "tb_attention_decode: null pointer");
   if ((reinterpret_cast<uintptr_t>(k_cache) & 15) != 0)
     return fail(TB_EINVAL, "tb_attention_decode: the key cache must be 16-byte aligned");
-  const size_t smem = (size_t)max_seq * sizeof(float);
+  constexpr int NC = 8;  // CTAs per head (a portable cluster)
+  const size_t smem = (size_t)((max_seq + NC - 1) / NC) * sizeof(float);
   if (smem > 200 * 1024) return fail(TB_EINVAL, "tb_attention_decode: cache of %lld rows too long", (long long)max_seq);
   DeviceState *st;
   TB_TRY(device_state(&st));
-  TB_TRY(ensure_smem_for(attention_decode_kernel<64>, smem));
-  attention_decode_kernel<64><<<(unsigned)heads, 256, smem, as_stream(stream)>>>(
-      q, k_cache, v_cache, (int)heads, (int)kv_heads, (int)max_seq, scale, pos_dev, out, st->err_word);
+  auto kern = attention_decode_kernel<64, NC>;
+  TB_TRY(ensure_smem_for(kern, smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(heads * NC), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = NC;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, q, k_cache, v_cache, (int)heads, (int)kv_heads, (int)max_seq, scale,
+                                     pos_dev, out, st->err_word);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_attention_decode: %s", cudaGetErrorString(e));
   return check_launch("tb_attention_decode");
 }
 

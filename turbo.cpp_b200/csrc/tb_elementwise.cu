@@ -312,11 +312,7 @@ __global__ void __launch_bounds__(256) copy_transpose_kernel(const T *__restrict
 // division and products are IEEE-rounded as in the reference; exp is the
 // correctly rounding exp_cr (the reference's glibc expf is too, but on ~0.03%
 // of inputs).
-__device__ __forceinline__ float swiglu1(float g, float u) {
-  float e = exp_cr(-g);
-  float s = __fdiv_rn(g, __fadd_rn(1.0f, e));
-  return __fmul_rn(s, u);
-}
+__device__ __forceinline__ float swiglu1(float g, float u) { return swiglu_f32(g, u); }
 __device__ __forceinline__ float swiglu1_bf16(float g, float u) {
   float e = __expf(-g);  // bf16 results: fp32 exp is far below the output rounding
   return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), u);

@@ -20,12 +20,11 @@
 #include <algorithm>
 
 #include "tb_internal.cuh"
+#include "tb_q8_row.cuh"
 
 namespace tb {
 namespace {
 
-constexpr uint32_t kMagicHi = 0x4B400000u;  // float 12582912 = 3 * 2^22
-constexpr float kMagic = 12582912.0f;
 
 // Stages the CTA's weight byte range [B0, B1) (relative to W) into smem.
 // Returns the shift of byte B0 inside the staged buffer.  Thread 0 issues the
@@ -49,20 +48,6 @@ __device__ __forceinline__ int stage_rows(const uint8_t *__restrict__ W, int64_t
     for (int64_t i = B0 + threadIdx.x; i < B1; i += blockDim.x) wsm[i - t0] = W[i];
   }
   return shift;
-}
-
-// Reads the 34-byte Q8_0 block at smem byte offset `off` (even): the scale as
-// float and the 32 quants as 8 little-endian words.
-__device__ __forceinline__ void load_q8_block(const uint8_t *wsm, int off, float &d,
-                                              uint32_t qw[8]) {
-  const uint32_t *w32 = reinterpret_cast<const uint32_t *>(wsm + (off & ~3));
-  uint32_t w[9];
-#pragma unroll
-  for (int k = 0; k < 9; ++k) w[k] = w32[k];
-  const uint32_t sh = (uint32_t)(off & 3) * 8u;  // 0 or 16
-  d = half_bits_to_float((uint16_t)(__funnelshift_rc(w[0], w[1], sh) & 0xFFFFu));
-#pragma unroll
-  for (int k = 0; k < 8; ++k) qw[k] = __funnelshift_rc(w[k], w[k + 1], 16u + sh);
 }
 
 template <int NW>
@@ -454,10 +439,6 @@ size_t pipe_smem_bytes(int K, const PipeCfg &c) {
 // read and y written only after it, and the kernel lets its dependents launch
 // at once.  A GEMV that follows another kernel in the stream therefore starts
 // streaming its weights while the predecessor drains.
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-__device__ __forceinline__ void pdl_launch_dependents() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
 
 struct SpanCfg {
   int span_rows;  // rows per span buffer
@@ -767,14 +748,8 @@ __global__ void __launch_bounds__(NW * 32) gemv_q8_0_ring_kernel(const uint8_t *
     }
   }
   __syncthreads();
-  const bool onepass = nb <= 64;
   uint64_t xp[32];
-  if (onepass) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      xp[j] = pack2(lane < nb ? xs[j * XS + lane] : 0.f, lane + 32 < nb ? xs[j * XS + lane + 32] : 0.f);
-  }
-  const uint64_t off2 = pack2(-(kMagic + 128.0f), -(kMagic + 128.0f));
+  if (nb <= 64) q8_load_xp(xp, xs, XS, nb, 0, lane);
 
   for (int k = 0; k < nspans; ++k) {
     const int slot = k % slots;
@@ -786,43 +761,7 @@ __global__ void __launch_bounds__(NW * 32) gemv_q8_0_ring_kernel(const uint8_t *
         return;
       }
       const uint8_t *wrow = ring + slot * slot_bytes + (size_t)warp * rb;
-      float racc = 0.f;
-      for (int p = 0; p * 64 < nb; ++p) {
-        const int b1 = p * 64 + lane, b2 = b1 + 32;
-        const bool v1 = b1 < nb, v2 = b2 < nb;
-        if (!onepass) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            xp[j] = pack2(v1 ? xs[j * XS + b1] : 0.f, v2 ? xs[j * XS + b2] : 0.f);
-        }
-        float d1, d2;
-        uint32_t q1[8], q2[8];
-        load_q8_block(wrow, 34 * (v1 ? b1 : 0), d1, q1);
-        load_q8_block(wrow, 34 * (v2 ? b2 : 0), d2, q2);
-        // two independent packed chains (elements 0-15 and 16-31 of each block)
-        uint64_t acc0 = pack2(0.f, 0.f), acc1 = pack2(0.f, 0.f);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          const uint32_t u1 = q1[kk] ^ 0x80808080u, u2 = q2[kk] ^ 0x80808080u;
-          const uint32_t w1 = q1[kk + 4] ^ 0x80808080u, w2 = q2[kk + 4] ^ 0x80808080u;
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const uint32_t sel = 0x7650u | (uint32_t)e;
-            const uint64_t m = pack2(__uint_as_float(__byte_perm(u1, kMagicHi, sel)),
-                                     __uint_as_float(__byte_perm(u2, kMagicHi, sel)));
-            const uint64_t n = pack2(__uint_as_float(__byte_perm(w1, kMagicHi, sel)),
-                                     __uint_as_float(__byte_perm(w2, kMagicHi, sel)));
-            acc0 = fma2(add2(m, off2), xp[4 * kk + e], acc0);
-            acc1 = fma2(add2(n, off2), xp[4 * kk + 16 + e], acc1);
-          }
-        }
-        float s1, s2;
-        unpack2(add2(acc0, acc1), s1, s2);
-        if (v1) racc = fmaf(s1, d1, racc);
-        if (v2) racc = fmaf(s2, d2, racc);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) racc += __shfl_xor_sync(0xffffffffu, racc, o);
+      const float racc = q8_row_dot(wrow, nb, xp, xs, XS, lane);
       if (lane == 0) Y[n0 + k * NW + warp] = racc;
       // The last of the span's nr warps refills the slot with span k + slots.
       // Only warps that waited for this span count: a warp without a row (only

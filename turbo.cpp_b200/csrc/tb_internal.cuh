@@ -270,4 +270,17 @@ __device__ __forceinline__ float exp_fast(float x) {
   return __fmul_rn(__fmul_rn(p, __int_as_float((k1 + 127) << 23)), __int_as_float((k2 + 127) << 23));
 }
 
+// silu(g) * u as src/nn/swiglu.cpp:25-31 rounds it: g / (1 + exp(-g)), then * u
+__device__ __forceinline__ float swiglu_f32(float g, float u) {
+  const float e = exp_cr(-g);
+  const float s = __fdiv_rn(g, __fadd_rn(1.0f, e));
+  return __fmul_rn(s, u);
+}
+
+// programmatic dependent launch
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 }  // namespace tb

@@ -18,7 +18,10 @@ class KVCache;
 // MiniGPT::forward runs for one token, except that each layer's attention is a
 // single fused kernel (tb_attention_decode) instead of the per-head loop of
 // attention.cpp:104-141; its softmax sum and probability-times-V order differ
-// within the fp32 tolerance.
+// within the fp32 tolerance.  Unless the bit-identical matmul kernels are
+// selected (set_exact_matmul), a layer with Q8_0 projections runs as six
+// launches: RMSNorm + Q/K/V GEMVs, RoPE + cache append, attention, O GEMV +
+// residual, RMSNorm + gate/up GEMVs + SwiGLU, down GEMV + residual.
 class DecodeGraph {
  public:
   // `kv` holds the prompt's keys/values (kv.get_current_seq_len() rows).
@@ -34,7 +37,9 @@ class DecodeGraph {
 
  private:
   void enqueue_step();
+  void enqueue_step_fused();
   void *buf(size_t bytes);
+  bool fused_ = false;
 
   MiniGPT &m_;
   KVCache &kv_;

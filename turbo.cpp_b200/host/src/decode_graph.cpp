@@ -41,6 +41,16 @@ DecodeGraph::DecodeGraph(MiniGPT &model, KVCache &kv, bool want_margins)
     for (nn::Linear *l : {&b.attention.q_proj, &b.attention.k_proj, &b.attention.v_proj, &b.attention.o_proj,
                           &b.ffn.gate_proj, &b.ffn.up_proj, &b.ffn.down_proj})
       if (!l->get_bias().is_empty()) throw std::invalid_argument("DecodeGraph: biased projections unsupported");
+  // the fused step needs Q8_0 projections with rows of whole 16-byte words
+  fused_ = !exact_matmul() && D_ == 64;
+  auto q8 = [&](nn::Linear &l) {
+    const Tensor &w = l.get_weight();
+    return w.dtype() == DataType::Q8_0 && w.get_shape()[0] % 256 == 0;
+  };
+  for (auto &b : m_.blocks)
+    fused_ = fused_ && q8(b.attention.q_proj) && q8(b.attention.k_proj) && q8(b.attention.v_proj) &&
+             q8(b.attention.o_proj) && q8(b.ffn.gate_proj) && q8(b.ffn.up_proj) && q8(b.ffn.down_proj);
+  fused_ = fused_ && q8(m_.lm_head);
   tb_check(tb_stream_create(&stream_));
   ids_ = static_cast<int32_t *>(buf(16));
   pos_ = static_cast<int32_t *>(buf(16));
@@ -116,7 +126,43 @@ tb_view head_view(float *p, int64_t heads, int64_t D) {
 }
 }  // namespace
 
+void DecodeGraph::enqueue_step_fused() {
+  tb_stream s = stream_;
+  const int64_t E = (int64_t)E_, F = (int64_t)F_, V = (int64_t)V_, KV = (int64_t)(KVH_ * D_);
+  auto wptr = [](nn::Linear &l) { return (const void *)l.get_weight().get_storage()->device_data(); };
+  auto gptr = [](nn::RMSNorm &n) { return static_cast<const float *>(n.get_weight().device_ptr()); };
+  const Tensor &emb = m_.tok_emb.get_weight();
+  tb_check(tb_embedding(tb_dtype_of(emb.dtype()), emb.get_storage()->device_data(), E, V, ids_, 1, x_, s));
+  for (size_t l = 0; l < m_.blocks.size(); ++l) {
+    nn::TransformerBlock &b = m_.blocks[l];
+    nn::MultiHeadAttention &a = b.attention;
+    tb_gemv_segment qkv[3] = {{wptr(a.q_proj), E, q_, nullptr},
+                              {wptr(a.k_proj), KV, k_, nullptr},
+                              {wptr(a.v_proj), KV, v_, nullptr}};
+    tb_check(tb_gemv_q8_0_multi(x_, E, gptr(b.attention_norm), b.attention_norm.epsilon, qkv, 3, s));
+    float *kc = static_cast<float *>(kv_.get_k_cache((int)l).device_ptr());
+    float *vc = static_cast<float *>(kv_.get_v_cache((int)l).device_ptr());
+    tb_check(tb_rope_kv_append(q_, k_, v_, (int64_t)H_, (int64_t)KVH_, (int64_t)D_,
+                               static_cast<const float *>(a.rope.dev_cos->device_ptr()),
+                               static_cast<const float *>(a.rope.dev_sin->device_ptr()), (int64_t)a.rope.max_seq_len,
+                               kc, vc, max_seq_, pos_, s));
+    tb_check(tb_attention_decode(q_, kc, vc, (int64_t)H_, (int64_t)KVH_, (int64_t)D_, max_seq_, scale_, pos_, ctx_, s));
+    tb_gemv_segment o = {wptr(a.o_proj), E, h_, x_};  // h = x + O ctx
+    tb_check(tb_gemv_q8_0_multi(ctx_, E, nullptr, 0.f, &o, 1, s));
+    tb_check(tb_gemv_q8_0_swiglu(h_, E, gptr(b.ffn_norm), b.ffn_norm.epsilon, wptr(b.ffn.gate_proj),
+                                 wptr(b.ffn.up_proj), F, sw_, s));
+    tb_gemv_segment d = {wptr(b.ffn.down_proj), E, x_, h_};  // x = h + down sw
+    tb_check(tb_gemv_q8_0_multi(sw_, F, nullptr, 0.f, &d, 1, s));
+  }
+  tb_gemv_segment lm = {wptr(m_.lm_head), V, logits_, nullptr};
+  tb_check(tb_gemv_q8_0_multi(x_, E, gptr(m_.norm), m_.norm.epsilon, &lm, 1, s));
+  tb_check(tb_argmax(logits_, 1, V, idx_, s));
+  if (margins_on_) tb_check(tb_decode_margin(logits_, V, idx_, pos_, max_seq_, margins_, s));
+  tb_check(tb_decode_advance(idx_, ids_, pos_, hist_, max_seq_, s));
+}
+
 void DecodeGraph::enqueue_step() {
+  if (fused_) return enqueue_step_fused();
   tb_stream s = stream_;
   const int64_t E = (int64_t)E_, F = (int64_t)F_, V = (int64_t)V_;
   const Tensor &emb = m_.tok_emb.get_weight();

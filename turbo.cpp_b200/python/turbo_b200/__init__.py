@@ -88,7 +88,15 @@ SIGNATURES = {
     "tb_capture_end": [_P, ctypes.POINTER(_P)],
     "tb_graph_launch": [_P, _P],
     "tb_graph_destroy": [_P],
+    "tb_gemv_q8_0_multi": [_P, _I64, _P, _F, _P, _I, _P],
+    "tb_gemv_q8_0_swiglu": [_P, _I64, _P, _F, _P, _P, _I64, _P, _P],
+    "tb_rope_kv_append": [_P, _P, _P, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _I64, _P, _P],
 }
+
+
+class GemvSegment(ctypes.Structure):
+    """tb_gemv_segment: w, n, y, residual."""
+    _fields_ = [("w", ctypes.c_void_p), ("n", ctypes.c_int64), ("y", ctypes.c_void_p), ("residual", ctypes.c_void_p)]
 
 _lib = None
 

@@ -321,13 +321,14 @@ tb_status tb_graph_destroy(tb_graph graph);
 
 /* ---------------------------------------------------------------- diagnostics -- */
 
-/* Evaluates the two fp32 exp implementations of the softmax and SwiGLU kernels
- * on every fp32 bit pattern against exp in double precision rounded to float,
- * on the current device, synchronously.  counts[0]: inputs where the
- * correctly-rounding version (SwiGLU) differs; counts[1]: its largest distance
- * in ulp; counts[2]: inputs where the fp32-only version (softmax) is more than
- * 2 ulp away; counts[3]: its largest distance.  No reference counterpart: the
- * reference calls glibc expf. */
+/* Evaluates the fp32 exp functions of the SwiGLU and softmax kernels on every
+ * fp32 bit pattern against exp in double precision rounded to float, on the
+ * current device, synchronously.  counts[0]: inputs where the correctly-
+ * rounding version (SwiGLU) differs; counts[1]: its largest distance in ulp;
+ * counts[2]: inputs in [-87, 0] where the softmax kernels' exp (the __expf
+ * intrinsic) exceeds its documented 2 + 1.173|x| ulp; counts[3]: its largest
+ * distance over [-20, 0].  No reference counterpart: the reference calls glibc
+ * expf. */
 tb_status tb_selfcheck_exp(uint64_t counts[4]);
 
 #if defined(__GNUC__)

@@ -459,9 +459,10 @@ def test_exp_selfcheck_every_float():
     T.call("tb_selfcheck_exp", ctypes.cast(counts, ctypes.c_void_p))
     n_cr, max_cr, n_fast, max_fast = list(counts)
     print("exp_cr: %d of 2^32 inputs differ from the double-precision exp (max %d ulp); "
-          "exp_fast: %d beyond 2 ulp (max %d ulp)" % (n_cr, max_cr, n_fast, max_fast))
+          "__expf: %d beyond its documented bound on [-87, 0] (max %d ulp on [-20, 0])"
+          % (n_cr, max_cr, n_fast, max_fast))
     assert max_cr <= 1 and n_cr <= 1024
-    assert n_fast == 0 and max_fast <= 2
+    assert n_fast == 0 and max_fast <= 26
 
 
 def test_softmax_kat():

@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(
   for (int r = 0; r < NC; ++r) M = fmaxf(M, *cluster.map_shared_rank(&part[0], r));
   float s = 0.f;
   for (int c = c0 + threadIdx.x; c < c1; c += 256) {
-    const float e = exp_fast(__fsub_rn(sc[c - c0], M));
+    const float e = __expf(__fsub_rn(sc[c - c0], M));
     sc[c - c0] = e;
     s = __fadd_rn(s, e);
   }

@@ -42,6 +42,7 @@ __global__ void __launch_bounds__(NW * 32) gemv_fused_kernel(const FusedArgs a, 
   __shared__ int done[kFusedSlots];
   __shared__ int abort_flag;
   __shared__ float red[NW];
+  __shared__ double tab[64];  // exp_cr table (SWIGLU epilogue)
   const int K = a.K, nb = K / 32, rb = nb * 34;
   const int XS = (nb & 1) ? nb + 2 : nb + 1;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);
@@ -90,6 +91,7 @@ __global__ void __launch_bounds__(NW * 32) gemv_fused_kernel(const FusedArgs a, 
     for (int k = 0; k < kFusedSlots && k < nspans; ++k) issue(k);
   }
   pdl_launch_dependents();
+  if (SWIGLU) exp_cr_table_init(tab);  // visible after the barrier below
   pdl_wait();  // x and the residuals come from the previous kernel
 
   // x (RMS-normalised as tb_rmsnorm does when gamma is given) -> smem, transposed
@@ -147,7 +149,7 @@ __global__ void __launch_bounds__(NW * 32) gemv_fused_kernel(const FusedArgs a, 
       if (SWIGLU) {
         const float g = q8_row_dot(wrow, nb, xp, xs, XS, lane);
         const float u = q8_row_dot(wrow + (size_t)NW * rb, nb, xp, xs, XS, lane);
-        if (lane == 0) a.y[0][r] = swiglu_f32(g, u);
+        if (lane == 0) a.y[0][r] = swiglu_f32(g, u, tab);
       } else {
         const float v = q8_row_dot(wrow, nb, xp, xs, XS, lane);
         if (lane == 0) {

@@ -312,14 +312,14 @@ __global__ void __launch_bounds__(256) copy_transpose_kernel(const T *__restrict
 // division and products are IEEE-rounded as in the reference; exp is the
 // correctly rounding exp_cr (the reference's glibc expf is too, but on ~0.03%
 // of inputs).
-__device__ __forceinline__ float swiglu1(float g, float u) { return swiglu_f32(g, u); }
+__device__ __forceinline__ float swiglu1(float g, float u, const double *tab) { return swiglu_f32(g, u, tab); }
 __device__ __forceinline__ float swiglu1_bf16(float g, float u) {
   float e = __expf(-g);  // bf16 results: fp32 exp is far below the output rounding
   return __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, e)), u);
 }
 
 template <typename T>
-__device__ __forceinline__ uint4 swiglu_vec(const uint4 a, const uint4 b) {
+__device__ __forceinline__ uint4 swiglu_vec(const uint4 a, const uint4 b, const double *tab) {
   constexpr int V = Vec<T>::N;
   const T *ga = reinterpret_cast<const T *>(&a), *ub = reinterpret_cast<const T *>(&b);
   uint4 r;
@@ -327,7 +327,7 @@ __device__ __forceinline__ uint4 swiglu_vec(const uint4 a, const uint4 b) {
 #pragma unroll
   for (int k = 0; k < V; ++k) {
     const float gf = to_f(ga[k]), uf = to_f(ub[k]);
-    rr[k] = from_f<T>(sizeof(T) == 4 ? swiglu1(gf, uf) : swiglu1_bf16(gf, uf));
+    rr[k] = from_f<T>(sizeof(T) == 4 ? swiglu1(gf, uf, tab) : swiglu1_bf16(gf, uf));
   }
   return r;
 }
@@ -338,6 +338,9 @@ __global__ void __launch_bounds__(kThreads) swiglu_kernel(const T *__restrict__ 
                                                           T *__restrict__ y, int64_t n,
                                                           int vec_ok) {
   constexpr int V = Vec<T>::N;
+  __shared__ double tab[64];
+  exp_cr_table_init(tab);
+  __syncthreads();
   const int64_t stride = (int64_t)gridDim.x * blockDim.x;
   int64_t base = 0;
   if (vec_ok) {
@@ -350,15 +353,15 @@ __global__ void __launch_bounds__(kThreads) swiglu_kernel(const T *__restrict__ 
     for (; i + stride < nvec; i += 2 * stride) {
       const uint4 a0 = __ldcs(gv + i), b0 = __ldcs(uv + i);
       const uint4 a1 = __ldcs(gv + i + stride), b1 = __ldcs(uv + i + stride);
-      __stcs(yv + i, swiglu_vec<T>(a0, b0));
-      __stcs(yv + i + stride, swiglu_vec<T>(a1, b1));
+      __stcs(yv + i, swiglu_vec<T>(a0, b0, tab));
+      __stcs(yv + i + stride, swiglu_vec<T>(a1, b1, tab));
     }
-    if (i < nvec) __stcs(yv + i, swiglu_vec<T>(__ldcs(gv + i), __ldcs(uv + i)));
+    if (i < nvec) __stcs(yv + i, swiglu_vec<T>(__ldcs(gv + i), __ldcs(uv + i), tab));
     base = nvec * V;
   }
   for (int64_t i = base + (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     float gf = to_f(g[i]), uf = to_f(u[i]);
-    y[i] = from_f<T>(sizeof(T) == 4 ? swiglu1(gf, uf) : swiglu1_bf16(gf, uf));
+    y[i] = from_f<T>(sizeof(T) == 4 ? swiglu1(gf, uf, tab) : swiglu1_bf16(gf, uf));
   }
 }
 

@@ -202,77 +202,49 @@ __device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
   return r;
 }
 
-// ---- exp for the softmax / SiLU paths -----------------------------------------
+// ---- exp for the SiLU path ------------------------------------------------------
 // The reference calls glibc expf, whose documented error bound is 0.502 ulp: it
-// is correctly rounded except on ~0.03% of inputs.  Two implementations here,
-// both written from the textbook method (argument reduction x = k ln2 + r,
-// |r| <= ln2/2, exp(r) from its Taylor series, scaling by 2^k in the exponent
-// field):
-//
-// exp_cr    reduction and series in double precision (series to degree 12: the
-//           truncation error is below 2^-51 on |r| <= ln2/2), rounded once to
-//           float.  Correctly rounded unless exp(x) lies within ~2^-50
-//           (relative) of a float rounding boundary.  Used where the reference's
-//           result is matched bit for bit (SwiGLU).
-// exp_fast  fp32 arithmetic only: ln2 split in a 16-bit head and a tail
-//           (Cody and Waite) so k*ln2_hi is exact, series to degree 7 (truncation
-//           below 2^-27), 2^k applied as two power-of-two factors so results in
-//           the subnormal range round once.  Within 2 ulp.  Used where the
-//           reference's result is matched within a tolerance (softmax).
-// exp_ref   double-precision libdevice exp rounded to float: the self-check's
-//           yardstick for the two above, not used on a product path.
+// is correctly rounded except on ~0.03% of inputs.  exp_cr is written from the
+// textbook table method (Tang): x = (64 m + j) ln2/64 + r, |r| <= ln2/128,
+// exp(x) = 2^m * 2^(j/64) * exp(r), exp(r) from its Taylor series to degree 5
+// (truncation below 2^-54 on that interval), all in double precision, rounded
+// once to float.  Correctly rounded unless exp(x) lies within ~2^-47
+// (relative) of a float rounding boundary.  The 64 table entries 2^(j/64) are
+// computed once per CTA into the caller's shared memory (exp_cr_table_init,
+// followed by a barrier).  exp_ref, double-precision libdevice exp rounded to
+// float, is the self-check's yardstick, not used on a product path.
+// The softmax kernels use the __expf intrinsic (2 + 1.17|x| ulp, documented),
+// which is far inside their tolerance and cheaper than any of these.
 __device__ __forceinline__ float exp_ref(float x) { return __double2float_rn(exp((double)x)); }
 
-__device__ __forceinline__ float exp_cr(float xf) {
+__device__ __forceinline__ void exp_cr_table_init(double *tab) {
+  for (int j = threadIdx.x; j < 64; j += blockDim.x) tab[j] = exp2((double)j * (1.0 / 64.0));
+}
+
+__device__ __forceinline__ float exp_cr(float xf, const double *tab) {
   if (xf != xf) return xf;
   // exp(-110) rounds to +0 and exp(100) to +inf, so clamping changes no result
   const double x = (double)fminf(fmaxf(xf, -110.0f), 100.0f);
-  const double kRound = 6755399441055744.0;  // 1.5 * 2^52: t's low word holds rint(x / ln2)
-  const double t = fma(x, 1.4426950408889634, kRound);
+  const double kRound = 6755399441055744.0;  // 1.5 * 2^52: t's low word holds rint(64 x / ln2)
+  const double t = fma(x, 92.33248261689366, kRound);  // 64 / ln2
   const int k = __double2loint(t);
   const double kd = t - kRound;
-  const double r = fma(kd, -0.6931471805599453, x);  // |k| <= 159: error ~1e-17, far below 2^-50
-  double p = 1.0 / 479001600.0;                      // 1/12!
-  p = fma(p, r, 1.0 / 39916800.0);
-  p = fma(p, r, 1.0 / 3628800.0);
-  p = fma(p, r, 1.0 / 362880.0);
-  p = fma(p, r, 1.0 / 40320.0);
-  p = fma(p, r, 1.0 / 5040.0);
-  p = fma(p, r, 1.0 / 720.0);
-  p = fma(p, r, 1.0 / 120.0);
+  const double r = fma(kd, -0.010830424696249145, x);  // ln2 / 64
+  double p = 1.0 / 120.0;
   p = fma(p, r, 1.0 / 24.0);
   p = fma(p, r, 1.0 / 6.0);
   p = fma(p, r, 0.5);
   p = fma(p, r, 1.0);
   p = fma(p, r, 1.0);
-  // p is in [0.70, 1.42]; 2^k (k in [-159, 145]) keeps the double normal
-  return __double2float_rn(__hiloint2double(__double2hiint(p) + (int)((unsigned)k << 20), __double2loint(p)));
-}
-
-__device__ __forceinline__ float exp_fast(float x) {
-  if (x != x) return x;
-  x = fminf(fmaxf(x, -104.0f), 89.0f);  // exp(-104) rounds to +0, exp(89) to +inf
-  const float kRound = 12582912.0f;     // 1.5 * 2^23
-  const float t = fmaf(x, 1.44269504f, kRound);
-  const int k = __float_as_int(t) - 0x4B400000;
-  const float kf = t - kRound;
-  float r = fmaf(kf, -0.693145751953125f, x);  // ln2 head: 16 significant bits
-  r = fmaf(kf, -1.4286068203094173e-6f, r);    // ln2 - head
-  float p = 1.0f / 5040.0f;
-  p = fmaf(p, r, 1.0f / 720.0f);
-  p = fmaf(p, r, 1.0f / 120.0f);
-  p = fmaf(p, r, 1.0f / 24.0f);
-  p = fmaf(p, r, 1.0f / 6.0f);
-  p = fmaf(p, r, 0.5f);
-  p = fmaf(p, r, 1.0f);
-  p = fmaf(p, r, 1.0f);
-  const int k1 = k >> 1, k2 = k - k1;  // each in [-75, 64]
-  return __fmul_rn(__fmul_rn(p, __int_as_float((k1 + 127) << 23)), __int_as_float((k2 + 127) << 23));
+  const double y = tab[k & 63] * p;  // in [0.99, 2.0): 2^m keeps it a normal double
+  const int m = k >> 6;              // arithmetic shift: floor(k / 64)
+  return __double2float_rn(__hiloint2double(__double2hiint(y) + (int)((unsigned)m << 20), __double2loint(y)));
 }
 
 // silu(g) * u as src/nn/swiglu.cpp:25-31 rounds it: g / (1 + exp(-g)), then * u
-__device__ __forceinline__ float swiglu_f32(float g, float u) {
-  const float e = exp_cr(-g);
+// (tab: the exp_cr table in shared memory)
+__device__ __forceinline__ float swiglu_f32(float g, float u, const double *tab) {
+  const float e = exp_cr(-g, tab);
   const float s = __fdiv_rn(g, __fadd_rn(1.0f, e));
   return __fmul_rn(s, u);
 }

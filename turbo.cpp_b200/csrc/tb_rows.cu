@@ -227,15 +227,15 @@ __global__ void __launch_bounds__(NT) softmax_cluster_kernel(
   float s = 0.f;
   for (int i = threadIdx.x; i < n4; i += NT) {
     float4 v = slice4[i];
-    v.x = exp_fast(__fsub_rn(v.x, M));
-    v.y = exp_fast(__fsub_rn(v.y, M));
-    v.z = exp_fast(__fsub_rn(v.z, M));
-    v.w = exp_fast(__fsub_rn(v.w, M));
+    v.x = __expf(__fsub_rn(v.x, M));
+    v.y = __expf(__fsub_rn(v.y, M));
+    v.z = __expf(__fsub_rn(v.z, M));
+    v.w = __expf(__fsub_rn(v.w, M));
     if (MODE == 0) slice4[i] = v;
     s = __fadd_rn(s, __fadd_rn(__fadd_rn(v.x, v.y), __fadd_rn(v.z, v.w)));
   }
   for (int i = 4 * n4 + threadIdx.x; i < n; i += NT) {
-    const float e = exp_fast(__fsub_rn(slice[i], M));
+    const float e = __expf(__fsub_rn(slice[i], M));
     if (MODE == 0) slice[i] = e;
     s = __fadd_rn(s, e);
   }
@@ -281,11 +281,11 @@ __global__ void __launch_bounds__(kRowThreads) softmax_long_kernel(const float *
     for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) m = xr[i] > m ? xr[i] : m;
     m = block_max(m, scratch);
     float s = 0.f;
-    for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) s = __fadd_rn(s, exp_fast(__fsub_rn(xr[i], m)));
+    for (int64_t i = threadIdx.x; i < cols; i += blockDim.x) s = __fadd_rn(s, __expf(__fsub_rn(xr[i], m)));
     s = block_sum(s, scratch);
     const float inv = __frcp_rn(s);
     for (int64_t i = threadIdx.x; i < cols; i += blockDim.x)
-      y[r * cols + i] = __fmul_rn(exp_fast(__fsub_rn(xr[i], m)), inv);
+      y[r * cols + i] = __fmul_rn(__expf(__fsub_rn(xr[i], m)), inv);
   }
 }
 
@@ -300,14 +300,14 @@ __global__ void __launch_bounds__(kRowThreads) softmax_finish_kernel(
     float *yr = y + r * ldy;
     for (int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; c < cols;
          c += (int64_t)gridDim.x * blockDim.x)
-      yr[c] = __fmul_rn(exp_fast(__fsub_rn(xr[c], M)), inv);
+      yr[c] = __fmul_rn(__expf(__fsub_rn(xr[c], M)), inv);
   }
 }
 
 __global__ void softmax_rescale_kernel(const float *__restrict__ lmax, const float *__restrict__ gmax,
                                        float *__restrict__ sum, int64_t rows) {
   int64_t r = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (r < rows) sum[r] = __fmul_rn(sum[r], exp_fast(__fsub_rn(lmax[r], gmax[r])));
+  if (r < rows) sum[r] = __fmul_rn(sum[r], __expf(__fsub_rn(lmax[r], gmax[r])));
 }
 
 // ----------------------------------------------------------------- argmax ----

@@ -428,6 +428,27 @@ def test_softmax(rows, cols):
     assert_softmax(host(y), x)
 
 
+@pytest.mark.parametrize("rows,cols", [(200, 128256), (160, 100004)])
+def test_softmax_many_rows_two_pass(rows, cols):
+    # at least one row per SM: the persistent CTA-per-row kernel
+    from oracle import refbind as R
+    x = synth.normal((rows, cols), 2.0, seed=rows)
+    x[7, 12345] = 30.0
+    x[11, ::3] = -np.inf
+    x[12, 5] = np.nan
+    x[13, :] = -np.inf
+    x[14, 99] = np.inf
+    y = torch.empty((rows, cols), dtype=torch.float32, device="cuda")
+    T.call("tb_softmax", T.ptr(dev(x)), T.ptr(y), rows, cols, S())
+    got = host(y)
+    ref = R.softmax(x) if R.available() else O.softmax(x)
+    assert np.array_equal(np.isnan(got), np.isnan(ref))
+    ok = [r for r in range(rows) if r not in (12, 13, 14)]
+    assert not got[11, ::3].any()
+    assert_softmax(got[ok], x[ok])
+    assert T.take_device_errors() == 0
+
+
 def test_softmax_many_short_rows():
     # more clusters than SMs: the 256-thread CTA variant
     x = synth.normal((160, 4099), 2.0, seed=5)

@@ -8,6 +8,8 @@
 #include <cooperative_groups.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
 
 #include "tb_internal.cuh"
 
@@ -269,6 +271,92 @@ __global__ void __launch_bounds__(NT) softmax_cluster_kernel(
   cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
 }
 
+// Many rows: one CTA per row, persistent over rows (grid = one CTA per SM).
+// Pass 1 reads the row once from HBM keeping a running (max, sum of exp) per
+// thread (the sum rescaled whenever the max grows), combined over the block;
+// pass 2 reads the row again -- from L2, which holds the rows in flight (one
+// 513 KB logits row per SM fits) -- and writes exp(x - M) * (1/S).  No
+// clusters and no shared-memory staging; HBM traffic is one read and one
+// write.  Rows must be 16-byte aligned (cols % 4 == 0).
+__device__ __forceinline__ void online_add(float v, float &m, float &s) {
+  if (v > m) {  // NaN never raises the maximum
+    s = __fadd_rn(__fmul_rn(s, __expf(__fsub_rn(m, v))), 1.0f);
+    m = v;
+  } else if (v != -INFINITY) {  // -inf adds exp(-inf) = 0; NaN makes the sum NaN
+    s = __fadd_rn(s, __expf(__fsub_rn(v, m)));
+  }
+}
+
+__global__ void __launch_bounds__(1024, 1) softmax_rows_kernel(const float *__restrict__ x, float *__restrict__ y,
+                                                               int64_t rows, int64_t cols) {
+  __shared__ float sm[32], ss[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int64_t n4 = cols >> 2;
+  for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
+    const float4 *x4 = reinterpret_cast<const float4 *>(x + r * cols);
+    float m = -INFINITY, s = 0.f;
+    int64_t i = threadIdx.x;
+    for (; i + 3 * (int64_t)blockDim.x < n4; i += 4 * (int64_t)blockDim.x) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldcg(x4 + i + u * (int64_t)blockDim.x);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        online_add(v[u].x, m, s);
+        online_add(v[u].y, m, s);
+        online_add(v[u].z, m, s);
+        online_add(v[u].w, m, s);
+      }
+    }
+    for (; i < n4; i += blockDim.x) {
+      const float4 v = __ldcg(x4 + i);
+      online_add(v.x, m, s);
+      online_add(v.y, m, s);
+      online_add(v.z, m, s);
+      online_add(v.w, m, s);
+    }
+    // combine (m, s) over the warp, then over the block, in a fixed order
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, m, o), s2 = __shfl_xor_sync(0xffffffffu, s, o);
+      const float mm = fmaxf(m, m2);
+      s = (mm == -INFINITY) ? 0.f
+                            : __fadd_rn(__fmul_rn(s, __expf(__fsub_rn(m, mm))), __fmul_rn(s2, __expf(__fsub_rn(m2, mm))));
+      m = mm;
+    }
+    __syncthreads();  // the previous row's sm/ss reads are done
+    if (lane == 0) {
+      sm[warp] = m;
+      ss[warp] = s;
+    }
+    __syncthreads();
+    float M = -INFINITY;
+    for (int w = 0; w < nw; ++w) M = fmaxf(M, sm[w]);
+    float S = 0.f;
+    if (M != -INFINITY)
+      for (int w = 0; w < nw; ++w) S = __fadd_rn(S, __fmul_rn(ss[w], __expf(__fsub_rn(sm[w], M))));
+    // NaN anywhere in the row makes the reference's sum NaN
+    const float inv = __frcp_rn(S);
+    float4 *y4 = reinterpret_cast<float4 *>(y + r * cols);
+    auto out = [&](float4 v) {
+      v.x = __fmul_rn(__expf(__fsub_rn(v.x, M)), inv);
+      v.y = __fmul_rn(__expf(__fsub_rn(v.y, M)), inv);
+      v.z = __fmul_rn(__expf(__fsub_rn(v.z, M)), inv);
+      v.w = __fmul_rn(__expf(__fsub_rn(v.w, M)), inv);
+      return v;
+    };
+    int64_t j = threadIdx.x;
+    for (; j + 3 * (int64_t)blockDim.x < n4; j += 4 * (int64_t)blockDim.x) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldcg(x4 + j + u * (int64_t)blockDim.x);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) __stcs(y4 + j + u * (int64_t)blockDim.x, out(v[u]));
+    }
+    for (; j < n4; j += blockDim.x) __stcs(y4 + j, out(__ldcg(x4 + j)));
+  }
+}
+
 // Rows too long for the cluster's shared memory: max, then sum, then the
 // output, each a pass over the row (the later passes mostly hit L2).
 __global__ void __launch_bounds__(kRowThreads) softmax_long_kernel(const float *__restrict__ x,
@@ -520,6 +608,13 @@ tb_status tb_softmax(const float *x, float *y, int64_t rows, int64_t cols, tb_st
     return check_launch("tb_softmax");
   }
   const int span = softmax_span(cols, cs);
+  // many rows of whole float4s: a persistent CTA per row (two passes, the
+  // second from L2)
+  if (cols % 4 == 0 && rows >= st->sm_count && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+    softmax_rows_kernel<<<st->sm_count, 1024, 0, s>>>(x, y, rows, cols);
+    return check_launch("tb_softmax");
+  }
   if (rows * cs <= st->sm_count)  // few rows: wide CTAs shorten each row's critical path
     return launch_cluster_nt<1024>(softmax_cluster_kernel<0, 1024>, rows, cs, (size_t)span * 4, s, x, y,
                                    rows, cols, cols, cols, span, (float *)nullptr, (float *)nullptr,

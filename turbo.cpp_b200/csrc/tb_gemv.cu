@@ -923,12 +923,17 @@ size_t q4_smem_bytes(int K, int rows) {
 // Q8_0 matmul on CUDA cores.  M == 1 with aligned operands runs the
 // pipelined GEMV (exact or fast arithmetic); everything else the one-shot
 // kernel, which always follows the reference's order.
+bool gemv_tc_eligible(int64_t K, int64_t N, const void *w, const float *x);
+tb_status launch_gemv_tc(const float *x, int64_t K, const void *w, int64_t N, float *y, cudaStream_t s,
+                         const DeviceState *st);
+
 tb_status launch_q8_0(const float *x, int64_t M, int64_t K, const void *w, int64_t N, float *y,
                       bool exact, cudaStream_t s, const DeviceState *st) {
   const int64_t rbytes = K / 32 * 34;
   if (M == 1 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 && rbytes % 16 == 0 &&
       (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
     if (exact) return launch_span<1>(x, K, w, N, y, s, st);
+    if (gemv_tc_eligible(K, N, w, x)) return launch_gemv_tc(x, K, w, N, y, s, st);
     return launch_ring<8>(x, K, w, N, y, kRingSlots, s, st, ring_ctas_per_sm(K, st));
   }
   if (false) {

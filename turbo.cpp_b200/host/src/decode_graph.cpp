@@ -154,8 +154,9 @@ void DecodeGraph::enqueue_step_fused() {
     tb_gemv_segment d = {wptr(b.ffn.down_proj), E, x_, h_};  // x = h + down sw
     tb_check(tb_gemv_q8_0_multi(sw_, F, nullptr, 0.f, &d, 1, s));
   }
-  tb_gemv_segment lm = {wptr(m_.lm_head), V, logits_, nullptr};
-  tb_check(tb_gemv_q8_0_multi(x_, E, gptr(m_.norm), m_.norm.epsilon, &lm, 1, s));
+  // the LM head (128256 rows) runs faster on the tensor-core GEMV than fused
+  tb_check(tb_rmsnorm(TB_F32, x_, gptr(m_.norm), xn_, 1, E, m_.norm.epsilon, s));
+  linear(m_.lm_head, xn_, logits_, s);
   tb_check(tb_argmax(logits_, 1, V, idx_, s));
   if (margins_on_) tb_check(tb_decode_margin(logits_, V, idx_, pos_, max_seq_, margins_, s));
   tb_check(tb_decode_advance(idx_, ids_, pos_, hist_, max_seq_, s));

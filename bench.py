@@ -434,6 +434,28 @@ def run_decode_suite(args):
     return 0
 
 
+def run_sharded_suite(args):
+    """Row-sharded sweep ops and the NCCL vocab-sharded softmax/argmax on every
+    rank (launch under torchrun for N > 1; N = 1 runs a one-rank group)."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    ws, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+    os.environ.setdefault("MASTER_PORT", "29533")
+    os.environ.setdefault("RANK", "0")
+    os.environ.setdefault("WORLD_SIZE", "1")
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
+    try:
+        from turbo_b200 import opbench
+        opbench.run_sharded()
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -443,7 +465,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--exact", action="store_true",
                     help="time tb_matmul_quant_exact (bit-identical to the reference) instead")
-    ap.add_argument("--suite", default="headline", choices=["headline", "ops", "decode"],
+    ap.add_argument("--suite", default="headline", choices=["headline", "ops", "decode", "sharded"],
                     help="ops: per-op throughput of every hot-path kernel (one JSON line per op); "
                          "decode: the 1B-shaped greedy decode in tokens/sec")
     ap.add_argument("--reps", type=int, default=3, help="with --suite decode: timed generate calls")
@@ -453,6 +475,8 @@ def main():
         return run_ops_suite(args)
     if args.suite == "decode":
         return run_decode_suite(args)
+    if args.suite == "sharded":
+        return run_sharded_suite(args)
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":

@@ -298,3 +298,83 @@ def run(only=None, min_ms=20.0, out=None):
             for r in results:
                 f.write(json.dumps(r) + "\n")
     return results
+
+
+def run_sharded(reps=20):
+    """The sharded sweep on every rank of a torch.distributed job (one GPU per
+    rank, NCCL): row-sharded ops on [262144, 4096] per rank (weak scaling, no
+    collective), and the vocab-sharded softmax and argmax of logits
+    [64, 128256] split over the ranks (two float all-reduces / one int64
+    all-reduce per call).  Time per call = max over ranks of the CUDA-event
+    time; GB/s = bytes moved by all ranks / that time.  Rank 0 prints one
+    JSON line per op."""
+    import torch
+    import torch.distributed as dist
+
+    import turbo_b200 as T
+    from .sharded import VocabShardGroup
+
+    ws, rank = dist.get_world_size(), dist.get_rank()
+    peak, kind = _peak()
+    dev = "cuda"
+    T.call("tb_init", torch.cuda.current_device())
+    stream = torch.cuda.current_stream()
+    sh = ctypes.c_void_p(stream.cuda_stream)
+    L = T.load()
+
+    def timed(fn, n):
+        fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([a.elapsed_time(b) / n], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def report(op, ms, nbytes_total, cfg):
+        if rank == 0:
+            gbs = nbytes_total / (ms * 1e-3) / 1e9
+            print(json.dumps({"suite": "sharded", "op": op, "n_gpus": ws, "config": cfg, "ms_per_call": round(ms, 4),
+                              "GB_s": round(gbs, 1), "hbm_frac_per_gpu": round(gbs / ws / peak, 4),
+                              "peak_GB_s": peak, "peak_source": kind, "timing": "max over ranks"}), flush=True)
+
+    R, C = 1 << 18, 4096  # rows per rank: 4 GiB per fp32 tensor
+    g = torch.Generator(dev).manual_seed(rank)
+    a = torch.randn((R, C), device=dev, generator=g)
+    b = torch.randn((R, C), device=dev, generator=g)
+    o = torch.empty_like(a)
+    va, vb, vo = T.view(a), T.view(b), T.view(o)
+    n = R * C
+    ms = timed(lambda: T.check(L.tb_binary(0, T.byref(va), T.byref(vb), T.byref(vo), sh)), 5)
+    report("add_f32", ms, 3 * 4 * n * ws, "[%d,%d] per rank, rows sharded" % (R, C))
+    row = torch.randn((C,), device=dev, generator=g)
+    vr = T.view(row)
+    ms = timed(lambda: T.check(L.tb_binary(1, T.byref(va), T.byref(vr), T.byref(vo), sh)), 5)
+    report("mul_rowvec_f32", ms, (2 * 4 * n + 4 * C) * ws, "[%d,%d] * [%d] per rank" % (R, C, C))
+    gam = torch.rand((C,), device=dev, generator=g) + 0.5
+    ms = timed(lambda: T.check(L.tb_rmsnorm(T.F32, T.ptr(a), T.ptr(gam), T.ptr(o), R, C, 1e-5, sh)), 5)
+    report("rmsnorm_f32", ms, (2 * 4 * n + 4 * C) * ws, "[%d,%d] per rank" % (R, C))
+    ms = timed(lambda: T.check(L.tb_swiglu(T.F32, T.ptr(a), T.ptr(b), T.ptr(o), n, sh)), 5)
+    report("swiglu_f32", ms, 3 * 4 * n * ws, "[%d,%d] per rank" % (R, C))
+    vt = T.view(b, 0, (C, R), (1, C))  # contiguous() of a transposed [R, C] slab
+    o2 = torch.empty((C, R), device=dev)
+    vo2 = T.view(o2)
+    ms = timed(lambda: T.check(L.tb_copy(T.byref(vo2), T.byref(vt), sh)), 5)
+    report("contiguous_transpose_f32", ms, 2 * 4 * n * ws, "[%d,%d]^T per rank" % (R, C))
+    del a, b, o, o2
+    torch.cuda.empty_cache()
+
+    V, rows = 128256, 64
+    grp = VocabShardGroup(V)
+    full = torch.randn((rows, V), device=dev, generator=torch.Generator(dev).manual_seed(7)) * 2.0
+    local = full[:, grp.col_base:grp.col_base + grp.cols].contiguous()
+    out = torch.empty_like(local)
+    ms = timed(lambda: grp.softmax(local, out), reps)
+    report("vocab_sharded_softmax", ms, 2 * 4 * rows * V, "logits [%d,%d] split over %d ranks, NCCL" % (rows, V, ws))
+    ms = timed(lambda: grp.argmax(local), reps)
+    report("vocab_sharded_argmax", ms, 4 * rows * V, "logits [%d,%d] split over %d ranks, NCCL" % (rows, V, ws))

@@ -7,11 +7,10 @@
 //   tb_gemv_q8_0_swiglu   RMSNorm(x) * gamma (optional), then silu(G x) * (U x)
 //   tb_rope_kv_append     RoPE of q and k at the device-held position and the
 //                         key/value cache append, in one launch
-// The GEMVs stream weights exactly as the ring GEMV does (spans of 8 rows per
-// CTA through two shared-memory slots, two CTAs per SM, programmatic dependent
-// launch) and compute each row with the same q8_row_dot; the fused prologue and
-// epilogue use the formulas of tb_rmsnorm, tb_binary(add) and tb_swiglu, so a
-// fused step differs from the op-by-op step only in the RMSNorm's sum order.
+// All of them, and tb_matmul_quant's default M = 1 Q8_0 path below the LM-head
+// size, run gemv_stream_kernel (below); the fused prologue and epilogue use the
+// formulas of tb_rmsnorm, tb_binary(add) and tb_swiglu, so a fused step differs
+// from the op-by-op step only in the RMSNorm's sum order.
 #include <algorithm>
 
 #include "tb_internal.cuh"
@@ -20,8 +19,8 @@
 namespace tb {
 namespace {
 
-constexpr int kFusedWarps = 8;
-constexpr int kFusedSlots = 2;
+constexpr int kStreamWarps = 4;     // rows per span (one per warp); 4 CTAs per SM
+constexpr int kStreamMaxSlots = 16;
 
 struct FusedArgs {
   const uint8_t *w[3];
@@ -33,20 +32,35 @@ struct FusedArgs {
   const float *gamma;  // RMSNorm weight, or null
   float eps;
   int K;
+  int slots;  // span buffers per CTA (kStreamMaxSlots at most)
 };
 
+// Streaming Q8_0 GEMV (M = 1), default tolerance.  Each CTA owns a contiguous
+// range of logical rows, cut into spans of kStreamWarps rows (one per warp;
+// SWIGLU: the gate rows and the up rows of the same indices).  Spans stream
+// through `slots` shared-memory buffers, one bulk copy per span and segment and
+// one mbarrier per buffer; when every span of the CTA fits (the common decode
+// case) all copies are in flight from the first instruction, otherwise the
+// last warp to finish a span refills its buffer with the span `slots` ahead.
+// Small CTAs, four per SM, so that rows are spread finely over the GPU and the
+// warps' issue slots, not one CTA's latency chain, bound the compute.
+// Programmatic dependent launch: the weight copies are issued before
+// griddepcontrol.wait (weights never depend on the previous kernel).
 // SWIGLU: segment 0 = gate, segment 1 = up (same rows), y[0] = silu(g) * u.
-template <int NW, bool NORM, bool SWIGLU>
-__global__ void __launch_bounds__(NW * 32) gemv_fused_kernel(const FusedArgs a, uint32_t *__restrict__ err) {
+template <bool NORM, bool SWIGLU>
+__global__ void __launch_bounds__(kStreamWarps * 32, 4) gemv_stream_kernel(const FusedArgs a,
+                                                                           uint32_t *__restrict__ err) {
+  constexpr int NW = kStreamWarps;
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ int done[kFusedSlots];
+  __shared__ int done[kStreamMaxSlots];
   __shared__ int abort_flag;
   __shared__ float red[NW];
-  __shared__ double tab[64];  // exp_cr table (SWIGLU epilogue)
+  __shared__ double tab[SWIGLU ? 64 : 1];  // exp_cr table (SWIGLU epilogue)
   const int K = a.K, nb = K / 32, rb = nb * 34;
-  const int XS = (nb & 1) ? nb + 2 : nb + 1;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-  float *xs = reinterpret_cast<float *>(smem + 128);
+  const int XS = nb + 2;  // even: a lane's x pair is one 8-byte load
+  const int slots = a.slots;
+  uint64_t *full = reinterpret_cast<uint64_t *>(smem);  // [kStreamMaxSlots]
+  float *xs = reinterpret_cast<float *>(smem + 8 * kStreamMaxSlots);
   uint8_t *ring = reinterpret_cast<uint8_t *>(xs + 32 * XS);
   ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(ring) + 127) & ~uintptr_t(127));
   constexpr int kRowsPerSlot = SWIGLU ? 2 * NW : NW;
@@ -61,7 +75,7 @@ __global__ void __launch_bounds__(NW * 32) gemv_fused_kernel(const FusedArgs a, 
   const int nspans = (cnt + NW - 1) / NW;
 
   auto issue = [&](int k) {  // span k -> slot k % slots (one thread)
-    const int slot = k % kFusedSlots;
+    const int slot = k % slots;
     const int r0 = n0 + k * NW;
     const int nr = min(NW, cnt - k * NW);
     uint8_t *dst = ring + slot * slot_bytes;
@@ -72,23 +86,26 @@ __global__ void __launch_bounds__(NW * 32) gemv_fused_kernel(const FusedArgs a, 
     } else {
       mbar_arrive_expect_tx(full + slot, (uint32_t)(nr * rb));
       int start = 0;
-      for (int s = 0; s < a.nseg; ++s) {  // the span may cross segment boundaries
-        const int lo = max(r0, start), hi = min(r0 + nr, start + a.n[s]);
-        if (lo < hi)
-          bulk_g2s(dst + (size_t)(lo - r0) * rb, a.w[s] + (int64_t)(lo - start) * rb, (uint32_t)((hi - lo) * rb),
-                   full + slot);
-        start += a.n[s];
+#pragma unroll
+      for (int s = 0; s < 3; ++s) {  // the span may cross segment boundaries
+        if (s < a.nseg) {
+          const int lo = max(r0, start), hi = min(r0 + nr, start + a.n[s]);
+          if (lo < hi)
+            bulk_g2s(dst + (size_t)(lo - r0) * rb, a.w[s] + (int64_t)(lo - start) * rb,
+                     (uint32_t)((hi - lo) * rb), full + slot);
+          start += a.n[s];
+        }
       }
     }
   };
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kFusedSlots; ++i) {
+    for (int i = 0; i < slots; ++i) {
       mbar_init(full + i, 1);
       done[i] = 0;
     }
     abort_flag = 0;
     fence_mbar_init();
-    for (int k = 0; k < kFusedSlots && k < nspans; ++k) issue(k);
+    for (int k = 0; k < slots && k < nspans; ++k) issue(k);
   }
   pdl_launch_dependents();
   if (SWIGLU) exp_cr_table_init(tab);  // visible after the barrier below
@@ -131,15 +148,15 @@ __global__ void __launch_bounds__(NW * 32) gemv_fused_kernel(const FusedArgs a, 
     xs[((i + 3) & 31) * XS + ((i + 3) >> 5)] = v.w;
   }
   __syncthreads();
-  uint64_t xp[32];
-  if (nb <= 64) q8_load_xp(xp, xs, XS, nb, 0, lane);
+  float2 xp[32];
+  if (nb <= 64) q8_pair_x(xp, xs, XS, 2 * lane, 2 * lane < nb);
 
   for (int k = 0; k < nspans; ++k) {
-    const int slot = k % kFusedSlots;
+    const int slot = k % slots;
     const int nr = min(NW, cnt - k * NW);
     if (warp < nr) {
       const bool ok =
-          !*(volatile int *)&abort_flag && mbar_wait_bounded(full + slot, (uint32_t)((k / kFusedSlots) & 1), err);
+          !*(volatile int *)&abort_flag && mbar_wait_bounded(full + slot, (uint32_t)((k / slots) & 1), err);
       if (!__all_sync(0xffffffffu, ok)) {
         if (lane == 0) abort_flag = 1;
         return;
@@ -147,27 +164,40 @@ __global__ void __launch_bounds__(NW * 32) gemv_fused_kernel(const FusedArgs a, 
       const uint8_t *wrow = ring + slot * slot_bytes + (size_t)warp * rb;
       const int r = n0 + k * NW + warp;
       if (SWIGLU) {
-        const float g = q8_row_dot(wrow, nb, xp, xs, XS, lane);
-        const float u = q8_row_dot(wrow + (size_t)NW * rb, nb, xp, xs, XS, lane);
+        const float g = q8_row_dot_pairs(wrow, nb, xp, xs, XS, lane);
+        const float u = q8_row_dot_pairs(wrow + (size_t)NW * rb, nb, xp, xs, XS, lane);
         if (lane == 0) a.y[0][r] = swiglu_f32(g, u, tab);
       } else {
-        const float v = q8_row_dot(wrow, nb, xp, xs, XS, lane);
+        const float v = q8_row_dot_pairs(wrow, nb, xp, xs, XS, lane);
         if (lane == 0) {
-          int s = 0, start = 0;
-          while (s + 1 < a.nseg && r >= start + a.n[s]) start += a.n[s++];
-          const int i = r - start;
-          a.y[s][i] = a.res[s] ? __fadd_rn(a.res[s][i], v) : v;
+          int i = r;
+          float *y = a.y[0];
+          const float *res = a.res[0];
+          if (a.nseg > 1 && i >= a.n[0]) {
+            i -= a.n[0];
+            y = a.y[1];
+            res = a.res[1];
+            if (a.nseg > 2 && i >= a.n[1]) {
+              i -= a.n[1];
+              y = a.y[2];
+              res = a.res[2];
+            }
+          }
+          y[i] = res ? __fadd_rn(res[i], v) : v;
         }
       }
-      // the last of the span's nr warps refills the slot (only warps that
-      // waited for the span count; see gemv_q8_0_ring_kernel)
-      if (lane == 0) {
+      // With a ring (nspans > slots), the last of the span's nr warps refills
+      // the slot with span k + slots.  Only warps that waited for this span
+      // count: a warp without a row (only in the last, partial span) must not
+      // touch a counter, or it could run ahead and count toward a span that is
+      // still being read.
+      if (nspans > slots && lane == 0) {
         __threadfence_block();
         if (atomicAdd(&done[slot], 1) == nr - 1) {
           done[slot] = 0;
-          if (k + kFusedSlots < nspans) {
+          if (k + slots < nspans) {
             fence_proxy_async_smem();
-            issue(k + kFusedSlots);
+            issue(k + slots);
           }
         }
       }
@@ -176,25 +206,39 @@ __global__ void __launch_bounds__(NW * 32) gemv_fused_kernel(const FusedArgs a, 
   }
 }
 
-size_t fused_smem_bytes(int K, bool swiglu) {
+size_t stream_fixed_smem(int K) {
   const int nb = K / 32;
-  const int XS = (nb & 1) ? nb + 2 : nb + 1;
-  size_t s = 128 + (size_t)32 * XS * 4;
-  s = (s + 127) & ~size_t(127);
-  return s + (size_t)kFusedSlots * (swiglu ? 2 : 1) * kFusedWarps * nb * 34 + 128;
+  const size_t s = 8 * kStreamMaxSlots + (size_t)32 * (nb + 2) * 4;
+  return (s + 127) & ~size_t(127);
 }
 
+// Grid and span buffers: four CTAs per SM when at least two buffers (or all
+// the CTA's spans) fit in a quarter of the SM's shared memory, else fewer CTAs
+// per SM; then as many buffers as the CTA has spans, up to what fits.
 template <bool NORM, bool SWIGLU>
-tb_status launch_fused(const FusedArgs &a, int total_rows, cudaStream_t s, const DeviceState *st) {
-  const size_t smem = fused_smem_bytes(a.K, SWIGLU);
-  if (smem > (size_t)st->smem_optin) return fail(TB_EINVAL, "fused GEMV: K=%d too large", a.K);
-  const int cps = 2 * smem <= (size_t)st->smem_optin ? 2 : 1;
-  const int grid = std::max(1, std::min(total_rows, st->sm_count * cps));
-  auto kern = gemv_fused_kernel<kFusedWarps, NORM, SWIGLU>;
+tb_status launch_stream(FusedArgs a, int total_rows, cudaStream_t s, const DeviceState *st) {
+  const int nb = a.K / 32;
+  const size_t slot_bytes = (size_t)(SWIGLU ? 2 : 1) * kStreamWarps * nb * 34;
+  const size_t fixed = stream_fixed_smem(a.K);
+  auto kern = gemv_stream_kernel<NORM, SWIGLU>;
+  int cps = 4, slots = 0, grid = 1;
+  for (; cps >= 1; --cps) {
+    grid = std::max(1, std::min(total_rows, st->sm_count * cps));
+    const int maxcnt = (total_rows + grid - 1) / grid;
+    const int nspans = (maxcnt + kStreamWarps - 1) / kStreamWarps;
+    const int64_t budget = std::min<int64_t>((int64_t)st->smem_per_sm / cps - st->smem_reserved - 2048,
+                                             (int64_t)st->smem_optin) - (int64_t)fixed;
+    const int fit = budget > 0 ? (int)std::min<int64_t>(budget / (int64_t)slot_bytes, kStreamMaxSlots) : 0;
+    slots = std::min(nspans, fit);
+    if (slots >= std::min(nspans, 2)) break;
+  }
+  if (cps < 1 || slots < 1) return fail(TB_EINVAL, "streaming GEMV: K=%d too large", a.K);
+  a.slots = slots;
+  const size_t smem = fixed + (size_t)slots * slot_bytes;
   TB_TRY(ensure_smem_for(kern, smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid, 1, 1);
-  cfg.blockDim = dim3(kFusedWarps * 32, 1, 1);
+  cfg.blockDim = dim3(kStreamWarps * 32, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
   cudaLaunchAttribute attr[1];
@@ -203,9 +247,34 @@ tb_status launch_fused(const FusedArgs &a, int total_rows, cudaStream_t s, const
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, st->err_word);
-  if (e != cudaSuccess) return fail(TB_ECUDA, "fused GEMV launch: %s", cudaGetErrorString(e));
+  if (e != cudaSuccess) return fail(TB_ECUDA, "streaming GEMV launch: %s", cudaGetErrorString(e));
   return TB_OK;
 }
+
+}  // namespace
+
+// Whether one span buffer and x fit in a CTA's shared memory at this K.
+bool stream_gemv_fits(int64_t K, const DeviceState *st) {
+  if (K <= 0 || K % 256 != 0 || K > 65536) return false;
+  return stream_fixed_smem((int)K) + (size_t)2 * kStreamWarps * (K / 32) * 34 <= (size_t)st->smem_optin;
+}
+
+// tb_matmul_quant(Q8_0), M = 1, default tolerance: one weight matrix, no norm,
+// no residual.  Operands as check_gemv_input requires (the caller checks).
+tb_status launch_stream_gemv(const float *x, int64_t K, const void *w, int64_t N, float *y, cudaStream_t s,
+                             const DeviceState *st) {
+  if (N <= 0 || N > 0x7FFFFFFF) return fail(TB_EINVAL, "tb_matmul_quant: N=%lld out of range", (long long)N);
+  FusedArgs a = {};
+  a.w[0] = static_cast<const uint8_t *>(w);
+  a.y[0] = y;
+  a.n[0] = (int)N;
+  a.nseg = 1;
+  a.x = x;
+  a.K = (int)K;
+  return launch_stream<false, false>(a, (int)N, s, st);
+}
+
+namespace {
 
 tb_status check_gemv_input(const float *x, int64_t K, const float *gamma, const void *w, const char *who) {
   if (K <= 0 || K % 32 != 0 || K > 65536) return fail(TB_EINVAL, "%s: K=%lld must be a positive multiple of 32", who, (long long)K);
@@ -282,7 +351,7 @@ tb_status tb_gemv_q8_0_multi(const float *x, int64_t K, const float *gamma, floa
   DeviceState *st;
   TB_TRY(device_state(&st));
   cudaStream_t s = as_stream(stream);
-  return gamma ? launch_fused<true, false>(a, (int)total, s, st) : launch_fused<false, false>(a, (int)total, s, st);
+  return gamma ? launch_stream<true, false>(a, (int)total, s, st) : launch_stream<false, false>(a, (int)total, s, st);
 }
 
 tb_status tb_gemv_q8_0_swiglu(const float *x, int64_t K, const float *gamma, float eps, const void *w_gate,
@@ -303,7 +372,7 @@ tb_status tb_gemv_q8_0_swiglu(const float *x, int64_t K, const float *gamma, flo
   DeviceState *st;
   TB_TRY(device_state(&st));
   cudaStream_t s = as_stream(stream);
-  return gamma ? launch_fused<true, true>(a, (int)n, s, st) : launch_fused<false, true>(a, (int)n, s, st);
+  return gamma ? launch_stream<true, true>(a, (int)n, s, st) : launch_stream<false, true>(a, (int)n, s, st);
 }
 
 tb_status tb_rope_kv_append(float *q, float *k, const float *v, int64_t heads, int64_t kv_heads, int64_t head_dim,

@@ -194,238 +194,8 @@ __global__ void __launch_bounds__(NW * 32) gemv_q8_0_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Persistent, pipelined decode GEMV (M == 1): same arithmetic as above.
-//
-// One CTA per SM.  Warp NC (the producer) streams "stages" of NC consecutive
-// rows (one contiguous byte range, one bulk TMA copy) through a ring of S
-// shared-memory slots; consumer warp w computes row w of each stage.  Stages
-// are fetched in order, so compute on early rows overlaps the transfer of later
-// ones, and x is read from L2 once per SM and kept in registers.  The
-// block-order final sums are deferred: each warp parks the block sums of up to
-// FLUSH rows and then FLUSH lanes add their rows' sums at once.
-struct PipeCfg {
-  int nc;       // consumer warps = rows per stage
-  int stages;   // ring slots
-  int flush;    // rows parked per warp before the final sums
-};
-
-// EXACT = 1: the reference's operation order, bit for bit (as gemv_q8_0_kernel).
-// EXACT = 0: per block, acc = sum_j q_j * x_j as an FMA chain (q exact as
-// float, products exact, one rounding per step), y += d * acc; the row total is
-// a warp reduction.  Within 1e-5 relative of the reference (typically ~1e-7)
-// at about a third of the instructions per weight.
-template <int NC, int EXACT>
-__global__ void __launch_bounds__((NC + 1) * 32, 1) gemv_q8_0_pipe_kernel(
-    const uint8_t *__restrict__ W, const float *__restrict__ X, float *__restrict__ Y, int N,
-    int K, int stages, int flush, uint32_t *__restrict__ err) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const int nb = K / 32;
-  const int rb = nb * 34;
-  const int XS = (nb & 1) ? nb + 2 : nb + 1;
-  const int BP = (nb + 4) & ~3;
-  const int units = (N + NC - 1) / NC;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem);
-  uint64_t *empty = full + stages;
-  float *xs = reinterpret_cast<float *>(smem + 256);
-  float *bsum = xs + 32 * XS;  // [NC][flush][BP]
-  uint8_t *ring = reinterpret_cast<uint8_t *>(bsum + NC * flush * BP);
-  ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(ring) + 127) & ~uintptr_t(127));
-  const int stage_bytes = NC * rb;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < stages; ++i) {
-      mbar_init(full + i, 1);
-      mbar_init(empty + i, NC);
-    }
-    fence_mbar_init();
-  }
-  // x -> shared memory, transposed [j][block] with an odd pitch.
-  {
-    const float4 *x4 = reinterpret_cast<const float4 *>(X);
-    const int nv = K >> 2;
-    for (int base = 0; base < nv; base += 4 * (NC + 1) * 32) {
-      float4 v[4];
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int iv = base + u * (NC + 1) * 32 + threadIdx.x;
-        v[u] = iv < nv ? __ldg(x4 + iv) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-#pragma unroll
-      for (int u = 0; u < 4; ++u) {
-        const int iv = base + u * (NC + 1) * 32 + threadIdx.x;
-        if (iv < nv) {
-          const int i = iv * 4;
-          xs[((i + 0) & 31) * XS + ((i + 0) >> 5)] = v[u].x;
-          xs[((i + 1) & 31) * XS + ((i + 1) >> 5)] = v[u].y;
-          xs[((i + 2) & 31) * XS + ((i + 2) >> 5)] = v[u].z;
-          xs[((i + 3) & 31) * XS + ((i + 3) >> 5)] = v[u].w;
-        }
-      }
-    }
-  }
-  __syncthreads();
-
-  if (warp == NC) {  // ---------------- producer
-    if (lane == 0) {
-      int i = 0;
-      for (int u = blockIdx.x; u < units; u += gridDim.x, ++i) {
-        const int slot = i % stages;
-        if (i >= stages && !mbar_wait_bounded(empty + slot, ((i / stages) + 1) & 1, err)) break;
-        const int r0 = u * NC;
-        const int nr = min(NC, N - r0);
-        const uint32_t bytes = (uint32_t)(nr * rb);
-        mbar_arrive_expect_tx(full + slot, bytes);
-        bulk_g2s(ring + slot * stage_bytes, W + (int64_t)r0 * rb, bytes, full + slot);
-      }
-    }
-    return;
-  }
-
-  // ------------------------------------ consumers
-  float *mysum = bsum + warp * flush * BP;
-  const bool onepass = nb <= 64;
-  uint64_t xp[32];
-  if (onepass) {
-    const int b1 = lane, b2 = lane + 32;
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      xp[j] = pack2(b1 < nb ? xs[j * XS + b1] : 0.f, b2 < nb ? xs[j * XS + b2] : 0.f);
-  }
-  int parked = 0;   // rows parked in mysum; parked row r came from iteration first_i + r
-  int first_i = 0;
-  int i = 0;
-  for (int u = blockIdx.x; u < units; u += gridDim.x, ++i) {
-    const int slot = i % stages;
-    if (!mbar_wait_bounded(full + slot, (i / stages) & 1, err)) return;
-    const int row = u * NC + warp;
-    if (!EXACT) {
-      if (row < N) {
-        const uint8_t *wrow = ring + slot * stage_bytes + warp * rb;
-        float racc = 0.f;
-        for (int p = 0; p * 64 < nb; ++p) {
-          const int b1 = p * 64 + lane, b2 = b1 + 32;
-          const bool v1 = b1 < nb, v2 = b2 < nb;
-          if (!onepass) {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              xp[j] = pack2(v1 ? xs[j * XS + b1] : 0.f, v2 ? xs[j * XS + b2] : 0.f);
-          }
-          float d1, d2;
-          uint32_t q1[8], q2[8];
-          load_q8_block(wrow, 34 * (v1 ? b1 : 0), d1, q1);
-          load_q8_block(wrow, 34 * (v2 ? b2 : 0), d2, q2);
-          uint64_t acc = pack2(0.f, 0.f);
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float f1 = (float)(int8_t)(q1[k] >> (8 * e));
-              const float f2 = (float)(int8_t)(q2[k] >> (8 * e));
-              acc = fma2(pack2(f1, f2), xp[4 * k + e], acc);
-            }
-          float s1, s2;
-          unpack2(acc, s1, s2);
-          if (v1) racc = fmaf(s1, d1, racc);
-          if (v2) racc = fmaf(s2, d2, racc);
-        }
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) racc += __shfl_xor_sync(0xffffffffu, racc, o);
-        if (lane == 0) Y[row] = racc;
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(empty + slot);
-      continue;
-    }
-    if (row < N) {
-      const uint8_t *wrow = ring + slot * stage_bytes + warp * rb;
-      float *bs = mysum + parked * BP;
-      for (int p = 0; p * 64 < nb; ++p) {
-        const int b1 = p * 64 + lane, b2 = b1 + 32;
-        const bool v1 = b1 < nb, v2 = b2 < nb;
-        if (!onepass) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            xp[j] = pack2(v1 ? xs[j * XS + b1] : 0.f, v2 ? xs[j * XS + b2] : 0.f);
-        }
-        float d1, d2;
-        uint32_t q1[8], q2[8];
-        load_q8_block(wrow, 34 * (v1 ? b1 : 0), d1, q1);
-        load_q8_block(wrow, 34 * (v2 ? b2 : 0), d2, q2);
-        float s1 = 0.f, s2 = 0.f;
-        if (isfinite(d1) && isfinite(d2)) {
-          const uint64_t dd = pack2(d1, d2);
-          const uint64_t c1 = pack2(-kMagic * d1, -kMagic * d2);
-          const uint64_t c2 = pack2(-128.0f * d1, -128.0f * d2);
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t u1 = q1[k] ^ 0x80808080u, u2 = q2[k] ^ 0x80808080u;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const uint32_t sel = 0x7650u | (uint32_t)e;
-              const float m1 = __uint_as_float(__byte_perm(u1, kMagicHi, sel));
-              const float m2 = __uint_as_float(__byte_perm(u2, kMagicHi, sel));
-              uint64_t t = fma2(pack2(m1, m2), dd, c1);
-              t = add2(t, c2);
-              float p1, p2;
-              unpack2(mul2(t, xp[4 * k + e]), p1, p2);
-              s1 = __fadd_rn(s1, p1);
-              s2 = __fadd_rn(s2, p2);
-            }
-          }
-        } else {
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              float x1, x2;
-              unpack2(xp[4 * k + e], x1, x2);
-              s1 = __fadd_rn(s1, __fmul_rn(__fmul_rn((float)(int8_t)(q1[k] >> (8 * e)), d1), x1));
-              s2 = __fadd_rn(s2, __fmul_rn(__fmul_rn((float)(int8_t)(q2[k] >> (8 * e)), d2), x2));
-            }
-        }
-        if (v1) bs[b1] = s1;
-        if (v2) bs[b2] = s2;
-      }
-      if (parked == 0) first_i = i;
-      ++parked;  // only the last unit can hold rows past N, so parked rows are consecutive
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty + slot);  // this warp is done with the slot
-    const bool last = u + (int)gridDim.x >= units;
-    if (parked == flush || (last && parked > 0)) {
-      // lane r adds the block sums of parked row r in block order
-      const int myrow = (blockIdx.x + (first_i + lane) * (int)gridDim.x) * NC + warp;
-      if (lane < parked) {
-        const float4 *b4 = reinterpret_cast<const float4 *>(mysum + lane * BP);
-        float s = 0.f;
-        int b = 0;
-        for (; b + 8 <= nb; b += 8) {
-          const float4 a = b4[b / 4], c = b4[b / 4 + 1];
-          s = __fadd_rn(s, a.x); s = __fadd_rn(s, a.y); s = __fadd_rn(s, a.z); s = __fadd_rn(s, a.w);
-          s = __fadd_rn(s, c.x); s = __fadd_rn(s, c.y); s = __fadd_rn(s, c.z); s = __fadd_rn(s, c.w);
-        }
-        for (; b < nb; ++b) s = __fadd_rn(s, mysum[lane * BP + b]);
-        Y[myrow] = s;
-      }
-      __syncwarp();
-      parked = 0;
-    }
-  }
-}
-
-size_t pipe_smem_bytes(int K, const PipeCfg &c) {
-  const int nb = K / 32;
-  const int XS = (nb & 1) ? nb + 2 : nb + 1;
-  const int BP = (nb + 4) & ~3;
-  size_t s = 256 + (size_t)32 * XS * 4 + (size_t)c.nc * c.flush * BP * 4;
-  s = (s + 127) & ~size_t(127);
-  // + slack: the last block's 9-word read may run 2 bytes past the ring
-  return s + (size_t)c.stages * c.nc * nb * 34 + 128;
-}
-
-// ---------------------------------------------------------------------------
-// Span GEMV (M == 1), the decode path.
+// Span GEMV (M == 1), tb_matmul_quant_exact's path (EXACT = 1; the EXACT = 0
+// arithmetic is the tolerance form, kept for comparison).
 //
 // One CTA per SM owns a contiguous range of rows.  The range is cut into spans
 // that fit in shared memory; two span buffers are in flight, and each span is
@@ -682,156 +452,6 @@ tb_status launch_span(const float *x, int64_t K, const void *w, int64_t N, float
 }
 
 // ---------------------------------------------------------------------------
-// Ring GEMV (M == 1, default tolerance), the decode path.
-//
-// One CTA per SM owns a contiguous range of rows, cut into spans of NW rows
-// (one row per warp).  Spans stream through a ring of `slots` shared-memory
-// buffers, one bulk copy and one mbarrier per span; the last warp to finish a
-// span refills its slot with the span `slots` ahead.  The ring keeps the
-// CTA's shared memory small (NW * slots rows), so that under programmatic
-// dependent launch the next GEMV's CTA fits on the SM beside this one and
-// starts streaming its weights while this one drains: back-to-back GEMVs of a
-// decode step become one continuous weight stream.
-template <int NW>
-__global__ void __launch_bounds__(NW * 32) gemv_q8_0_ring_kernel(const uint8_t *__restrict__ W,
-                                                                 const float *__restrict__ X,
-                                                                 float *__restrict__ Y, int N, int K, int slots,
-                                                                 uint32_t *__restrict__ err) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ int done[8];
-  __shared__ int abort_flag;
-  const int nb = K / 32;
-  const int rb = nb * 34;
-  const int XS = (nb & 1) ? nb + 2 : nb + 1;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem);  // [slots], slots <= 8
-  float *xs = reinterpret_cast<float *>(smem + 128);
-  uint8_t *ring = reinterpret_cast<uint8_t *>(xs + 32 * XS);
-  ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(ring) + 127) & ~uintptr_t(127));
-  const size_t slot_bytes = (size_t)NW * rb;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-
-  const int G = gridDim.x, base = N / G, rem = N % G;
-  const int n0 = blockIdx.x * base + min((int)blockIdx.x, rem);
-  const int cnt = base + ((int)blockIdx.x < rem ? 1 : 0);
-  const int nspans = (cnt + NW - 1) / NW;
-
-  auto issue = [&](int k) {  // span k -> slot k % slots (one thread)
-    const int slot = k % slots;
-    const int nr = min(NW, cnt - k * NW);
-    const uint32_t bytes = (uint32_t)(nr * rb);
-    mbar_arrive_expect_tx(full + slot, bytes);
-    bulk_g2s(ring + slot * slot_bytes, W + ((int64_t)n0 + (int64_t)k * NW) * rb, bytes, full + slot);
-  };
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < slots; ++i) {
-      mbar_init(full + i, 1);
-      done[i] = 0;
-    }
-    abort_flag = 0;
-    fence_mbar_init();
-    for (int k = 0; k < slots && k < nspans; ++k) issue(k);
-  }
-  pdl_launch_dependents();
-  pdl_wait();  // x (and the order of our y writes) depend on the previous kernel
-
-  // x -> shared memory, transposed [j][block] with an odd pitch
-  {
-    const float4 *x4 = reinterpret_cast<const float4 *>(X);
-    const int nv = K >> 2;
-    for (int b4 = threadIdx.x; b4 < nv; b4 += NW * 32) {
-      const float4 v = __ldg(x4 + b4);
-      const int i = b4 * 4;
-      xs[((i + 0) & 31) * XS + ((i + 0) >> 5)] = v.x;
-      xs[((i + 1) & 31) * XS + ((i + 1) >> 5)] = v.y;
-      xs[((i + 2) & 31) * XS + ((i + 2) >> 5)] = v.z;
-      xs[((i + 3) & 31) * XS + ((i + 3) >> 5)] = v.w;
-    }
-  }
-  __syncthreads();
-  uint64_t xp[32];
-  if (nb <= 64) q8_load_xp(xp, xs, XS, nb, 0, lane);
-
-  for (int k = 0; k < nspans; ++k) {
-    const int slot = k % slots;
-    const int nr = min(NW, cnt - k * NW);
-    if (warp < nr) {
-      bool ok = !*(volatile int *)&abort_flag && mbar_wait_bounded(full + slot, (uint32_t)((k / slots) & 1), err);
-      if (!__all_sync(0xffffffffu, ok)) {
-        if (lane == 0) abort_flag = 1;
-        return;
-      }
-      const uint8_t *wrow = ring + slot * slot_bytes + (size_t)warp * rb;
-      const float racc = q8_row_dot(wrow, nb, xp, xs, XS, lane);
-      if (lane == 0) Y[n0 + k * NW + warp] = racc;
-      // The last of the span's nr warps refills the slot with span k + slots.
-      // Only warps that waited for this span count: a warp without a row (only
-      // in the last, partial span) must not touch a counter, or it could run
-      // ahead and count toward a span that is still being read.
-      if (lane == 0) {
-        __threadfence_block();
-        if (atomicAdd(&done[slot], 1) == nr - 1) {
-          done[slot] = 0;
-          if (k + slots < nspans) {
-            fence_proxy_async_smem();
-            issue(k + slots);
-          }
-        }
-      }
-      __syncwarp();
-    }
-  }
-}
-
-size_t ring_smem_bytes(int K, int NW, int slots) {
-  const int nb = K / 32;
-  const int XS = (nb & 1) ? nb + 2 : nb + 1;
-  size_t s = 128 + (size_t)32 * XS * 4;
-  s = (s + 127) & ~size_t(127);
-  // + slack: the last block's 9-word read may run 2 bytes past the ring
-  return s + (size_t)slots * NW * nb * 34 + 128;
-}
-
-template <int NW>
-tb_status launch_ring(const float *x, int64_t K, const void *w, int64_t N, float *y, int slots, cudaStream_t s,
-                      const DeviceState *st, int ctas_per_sm = 1) {
-  const int grid = (int)std::min<int64_t>(N, (int64_t)st->sm_count * ctas_per_sm);
-  const size_t smem = ring_smem_bytes((int)K, NW, slots);
-  if (smem > (size_t)st->smem_optin) return fail(TB_EINVAL, "tb_matmul_quant: K=%lld too large", (long long)K);
-  auto kern = gemv_q8_0_ring_kernel<NW>;
-  TB_TRY(ensure_smem_for(kern, smem));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)grid, 1, 1);
-  cfg.blockDim = dim3(NW * 32, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = s;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, (const uint8_t *)w, x, y, (int)N, (int)K, slots, st->err_word);
-  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_matmul_quant(Q8_0 ring): %s", cudaGetErrorString(e));
-  return TB_OK;
-}
-
-// Ring shape: 8 rows (warps) per span, two slots, two CTAs per SM when two fit
-// in shared memory (K <= 4096); measured on the 8192 x 2048 decode GEMV and a
-// 16-layer mix of the 1B decoder's projections against deeper rings, 4 and 16
-// warps and one or three CTAs per SM.
-constexpr int kRingSlots = 2;
-int ring_ctas_per_sm(int64_t K, const DeviceState *st) {
-  return 2 * ring_smem_bytes((int)K, 8, kRingSlots) <= (size_t)st->smem_optin ? 2 : 1;
-}
-
-tb_status launch_ring_cfg(const float *x, int64_t K, const void *w, int64_t N, float *y, int nw, int slots,
-                          cudaStream_t s, const DeviceState *st, int ctas_per_sm) {
-  if (nw == 4) return launch_ring<4>(x, K, w, N, y, slots, s, st, ctas_per_sm);
-  if (nw == 16) return launch_ring<16>(x, K, w, N, y, slots, s, st, ctas_per_sm);
-  if (nw == 32) return launch_ring<32>(x, K, w, N, y, slots, s, st, ctas_per_sm);
-  return launch_ring<8>(x, K, w, N, y, slots, s, st, ctas_per_sm);
-}
-
-// ---------------------------------------------------------------------------
 // Q4_0 weights times Q8_0-quantized activations, in the order of
 // vec_dot_q4_0_q8_0_avx2 (quant_math.hpp:184-248): eight fp32 lanes, lane l
 // accumulating, block after block, fma(p0, d, acc) then fma(p1, d, acc) where
@@ -924,6 +544,9 @@ size_t q4_smem_bytes(int K, int rows) {
 // pipelined GEMV (exact or fast arithmetic); everything else the one-shot
 // kernel, which always follows the reference's order.
 bool gemv_tc_eligible(int64_t K, int64_t N, const void *w, const float *x);
+tb_status launch_stream_gemv(const float *x, int64_t K, const void *w, int64_t N, float *y, cudaStream_t s,
+                             const DeviceState *st);
+bool stream_gemv_fits(int64_t K, const DeviceState *st);
 tb_status launch_gemv_tc(const float *x, int64_t K, const void *w, int64_t N, float *y, cudaStream_t s,
                          const DeviceState *st);
 
@@ -934,31 +557,7 @@ tb_status launch_q8_0(const float *x, int64_t M, int64_t K, const void *w, int64
       (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
     if (exact) return launch_span<1>(x, K, w, N, y, s, st);
     if (gemv_tc_eligible(K, N, w, x)) return launch_gemv_tc(x, K, w, N, y, s, st);
-    return launch_ring<8>(x, K, w, N, y, kRingSlots, s, st, ring_ctas_per_sm(K, st));
-  }
-  if (false) {
-    constexpr int NC = 8;
-    const int nb = (int)(K / 32);
-    PipeCfg c;
-    c.nc = NC;
-    c.flush = exact ? (nb <= 64 ? 16 : nb <= 128 ? 8 : 4) : 0;
-    c.stages = 6;
-    while (c.stages > 2 && pipe_smem_bytes((int)K, c) > (size_t)st->smem_optin) --c.stages;
-    if (pipe_smem_bytes((int)K, c) <= (size_t)st->smem_optin) {
-      const size_t smem = pipe_smem_bytes((int)K, c);
-      const int64_t units = (N + NC - 1) / NC;
-      const int grid = (int)std::min<int64_t>(units, st->sm_count);
-      if (exact) {
-        TB_TRY(ensure_smem_for(gemv_q8_0_pipe_kernel<NC, 1>, smem));
-        gemv_q8_0_pipe_kernel<NC, 1><<<grid, (NC + 1) * 32, smem, s>>>(
-            (const uint8_t *)w, x, y, (int)N, (int)K, c.stages, c.flush, st->err_word);
-      } else {
-        TB_TRY(ensure_smem_for(gemv_q8_0_pipe_kernel<NC, 0>, smem));
-        gemv_q8_0_pipe_kernel<NC, 0><<<grid, (NC + 1) * 32, smem, s>>>(
-            (const uint8_t *)w, x, y, (int)N, (int)K, c.stages, c.flush, st->err_word);
-      }
-      return check_launch("tb_matmul_quant(Q8_0 pipe)");
-    }
+    if (stream_gemv_fits(K, st)) return launch_stream_gemv(x, K, w, N, y, s, st);
   }
   constexpr int NW = 4;
   // ~36 KB of weights per CTA (a multiple of NW rows), several CTAs per SM.

@@ -17,6 +17,8 @@ struct DeviceState {
   int device = -1;
   int sm_count = 0;
   int smem_optin = 0;     // max dynamic shared memory per block (opt-in)
+  int smem_per_sm = 0;    // shared memory per SM, all resident blocks together
+  int smem_reserved = 0;  // shared memory the system reserves per block
   uint32_t *err_word = nullptr;  // device error word (bit 0 timeout, bit 1 index)
 };
 

@@ -1,5 +1,5 @@
 // tb_q8_row.cuh -- reading Q8_0 blocks from shared memory and the default
-// (tolerance) dot product of one weight row with x, shared by the decode GEMVs.
+// (tolerance) dot product of one weight row with x used by the streaming GEMVs.
 #pragma once
 #include "tb_internal.cuh"
 
@@ -21,59 +21,74 @@ __device__ __forceinline__ void load_q8_block(const uint8_t *wsm, int off, float
   for (int k = 0; k < 8; ++k) qw[k] = __funnelshift_rc(w[k], w[k + 1], 16u + sh);
 }
 
-// x staged in shared memory transposed, xs[j * XS + b] = x[32 b + j], with an
-// odd pitch XS; lane l works on blocks l and l + 32 of each 64-block pass and
-// keeps those blocks' x in xp[j] = (x[32 b1 + j], x[32 b2 + j]).
-__device__ __forceinline__ void q8_load_xp(uint64_t (&xp)[32], const float *xs, int XS, int nb, int pass,
-                                           int lane) {
-  const int b1 = pass * 64 + lane, b2 = b1 + 32;
+// ---- block pairs: the streaming GEMVs' row dot --------------------------------
+//
+// Lane l of a warp owns the consecutive blocks (2l, 2l + 1) of each 64-block
+// pass: 68 bytes that start on a 4-byte boundary whenever the row length is a
+// multiple of 4 (nb even), read as 17 words with no bank conflicts (the lanes'
+// word offsets 17 l are distinct modulo 32).  Quants are taken straight from
+// those words by prmt into the mantissa of 1.5 * 2^23 (after flipping every
+// quant byte's sign bit once per word), so no funnel shifts are needed.
+// x is staged as xs[j * XS + b] = x[32 b + j] with an even pitch XS, and a
+// lane's pair of x columns, xp[j] = (x[32 b + j], x[32 (b + 1) + j]), is one
+// 8-byte load per j.
+
+__device__ __forceinline__ void q8_pair_x(float2 (&xp)[32], const float *xs, int XS, int b, bool valid) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) xp[j] = pack2(b1 < nb ? xs[j * XS + b1] : 0.f, b2 < nb ? xs[j * XS + b2] : 0.f);
+  for (int j = 0; j < 32; ++j)
+    xp[j] = valid ? *reinterpret_cast<const float2 *>(xs + j * XS + b) : make_float2(0.f, 0.f);
 }
 
-// Dot product of the Q8_0 row at `wrow` (nb blocks) with x, reduced over the
-// warp (every lane returns it).  Each block: quants to float through the
-// mantissa of 1.5 * 2^23 (prmt, packed subtraction), two packed fma chains
-// (elements 0-15 and 16-31), times the block scale, accumulated per lane in
-// block order, then a butterfly sum over the lanes.  With nb <= 64, xp must
-// hold pass 0 on entry; otherwise it is reloaded from xs per pass.
-__device__ __forceinline__ float q8_row_dot(const uint8_t *wrow, int nb, uint64_t (&xp)[32], const float *xs,
-                                            int XS, int lane) {
-  const bool onepass = nb <= 64;
-  const uint64_t off2 = pack2(-(kMagic + 128.0f), -(kMagic + 128.0f));
-  float racc = 0.f;
-  for (int p = 0; p * 64 < nb; ++p) {
-    const int b1 = p * 64 + lane, b2 = b1 + 32;
-    const bool v1 = b1 < nb, v2 = b2 < nb;
-    if (!onepass) q8_load_xp(xp, xs, XS, nb, p, lane);
-    float d1, d2;
-    uint32_t q1[8], q2[8];
-    load_q8_block(wrow, 34 * (v1 ? b1 : 0), d1, q1);
-    load_q8_block(wrow, 34 * (v2 ? b2 : 0), d2, q2);
-    uint64_t acc0 = pack2(0.f, 0.f), acc1 = pack2(0.f, 0.f);
+// acc + d1 * (q1 . x1) + d2 * (q2 . x2) for the two blocks at `wp` (4-byte
+// aligned): per block two packed fma chains (elements 0-15 and 16-31) over
+// exact quants, added, times the block scale.
+__device__ __forceinline__ float q8_pair_dot(const uint8_t *wp, const float2 (&xp)[32], float acc) {
+  const uint32_t *w32 = reinterpret_cast<const uint32_t *>(wp);
+  uint32_t w[17];
 #pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      const uint32_t u1 = q1[kk] ^ 0x80808080u, u2 = q2[kk] ^ 0x80808080u;
-      const uint32_t w1 = q1[kk + 4] ^ 0x80808080u, w2 = q2[kk + 4] ^ 0x80808080u;
+  for (int k = 0; k < 17; ++k) w[k] = w32[k];
+  const float d1 = half_bits_to_float((uint16_t)(w[0] & 0xFFFFu));
+  const float d2 = half_bits_to_float((uint16_t)(w[8] >> 16));
+  // quant bytes: 2..33 (first block) and 36..67 (second); bytes 0-1 and 34-35 are the scales
+  w[0] ^= 0x80800000u;
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const uint32_t sel = 0x7650u | (uint32_t)e;
-        const uint64_t m = pack2(__uint_as_float(__byte_perm(u1, kMagicHi, sel)),
-                                 __uint_as_float(__byte_perm(u2, kMagicHi, sel)));
-        const uint64_t n = pack2(__uint_as_float(__byte_perm(w1, kMagicHi, sel)),
-                                 __uint_as_float(__byte_perm(w2, kMagicHi, sel)));
-        acc0 = fma2(add2(m, off2), xp[4 * kk + e], acc0);
-        acc1 = fma2(add2(n, off2), xp[4 * kk + 16 + e], acc1);
-      }
+  for (int k = 1; k < 8; ++k) w[k] ^= 0x80808080u;
+  w[8] ^= 0x00008080u;
+#pragma unroll
+  for (int k = 9; k < 17; ++k) w[k] ^= 0x80808080u;
+  const float2 off2 = make_float2(-(kMagic + 128.0f), -(kMagic + 128.0f));
+  float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    const int a = 2 + j, b = 36 + j, c = 18 + j, e = 52 + j;  // byte offsets of elements j, j + 16
+    const float2 m = make_float2(__uint_as_float(__byte_perm(w[a >> 2], kMagicHi, 0x7650u | (a & 3))),
+                                 __uint_as_float(__byte_perm(w[b >> 2], kMagicHi, 0x7650u | (b & 3))));
+    const float2 n = make_float2(__uint_as_float(__byte_perm(w[c >> 2], kMagicHi, 0x7650u | (c & 3))),
+                                 __uint_as_float(__byte_perm(w[e >> 2], kMagicHi, 0x7650u | (e & 3))));
+    acc0 = __ffma2_rn(__fadd2_rn(m, off2), xp[j], acc0);
+    acc1 = __ffma2_rn(__fadd2_rn(n, off2), xp[16 + j], acc1);
+  }
+  const float2 s = __fadd2_rn(acc0, acc1);
+  return fmaf(s.y, d2, fmaf(s.x, d1, acc));
+}
+
+// Dot product of the Q8_0 row at `wrow` (nb blocks, nb even, 4-byte aligned)
+// with x, reduced over the warp (every lane returns it).  With nb <= 64, xp
+// must hold pass 0 (q8_pair_x at b = 2 lane); otherwise each pass reloads it.
+__device__ __forceinline__ float q8_row_dot_pairs(const uint8_t *wrow, int nb, float2 (&xp)[32], const float *xs,
+                                                  int XS, int lane) {
+  float acc = 0.f;
+  if (nb <= 64) {
+    if (2 * lane < nb) acc = q8_pair_dot(wrow + 68 * lane, xp, 0.f);
+  } else {
+    for (int b = 2 * lane; b < nb; b += 64) {
+      q8_pair_x(xp, xs, XS, b, true);
+      acc = q8_pair_dot(wrow + 34 * b, xp, acc);
     }
-    float s1, s2;
-    unpack2(add2(acc0, acc1), s1, s2);
-    if (v1) racc = fmaf(s1, d1, racc);
-    if (v2) racc = fmaf(s2, d2, racc);
   }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) racc += __shfl_xor_sync(0xffffffffu, racc, o);
-  return racc;
+  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  return acc;
 }
 
 }  // namespace tb

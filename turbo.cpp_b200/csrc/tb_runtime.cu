@@ -68,6 +68,8 @@ tb_status device_state(DeviceState **out) {
       if (e != cudaSuccess) return fail(TB_ECUDA, "cudaMemset: %s", cudaGetErrorString(e));
       st.sm_count = p.multiProcessorCount;
       st.smem_optin = (int)p.sharedMemPerBlockOptin;
+      st.smem_per_sm = (int)p.sharedMemPerMultiprocessor;
+      st.smem_reserved = (int)p.reservedSharedMemPerBlock;
       st.err_word = w;
       st.device = dev;
     }

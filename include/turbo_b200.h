@@ -269,6 +269,15 @@ tb_status tb_kv_append(float *k_cache_dev, float *v_cache_dev, const float *k_de
 tb_status tb_attention_decode(const float *q_dev, const float *k_cache_dev, const float *v_cache_dev,
                               int64_t heads, int64_t kv_heads, int64_t head_dim, int64_t max_seq, float scale,
                               const int32_t *pos_dev, float *out_dev, tb_stream stream);
+/* tb_rope_kv_append followed by tb_attention_decode, in one launch: q [heads,
+ * head_dim] and k [kv_heads, head_dim] are rotated at position *pos_dev
+ * inside the attention kernel (q_dev and k_dev are not modified), the rotated
+ * k and v are appended to the caches' row *pos_dev, and out holds the
+ * attention output.  Results equal the two-call sequence bit for bit. */
+tb_status tb_rope_attention_decode(const float *q_dev, const float *k_dev, const float *v_dev, int64_t heads,
+                                   int64_t kv_heads, int64_t head_dim, const float *cos_dev, const float *sin_dev,
+                                   int64_t rope_max_seq, float *k_cache_dev, float *v_cache_dev, int64_t max_seq,
+                                   float scale, const int32_t *pos_dev, float *out_dev, tb_stream stream);
 /* margins[*pos_dev] = logits[*idx_dev] - the largest other logit. */
 tb_status tb_decode_margin(const float *logits_dev, int64_t vocab, const int64_t *idx_dev,
                            const int32_t *pos_dev, int64_t max_seq, float *margins_dev, tb_stream stream);
@@ -308,6 +317,15 @@ tb_status tb_rope_kv_append(float *q_dev, float *k_dev, const float *v_dev, int6
                             int64_t head_dim, const float *cos_dev, const float *sin_dev, int64_t rope_max_seq,
                             float *k_cache_dev, float *v_cache_dev, int64_t max_seq, const int32_t *pos_dev,
                             tb_stream stream);
+
+/* Asks L2 to fetch up to 8 device byte ranges (each trimmed inward to 16-byte
+ * boundaries) in the background, for weights that a later kernel of the same
+ * step will read: the copies overlap the kernels in between, which leave HBM
+ * idle.  A hint: results never depend on it.  The launch completes only after
+ * the preceding kernel of the stream has (programmatic dependent launch), so
+ * it may sit anywhere in a dependent chain.  No reference counterpart (the
+ * reference's weights are host memory). */
+tb_status tb_prefetch_l2(const void *const *ptrs_dev, const int64_t *bytes, int n, tb_stream stream);
 
 /* Streams and CUDA graphs for callers without the CUDA runtime: capture a
  * sequence of calls on a created stream once, replay it many times. */

@@ -773,8 +773,52 @@ def test_gemv_multi_segments_and_residual(sizes, K):
             assert_bits(host(fused[i]), host(out))
 
 
-def test_gemv_multi_with_rmsnorm_within_tolerance():
-    K, N = 2048, 3072
+@pytest.mark.parametrize("N,K", [(40000, 2048), (1, 2048), (5, 256), (1024, 16384), (3000, 4096)])
+def test_gemv_stream_ring_multipass_and_tiny(N, K):
+    # 40000 x 2048 through tb_gemv_q8_0_multi runs the span buffers as a ring
+    # (more spans per CTA than buffers); K = 16384 and 4096 take several
+    # 64-block passes per row and fewer CTAs per SM; 1 and 5 rows leave most
+    # warps without a row
+    xh = synth.normal((K,), 1.0, seed=K + N)
+    x = dev(xh)
+    wq, dw = _q8_dev(N, K, seed=N)
+    y = torch.empty(N, device="cuda")
+    seg = (T.GemvSegment * 1)(T.GemvSegment(dw.data_ptr(), N, y.data_ptr(), None))
+    T.call("tb_gemv_q8_0_multi", T.ptr(x), K, None, 0.0, ctypes.cast(seg, ctypes.c_void_p), 1, S())
+    assert_dot_tol(host(y).reshape(1, N), xh.reshape(1, K), wq, K)
+    if N < 32768:  # tb_matmul_quant's M = 1 path below the tensor-core size is the same kernel
+        y2 = torch.empty(N, device="cuda")
+        T.call("tb_matmul_quant", T.Q8_0, T.ptr(x), 1, K, T.ptr(dw), N, T.ptr(y2), S())
+        assert_bits(host(y2), host(y))
+
+
+def test_prefetch_l2_is_only_a_hint():
+    K, N = 2048, 4096
+    xh = synth.normal((K,), 1.0, seed=77)
+    x = dev(xh)
+    wq, dw = _q8_dev(N, K, seed=78)
+    y0, y1 = torch.empty(N, device="cuda"), torch.empty(N, device="cuda")
+    T.call("tb_matmul_quant", T.Q8_0, T.ptr(x), 1, K, T.ptr(dw), N, T.ptr(y0), S())
+    # ranges trimmed inward to 16 bytes (an unaligned start, a ragged end, one
+    # range shorter than 16 bytes, a null pointer) are accepted
+    base = dw.data_ptr()
+    ptrs = (ctypes.c_void_p * 4)(base + 3, base, base + 5, None)
+    sizes = (ctypes.c_int64 * 4)(dw.numel() - 3, 1000, 7, 64)
+    T.call("tb_prefetch_l2", ctypes.cast(ptrs, ctypes.c_void_p), ctypes.cast(sizes, ctypes.c_void_p), 4, S())
+    T.call("tb_prefetch_l2", None, None, 0, S())
+    T.call("tb_matmul_quant", T.Q8_0, T.ptr(x), 1, K, T.ptr(dw), N, T.ptr(y1), S())
+    assert_bits(host(y1), host(y0))
+    ptrs9 = (ctypes.c_void_p * 9)(*([base] * 9))
+    sizes9 = (ctypes.c_int64 * 9)(*([64] * 9))
+    with pytest.raises(T.TbError) as e:
+        T.call("tb_prefetch_l2", ctypes.cast(ptrs9, ctypes.c_void_p), ctypes.cast(sizes9, ctypes.c_void_p), 9, S())
+    assert e.value.status == T.EINVAL
+
+
+@pytest.mark.parametrize("K,N", [(2048, 3072), (8192, 2048), (16384, 600)])
+def test_gemv_multi_with_rmsnorm_within_tolerance(K, N):
+    # K = 8192 and 16384 take the split-K form (x normalised while loaded
+    # into registers, one or two passes per warp)
     xh = synth.normal((K,), 1.0, seed=50)
     g = synth.uniform((K,), 0.5, 1.5, seed=51)
     wq, dw = _q8_dev(N, K, seed=52)
@@ -835,3 +879,43 @@ def test_rope_kv_append_equals_separate_ops():
     for a, b in ((q1, q2), (k1, k2), (kc1, kc2), (vc1, vc2)):
         assert_bits(host(a), host(b))
     assert T.take_device_errors() == 0
+
+
+@pytest.mark.parametrize("p", [0, 1, 300, 1023])
+def test_rope_attention_decode_equals_separate_ops(p):
+    # tb_rope_attention_decode == tb_rope_kv_append then tb_attention_decode,
+    # bit for bit: the output and both caches (the prefix rows random, so the
+    # new row is not the only one that counts); q, k, v are left unchanged
+    H, KVH, D, max_seq = 32, 8, 64, 1024
+    c, s_ = O.rope_tables(D, max_seq, 500000.0)
+    dc, ds = dev(c), dev(s_)
+    qh = synth.normal((H * D,), 1.0, seed=60 + p)
+    kh = synth.normal((KVH * D,), 1.0, seed=61 + p)
+    vh = synth.normal((KVH * D,), 1.0, seed=62 + p)
+    prefix_k = synth.normal((max_seq * KVH * D,), 1.0, seed=63)
+    prefix_v = synth.normal((max_seq * KVH * D,), 1.0, seed=64)
+    pos = _pos(p)
+    scale = 1.0 / 8.0
+    q1, k1, v1 = dev(qh), dev(kh), dev(vh)
+    kc1, vc1 = dev(prefix_k), dev(prefix_v)
+    out1 = torch.empty(H * D, device="cuda")
+    T.call("tb_rope_kv_append", T.ptr(q1), T.ptr(k1), T.ptr(v1), H, KVH, D, T.ptr(dc), T.ptr(ds), max_seq,
+           T.ptr(kc1), T.ptr(vc1), max_seq, T.ptr(pos), S())
+    T.call("tb_attention_decode", T.ptr(q1), T.ptr(kc1), T.ptr(vc1), H, KVH, D, max_seq, scale, T.ptr(pos),
+           T.ptr(out1), S())
+    q2, k2, v2 = dev(qh), dev(kh), dev(vh)
+    kc2, vc2 = dev(prefix_k), dev(prefix_v)
+    out2 = torch.empty(H * D, device="cuda")
+    T.call("tb_rope_attention_decode", T.ptr(q2), T.ptr(k2), T.ptr(v2), H, KVH, D, T.ptr(dc), T.ptr(ds), max_seq,
+           T.ptr(kc2), T.ptr(vc2), max_seq, scale, T.ptr(pos), T.ptr(out2), S())
+    for a, b in ((out1, out2), (kc1, kc2), (vc1, vc2)):
+        assert_bits(host(a), host(b))
+    for t, h_ in ((q2, qh), (k2, kh), (v2, vh)):
+        assert_bits(host(t), h_)
+    assert T.take_device_errors() == 0
+    # a position outside the RoPE table is refused on the device: error bit, caches untouched
+    bad = _pos(max_seq)
+    T.call("tb_rope_attention_decode", T.ptr(q2), T.ptr(k2), T.ptr(v2), H, KVH, D, T.ptr(dc), T.ptr(ds), max_seq,
+           T.ptr(kc2), T.ptr(vc2), max_seq, scale, T.ptr(bad), T.ptr(out2), S())
+    assert T.take_device_errors() & 2
+    assert_bits(host(kc2), host(kc1))

@@ -5,6 +5,9 @@
 //                        (attention.cpp:66-84 with S = 1: Kc.slice(pos).copy_(K))
 //   tb_attention_decode  all query heads of one token against the cache
 //                        (attention.cpp:104-141 with S = 1, fused per head)
+//   tb_rope_attention_decode  the same with RoPE of q and k and the cache
+//                        append of k and v fused in (one launch for
+//                        attention.cpp:50-141 at S = 1)
 //   tb_decode_margin     top-1 minus top-2 logit (a diagnostic for callers)
 //   tb_decode_advance    next token id, history, pos += 1
 // plus stream and graph handles for callers without the CUDA runtime.
@@ -57,23 +60,60 @@ __global__ void kv_append_kernel(float *__restrict__ kc, float *__restrict__ vc,
 //   out[d]   = sum over c of p[c] * V[c][d]: per CTA four consecutive ranges
 //              of its keys, each an fma chain, then the CTAs' partials added
 //              in cluster-rank order by rank 0
-template <int D, int NC>
-__global__ void __launch_bounds__(256) attention_decode_kernel(
-    const float *__restrict__ q, const float *__restrict__ kc, const float *__restrict__ vc, int H, int KVH,
-    int max_seq, float scale, const int32_t *__restrict__ pos_dev, float *__restrict__ out,
-    uint32_t *__restrict__ err) {
+// fma chain over d of q[d] * k[d] (the fp32 matmul's order); k from global
+// memory through the read-only path, or from shared memory
+template <int D, bool GLOBAL>
+__device__ __forceinline__ float qk_dot(const float *qs, const float4 *kr) {
+  float acc = 0.f;
+#pragma unroll
+  for (int d4 = 0; d4 < D / 4; ++d4) {
+    const float4 kv = GLOBAL ? __ldg(kr + d4) : kr[d4];
+    acc = __fmaf_rn(qs[4 * d4 + 0], kv.x, acc);
+    acc = __fmaf_rn(qs[4 * d4 + 1], kv.y, acc);
+    acc = __fmaf_rn(qs[4 * d4 + 2], kv.z, acc);
+    acc = __fmaf_rn(qs[4 * d4 + 3], kv.w, acc);
+  }
+  return acc;
+}
+
+struct AttnArgs {
+  const float *q;      // [H, D]
+  const float *kc;     // key cache [max_seq, KVH, D]
+  const float *vc;     // value cache
+  float *kc_w, *vc_w;  // ROPE: the caches again, for the append
+  const float *k_new;  // ROPE: this token's keys [KVH, D] before RoPE
+  const float *v_new;  // ROPE: this token's values [KVH, D]
+  const float *cos_t, *sin_t;  // ROPE: [rope_max_seq, D / 2]
+  int rope_max_seq;
+  int H, KVH, max_seq;
+  float scale;
+  const int32_t *pos_dev;
+  float *out;  // [H, D]
+};
+
+// ROPE: RoPE of q and of the new key at pos (tb_rope_at's arithmetic) and the
+// cache append of this token's key and value, fused in: each cluster rotates
+// its query head and its key/value head's new key itself, uses the new key and
+// value from shared memory for position pos, and the first cluster of each
+// key/value group (rank 0) writes them into the caches.  No cluster reads the
+// cache row pos, so the writes race with nothing.
+template <int D, int NC, bool ROPE>
+__global__ void __launch_bounds__(256) attention_decode_kernel(const AttnArgs a, uint32_t *__restrict__ err) {
   extern __shared__ float sc[];  // this CTA's scores, ceil(max_seq / NC) floats
   __shared__ float qs[D];
+  __shared__ float kn[ROPE ? D : 1], vn[ROPE ? D : 1];  // the new key (rotated) and value
   __shared__ float red[8];
   __shared__ float part[2];           // this CTA's [max, sum]
   __shared__ float pv[256 / D][D];    // partial outputs of the four key ranges
   __shared__ float octa[D];           // this CTA's partial output
   cg::cluster_group cluster = cg::this_cluster();
   const int cr = (int)cluster.block_rank();
+  const int H = a.H, KVH = a.KVH;
   const int h = blockIdx.x / NC;
   const int kvh = h / (H / KVH);
-  const int pos = *pos_dev;
-  if (pos < 0 || pos >= max_seq) {  // every CTA of the cluster leaves here together
+  pdl_launch_dependents();
+  const int pos = *a.pos_dev;
+  if (pos < 0 || pos >= a.max_seq || (ROPE && pos >= a.rope_max_seq)) {  // the cluster leaves together
     if (blockIdx.x == 0 && threadIdx.x == 0) atomicOr(err, ERR_INDEX);
     return;
   }
@@ -81,23 +121,38 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(
   const int chunk = (ctx + NC - 1) / NC;
   const int c0 = min(ctx, cr * chunk), c1 = min(ctx, c0 + chunk);
   const int rs = KVH * D;  // cache row stride (floats)
-  if (threadIdx.x < D) qs[threadIdx.x] = q[h * D + threadIdx.x];
-  __syncthreads();
+  if (ROPE) {
+    constexpr int half = D / 2;
+    const int t = threadIdx.x;
+    if (t < 2 * half) {
+      const bool isq = t < half;
+      const int i = isq ? t : t - half;
+      const float *src = isq ? a.q + h * D : a.k_new + kvh * D;
+      float *dst = isq ? qs : kn;
+      const float c = __ldg(a.cos_t + (int64_t)pos * half + i), s = __ldg(a.sin_t + (int64_t)pos * half + i);
+      const float x0 = src[i], x1 = src[i + half];
+      dst[i] = __fmaf_rn(x0, c, -__fmul_rn(x1, s));
+      dst[i + half] = __fmaf_rn(x0, s, __fmul_rn(x1, c));
+    } else if (t < 2 * half + D) {
+      vn[t - 2 * half] = a.v_new[kvh * D + t - 2 * half];
+    }
+    __syncthreads();
+    if (h % (H / KVH) == 0 && cr == 0 && threadIdx.x < D) {
+      a.kc_w[(int64_t)pos * rs + kvh * D + threadIdx.x] = kn[threadIdx.x];
+      a.vc_w[(int64_t)pos * rs + kvh * D + threadIdx.x] = vn[threadIdx.x];
+    }
+  } else {
+    if (threadIdx.x < D) qs[threadIdx.x] = a.q[h * D + threadIdx.x];
+    __syncthreads();
+  }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   float m = -INFINITY;
   for (int c = c0 + threadIdx.x; c < c1; c += 256) {
-    const float4 *kr = reinterpret_cast<const float4 *>(kc + (int64_t)c * rs + kvh * D);
-    float acc = 0.f;
-#pragma unroll
-    for (int d4 = 0; d4 < D / 4; ++d4) {
-      const float4 kv = __ldg(kr + d4);
-      acc = __fmaf_rn(qs[4 * d4 + 0], kv.x, acc);
-      acc = __fmaf_rn(qs[4 * d4 + 1], kv.y, acc);
-      acc = __fmaf_rn(qs[4 * d4 + 2], kv.z, acc);
-      acc = __fmaf_rn(qs[4 * d4 + 3], kv.w, acc);
-    }
-    const float s = __fmul_rn(acc, scale);
+    const float acc = (ROPE && c == pos)
+                          ? qk_dot<D, false>(qs, reinterpret_cast<const float4 *>(kn))
+                          : qk_dot<D, true>(qs, reinterpret_cast<const float4 *>(a.kc + (int64_t)c * rs + kvh * D));
+    const float s = __fmul_rn(acc, a.scale);
     sc[c - c0] = s;
     m = s > m ? s : m;
   }
@@ -136,9 +191,12 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(
   const int d = threadIdx.x % D, ch = threadIdx.x / D;
   const int n = c1 - c0, len = (n + NCH - 1) / NCH;
   const int a0 = c0 + ch * len, a1 = min(c1, a0 + len);
-  const float *vcol = vc + kvh * D + d;
+  const float *vcol = a.vc + kvh * D + d;
   float acc = 0.f;
-  for (int c = a0; c < a1; ++c) acc = __fmaf_rn(__fmul_rn(sc[c - c0], inv), __ldg(vcol + (int64_t)c * rs), acc);
+  for (int c = a0; c < a1; ++c) {
+    const float v = (ROPE && c == pos) ? vn[d] : __ldg(vcol + (int64_t)c * rs);
+    acc = __fmaf_rn(__fmul_rn(sc[c - c0], inv), v, acc);
+  }
   pv[ch][d] = acc;
   __syncthreads();
   if (threadIdx.x < D) {
@@ -150,9 +208,40 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(
   if (cr == 0 && threadIdx.x < D) {
     float o = octa[threadIdx.x];
     for (int r = 1; r < NC; ++r) o = __fadd_rn(o, *cluster.map_shared_rank(&octa[threadIdx.x], r));
-    out[h * D + threadIdx.x] = o;
+    a.out[h * D + threadIdx.x] = o;
   }
   cluster.sync();  // peers' shared memory stays alive until rank 0 has read it
+}
+
+template <bool ROPE>
+tb_status launch_attention(const AttnArgs &a, const char *who, cudaStream_t s) {
+  constexpr int NC = 8;  // CTAs per head (a portable cluster)
+  const size_t smem = (size_t)((a.max_seq + NC - 1) / NC) * sizeof(float);
+  if (smem > 200 * 1024) return fail(TB_EINVAL, "%s: cache of %d rows too long", who, a.max_seq);
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  auto kern = attention_decode_kernel<64, NC, ROPE>;
+  TB_TRY(ensure_smem_for(kern, smem));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(a.H * NC), 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  // No programmatic serialization for this launch: the clusters would then be
+  // launched while the preceding GEMV's CTAs still hold the SMs, and waiting
+  // for eight co-resident CTAs per GPC cost more than it saved (measured on
+  // the 1B decode: 1282 against 1377 tokens/s).  The kernel still lets the
+  // next kernel launch early (griddepcontrol.launch_dependents).
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = NC;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, st->err_word);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "%s: %s", who, cudaGetErrorString(e));
+  return check_launch(who);
 }
 
 // margins[pos] = logits[idx] - (largest other logit; NaN never counts)
@@ -214,29 +303,52 @@ tb_status tb_attention_decode(const float *q, const float *k_cache, const float 
   if (!q || !k_cache || !v_cache || !pos_dev || !out) return fail(TB_EINVAL, "tb_attention_decode: null pointer");
   if ((reinterpret_cast<uintptr_t>(k_cache) & 15) != 0)
     return fail(TB_EINVAL, "tb_attention_decode: the key cache must be 16-byte aligned");
-  constexpr int NC = 8;  // CTAs per head (a portable cluster)
-  const size_t smem = (size_t)((max_seq + NC - 1) / NC) * sizeof(float);
-  if (smem > 200 * 1024) return fail(TB_EINVAL, "tb_attention_decode: cache of %lld rows too long", (long long)max_seq);
-  DeviceState *st;
-  TB_TRY(device_state(&st));
-  auto kern = attention_decode_kernel<64, NC>;
-  TB_TRY(ensure_smem_for(kern, smem));
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(heads * NC), 1, 1);
-  cfg.blockDim = dim3(256, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = as_stream(stream);
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = NC;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, q, k_cache, v_cache, (int)heads, (int)kv_heads, (int)max_seq, scale,
-                                     pos_dev, out, st->err_word);
-  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_attention_decode: %s", cudaGetErrorString(e));
-  return check_launch("tb_attention_decode");
+  if (max_seq > 0x7FFFFFFF || heads > 4096) return fail(TB_EINVAL, "tb_attention_decode: extents too large");
+  AttnArgs a = {};
+  a.q = q;
+  a.kc = k_cache;
+  a.vc = v_cache;
+  a.H = (int)heads;
+  a.KVH = (int)kv_heads;
+  a.max_seq = (int)max_seq;
+  a.scale = scale;
+  a.pos_dev = pos_dev;
+  a.out = out;
+  return launch_attention<false>(a, "tb_attention_decode", as_stream(stream));
+}
+
+tb_status tb_rope_attention_decode(const float *q, const float *k, const float *v, int64_t heads, int64_t kv_heads,
+                                   int64_t head_dim, const float *cos_dev, const float *sin_dev,
+                                   int64_t rope_max_seq, float *k_cache, float *v_cache, int64_t max_seq,
+                                   float scale, const int32_t *pos_dev, float *out, tb_stream stream) {
+  if (heads <= 0 || kv_heads <= 0 || heads % kv_heads != 0 || max_seq <= 0 || rope_max_seq <= 0)
+    return fail(TB_EINVAL, "tb_rope_attention_decode: heads must be a positive multiple of kv_heads");
+  if (head_dim != 64)
+    return fail(TB_EINVAL, "tb_rope_attention_decode: head_dim %lld (64 supported)", (long long)head_dim);
+  if (!q || !k || !v || !cos_dev || !sin_dev || !k_cache || !v_cache || !pos_dev || !out)
+    return fail(TB_EINVAL, "tb_rope_attention_decode: null pointer");
+  if ((reinterpret_cast<uintptr_t>(k_cache) & 15) != 0)
+    return fail(TB_EINVAL, "tb_rope_attention_decode: the key cache must be 16-byte aligned");
+  if (max_seq > 0x7FFFFFFF || rope_max_seq > 0x7FFFFFFF || heads > 4096)
+    return fail(TB_EINVAL, "tb_rope_attention_decode: extents too large");
+  AttnArgs a = {};
+  a.q = q;
+  a.kc = k_cache;
+  a.vc = v_cache;
+  a.kc_w = k_cache;
+  a.vc_w = v_cache;
+  a.k_new = k;
+  a.v_new = v;
+  a.cos_t = cos_dev;
+  a.sin_t = sin_dev;
+  a.rope_max_seq = (int)rope_max_seq;
+  a.H = (int)heads;
+  a.KVH = (int)kv_heads;
+  a.max_seq = (int)max_seq;
+  a.scale = scale;
+  a.pos_dev = pos_dev;
+  a.out = out;
+  return launch_attention<true>(a, "tb_rope_attention_decode", as_stream(stream));
 }
 
 tb_status tb_decode_margin(const float *logits, int64_t vocab, const int64_t *idx_dev, const int32_t *pos_dev,

@@ -7,6 +7,7 @@
 //   tb_gemv_q8_0_swiglu   RMSNorm(x) * gamma (optional), then silu(G x) * (U x)
 //   tb_rope_kv_append     RoPE of q and k at the device-held position and the
 //                         key/value cache append, in one launch
+//   tb_prefetch_l2        background L2 fills of weights a later kernel reads
 // All of them, and tb_matmul_quant's default M = 1 Q8_0 path below the LM-head
 // size, run gemv_stream_kernel (below); the fused prologue and epilogue use the
 // formulas of tb_rmsnorm, tb_binary(add) and tb_swiglu, so a fused step differs
@@ -40,11 +41,11 @@ struct FusedArgs {
 // SWIGLU: the gate rows and the up rows of the same indices).  Spans stream
 // through `slots` shared-memory buffers, one bulk copy per span and segment and
 // one mbarrier per buffer; when every span of the CTA fits (the common decode
-// case) all copies are in flight from the first instruction, otherwise the
-// last warp to finish a span refills its buffer with the span `slots` ahead.
+// case) all copies are in flight once x is staged, otherwise the last warp to
+// finish a span refills its buffer with the span `slots` ahead.
 // Small CTAs, four per SM, so that rows are spread finely over the GPU and the
 // warps' issue slots, not one CTA's latency chain, bound the compute.
-// Programmatic dependent launch: the weight copies are issued before
+// Programmatic dependent launch: the first span's copy is issued before
 // griddepcontrol.wait (weights never depend on the previous kernel).
 // SWIGLU: segment 0 = gate, segment 1 = up (same rows), y[0] = silu(g) * u.
 template <bool NORM, bool SWIGLU>
@@ -98,6 +99,23 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 4) gemv_stream_kernel(const
       }
     }
   };
+  // logical row r's output: y[r] of its segment, plus the segment's residual
+  auto store = [&](int r, float v) {
+    int i = r;
+    float *y = a.y[0];
+    const float *res = a.res[0];
+    if (a.nseg > 1 && i >= a.n[0]) {
+      i -= a.n[0];
+      y = a.y[1];
+      res = a.res[1];
+      if (a.nseg > 2 && i >= a.n[1]) {
+        i -= a.n[1];
+        y = a.y[2];
+        res = a.res[2];
+      }
+    }
+    y[i] = res ? __fadd_rn(res[i], v) : v;
+  };
   if (threadIdx.x == 0) {
     for (int i = 0; i < slots; ++i) {
       mbar_init(full + i, 1);
@@ -105,7 +123,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 4) gemv_stream_kernel(const
     }
     abort_flag = 0;
     fence_mbar_init();
-    for (int k = 0; k < slots && k < nspans; ++k) issue(k);
+    if (nspans > 0) issue(0);  // the rest after x is staged (below)
   }
   pdl_launch_dependents();
   if (SWIGLU) exp_cr_table_init(tab);  // visible after the barrier below
@@ -148,6 +166,11 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 4) gemv_stream_kernel(const
     xs[((i + 3) & 31) * XS + ((i + 3) >> 5)] = v.w;
   }
   __syncthreads();
+  // Span 0 went out before griddepcontrol.wait; the other buffers are filled
+  // only now, so that the loads of x above do not queue behind a CTA's whole
+  // weight range (measured: 6.4 us against 6.8-7.1 us per 8192 x 2048 GEMV).
+  if (threadIdx.x == 0)
+    for (int k = 1; k < slots && k < nspans; ++k) issue(k);
   float2 xp[32];
   if (nb <= 64) q8_pair_x(xp, xs, XS, 2 * lane, 2 * lane < nb);
 
@@ -169,22 +192,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 4) gemv_stream_kernel(const
         if (lane == 0) a.y[0][r] = swiglu_f32(g, u, tab);
       } else {
         const float v = q8_row_dot_pairs(wrow, nb, xp, xs, XS, lane);
-        if (lane == 0) {
-          int i = r;
-          float *y = a.y[0];
-          const float *res = a.res[0];
-          if (a.nseg > 1 && i >= a.n[0]) {
-            i -= a.n[0];
-            y = a.y[1];
-            res = a.res[1];
-            if (a.nseg > 2 && i >= a.n[1]) {
-              i -= a.n[1];
-              y = a.y[2];
-              res = a.res[2];
-            }
-          }
-          y[i] = res ? __fadd_rn(res[i], v) : v;
-        }
+        if (lane == 0) store(r, v);
       }
       // With a ring (nspans > slots), the last of the span's nr warps refills
       // the slot with span k + slots.  Only warps that waited for this span
@@ -275,6 +283,30 @@ tb_status launch_stream_gemv(const float *x, int64_t K, const void *w, int64_t N
 }
 
 namespace {
+
+struct PrefetchRanges {
+  const uint8_t *p[8];
+  int64_t n[8];  // bytes, multiples of 16
+  int count;
+};
+
+// One warp: lane i issues the 1 MiB chunks i, i + 32, ... of the ranges in
+// turn; the L2 fills continue after the kernel exits.  griddepcontrol.wait at
+// the end makes this kernel's completion imply its predecessor's, so the next
+// kernel's own wait still orders it after every earlier kernel.
+__global__ void __launch_bounds__(32) prefetch_l2_kernel(const PrefetchRanges r) {
+  pdl_launch_dependents();
+  constexpr int64_t kChunk = 1 << 20;
+  for (int i = 0; i < r.count; ++i) {
+    const int64_t chunks = (r.n[i] + kChunk - 1) / kChunk;
+    for (int64_t c = threadIdx.x; c < chunks; c += 32) {
+      const int64_t off = c * kChunk;
+      const uint32_t len = (uint32_t)(r.n[i] - off < kChunk ? r.n[i] - off : kChunk);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(r.p[i] + off), "r"(len) : "memory");
+    }
+  }
+  pdl_wait();
+}
 
 tb_status check_gemv_input(const float *x, int64_t K, const float *gamma, const void *w, const char *who) {
   if (K <= 0 || K % 32 != 0 || K > 65536) return fail(TB_EINVAL, "%s: K=%lld must be a positive multiple of 32", who, (long long)K);
@@ -373,6 +405,35 @@ tb_status tb_gemv_q8_0_swiglu(const float *x, int64_t K, const float *gamma, flo
   TB_TRY(device_state(&st));
   cudaStream_t s = as_stream(stream);
   return gamma ? launch_stream<true, true>(a, (int)n, s, st) : launch_stream<false, true>(a, (int)n, s, st);
+}
+
+tb_status tb_prefetch_l2(const void *const *ptrs, const int64_t *bytes, int n, tb_stream stream) {
+  if (n < 0 || n > 8 || (n > 0 && (!ptrs || !bytes))) return fail(TB_EINVAL, "tb_prefetch_l2: 0 to 8 ranges");
+  PrefetchRanges r = {};
+  for (int i = 0; i < n; ++i) {
+    if (bytes[i] < 0) return fail(TB_EINVAL, "tb_prefetch_l2: negative size");
+    const uintptr_t a = reinterpret_cast<uintptr_t>(ptrs[i]);
+    const uintptr_t lo = (a + 15) & ~uintptr_t(15), hi = (a + (uintptr_t)bytes[i]) & ~uintptr_t(15);
+    if (!ptrs[i] || hi <= lo) continue;
+    r.p[r.count] = reinterpret_cast<const uint8_t *>(lo);
+    r.n[r.count] = (int64_t)(hi - lo);
+    ++r.count;
+  }
+  if (r.count == 0) return TB_OK;
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, 1, 1);
+  cfg.blockDim = dim3(32, 1, 1);
+  cfg.stream = as_stream(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, prefetch_l2_kernel, r);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_prefetch_l2: %s", cudaGetErrorString(e));
+  return TB_OK;
 }
 
 tb_status tb_rope_kv_append(float *q, float *k, const float *v, int64_t heads, int64_t kv_heads, int64_t head_dim,

@@ -19,8 +19,8 @@ class KVCache;
 // single fused kernel (tb_attention_decode) instead of the per-head loop of
 // attention.cpp:104-141; its softmax sum and probability-times-V order differ
 // within the fp32 tolerance.  Unless the bit-identical matmul kernels are
-// selected (set_exact_matmul), a layer with Q8_0 projections runs as six
-// launches: RMSNorm + Q/K/V GEMVs, RoPE + cache append, attention, O GEMV +
+// selected (set_exact_matmul), a layer with Q8_0 projections runs as five
+// launches: RMSNorm + Q/K/V GEMVs, RoPE + cache append + attention, O GEMV +
 // residual, RMSNorm + gate/up GEMVs + SwiGLU, down GEMV + residual.
 class DecodeGraph {
  public:

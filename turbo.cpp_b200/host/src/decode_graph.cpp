@@ -142,11 +142,10 @@ void DecodeGraph::enqueue_step_fused() {
     tb_check(tb_gemv_q8_0_multi(x_, E, gptr(b.attention_norm), b.attention_norm.epsilon, qkv, 3, s));
     float *kc = static_cast<float *>(kv_.get_k_cache((int)l).device_ptr());
     float *vc = static_cast<float *>(kv_.get_v_cache((int)l).device_ptr());
-    tb_check(tb_rope_kv_append(q_, k_, v_, (int64_t)H_, (int64_t)KVH_, (int64_t)D_,
-                               static_cast<const float *>(a.rope.dev_cos->device_ptr()),
-                               static_cast<const float *>(a.rope.dev_sin->device_ptr()), (int64_t)a.rope.max_seq_len,
-                               kc, vc, max_seq_, pos_, s));
-    tb_check(tb_attention_decode(q_, kc, vc, (int64_t)H_, (int64_t)KVH_, (int64_t)D_, max_seq_, scale_, pos_, ctx_, s));
+    tb_check(tb_rope_attention_decode(q_, k_, v_, (int64_t)H_, (int64_t)KVH_, (int64_t)D_,
+                                      static_cast<const float *>(a.rope.dev_cos->device_ptr()),
+                                      static_cast<const float *>(a.rope.dev_sin->device_ptr()),
+                                      (int64_t)a.rope.max_seq_len, kc, vc, max_seq_, scale_, pos_, ctx_, s));
     tb_gemv_segment o = {wptr(a.o_proj), E, h_, x_};  // h = x + O ctx
     tb_check(tb_gemv_q8_0_multi(ctx_, E, nullptr, 0.f, &o, 1, s));
     tb_check(tb_gemv_q8_0_swiglu(h_, E, gptr(b.ffn_norm), b.ffn_norm.epsilon, wptr(b.ffn.gate_proj),

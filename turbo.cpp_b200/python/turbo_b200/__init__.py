@@ -91,6 +91,8 @@ SIGNATURES = {
     "tb_gemv_q8_0_multi": [_P, _I64, _P, _F, _P, _I, _P],
     "tb_gemv_q8_0_swiglu": [_P, _I64, _P, _F, _P, _P, _I64, _P, _P],
     "tb_rope_kv_append": [_P, _P, _P, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _I64, _P, _P],
+    "tb_prefetch_l2": [_P, _P, _I, _P],
+    "tb_rope_attention_decode": [_P, _P, _P, _I64, _I64, _I64, _P, _P, _I64, _P, _P, _I64, _F, _P, _P, _P],
 }
 
 

@@ -274,10 +274,18 @@ __global__ void __launch_bounds__(NT) softmax_cluster_kernel(
 // Many rows: one CTA per row, persistent over rows (grid = one CTA per SM).
 // Pass 1 reads the row once from HBM keeping a running (max, sum of exp) per
 // thread (the sum rescaled whenever the max grows), combined over the block;
-// pass 2 reads the row again -- from L2, which holds the rows in flight (one
-// 513 KB logits row per SM fits) -- and writes exp(x - M) * (1/S).  No
-// clusters and no shared-memory staging; HBM traffic is one read and one
-// write.  Rows must be 16-byte aligned (cols % 4 == 0).
+// pass 2 writes exp(x - M) * (1/S).  Between the passes the row stays on chip
+// as far as it fits: each thread keeps its first kRowRegF4 float4s in
+// registers (96 KB per CTA; eight would spill) and the next ones in shared memory (up
+// to the opt-in limit, ~226 KB; each thread stores and later reads only its
+// own float4s, so no barrier guards them); only the rest is read again, from
+// L2 (for a 513 KB logits row ~190 KB, ~28 MB for 148 rows in flight).  With
+// the whole row re-read from L2 (76 MB in flight) half of it came from HBM
+// again (ncu, [1024, 128256]: 771 MB read for 525 MB of logits; now 530 MB).
+// Filling the shared-memory tier by one bulk copy per row instead, single- or
+// double-buffered across rows, measured 2-6 % slower.  Every thread walks its
+// float4s i = t, t + T, t + 2T, ... in order in both passes, whichever tier
+// holds them.  Rows must be 16-byte aligned (cols % 4 == 0).
 __device__ __forceinline__ void online_add(float v, float &m, float &s) {
   if (v > m) {  // NaN never raises the maximum
     s = __fadd_rn(__fmul_rn(s, __expf(__fsub_rn(m, v))), 1.0f);
@@ -286,35 +294,60 @@ __device__ __forceinline__ void online_add(float v, float &m, float &s) {
     s = __fadd_rn(s, __expf(__fsub_rn(v, m)));
   }
 }
+__device__ __forceinline__ void online_add4(const float4 &v, float &m, float &s) {
+  online_add(v.x, m, s);
+  online_add(v.y, m, s);
+  online_add(v.z, m, s);
+  online_add(v.w, m, s);
+}
+
+constexpr int kRowRegF4 = 6;  // float4s per thread kept in registers between the passes
 
 __global__ void __launch_bounds__(1024, 1) softmax_rows_kernel(const float *__restrict__ x, float *__restrict__ y,
-                                                               int64_t rows, int64_t cols) {
+                                                               int64_t rows, int64_t cols, int stash_f4) {
+  extern __shared__ float4 stash[];  // [stash_f4], each thread's own elements only
   __shared__ float sm[32], ss[32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int T = blockDim.x;
   const int64_t n4 = cols >> 2;
+  const int64_t RG = min(n4, (int64_t)kRowRegF4 * T);  // [0, RG): registers
+  const int64_t SG = RG + min(n4 - RG, (int64_t)stash_f4);  // [RG, SG): shared memory; [SG, n4): L2
   for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
     const float4 *x4 = reinterpret_cast<const float4 *>(x + r * cols);
     float m = -INFINITY, s = 0.f;
-    int64_t i = threadIdx.x;
-    for (; i + 3 * (int64_t)blockDim.x < n4; i += 4 * (int64_t)blockDim.x) {
+    float4 reg[kRowRegF4];
+#pragma unroll
+    for (int u = 0; u < kRowRegF4; ++u) {
+      const int64_t i = threadIdx.x + (int64_t)u * T;
+      if (i < RG) reg[u] = __ldcg(x4 + i);
+    }
+#pragma unroll
+    for (int u = 0; u < kRowRegF4; ++u)
+      if (threadIdx.x + (int64_t)u * T < RG) online_add4(reg[u], m, s);
+    int64_t i = RG + threadIdx.x;
+    for (; i + 3 * (int64_t)T < SG; i += 4 * (int64_t)T) {
       float4 v[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) v[u] = __ldcg(x4 + i + u * (int64_t)blockDim.x);
+      for (int u = 0; u < 4; ++u) v[u] = __ldcg(x4 + i + u * (int64_t)T);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
-        online_add(v[u].x, m, s);
-        online_add(v[u].y, m, s);
-        online_add(v[u].z, m, s);
-        online_add(v[u].w, m, s);
+        stash[i - RG + u * (int64_t)T] = v[u];
+        online_add4(v[u], m, s);
       }
     }
-    for (; i < n4; i += blockDim.x) {
+    for (; i < SG; i += T) {
       const float4 v = __ldcg(x4 + i);
-      online_add(v.x, m, s);
-      online_add(v.y, m, s);
-      online_add(v.z, m, s);
-      online_add(v.w, m, s);
+      stash[i - RG] = v;
+      online_add4(v, m, s);
     }
+    for (; i + 3 * (int64_t)T < n4; i += 4 * (int64_t)T) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = __ldcg(x4 + i + u * (int64_t)T);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) online_add4(v[u], m, s);
+    }
+    for (; i < n4; i += T) online_add4(__ldcg(x4 + i), m, s);
     // combine (m, s) over the warp, then over the block, in a fixed order
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -345,15 +378,21 @@ __global__ void __launch_bounds__(1024, 1) softmax_rows_kernel(const float *__re
       v.w = __fmul_rn(__expf(__fsub_rn(v.w, M)), inv);
       return v;
     };
-    int64_t j = threadIdx.x;
-    for (; j + 3 * (int64_t)blockDim.x < n4; j += 4 * (int64_t)blockDim.x) {
+#pragma unroll
+    for (int u = 0; u < kRowRegF4; ++u) {
+      const int64_t j = threadIdx.x + (int64_t)u * T;
+      if (j < RG) __stcs(y4 + j, out(reg[u]));
+    }
+    for (int64_t j = RG + threadIdx.x; j < SG; j += T) __stcs(y4 + j, out(stash[j - RG]));
+    int64_t j = SG + threadIdx.x;
+    for (; j + 3 * (int64_t)T < n4; j += 4 * (int64_t)T) {
       float4 v[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) v[u] = __ldcg(x4 + j + u * (int64_t)blockDim.x);
+      for (int u = 0; u < 4; ++u) v[u] = __ldcg(x4 + j + u * (int64_t)T);
 #pragma unroll
-      for (int u = 0; u < 4; ++u) __stcs(y4 + j + u * (int64_t)blockDim.x, out(v[u]));
+      for (int u = 0; u < 4; ++u) __stcs(y4 + j + u * (int64_t)T, out(v[u]));
     }
-    for (; j < n4; j += blockDim.x) __stcs(y4 + j, out(__ldcg(x4 + j)));
+    for (; j < n4; j += T) __stcs(y4 + j, out(__ldcg(x4 + j)));
   }
 }
 
@@ -612,7 +651,12 @@ tb_status tb_softmax(const float *x, float *y, int64_t rows, int64_t cols, tb_st
   // second from L2)
   if (cols % 4 == 0 && rows >= st->sm_count && (reinterpret_cast<uintptr_t>(x) & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
-    softmax_rows_kernel<<<st->sm_count, 1024, 0, s>>>(x, y, rows, cols);
+    // shared memory for as much of a row as the SM allows, beyond the registers
+    const int64_t beyond = std::max<int64_t>(0, cols / 4 - (int64_t)kRowRegF4 * 1024);
+    const int stash_f4 = (int)std::min<int64_t>(beyond, (st->smem_optin - 1024) / 16);
+    const size_t smem = (size_t)stash_f4 * 16;
+    TB_TRY(ensure_smem_for(softmax_rows_kernel, smem));
+    softmax_rows_kernel<<<st->sm_count, 1024, smem, s>>>(x, y, rows, cols, stash_f4);
     return check_launch("tb_softmax");
   }
   if (rows * cs <= st->sm_count)  // few rows: wide CTAs shorten each row's critical path

@@ -159,6 +159,7 @@ def _cases(T, torch):
 
     rows_case("softmax", 1, 128256, "1x128256", "configs[0]: softmax logits[1,128256]")
     rows_case("softmax", 64, 128256, "64x128256", "sweep: softmax [64,128256]")
+    rows_case("softmax", 1024, 128256, "1024x128256", "sweep: softmax [1024,128256] (525 MB)")
     rows_case("softmax", 8192, 128256, "8192x128256", "large: softmax [8192,128256] (4.2 GB)")
     rows_case("argmax", 1, 128256, "1x128256", "configs[0]: argmax [1,128256]")
     rows_case("argmax", 64, 128256, "64x128256", "sweep: argmax [64,128256]")

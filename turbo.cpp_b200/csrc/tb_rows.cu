@@ -282,8 +282,10 @@ __global__ void __launch_bounds__(NT) softmax_cluster_kernel(
 // L2 (for a 513 KB logits row ~190 KB, ~28 MB for 148 rows in flight).  With
 // the whole row re-read from L2 (76 MB in flight) half of it came from HBM
 // again (ncu, [1024, 128256]: 771 MB read for 525 MB of logits; now 530 MB).
-// Filling the shared-memory tier by one bulk copy per row instead, single- or
-// double-buffered across rows, measured 2-6 % slower.  Every thread walks its
+// The register and shared-memory tiers are loaded evict-first (they are not
+// read again from memory), the L2 tier normally.  Filling the shared-memory
+// tier by one bulk copy per row instead, single- or double-buffered across
+// rows, measured 2-6 % slower.  Every thread walks its
 // float4s i = t, t + T, t + 2T, ... in order in both passes, whichever tier
 // holds them.  Rows must be 16-byte aligned (cols % 4 == 0).
 __device__ __forceinline__ void online_add(float v, float &m, float &s) {
@@ -319,7 +321,7 @@ __global__ void __launch_bounds__(1024, 1) softmax_rows_kernel(const float *__re
 #pragma unroll
     for (int u = 0; u < kRowRegF4; ++u) {
       const int64_t i = threadIdx.x + (int64_t)u * T;
-      if (i < RG) reg[u] = __ldcg(x4 + i);
+      if (i < RG) reg[u] = __ldcs(x4 + i);
     }
 #pragma unroll
     for (int u = 0; u < kRowRegF4; ++u)
@@ -328,7 +330,7 @@ __global__ void __launch_bounds__(1024, 1) softmax_rows_kernel(const float *__re
     for (; i + 3 * (int64_t)T < SG; i += 4 * (int64_t)T) {
       float4 v[4];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) v[u] = __ldcg(x4 + i + u * (int64_t)T);
+      for (int u = 0; u < 4; ++u) v[u] = __ldcs(x4 + i + u * (int64_t)T);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         stash[i - RG + u * (int64_t)T] = v[u];
@@ -336,7 +338,7 @@ __global__ void __launch_bounds__(1024, 1) softmax_rows_kernel(const float *__re
       }
     }
     for (; i < SG; i += T) {
-      const float4 v = __ldcg(x4 + i);
+      const float4 v = __ldcs(x4 + i);
       stash[i - RG] = v;
       online_add4(v, m, s);
     }

@@ -8,6 +8,8 @@ Each method has the meaning of the CUDA entry point of the same role:
   finish     tb_softmax_shard_finish: y = exp(x - M) / S
   keys       tb_argmax_shard_keys: the 64-bit candidate key, top bit flipped
   key_index  tb_argmax_key_index: the column of a winning key
+  gemv_q8_0  tb_matmul_quant(Q8_0, M = 1) on a rank's rows (the oracle's
+             reference-order product)
 The argmax key restates greedy_sample (src/core/sampler.cpp:13-26): only
 values > -inf that are not NaN are candidates, the first (lowest-column) maximum
 wins, +0.0 and -0.0 tie, and a row without candidates selects column 0.
@@ -58,3 +60,9 @@ class OracleShardOps:
         k = keys.numpy().view(np.uint64) ^ SIGN_FLIP
         idx = np.where(k == 0, 0, np.uint64(0xFFFFFFFF) - (k & np.uint64(0xFFFFFFFF))).astype(np.int64)
         return torch.from_numpy(idx)
+
+    def gemv_q8_0(self, x, w_rows, n, y):
+        from oracle import orbind as O
+        K = x.numel()
+        r = O.matmul_q8_0(x.numpy().reshape(1, K).astype(np.float32), w_rows.numpy(), n)
+        y.copy_(torch.from_numpy(np.asarray(r, np.float32).reshape(n)))

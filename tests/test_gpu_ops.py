@@ -334,10 +334,12 @@ def test_kv_cache_append_and_transpose_copy():
     assert_bits(host(dc2), cache)
 
 
-@pytest.mark.parametrize("shape", [(300, 200), (3, 100, 90), (64, 64), (2, 33, 70)])
+@pytest.mark.parametrize("shape", [(300, 200), (3, 100, 90), (64, 64), (2, 33, 70), (130, 258), (4, 66, 2050)])
 def test_contiguous_of_transpose_tiles_bit_exact(shape):
     # contiguous() of a view whose last two dims are swapped: the tiled
-    # transpose path (64x64 tiles when both extents reach 64, else 32x32)
+    # transpose path (64x64 tiles when both extents reach 64, else 32x32;
+    # 16-bit elements move as 32-bit pairs when every extent and offset is
+    # even, partial tiles included)
     *lead, R, C = shape
     n = int(np.prod(shape))
     src = synth.normal((n,), 1.0, seed=n)

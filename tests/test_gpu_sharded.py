@@ -1,7 +1,10 @@
-"""The vocab-sharded softmax/argmax over NCCL on two GPUs (one process per
-GPU), with the per-shard halves as the CUDA kernels: turbo_b200.sharded on
-[64, 128256] logits against the oracle's single-process results.  Skipped on
-machines with fewer than two GPUs."""
+"""The vocab-sharded softmax/argmax and the tensor-parallel Q8_0 GEMV over
+NCCL on two GPUs (one process per GPU), with the per-shard halves as the CUDA
+kernels: turbo_b200.sharded on [64, 128256] logits, a row-split 8192 x 2048
+GEMV and a vocab-split 128256 x 2048 LM head feeding the sharded argmax,
+against the oracle's single-process results.  Skipped on machines with fewer
+than two GPUs."""
+import ctypes
 import os
 import socket
 import sys
@@ -59,3 +62,51 @@ def _rank(rank, world, port, rows, vocab):
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_vocab_sharded_nccl_two_gpus():
     mp.start_processes(_rank, args=(2, _free_port(), 64, 128256), nprocs=2, join=True, start_method="spawn")
+
+
+def _tp_rank(rank, world, port):
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "turbo.cpp_b200", "python"))
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method="tcp://127.0.0.1:%d" % port, rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    try:
+        import turbo_b200 as T
+        from oracle import orbind as O
+        from turbo_b200 import synth
+        from turbo_b200.sharded import RowShardedGemv, VocabShardGroup
+        T.call("tb_init", rank)
+        N, K, V = 8192, 2048, 128256
+        wq = synth.quantize_q8_0(synth.normal((N, K), 0.02, seed=31))
+        xh = synth.normal((K,), 1.0, seed=32)
+        x = torch.from_numpy(xh).cuda()
+        tp = RowShardedGemv(N, K)
+        w_local = tp.local_rows(torch.from_numpy(wq.ravel())).cuda()
+        y = tp(x, w_local).cpu().numpy()
+        ref = O.matmul_q8_0(xh.reshape(1, K), wq, N)[0].astype(np.float64)
+        scale = np.abs(synth.dequantize_q8_0(wq, K)).astype(np.float64) @ np.abs(xh).astype(np.float64)
+        assert np.max(np.abs(y - ref) / scale) <= 1e-5
+        # vocab-split LM head -> sharded argmax == argmax of the full product on one GPU
+        wl = synth.quantize_q8_0(synth.normal((V, K), 0.02, seed=33))
+        g = VocabShardGroup(V)
+        rb = K // 32 * 34
+        mine = torch.from_numpy(wl.ravel()[g.col_base * rb:(g.col_base + g.cols) * rb].copy()).cuda()
+        logits = torch.empty((1, g.cols), dtype=torch.float32, device="cuda")
+        T.call("tb_matmul_quant", T.Q8_0, T.ptr(x), 1, K, T.ptr(mine), g.cols, T.ptr(logits),
+               ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        idx = int(g.argmax(logits)[0])
+        wl_d = torch.from_numpy(wl.ravel()).cuda()
+        full = torch.empty((1, V), dtype=torch.float32, device="cuda")
+        T.call("tb_matmul_quant", T.Q8_0, T.ptr(x), 1, K, T.ptr(wl_d), V, T.ptr(full),
+               ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert idx == O.argmax(full.cpu().numpy()[0])
+        assert T.take_device_errors() == 0
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_tensor_parallel_gemv_nccl_two_gpus():
+    mp.start_processes(_tp_rank, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")

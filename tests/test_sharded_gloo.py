@@ -77,7 +77,7 @@ def _rank_main(rank, world, port, rows, vocab, seed):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,vocab", [(2, 128256), (3, 1001)])
+@pytest.mark.parametrize("world,vocab", [(1, 1001), (2, 128256), (3, 1001)])
 def test_vocab_sharded_gloo(world, vocab):
     mp.start_processes(_rank_main, args=(world, _free_port(), 8, vocab, world), nprocs=world, join=True,
                        start_method="spawn")
@@ -109,3 +109,57 @@ def test_oracle_keys_match_greedy_sample():
         k = candidate_keys(x[r], 0).max()
         got = 0 if k == 0 else int(np.uint64(0xFFFFFFFF) - (k & np.uint64(0xFFFFFFFF)))
         assert got == R.greedy_sample(x[r]), r
+
+
+def _tp_rank_main(rank, world, port, n, k, vocab, seed):
+    # tensor-parallel GEMV (row split + all-gather) and the vocab-split LM head
+    # feeding the sharded argmax, with the per-rank products from the oracle
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "turbo.cpp_b200", "python"))
+    from oracle import orbind as O
+    from oracle.shard_ops import OracleShardOps
+    from turbo_b200 import synth
+    from turbo_b200.sharded import RowShardedGemv, VocabShardGroup
+    dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % port, rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60))
+    try:
+        ops = OracleShardOps()
+        wq = synth.quantize_q8_0(synth.normal((n, k), 0.02, seed=seed))
+        x = synth.normal((k,), 1.0, seed=seed + 1)
+        tp = RowShardedGemv(n, k, ops=ops)
+        w_local = tp.local_rows(torch.from_numpy(wq.ravel()))
+        y = tp(torch.from_numpy(x), w_local)
+        want = O.matmul_q8_0(x.reshape(1, k), wq, n)[0]
+        assert np.array_equal(y.numpy().view(np.uint32), want.view(np.uint32))  # the same per-row order
+        # LM head split by vocabulary rows: each rank's logits slice -> sharded argmax
+        wl = synth.quantize_q8_0(synth.normal((vocab, k), 0.02, seed=seed + 2))
+        g = VocabShardGroup(vocab, ops=ops)
+        rb = k // 32 * 34
+        mine = torch.from_numpy(wl.ravel()[g.col_base * rb:(g.col_base + g.cols) * rb].copy())
+        logits = torch.empty(g.cols, dtype=torch.float32)
+        ops.gemv_q8_0(torch.from_numpy(x), mine, g.cols, logits)
+        idx = int(g.argmax(logits.reshape(1, g.cols))[0])
+        full = O.matmul_q8_0(x.reshape(1, k), wl, vocab)[0]
+        assert idx == greedy(full)
+        dist.barrier()
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [1, 2, 3])
+def test_tensor_parallel_gemv_gloo(world):
+    mp.start_processes(_tp_rank_main, args=(world, _free_port(), 96 * world, 256, 1003, 11), nprocs=world,
+                       join=True, start_method="spawn")
+
+
+def test_tensor_parallel_gemv_checks_k():
+    from turbo_b200.sharded import RowShardedGemv
+    port = _free_port()
+    dist.init_process_group("gloo", init_method="tcp://127.0.0.1:%d" % port, rank=0, world_size=1,
+                            timeout=timedelta(seconds=30))
+    try:
+        RowShardedGemv(100, 256, ops=object())  # one rank: any row count divides
+        with pytest.raises(ValueError):
+            RowShardedGemv(100, 250, ops=object())
+    finally:
+        dist.destroy_process_group()

@@ -179,14 +179,18 @@ def _cases(T, torch):
 
     dequant_case(8192, 2048)
 
-    def quantize_case(M, K):
-        def make():
-            X = f32((M, K), 12)
-            Q = torch.empty(M * K // 32 * 34, dtype=torch.uint8, device=dev)
-            return (lambda i, s: T.load().tb_quantize_q8_0(T.ptr(X), M, K, T.ptr(Q), s)), (X, Q)
-        cases.append(Case("quantize_q8_0_512x8192", "configs[2]: X[512,8192] -> Q8_0", make, M * K * 4 + M * K // 32 * 34))
+    def quantize_case(M, K, cfg):
+        nbytes = M * K * 4 + M * K // 32 * 34
+        k = rot(nbytes)
 
-    quantize_case(512, 8192)
+        def make():
+            X = [f32((M, K), 12 + i) for i in range(k)]
+            Q = [torch.empty(M * K // 32 * 34, dtype=torch.uint8, device=dev) for _ in range(k)]
+            return (lambda i, s: T.load().tb_quantize_q8_0(T.ptr(X[i % k]), M, K, T.ptr(Q[i % k]), s)), (X, Q)
+        cases.append(Case("quantize_q8_0_%dx%d" % (M, K), cfg, make, nbytes))
+
+    quantize_case(512, 8192, "configs[2]: X[512,8192] -> Q8_0")
+    quantize_case(65536, 8192, "sweep: X[65536,8192] -> Q8_0 (2.1 GB in)")
 
     def embed_case(n, dim, vocab):
         def make():
@@ -301,19 +305,31 @@ def run(only=None, min_ms=20.0, out=None):
     return results
 
 
-def run_sharded(reps=20):
+def _rand_q8(torch, rows, K, seed):
+    """rows x K/32 random Q8_0 blocks on the device, every scale the finite
+    half 0x1419 (about 1e-3)."""
+    g = torch.Generator("cuda").manual_seed(seed)
+    w = torch.randint(0, 256, (rows * (K // 32), 34), dtype=torch.uint8, device="cuda", generator=g)
+    w[:, 0] = 0x19
+    w[:, 1] = 0x14
+    return w.reshape(-1)
+
+
+def run_sharded(reps=20, sizes=None):
     """The sharded sweep on every rank of a torch.distributed job (one GPU per
-    rank, NCCL): row-sharded ops on [262144, 4096] per rank (weak scaling, no
-    collective), and the vocab-sharded softmax and argmax of logits
+    rank, NCCL).  Row-sharded ops (add, row-vector mul, RMSNorm, SwiGLU,
+    contiguous() of a transposed slab) on [R, 4096] tensors of 1 MiB, 64 MiB,
+    1 GiB and 16 GiB in fp32 and bf16, the rows of each tensor split over the
+    ranks (no collective); then the vocab-sharded softmax and argmax of logits
     [64, 128256] split over the ranks (two float all-reduces / one int64
     all-reduce per call).  Time per call = max over ranks of the CUDA-event
-    time; GB/s = bytes moved by all ranks / that time.  Rank 0 prints one
-    JSON line per op."""
+    time; GB/s = bytes moved by all ranks / that time.  Rank 0 prints one JSON
+    line per op and size."""
     import torch
     import torch.distributed as dist
 
     import turbo_b200 as T
-    from .sharded import VocabShardGroup
+    from .sharded import VocabShardGroup, shard_range
 
     ws, rank = dist.get_world_size(), dist.get_rank()
     peak, kind = _peak()
@@ -344,30 +360,67 @@ def run_sharded(reps=20):
                               "GB_s": round(gbs, 1), "hbm_frac_per_gpu": round(gbs / ws / peak, 4),
                               "peak_GB_s": peak, "peak_source": kind, "timing": "max over ranks"}), flush=True)
 
-    R, C = 1 << 18, 4096  # rows per rank: 4 GiB per fp32 tensor
-    g = torch.Generator(dev).manual_seed(rank)
-    a = torch.randn((R, C), device=dev, generator=g)
-    b = torch.randn((R, C), device=dev, generator=g)
-    o = torch.empty_like(a)
-    va, vb, vo = T.view(a), T.view(b), T.view(o)
-    n = R * C
-    ms = timed(lambda: T.check(L.tb_binary(0, T.byref(va), T.byref(vb), T.byref(vo), sh)), 5)
-    report("add_f32", ms, 3 * 4 * n * ws, "[%d,%d] per rank, rows sharded" % (R, C))
-    row = torch.randn((C,), device=dev, generator=g)
-    vr = T.view(row)
-    ms = timed(lambda: T.check(L.tb_binary(1, T.byref(va), T.byref(vr), T.byref(vo), sh)), 5)
-    report("mul_rowvec_f32", ms, (2 * 4 * n + 4 * C) * ws, "[%d,%d] * [%d] per rank" % (R, C, C))
-    gam = torch.rand((C,), device=dev, generator=g) + 0.5
-    ms = timed(lambda: T.check(L.tb_rmsnorm(T.F32, T.ptr(a), T.ptr(gam), T.ptr(o), R, C, 1e-5, sh)), 5)
-    report("rmsnorm_f32", ms, (2 * 4 * n + 4 * C) * ws, "[%d,%d] per rank" % (R, C))
-    ms = timed(lambda: T.check(L.tb_swiglu(T.F32, T.ptr(a), T.ptr(b), T.ptr(o), n, sh)), 5)
-    report("swiglu_f32", ms, 3 * 4 * n * ws, "[%d,%d] per rank" % (R, C))
-    vt = T.view(b, 0, (C, R), (1, C))  # contiguous() of a transposed [R, C] slab
-    o2 = torch.empty((C, R), device=dev)
-    vo2 = T.view(o2)
-    ms = timed(lambda: T.check(L.tb_copy(T.byref(vo2), T.byref(vt), sh)), 5)
-    report("contiguous_transpose_f32", ms, 2 * 4 * n * ws, "[%d,%d]^T per rank" % (R, C))
-    del a, b, o, o2
+    C = 4096
+    sizes = sizes or [1 << 20, 1 << 26, 1 << 30, 1 << 34]  # bytes per tensor, whole job
+    for tdt, code, es, tag in ((torch.float32, T.F32, 4, "f32"), (torch.bfloat16, T.BF16, 2, "bf16")):
+        for total in sizes:
+            R_total = total // (C * es)
+            _, R = shard_range(R_total, ws, rank)
+            n_all = R_total * C
+            n = R * C
+            cfg = "[%d,%d] %s (%d MiB per tensor), rows split over %d ranks" % (R_total, C, tag, total >> 20, ws)
+            it = 200 if total <= (1 << 26) else (20 if total <= (1 << 30) else 5)
+            g = torch.Generator(dev).manual_seed(rank)
+            a = torch.randn((R, C), device=dev, generator=g).to(tdt)
+            b = torch.randn((R, C), device=dev, generator=g).to(tdt)
+            o = torch.empty_like(a)
+            va, vb, vo = T.view(a), T.view(b), T.view(o)
+            ms = timed(lambda: T.check(L.tb_binary(0, T.byref(va), T.byref(vb), T.byref(vo), sh)), it)
+            report("add_" + tag, ms, 3 * es * n_all, cfg)
+            row = torch.randn((C,), device=dev, generator=g).to(tdt)
+            vr = T.view(row)
+            ms = timed(lambda: T.check(L.tb_binary(1, T.byref(va), T.byref(vr), T.byref(vo), sh)), it)
+            report("mul_rowvec_" + tag, ms, 2 * es * n_all + es * C * ws, cfg)
+            gam = torch.rand((C,), device=dev, generator=g) + 0.5
+            ms = timed(lambda: T.check(L.tb_rmsnorm(code, T.ptr(a), T.ptr(gam), T.ptr(o), R, C, 1e-5, sh)), it)
+            report("rmsnorm_" + tag, ms, 2 * es * n_all + 4 * C * ws, cfg)
+            ms = timed(lambda: T.check(L.tb_swiglu(code, T.ptr(a), T.ptr(b), T.ptr(o), n, sh)), it)
+            report("swiglu_" + tag, ms, 3 * es * n_all, cfg)
+            vt = T.view(b, 0, (C, R), (1, C))  # contiguous() of a transposed [R, C] slab
+            o2 = torch.empty((C, R), device=dev, dtype=tdt)
+            vo2 = T.view(o2)
+            ms = timed(lambda: T.check(L.tb_copy(T.byref(vo2), T.byref(vt), sh)), it)
+            report("contiguous_transpose_" + tag, ms, 2 * es * n_all, cfg)
+            del a, b, o, o2, row, gam
+            torch.cuda.empty_cache()
+
+    # tensor-parallel Q8_0 GEMV (row split + all-gather of y) and the
+    # vocab-split LM head feeding the sharded argmax (no gather)
+    from .sharded import RowShardedGemv
+    for N, K in ((8192, 2048), (2048, 8192)):
+        tp = RowShardedGemv(N, K)
+        rb = K // 32 * 34
+        w_local = _rand_q8(torch, tp.rows, K, seed=40 + rank)
+        x = torch.randn(K, device=dev, generator=torch.Generator(dev).manual_seed(41))
+        y = torch.empty(N, dtype=torch.float32, device=dev)
+        ms = timed(lambda: tp(x, w_local, y), 200)
+        report("tp_gemv_q8_0_%dx%d" % (N, K), ms, N * rb + K * 4 * ws + N * 4,
+               "W[%d,%d] Q8_0 rows split over %d ranks, NCCL all-gather of y" % (N, K, ws))
+        del w_local
+    V, K = 128256, 2048
+    grp = VocabShardGroup(V)
+    w_local = _rand_q8(torch, grp.cols, K, seed=50 + rank)
+    x = torch.randn(K, device=dev, generator=torch.Generator(dev).manual_seed(51))
+    logits = torch.empty((1, grp.cols), dtype=torch.float32, device=dev)
+
+    def lm_head_argmax():
+        T.check(L.tb_matmul_quant(T.Q8_0, T.ptr(x), 1, K, T.ptr(w_local), grp.cols, T.ptr(logits), sh),
+                "tb_matmul_quant")
+        return grp.argmax(logits)
+    ms = timed(lm_head_argmax, 100)
+    report("tp_lm_head_argmax_%dx%d" % (V, K), ms, V * (K // 32 * 34) + K * 4 * ws + V * 4,
+           "LM head W[%d,%d] Q8_0 vocab rows split over %d ranks -> sharded argmax" % (V, K, ws))
+    del w_local
     torch.cuda.empty_cache()
 
     V, rows = 128256, 64

@@ -14,6 +14,12 @@ GPUs):
 
 The single-process forms these replace are Softmax::forward
 (src/nn/softmax.cpp:13-54) and greedy_sample (src/core/sampler.cpp:13-26).
+
+RowShardedGemv is the tensor-parallel Q8_0 GEMV: W's rows split over the ranks,
+each rank multiplying its rows with the full x (tb_matmul_quant) straight into
+its slot of the output, then one in-place all-gather of y.  Its vocab-split
+LM-head form (each rank's logits slice) feeds VocabShardGroup.argmax directly,
+with no gather.
 The per-shard operations are an object (`ops`) so the protocol can be driven by
 any implementation of them; the default is the CUDA kernels, and there is no
 other implementation in this package.
@@ -82,6 +88,13 @@ class DeviceShardOps:
                     "tb_argmax_key_index")
         return idx
 
+    def gemv_q8_0(self, x, w_rows, n, y):
+        """y[:n] = W_rows . x for n Q8_0 rows of K = x.numel() (tb_matmul_quant, M = 1)."""
+        from . import Q8_0
+        K = x.numel()
+        self._check(self.L.tb_matmul_quant(Q8_0, x.data_ptr(), 1, K, w_rows.data_ptr(), n, y.data_ptr(), self._s()),
+                    "tb_matmul_quant")
+
 
 class VocabShardGroup:
     """Softmax and argmax over logits whose columns are split across the ranks
@@ -111,6 +124,9 @@ class VocabShardGroup:
         if out is None:
             out = torch.empty_like(x)
         m, s = self.ops.stats(x, x.stride(0))
+        if self.world == 1:  # a group of one: the local statistics are the global ones
+            self.ops.finish(x, x.stride(0), m, s, out, out.stride(0))
+            return out
         gmax = m.clone()
         dist.all_reduce(gmax, op=dist.ReduceOp.MAX, group=self.group)
         self.ops.rescale(m, gmax, s)
@@ -123,5 +139,48 @@ class VocabShardGroup:
         same int64 tensor [rows] on every rank."""
         self._check_local(x)
         keys = self.ops.keys(x, x.stride(0), self.col_base)
-        dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=self.group)
+        if self.world > 1:
+            dist.all_reduce(keys, op=dist.ReduceOp.MAX, group=self.group)
         return self.ops.key_index(keys)
+
+
+class RowShardedGemv:
+    """Tensor-parallel Q8_0 GEMV y[N] = W[N, K] . x[K] over the ranks of a
+    torch.distributed group: rank r holds rows [r N/G, (r + 1) N/G) of W (its
+    Q8_0 blocks, contiguous) and the full x; it writes its rows straight into
+    its slot of y, then one in-place all-gather gives every rank the full y.
+    N must be a multiple of the world size (equal slots for the all-gather).
+    Every rank calls in the same order."""
+
+    def __init__(self, n, k, group=None, ops=None):
+        if not dist.is_initialized():
+            raise RuntimeError("RowShardedGemv needs an initialised torch.distributed process group")
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if n <= 0 or n % self.world != 0:
+            raise ValueError("rows %d must be a positive multiple of the world size %d" % (n, self.world))
+        if k <= 0 or k % 32 != 0:
+            raise ValueError("K=%d must be a positive multiple of 32" % k)
+        self.n, self.k = int(n), int(k)
+        self.rows = self.n // self.world
+        self.row_base = self.rank * self.rows
+        self.ops = ops if ops is not None else DeviceShardOps()
+
+    def local_rows(self, w_full_blocks):
+        """This rank's slice of W's Q8_0 bytes (N rows of K/32 34-byte blocks)."""
+        rb = self.k // 32 * 34
+        return w_full_blocks[self.row_base * rb:(self.row_base + self.rows) * rb]
+
+    def __call__(self, x, w_local, y=None):
+        if x.numel() != self.k:
+            raise ValueError("x must hold K=%d values" % self.k)
+        if w_local.numel() != self.rows * (self.k // 32) * 34:
+            raise ValueError("w_local must hold this rank's %d rows of Q8_0 blocks" % self.rows)
+        if y is None:
+            y = torch.empty(self.n, dtype=torch.float32, device=x.device)
+        slot = y[self.row_base:self.row_base + self.rows]
+        self.ops.gemv_q8_0(x, w_local, self.rows, slot)
+        if self.world > 1:
+            dist.all_gather_into_tensor(y, slot, group=self.group)
+        return y

@@ -187,6 +187,11 @@ tb_status tb_embedding(int dtype, const void *w_dev, int64_t dim, int64_t vocab,
  *  - dtype TB_Q4_0: X rows are first quantized to Q8_0 (tensor.cpp:413-421),
  *    bit for bit, then multiplied with the Q4_0 rows in the order of
  *    vec_dot_q4_0_q8_0_avx2 (quant_math.hpp:184-248).
+ *  - M >= 32 with K a multiple of 256 and 16-byte aligned X and W runs on the
+ *    tensor cores (both dtypes): exact per-block integer (Q4_0) or 22-bit
+ *    (Q8_0) products accumulated in fp32 tensor memory, block scales applied
+ *    in fp32 -- within 1e-5 of sum |w x| per output, typically ~1e-7; it
+ *    allocates stream-ordered scratch for the packed operands.
  * K must be a multiple of 32. */
 tb_status tb_matmul_quant(int dtype, const float *x_dev, int64_t M, int64_t K,
                           const void *w_dev, int64_t N, float *y_dev, tb_stream stream);

@@ -9,9 +9,9 @@ tb_status launch_q8_0(const float *x, int64_t M, int64_t K, const void *w, int64
                       bool exact, cudaStream_t s, const DeviceState *st);
 tb_status launch_q4_0_exact(const uint8_t *xq, int64_t M, int64_t K, const void *w, int64_t N,
                             float *y, cudaStream_t s, const DeviceState *st);
-bool gemm_tc_eligible(int64_t M, int64_t K, const float *x, const void *w);
-tb_status launch_gemm_tc(int dtype, const float *x, int64_t M, int64_t K, const void *w, int64_t N, float *y,
-                         cudaStream_t s, const DeviceState *st);
+bool gemm_f16_eligible(int64_t M, int64_t K, const float *x, const void *w);
+tb_status launch_gemm_f16(int dtype, const float *x, int64_t M, int64_t K, const void *w, int64_t N, float *y,
+                          cudaStream_t s, const DeviceState *st);
 }  // namespace tb
 
 using namespace tb;
@@ -30,8 +30,8 @@ tb_status matmul_quant(int dtype, const float *x, int64_t M, int64_t K, const vo
   DeviceState *st;
   TB_TRY(device_state(&st));
   cudaStream_t s = as_stream(stream);
-  // prefill-sized M: tcgen05 tensor cores (3xTF32, within 1e-5 of sum |w x|)
-  if (!exact && gemm_tc_eligible(M, K, x, w)) return launch_gemm_tc(dtype, x, M, K, w, N, y, s, st);
+  // prefill-sized M: tcgen05 tensor cores (within 1e-5 of sum |w x|)
+  if (!exact && gemm_f16_eligible(M, K, x, w)) return launch_gemm_f16(dtype, x, M, K, w, N, y, s, st);
   if (dtype == TB_Q8_0) return launch_q8_0(x, M, K, w, N, y, exact, s, st);
   // Q4_0: X rows -> Q8_0 (tensor.cpp:413-421) into stream-ordered scratch.
   size_t xq_bytes = (size_t)M * (size_t)(K / 32) * 34;

@@ -194,8 +194,8 @@ __global__ void __launch_bounds__(NW * 32) gemv_q8_0_kernel(
 }
 
 // ---------------------------------------------------------------------------
-// Span GEMV (M == 1), tb_matmul_quant_exact's path (EXACT = 1; the EXACT = 0
-// arithmetic is the tolerance form, kept for comparison).
+// Span GEMV (M == 1), tb_matmul_quant_exact's path: the reference's order bit
+// for bit.
 //
 // One CTA per SM owns a contiguous range of rows.  The range is cut into spans
 // that fit in shared memory; two span buffers are in flight, and each span is
@@ -214,7 +214,7 @@ struct SpanCfg {
   int span_rows;  // rows per span buffer
 };
 
-template <int NWARP, int EXACT>
+template <int NWARP>
 __global__ void __launch_bounds__(NWARP * 32, 1) gemv_q8_0_span_kernel(
     const uint8_t *__restrict__ W, const float *__restrict__ X, float *__restrict__ Y, int N,
     int K, int span_rows, uint32_t *__restrict__ err) {
@@ -226,8 +226,8 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gemv_q8_0_span_kernel(
   const int BP = (nb + 4) & ~3;
   uint64_t *bar = reinterpret_cast<uint64_t *>(smem);  // [2 buffers][4 quarters]
   float *xs = reinterpret_cast<float *>(smem + 256);
-  float *bsum = xs + 32 * XS;  // [span_rows][BP] (exact only)
-  uint8_t *buf0 = reinterpret_cast<uint8_t *>(bsum + (EXACT ? span_rows * BP : 0));
+  float *bsum = xs + 32 * XS;  // [span_rows][BP] block sums
+  uint8_t *buf0 = reinterpret_cast<uint8_t *>(bsum + span_rows * BP);
   buf0 = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(buf0) + 127) & ~uintptr_t(127));
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
 
@@ -315,7 +315,6 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gemv_q8_0_span_kernel(
         waited = q;
       }
       const uint8_t *wrow = sbuf + (size_t)r * rb;
-      float racc = 0.f;
       for (int p = 0; p * 64 < nb; ++p) {
         const int b1 = p * 64 + lane, b2 = b1 + 32;
         const bool v1 = b1 < nb, v2 = b2 < nb;
@@ -328,27 +327,7 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gemv_q8_0_span_kernel(
         uint32_t q1[8], q2[8];
         load_q8_block(wrow, 34 * (v1 ? b1 : 0), d1, q1);
         load_q8_block(wrow, 34 * (v2 ? b2 : 0), d2, q2);
-        if (!EXACT) {
-          // q as float without an int->float conversion: byte_perm builds the
-          // float 12582912 + (q + 128), an exact packed subtraction leaves q.
-          const uint64_t off2 = pack2(-(kMagic + 128.0f), -(kMagic + 128.0f));
-          uint64_t acc = pack2(0.f, 0.f);
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            const uint32_t u1 = q1[kk] ^ 0x80808080u, u2 = q2[kk] ^ 0x80808080u;
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const uint32_t sel = 0x7650u | (uint32_t)e;
-              const uint64_t m = pack2(__uint_as_float(__byte_perm(u1, kMagicHi, sel)),
-                                       __uint_as_float(__byte_perm(u2, kMagicHi, sel)));
-              acc = fma2(add2(m, off2), xp[4 * kk + e], acc);
-            }
-          }
-          float s1, s2;
-          unpack2(acc, s1, s2);
-          if (v1) racc = fmaf(s1, d1, racc);
-          if (v2) racc = fmaf(s2, d2, racc);
-        } else {
+        {
           float s1 = 0.f, s2 = 0.f;
           if (isfinite(d1) && isfinite(d2)) {
             const uint64_t dd = pack2(d1, d2);
@@ -385,15 +364,10 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gemv_q8_0_span_kernel(
           if (v2) bsum[r * BP + b2] = s2;
         }
       }
-      if (!EXACT) {
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) racc += __shfl_xor_sync(0xffffffffu, racc, o);
-        if (lane == 0) Y[n0 + r0 + r] = racc;
-      }
     }
-    __syncthreads();  // span buffer (and block sums) complete
+    __syncthreads();  // span buffer and block sums complete
     if (abort_flag) return;
-    if (EXACT) {
+    {
       // thread t adds the block sums of row t in block order (quant_math.hpp:56)
       for (int t = threadIdx.x; t < nr; t += NWARP * 32) {
         const float4 *b4 = reinterpret_cast<const float4 *>(bsum + t * BP);
@@ -413,28 +387,27 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gemv_q8_0_span_kernel(
   }
 }
 
-size_t span_smem_bytes(int K, int span_rows, bool exact) {
+size_t span_smem_bytes(int K, int span_rows) {
   const int nb = K / 32;
   const int XS = (nb & 1) ? nb + 2 : nb + 1;
   const int BP = (nb + 4) & ~3;
-  size_t s = 256 + (size_t)32 * XS * 4 + (exact ? (size_t)span_rows * BP * 4 : 0);
+  size_t s = 256 + (size_t)32 * XS * 4 + (size_t)span_rows * BP * 4;
   s = (s + 127) & ~size_t(127);
   // + slack: up to 127 bytes of alignment of the buffers, and the last block's
   // 9-word read may run 2 bytes past them
   return s + (size_t)2 * span_rows * nb * 34 + 256;
 }
 
-template <int EXACT>
-tb_status launch_span(const float *x, int64_t K, const void *w, int64_t N, float *y,
-                      cudaStream_t s, const DeviceState *st) {
+tb_status launch_span(const float *x, int64_t K, const void *w, int64_t N, float *y, cudaStream_t s,
+                      const DeviceState *st) {
   constexpr int NWARP = 16;
   const int grid = (int)std::min<int64_t>(N, st->sm_count);
   const int64_t rows_per_cta = (N + grid - 1) / grid;
   int sr = (int)((rows_per_cta + 1) / 2);
-  while (sr > 1 && span_smem_bytes((int)K, sr, EXACT) > (size_t)st->smem_optin) --sr;
-  const size_t smem = span_smem_bytes((int)K, sr, EXACT);
+  while (sr > 1 && span_smem_bytes((int)K, sr) > (size_t)st->smem_optin) --sr;
+  const size_t smem = span_smem_bytes((int)K, sr);
   if (smem > (size_t)st->smem_optin) return fail(TB_EINVAL, "tb_matmul_quant: K=%lld too large", (long long)K);
-  auto kern = gemv_q8_0_span_kernel<NWARP, EXACT>;
+  auto kern = gemv_q8_0_span_kernel<NWARP>;
   TB_TRY(ensure_smem_for(kern, smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid, 1, 1);
@@ -555,7 +528,7 @@ tb_status launch_q8_0(const float *x, int64_t M, int64_t K, const void *w, int64
   const int64_t rbytes = K / 32 * 34;
   if (M == 1 && (reinterpret_cast<uintptr_t>(w) & 15) == 0 && rbytes % 16 == 0 &&
       (reinterpret_cast<uintptr_t>(x) & 15) == 0) {
-    if (exact) return launch_span<1>(x, K, w, N, y, s, st);
+    if (exact) return launch_span(x, K, w, N, y, s, st);
     if (gemv_tc_eligible(K, N, w, x)) return launch_gemv_tc(x, K, w, N, y, s, st);
     if (stream_gemv_fits(K, st)) return launch_stream_gemv(x, K, w, N, y, s, st);
   }

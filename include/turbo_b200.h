@@ -139,6 +139,23 @@ tb_status tb_softmax(const float *x_dev, float *y_dev, int64_t rows, int64_t col
 tb_status tb_argmax(const float *x_dev, int64_t rows, int64_t cols, int64_t *idx_dev,
                     tb_stream stream);
 
+/* Nucleus (top-p) sampling of one row of logits: sample_top_p
+ * (src/core/sampler.cpp:28-86).  Probabilities softmax(logits / temperature),
+ * ordered by descending probability (equal ones by ascending id); the prefix
+ * ends at the first position whose cumulative probability reaches top_p; the
+ * result is the first prefix position whose cumulative mass reaches u times
+ * the prefix mass, i.e. std::discrete_distribution's draw for the uniform
+ * number u in [0, 1), which the caller supplies (the reference draws it from a
+ * random_device-seeded mt19937).  Prefix sums are exact (integer masses
+ * floor(p * 2^62)); the result differs from a reference draw with the same u
+ * only where top_p or u lies within fp32 rounding of a prefix boundary.  With
+ * no positive finite probability (a NaN or +inf logit) *out_dev is the first
+ * maximum, as greedy_sample.  temperature must be > 0; vocab at most what a
+ * 16-CTA cluster holds in shared memory (about 530k).  One cluster launch, no
+ * allocation; *out_dev is written on the device. */
+tb_status tb_sample_top_p(const float *logits_dev, int64_t vocab, float temperature, float top_p,
+                          double u, int32_t *out_dev, tb_stream stream);
+
 /* Causal mask of the prefill attention scores (src/nn/attention.cpp:120-129):
  * x[r, c] = value wherever c > r + diag_offset, for x[rows, cols] with row
  * stride ld (elements). */

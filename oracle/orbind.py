@@ -44,6 +44,8 @@ _SIGS = {
     "or_swiglu": (None, [_P, _P, _SZ, _P]),
     "or_softmax": (None, [_P, _SZ, _SZ, _P]),
     "or_argmax": (ctypes.c_int64, [_P, _SZ]),
+    "or_sample_top_p": (_I, [_P, _SZ, _F, _F, ctypes.c_double, ctypes.POINTER(_I),
+                             ctypes.POINTER(_SZ), ctypes.POINTER(_SZ), ctypes.POINTER(ctypes.c_double)]),
     "or_rope_tables": (None, [_SZ, _SZ, _F, _P, _P]),
     "or_rope": (_I, [_P, _VP, _SZ, _SZ, _P, _P, _SZ]),
     "or_embedding": (_I, [_P, _I, _SZ, _SZ, _P, _SZ, _P]),
@@ -195,6 +197,18 @@ def softmax(x):
 def argmax(x):
     x = np.ascontiguousarray(x, np.float32)
     return int(lib().or_argmax(ptr(x), x.size))
+
+
+def sample_top_p(logits, temperature, top_p, u):
+    """Nucleus sample with the uniform number `u` given.  Returns (id, nucleus
+    length, the reference's fp32-running-sum nucleus length, slack)."""
+    x = np.ascontiguousarray(logits, np.float32).ravel()
+    tid, nuc, nuc32, slack = _I(), _SZ(), _SZ(), ctypes.c_double()
+    st = lib().or_sample_top_p(ptr(x), x.size, float(temperature), float(top_p), float(u), ctypes.byref(tid),
+                               ctypes.byref(nuc), ctypes.byref(nuc32), ctypes.byref(slack))
+    if st == 1:
+        raise ValueError("sample_top_p: bad arguments")
+    return tid.value, nuc.value, nuc32.value, (slack.value if st == 0 else 0.0)
 
 
 def rope_tables(head_dim, max_seq, theta):

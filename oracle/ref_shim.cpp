@@ -172,6 +172,13 @@ REF_API int ref_greedy_sample(const float *logits, size_t n) {
   return turbo::greedy_sample(logits, n);
 }
 
+// sample_top_p (src/core/sampler.cpp:28-86): `draws` calls, each drawing from the
+// reference's own random_device-seeded generator.
+REF_API void ref_sample_top_p(const float *logits, size_t n, float temperature, float top_p, int draws,
+                              int *out) {
+  for (int i = 0; i < draws; ++i) out[i] = turbo::sample_top_p(logits, n, temperature, top_p);
+}
+
 // nn::RoPE ctor + apply_in_place (src/nn/rope.cpp:9-103) on a rank-2 or rank-4
 // strided view over `x`, modified in place.
 REF_API int ref_rope(float *x, size_t len, size_t off, const size_t *shape,

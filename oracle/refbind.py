@@ -28,6 +28,7 @@ _SIGS = {
     "ref_swiglu": (_I, [_P, _P, _SZ, _P]),
     "ref_softmax": (_I, [_P, _SZ, _SZ, _P]),
     "ref_greedy_sample": (_I, [_P, _SZ]),
+    "ref_sample_top_p": (None, [_P, _SZ, _F, _F, _I, _P]),
     "ref_rope": (_I, [_P, _SZ, _SZ, _SZP, _SZP, _I, _SZ, _SZ, _F, _SZ]),
     "ref_rope_tables": (None, [_SZ, _SZ, _F, _P, _P]),
     "ref_embedding": (_I, [_P, _I, _SZ, _SZ, _P, _SZ, _P]),
@@ -146,6 +147,14 @@ def softmax(x):
 def greedy_sample(logits):
     logits = np.ascontiguousarray(logits, np.float32)
     return int(lib().ref_greedy_sample(ptr(logits), logits.size))
+
+
+def sample_top_p(logits, temperature, top_p, draws):
+    """`draws` calls of the reference's sample_top_p (its own random stream)."""
+    logits = np.ascontiguousarray(logits, np.float32)
+    out = np.zeros(int(draws), np.int32)
+    lib().ref_sample_top_p(ptr(logits), logits.size, float(temperature), float(top_p), int(draws), ptr(out))
+    return out
 
 
 def rope(base, off, shape, strides, head_dim, max_seq, theta, pos_offset):

@@ -389,6 +389,119 @@ int64_t or_argmax(const float *x, size_t n) {
   return best;
 }
 
+/* ---- nucleus sampling ----------------------------------------------------------
+ * sample_top_p: src/core/sampler.cpp:28-86.  The probabilities are the
+ * reference's bit for bit (temperature divide, strict '>' max, expf, a
+ * sequential fp32 sum, divide).  The pairs are ordered by descending
+ * probability with ties by ascending token id (std::sort leaves ties in an
+ * unspecified order).  Two cut points follow, both over exact prefix sums of
+ * the masses q = floor(p * 2^62):
+ *   cut:  the first position whose prefix mass reaches ceil(top_p * 2^62)
+ *         (capped at the total), the reference's `cumulative_prob >= top_p`;
+ *   pick: the first position whose prefix mass reaches ceil(u * C), C the
+ *         prefix mass through `cut` -- what std::discrete_distribution's
+ *         lower_bound over the normalised partial sums selects for the uniform
+ *         number u in [0, 1) (the reference draws u from a random_device-seeded
+ *         mt19937; here the caller passes it).
+ * Outputs: *id, *nucleus = cut + 1, *nucleus_f32 = the prefix length the
+ * reference's own fp32 running sum gives, *slack = the smaller distance, in
+ * units of the total / of C, from top_p / u to the nearest prefix boundary
+ * (how much rounding either cut can absorb; for a top_p above the total, its
+ * distance from the total).  Returns 1 for bad arguments,
+ * 3 when no probability is finite and positive (then *id = greedy choice). */
+typedef struct {
+  uint32_t bits;
+  uint32_t id;
+} or_pb;
+
+static int or_pb_cmp(const void *a, const void *b) {
+  const or_pb *x = (const or_pb *)a, *y = (const or_pb *)b;
+  if (x->bits != y->bits) return x->bits > y->bits ? -1 : 1;
+  return x->id < y->id ? -1 : (x->id > y->id ? 1 : 0);
+}
+
+static uint64_t or_qmass(float p) {
+  return (p > 0.f && p <= 1.f) ? (uint64_t)((double)p * 4611686018427387904.0) : 0u;
+}
+
+int or_sample_top_p(const float *logits, size_t n, float temperature, float top_p, double u,
+                    int *id, size_t *nucleus, size_t *nucleus_f32, double *slack) {
+  if (n == 0 || n > 0x7FFFFFFFu || !(temperature > 0.f)) return E_INVAL;
+  float *p = (float *)malloc(n * sizeof(float));
+  or_pb *pb = (or_pb *)malloc(n * sizeof(or_pb));
+  uint64_t *cum = (uint64_t *)malloc(n * sizeof(uint64_t));
+  if (!p || !pb || !cum) {
+    free(p), free(pb), free(cum);
+    return E_RUNTIME;
+  }
+  float mx = -INFINITY;
+  size_t mi = 0;
+  for (size_t i = 0; i < n; ++i) {
+    p[i] = logits[i] / temperature;
+    if (p[i] > mx) {
+      mx = p[i];
+      mi = i;
+    }
+  }
+  float sum = 0.f;
+  for (size_t i = 0; i < n; ++i) {
+    p[i] = expf(p[i] - mx);
+    sum += p[i];
+  }
+  uint64_t tot = 0;
+  for (size_t i = 0; i < n; ++i) {
+    p[i] /= sum;
+    uint32_t b = 0u; /* NaN and 0 order last */
+    if (p[i] > 0.f) memcpy(&b, &p[i], sizeof b);
+    pb[i].bits = b;
+    pb[i].id = (uint32_t)i;
+    tot += or_qmass(p[i]);
+  }
+  *id = (int)mi;
+  *nucleus = *nucleus_f32 = 1;
+  *slack = 0.0;
+  if (tot == 0) {
+    free(p), free(pb), free(cum);
+    return E_RUNTIME;
+  }
+  qsort(pb, n, sizeof(or_pb), or_pb_cmp);
+  uint64_t acc = 0;
+  float accf = 0.f;
+  size_t nf = n;
+  for (size_t i = 0; i < n; ++i) {
+    const float pi = p[pb[i].id];
+    acc += or_qmass(pi);
+    cum[i] = acc;
+    if (nf == n) {
+      accf += pi;
+      if (accf >= top_p) nf = i + 1;
+    }
+  }
+  const double tq = ceil((double)top_p * 4611686018427387904.0);
+  const uint64_t t1 = !(tq < (double)tot) ? tot : (tq <= 0.0 ? 0u : (uint64_t)tq);
+  size_t cut = 0;
+  while (cum[cut] < t1) ++cut;
+  const uint64_t C = cum[cut];
+  const double uu = u > 0.0 ? u : 0.0, tu = ceil(uu * (double)C);
+  const uint64_t t2 = !(tu < (double)C) ? C : (uint64_t)tu;
+  size_t pick = 0;
+  while (cum[pick] < t2) ++pick;
+  /* a target capped at the total keeps the cut at the last positive mass however the total rounds */
+  const int capped = t1 == tot && tq > (double)tot;
+  double s1 = capped ? tq - (double)tot : (double)(cum[cut] - t1);
+  double s2 = (double)(cum[pick] - t2);
+  if (!capped && cut > 0 && (double)(t1 - cum[cut - 1]) < s1) s1 = (double)(t1 - cum[cut - 1]);
+  if (pick > 0 && (double)(t2 - cum[pick - 1]) < s2) s2 = (double)(t2 - cum[pick - 1]);
+  s1 /= (double)tot;
+  s2 /= (double)C;
+  *id = (int)pb[pick].id;
+  *nucleus = cut + 1;
+  *nucleus_f32 = nf;
+  *slack = s1 < s2 ? s1 : s2;
+  free(p), free(pb), free(cum);
+  return OK;
+}
+
 /* ---- RoPE --------------------------------------------------------------------- */
 
 /* RoPE constructor tables: src/nn/rope.cpp:16-32. */

@@ -533,6 +533,79 @@ def test_argmax_ties_nan_inf():
     assert argmax_gpu(big)[0] == 77777 == O.argmax(big[0])
 
 
+# -------------------------------------------------------------- sampling ----
+# Nucleus sampling with the uniform number given.  The device's exp and sum
+# order differ from the reference's within rounding, so a draw is compared
+# exactly wherever the oracle reports that top_p and u lie more than 1e-5
+# (relative) from a prefix boundary; rows whose probabilities are exact on both
+# sides (equal logits, -inf) are compared at every u.
+
+def sample_many(xd, V, temperature, top_p, us):
+    out = torch.full((len(us),), -1, dtype=torch.int32, device="cuda")
+    for i, u in enumerate(us):
+        T.call("tb_sample_top_p", T.ptr(xd), V, float(temperature), float(top_p), float(u), T.ptr(out[i:]), S())
+    return host(out)
+
+
+US = [0.0] + list((np.arange(16) + 0.37) / 16) + [0.999999]
+
+
+@pytest.mark.parametrize("V", [1, 7, 1000, 32000, 128256, 151936, 262144, 300001])
+def test_sample_top_p_matches_oracle(V):
+    x = synth.normal((V,), 2.5, seed=V)
+    xd = dev(x)
+    checked = total = 0
+    for temperature, top_p in [(0.8, 0.9), (1.0, 0.5), (1.3, 0.99), (0.6, 0.0), (1.0, 1.5), (0.9, 0.95)]:
+        got = sample_many(xd, V, temperature, top_p, US)
+        for u, g in zip(US, got):
+            tid, nuc, _, slack = O.sample_top_p(x, temperature, top_p, u)
+            total += 1
+            if slack > 1e-5:
+                assert g == tid, (temperature, top_p, u, g, tid, nuc)
+                checked += 1
+    assert checked >= 0.9 * total, (checked, total)
+
+
+@pytest.mark.parametrize("V,every", [(1000, 1), (128256, 1), (128256, 5), (300001, 7), (262144, 3)])
+def test_sample_top_p_ties_across_slices(V, every):
+    # equal logits (every `every`-th id, the rest -inf): exact equal probabilities,
+    # ordered by id across the cluster's slices
+    x = np.full(V, -np.inf, np.float32)
+    x[::every] = 0.0
+    xd = dev(x)
+    for top_p in (0.5, 0.9, 0.0, 2.0):
+        got = sample_many(xd, V, 1.0, top_p, US)
+        for u, g in zip(US, got):
+            assert g == O.sample_top_p(x, 1.0, top_p, u)[0], (top_p, u)
+
+
+def test_sample_top_p_degenerate_rows():
+    cases = [np.array([1.0, np.nan, 3.0, 3.0], np.float32),       # NaN: greedy's first maximum
+             np.full(5, -np.inf, np.float32),                     # no finite logit: 0
+             np.array([0.0, np.inf, 1.0, np.inf], np.float32),    # +inf: first +inf
+             np.array([2.0], np.float32)]
+    for x in cases:
+        got = sample_many(dev(x), x.size, 0.7, 0.9, [0.3])[0]
+        assert got == O.sample_top_p(x, 0.7, 0.9, 0.3)[0] == O.argmax(x), x
+
+
+def test_sample_top_p_unaligned_row_and_errors():
+    V = 5001
+    x = synth.normal((V + 1,), 2.0, seed=9)
+    xd = dev(x)
+    out = torch.full((1,), -1, dtype=torch.int32, device="cuda")
+    T.call("tb_sample_top_p", T.ptr(xd[1:]), V, 0.8, 0.9, 0.4, T.ptr(out), S())  # a row 4 bytes past 16-byte alignment
+    tid, _, _, slack = O.sample_top_p(x[1:], 0.8, 0.9, 0.4)
+    assert slack > 1e-5 and host(out)[0] == tid
+    for args in [(0.0, 0.9), (-1.0, 0.9), (float("nan"), 0.9)]:
+        with pytest.raises(T.TbError):
+            T.call("tb_sample_top_p", T.ptr(xd), V, args[0], args[1], 0.5, T.ptr(out), S())
+    with pytest.raises(T.TbError):
+        T.call("tb_sample_top_p", T.ptr(xd), 0, 1.0, 0.9, 0.5, T.ptr(out), S())
+    with pytest.raises(T.TbError):  # larger than a 16-CTA cluster holds; rejected before any launch
+        T.call("tb_sample_top_p", T.ptr(xd), 10**6, 1.0, 0.9, 0.5, T.ptr(out), S())
+
+
 # ------------------------------------------------------------------ RoPE ----
 
 @pytest.mark.parametrize("rank", [2, 4])

@@ -244,3 +244,63 @@ def test_matmul_f32_batched_bit_exact():
     b = synth.normal((2 * 3 * 7 * 11,), 1.0, seed=33)
     args = (a, 0, (2, 3, 5, 7), (105, 35, 7, 1), b, 0, (2, 3, 7, 11), (231, 77, 11, 1))
     assert_bits(O.matmul_f32(*args), R.matmul_f32(*args))
+
+
+# -------------------------------------------------------------- sampling ----
+# The reference draws its uniform number from a random_device-seeded mt19937,
+# so its draws are pinned statistically: every draw lies in the oracle's
+# nucleus, and the draw frequencies match the oracle's renormalised
+# probabilities.
+
+def _sorted_probs(x, temperature):
+    p = O.softmax((np.asarray(x, f32) / f32(temperature)).astype(f32)[None])[0]
+    order = np.lexsort((np.arange(p.size), -p))
+    return p, order
+
+
+@pytest.mark.parametrize("V,temperature,top_p", [(1000, 0.8, 0.9), (4000, 1.0, 0.9), (1000, 1.3, 0.5),
+                                                 (600, 0.7, 0.95)])
+def test_sample_top_p_reference_draws_lie_in_oracle_nucleus(V, temperature, top_p):
+    x = synth.normal((V,), 2.0, seed=V + int(100 * top_p))
+    _, nuc, nuc32, slack = O.sample_top_p(x, temperature, top_p, 0.5)
+    assert nuc == nuc32  # the exact prefix mass and the reference's fp32 running sum agree here
+    p, order = _sorted_probs(x, temperature)
+    nucleus = order[:nuc]
+    draws = R.sample_top_p(x, temperature, top_p, 4000)
+    assert np.isin(draws, nucleus).all()
+    freq = np.bincount(draws, minlength=V)[nucleus] / draws.size
+    want = p[nucleus].astype(np.float64) / p[nucleus].astype(np.float64).sum()
+    sigma = np.sqrt(want * (1 - want) / draws.size)
+    assert (np.abs(freq - want) <= 5 * sigma + 2e-3).all()
+    # the oracle's draw for u is the inverse of the same distribution function
+    us = (np.arange(400) + 0.5) / 400
+    ids = np.array([O.sample_top_p(x, temperature, top_p, u)[0] for u in us])
+    cdf = np.cumsum(want)
+    expect = nucleus[np.minimum(np.searchsorted(cdf, us), nuc - 1)]
+    close = np.abs(cdf[np.minimum(np.searchsorted(cdf, us), nuc - 1)] - us) < 1e-6
+    assert (ids[~close] == expect[~close]).all()
+
+
+def test_sample_top_p_tiny_top_p_is_greedy():
+    x = synth.normal((5000,), 2.0, seed=11)
+    g = R.greedy_sample(x)
+    assert (R.sample_top_p(x, 0.9, 1e-6, 200) == g).all()
+    for u in (0.0, 0.3, 0.999999):
+        tid, nuc, _, _ = O.sample_top_p(x, 0.9, 1e-6, u)
+        assert tid == g and nuc == 1
+
+
+def test_sample_top_p_oracle_ties_by_id_and_nan():
+    V = 1000
+    x = np.zeros(V, f32)  # every probability 1/V: ties ordered by id
+    q = int(np.float64(f32(1) / f32(V)) * 2.0**62)
+    for u in (0.0, 0.1234, 0.5, 0.9999):
+        tid, nuc, _, _ = O.sample_top_p(x, 1.0, 0.5, u)
+        assert nuc == -(-int(np.ceil(0.5 * 2.0**62)) // q)
+        C = nuc * q
+        t2 = int(np.ceil(u * float(C)))
+        assert tid == max(1, -(-t2 // q)) - 1
+    y = synth.normal((300,), 1.0, seed=2)
+    y[7] = np.nan  # the reference's sum turns NaN: no positive probability, greedy's choice
+    tid, _, _, slack = O.sample_top_p(y, 1.0, 0.9, 0.5)
+    assert tid == O.argmax(y) and slack == 0.0

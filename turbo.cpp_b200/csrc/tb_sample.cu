@@ -1,0 +1,489 @@
+// tb_sample.cu -- nucleus (top-p) sampling of one row of logits on the device
+// (sample_top_p, src/core/sampler.cpp:28-86).
+//
+// The reference: probabilities softmax(logits / temperature) with a
+// sequential fp32 sum, (probability, id) pairs sorted by descending
+// probability (std::sort), the shortest prefix whose fp32 running sum reaches
+// top_p, then a draw from std::discrete_distribution over that prefix with a
+// random_device-seeded mt19937.  Here the caller supplies the uniform number
+// u in [0, 1); the draw is the first prefix position whose cumulative mass
+// reaches u times the prefix's mass (discrete_distribution's lower_bound over
+// its normalised partial sums).
+//
+// No sort.  Both cut points -- the end of the top_p prefix and the drawn
+// token -- are found by a radix select over the probabilities' bit patterns
+// (non-negative floats order as their bits) with each bucket's probability
+// mass summed exactly as an integer, q(p) = floor(p * 2^62), so a prefix mass
+// is exact.  Digits are bits 30..19, 18..7 and 6..0 (bit 31 is always 0);
+// equal probabilities are ordered by token id (std::sort leaves them in an
+// unspecified order).  The result can differ from the reference's only where
+// top_p or u lies within fp32 rounding of a prefix boundary: the device's exp
+// is CUDA's expf (within 2 ulp), its sum is taken in another order, and the
+// reference's prefix sums are fp32 running sums.  A NaN logit makes the sum
+// NaN (in the reference too); no probability is then positive and finite and
+// the result is greedy_sample's choice, the first maximum.
+//
+// Layout: one thread-block cluster of CL CTAs x 1024 threads.  CTA r keeps
+// the contiguous slice [r*n_loc, (r+1)*n_loc) of the row in shared memory for
+// the whole kernel (read from HBM once), turned in place into scaled logits,
+// exp values and probabilities.  Per digit level each CTA histograms its slice
+// (count and exact mass per bucket, warp-aggregated shared atomics); CTA r
+// then owns 1/CL of the buckets, sums them over the cluster through
+// distributed shared memory, scans them, and the cluster agrees on the bucket
+// where the running mass reaches the target.  Waits are the hardware cluster
+// barrier only.
+#include <cooperative_groups.h>
+
+#include <climits>
+
+#include "tb_internal.cuh"
+
+namespace tb {
+namespace {
+
+namespace cg = cooperative_groups;
+
+constexpr int kSampThreads = 1024;
+constexpr int kSampBuckets = 4096;  // buckets of a 12-bit digit
+constexpr int kHistBytes = kSampBuckets * 12;
+constexpr double kQ62 = 4611686018427387904.0;  // 2^62
+constexpr size_t kStaticReserve = 2048;  // bytes kept for the kernel's static shared memory
+
+__device__ __forceinline__ uint64_t qmass(float p) {  // floor(p * 2^62); 0 unless 0 < p <= 1
+  return (p > 0.f && p <= 1.f) ? (uint64_t)((double)p * kQ62) : 0ull;
+}
+__device__ __forceinline__ uint32_t pbits(float p) { return p > 0.f ? __float_as_uint(p) : 0u; }
+__device__ __forceinline__ int level_shift(int l) { return l == 0 ? 19 : (l == 1 ? 7 : 0); }
+__device__ __forceinline__ int level_width(int l) { return l == 2 ? 7 : 12; }
+
+// What each CTA publishes to the others (read through distributed shared memory).
+struct SamplePub {
+  float maxv;        // slice maximum of the scaled logits
+  int32_t maxi;      // its first global index
+  float esum;        // slice sum of exp(scaled - M)
+  uint64_t mass;     // slice total of q(p)
+  uint64_t seg;      // per level: total mass of this CTA's bucket range
+  int32_t cand_q;    // per level: first bucket (descending) of this range where the target is reached, or INT_MAX
+  uint32_t cand_digit, cand_count;
+  uint64_t cand_above;  // mass before that bucket
+  int32_t last_q;       // per level: last non-empty bucket of this range, or -1
+  uint32_t last_digit, last_count;
+  uint64_t last_above;
+};
+
+// Cluster-uniform selection state (every CTA holds the same values).
+struct SelState {
+  uint32_t prefix, mask;  // bits fixed so far
+  uint64_t above;         // mass of every element ordered before the group
+  uint32_t count;         // elements in the group
+  uint32_t reached;       // 0 when the target exceeded the mass (fallback taken)
+};
+
+struct SampleScratch {
+  float redf[32];
+  int32_t redi[32];
+  uint64_t red64[32];
+  float M, S;
+  int32_t Mi;
+  uint64_t off;
+  int32_t qmin, qlast, owner, jl;
+};
+
+// Adds (count 1, mass q) to bucket d for every valid lane, one shared atomic
+// pair per distinct bucket of the warp.  All 32 lanes must call it.
+__device__ __forceinline__ void hist_add(uint64_t *hm, uint32_t *hc, uint32_t d, bool valid, uint64_t q) {
+  const uint32_t peers = __match_any_sync(0xffffffffu, valid ? d : 0xFFFFFFFFu);
+  if (!valid) return;
+  const uint32_t lo = (uint32_t)q & 0x1FFFFFu, mid = (uint32_t)(q >> 21) & 0x1FFFFFu, hi = (uint32_t)(q >> 42);
+  const uint64_t s = (uint64_t)__reduce_add_sync(peers, lo) + ((uint64_t)__reduce_add_sync(peers, mid) << 21) +
+                     ((uint64_t)__reduce_add_sync(peers, hi) << 42);
+  if ((int)(threadIdx.x & 31) == __ffs(peers) - 1) {
+    atomicAdd(reinterpret_cast<unsigned long long *>(&hm[d]), (unsigned long long)s);
+    atomicAdd(&hc[d], (uint32_t)__popc(peers));
+  }
+}
+
+// Histogram of the slice elements in the current group by the digit of level l.
+__device__ void build_hist(const float *sl, int len, int l, const SelState &st, uint64_t *hm, uint32_t *hc) {
+  const int shift = level_shift(l), nbk = 1 << level_width(l);
+  for (int d = threadIdx.x; d < nbk; d += blockDim.x) {
+    hm[d] = 0ull;
+    hc[d] = 0u;
+  }
+  __syncthreads();
+  const uint32_t prefix = st.prefix, mask = st.mask;
+  const int rounds = (len + kSampThreads - 1) / kSampThreads;
+  for (int it = 0; it < rounds; ++it) {
+    const int k = it * kSampThreads + threadIdx.x;
+    const float p = k < len ? sl[k] : 0.f;
+    const uint32_t b = pbits(p);
+    const bool valid = k < len && (b & mask) == prefix;
+    if (__ballot_sync(0xffffffffu, valid)) hist_add(hm, hc, (b >> shift) & (uint32_t)(nbk - 1), valid, qmass(p));
+  }
+  __syncthreads();
+}
+
+// One digit level across the cluster: finds the bucket where the running mass
+// (descending order, from st.above) first reaches `target` and narrows st to it.
+template <int CL>
+__device__ void cluster_level(cg::cluster_group &cluster, int l, uint64_t *hm, uint32_t *hc, uint64_t target,
+                              SelState &st, SamplePub &pub, SampleScratch &scr) {
+  const int r = (int)cluster.block_rank(), tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nbk = 1 << level_width(l), per = nbk / CL;
+  // bucket q of this CTA's range (descending digit order), summed over the cluster
+  const int q = r * per + tid;
+  const uint32_t d = (uint32_t)(nbk - 1 - q);
+  uint64_t gm = 0;
+  uint32_t gc = 0;
+  if (tid < per) {
+#pragma unroll
+    for (int rr = 0; rr < CL; ++rr) {
+      gm += *cluster.map_shared_rank(&hm[d], rr);
+      gc += *cluster.map_shared_rank(&hc[d], rr);
+    }
+  }
+  // inclusive scan of gm over the range (threads >= per hold 0)
+  uint64_t incl = gm;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint64_t t = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += t;
+  }
+  if (lane == 31) scr.red64[warp] = incl;
+  if (tid == 0) {
+    scr.qmin = INT_MAX;
+    scr.qlast = -1;
+  }
+  __syncthreads();
+  for (int w = 0; w < warp; ++w) incl += scr.red64[w];
+  if (tid == per - 1) pub.seg = incl;
+  cluster.sync();  // every range total published; the level's histograms are no longer read
+  if (warp == 0) {
+    uint64_t v = lane < r ? cluster.map_shared_rank(&pub, lane)->seg : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) scr.off = st.above + v;
+  }
+  __syncthreads();
+  const uint64_t acc = scr.off + incl;  // mass through bucket q
+  if (tid < per && gc > 0) {
+    if (acc >= target) atomicMin(&scr.qmin, q);
+    atomicMax(&scr.qlast, q);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    pub.cand_q = scr.qmin;
+    pub.last_q = scr.qlast;
+  }
+  if (tid < per && q == scr.qmin) {
+    pub.cand_digit = d;
+    pub.cand_count = gc;
+    pub.cand_above = acc - gm;
+  }
+  if (tid < per && q == scr.qlast) {
+    pub.last_digit = d;
+    pub.last_count = gc;
+    pub.last_above = acc - gm;
+  }
+  cluster.sync();  // candidates published
+  if (warp == 0) {
+    const SamplePub *rp = cluster.map_shared_rank(&pub, lane < CL ? lane : 0);
+    const bool has = lane < CL && rp->cand_q != INT_MAX;
+    const bool nonempty = lane < CL && rp->last_q >= 0;
+    const uint32_t hb = __ballot_sync(0xffffffffu, has), nb = __ballot_sync(0xffffffffu, nonempty);
+    // the first range holding a candidate; if none, the last non-empty bucket
+    const int src = hb ? __ffs(hb) - 1 : (nb ? 31 - __clz(nb) : 0);
+    if (lane == src) {
+      const uint32_t dig = hb ? rp->cand_digit : rp->last_digit;
+      st.prefix |= dig << level_shift(l);
+      st.mask |= (uint32_t)(nbk - 1) << level_shift(l);
+      st.above = hb ? rp->cand_above : rp->last_above;
+      st.count = hb ? rp->cand_count : rp->last_count;
+      if (!hb) st.reached = 0u;
+    }
+  }
+  __syncthreads();
+}
+
+// Position j (1-based, among elements of equal bits ordered by id) of the
+// element where the running mass reaches `target` inside the final group.
+__device__ __forceinline__ uint32_t tie_rank(const SelState &st, uint64_t target) {
+  if (!st.reached) return st.count > 0 ? st.count : 1u;
+  const uint64_t qs = qmass(__uint_as_float(st.prefix));
+  if (qs == 0 || target <= st.above) return 1u;
+  const uint64_t j = (target - st.above + qs - 1) / qs;
+  return (uint32_t)max((uint64_t)1, min(j, (uint64_t)max(st.count, 1u)));
+}
+
+template <int CL>
+__device__ void select_desc(cg::cluster_group &cluster, uint64_t target, const float *sl, int len, uint64_t *h0m,
+                            uint32_t *h0c, uint64_t *h1m, uint32_t *h1c, SelState &st, SamplePub &pub,
+                            SampleScratch &scr) {
+  __syncthreads();  // every thread is done with the previous selection's state
+  if (threadIdx.x == 0) st = SelState{0u, 0u, 0ull, 0u, 1u};
+  __syncthreads();
+  cluster_level<CL>(cluster, 0, h0m, h0c, target, st, pub, scr);
+  for (int l = 1; l < 3; ++l) {
+    build_hist(sl, len, l, st, h1m, h1c);
+    cluster_level<CL>(cluster, l, h1m, h1c, target, st, pub, scr);
+  }
+}
+
+template <int CL>
+__global__ void __launch_bounds__(kSampThreads, 1)
+    sample_top_p_kernel(const float *__restrict__ logits, int V, int n_loc, float temperature, float top_p, double u,
+                        int32_t *__restrict__ out) {
+  cg::cluster_group cluster = cg::this_cluster();
+  extern __shared__ __align__(16) uint8_t smem[];
+  uint64_t *h0m = reinterpret_cast<uint64_t *>(smem);
+  uint32_t *h0c = reinterpret_cast<uint32_t *>(h0m + kSampBuckets);
+  uint64_t *h1m = reinterpret_cast<uint64_t *>(h0c + kSampBuckets);
+  uint32_t *h1c = reinterpret_cast<uint32_t *>(h1m + kSampBuckets);
+  float *sl = reinterpret_cast<float *>(h1c + kSampBuckets);
+  __shared__ SamplePub pub;
+  __shared__ SampleScratch scr;
+  __shared__ SelState st;
+  const int r = (int)cluster.block_rank(), tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int start = r * n_loc, len = max(0, min(n_loc, V - start));
+
+  // 1. the slice, scaled by 1/temperature (a division, as the reference), and its first maximum
+  for (int d = tid; d < kSampBuckets; d += kSampThreads) {
+    h0m[d] = 0ull;
+    h0c[d] = 0u;
+  }
+  float m = -INFINITY;
+  int mi = INT_MAX;
+  const float *src = logits + start;
+  if ((reinterpret_cast<uintptr_t>(src) & 15) == 0) {
+    const int nq = len >> 2;
+    for (int k = tid; k < nq; k += kSampThreads) {
+      float4 v = __ldg(reinterpret_cast<const float4 *>(src) + k);
+      v.x = __fdiv_rn(v.x, temperature);
+      v.y = __fdiv_rn(v.y, temperature);
+      v.z = __fdiv_rn(v.z, temperature);
+      v.w = __fdiv_rn(v.w, temperature);
+      reinterpret_cast<float4 *>(sl)[k] = v;
+      if (v.x > m) m = v.x, mi = start + 4 * k;
+      if (v.y > m) m = v.y, mi = start + 4 * k + 1;
+      if (v.z > m) m = v.z, mi = start + 4 * k + 2;
+      if (v.w > m) m = v.w, mi = start + 4 * k + 3;
+    }
+    for (int k = 4 * nq + tid; k < len; k += kSampThreads) {
+      const float v = __fdiv_rn(__ldg(src + k), temperature);
+      sl[k] = v;
+      if (v > m) m = v, mi = start + k;
+    }
+  } else {
+    for (int k = tid; k < len; k += kSampThreads) {
+      const float v = __fdiv_rn(__ldg(src + k), temperature);
+      sl[k] = v;
+      if (v > m) m = v, mi = start + k;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float m2 = __shfl_xor_sync(0xffffffffu, m, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, mi, o);
+    if (m2 > m || (m2 == m && i2 < mi)) m = m2, mi = i2;
+  }
+  if (lane == 0) scr.redf[warp] = m, scr.redi[warp] = mi;
+  __syncthreads();
+  if (tid == 0) {
+    float bm = -INFINITY;
+    int bi = INT_MAX;
+    for (int w = 0; w < kSampThreads / 32; ++w)
+      if (scr.redf[w] > bm || (scr.redf[w] == bm && scr.redi[w] < bi)) bm = scr.redf[w], bi = scr.redi[w];
+    pub.maxv = bm;
+    pub.maxi = bi;
+  }
+  cluster.sync();
+
+  // 2. M = the row maximum; e = exp(scaled - M) in place and the slice sum
+  if (warp == 0) {
+    const SamplePub *rp = cluster.map_shared_rank(&pub, lane < CL ? lane : 0);
+    float bm = lane < CL ? rp->maxv : -INFINITY;
+    int bi = lane < CL ? rp->maxi : INT_MAX;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float m2 = __shfl_xor_sync(0xffffffffu, bm, o);
+      const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (m2 > bm || (m2 == bm && i2 < bi)) bm = m2, bi = i2;
+    }
+    if (lane == 0) scr.M = bm, scr.Mi = bi == INT_MAX ? 0 : bi;
+  }
+  __syncthreads();
+  const float M = scr.M;
+  float s = 0.f;
+  for (int k = tid; k < len; k += kSampThreads) {
+    const float e = expf(__fsub_rn(sl[k], M));
+    sl[k] = e;
+    s = __fadd_rn(s, e);
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s = __fadd_rn(s, __shfl_xor_sync(0xffffffffu, s, o));
+  if (lane == 0) scr.redf[warp] = s;
+  __syncthreads();
+  if (tid == 0) {
+    float t = 0.f;
+    for (int w = 0; w < kSampThreads / 32; ++w) t = __fadd_rn(t, scr.redf[w]);
+    pub.esum = t;
+  }
+  cluster.sync();
+
+  // 3. S = the row sum (slices in order); p = e / S in place, the level-0 histogram, the slice mass
+  if (warp == 0) {
+    const float v = lane < CL ? cluster.map_shared_rank(&pub, lane)->esum : 0.f;
+    float t = 0.f;
+    for (int rr = 0; rr < CL; ++rr) t = __fadd_rn(t, __shfl_sync(0xffffffffu, v, rr));
+    if (lane == 0) scr.S = t;
+  }
+  __syncthreads();
+  const float S = scr.S;
+  uint64_t mass = 0;
+  {
+    const int rounds = (len + kSampThreads - 1) / kSampThreads;
+    for (int it = 0; it < rounds; ++it) {
+      const int k = it * kSampThreads + tid;
+      float p = 0.f;
+      if (k < len) {
+        p = __fdiv_rn(sl[k], S);
+        sl[k] = p;
+      }
+      const uint64_t qm = qmass(p);
+      mass += qm;
+      hist_add(h0m, h0c, pbits(p) >> 19, k < len, qm);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mass += __shfl_xor_sync(0xffffffffu, mass, o);
+  if (lane == 0) scr.red64[warp] = mass;
+  __syncthreads();
+  if (tid == 0) {
+    uint64_t t = 0;
+    for (int w = 0; w < kSampThreads / 32; ++w) t += scr.red64[w];
+    pub.mass = t;
+  }
+  cluster.sync();
+  uint64_t tot = 0;
+  if (warp == 0) {
+    uint64_t v = lane < CL ? cluster.map_shared_rank(&pub, lane)->mass : 0ull;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if (lane == 0) scr.off = v;
+  }
+  __syncthreads();
+  tot = scr.off;
+  if (r == 0 && tid == 0) *out = scr.Mi;  // greedy choice unless a draw replaces it
+  if (tot == 0) {  // no positive finite probability (a NaN or infinite logit)
+    cluster.sync();
+    return;
+  }
+
+  // 4. end of the top_p prefix: first position whose prefix mass reaches ceil(top_p * 2^62)
+  const double tq = ceil((double)top_p * kQ62);
+  const uint64_t t1 = !(tq < (double)tot) ? tot : (tq <= 0.0 ? 0ull : (uint64_t)tq);
+  select_desc<CL>(cluster, t1, sl, len, h0m, h0c, h1m, h1c, st, pub, scr);
+  const uint64_t C = st.above + (uint64_t)tie_rank(st, t1) * qmass(__uint_as_float(st.prefix));
+
+  // 5. the draw: first position whose prefix mass reaches ceil(u * C)
+  const double uu = u > 0.0 ? u : 0.0;
+  const double tu = ceil(uu * (double)C);
+  const uint64_t t2 = !(tu < (double)C) ? C : (uint64_t)tu;
+  select_desc<CL>(cluster, t2, sl, len, h0m, h0c, h1m, h1c, st, pub, scr);
+  const uint32_t j = tie_rank(st, t2);
+  const uint32_t bstar = st.prefix, dlast = bstar & 0x7Fu;
+  // the j-th element (by id) of the final group: find the CTA that holds it
+  if (warp == 0) {
+    const uint32_t c = lane < CL ? *cluster.map_shared_rank(&h1c[dlast], lane) : 0u;
+    uint32_t incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += t;
+    }
+    const uint32_t hit = __ballot_sync(0xffffffffu, lane < CL && c > 0 && incl - c < j && j <= incl);
+    const int own = hit ? __ffs(hit) - 1 : -1;
+    const uint32_t before = __shfl_sync(0xffffffffu, incl - c, own < 0 ? 0 : own);
+    if (lane == 0) {
+      scr.owner = own;
+      scr.jl = (int)(j - before);
+    }
+  }
+  __syncthreads();
+  if (r == scr.owner) {
+    const int jl = scr.jl;
+    int running = 0;
+    const int rounds = (len + kSampThreads - 1) / kSampThreads;
+    for (int it = 0; it < rounds; ++it) {
+      const int k = it * kSampThreads + tid;
+      const bool match = k < len && pbits(sl[k]) == bstar;
+      const int cnt = __syncthreads_count(match);
+      if (running + cnt >= jl) {
+        const uint32_t bal = __ballot_sync(0xffffffffu, match);
+        if (lane == 0) scr.redi[warp] = __popc(bal);
+        __syncthreads();
+        if (match) {
+          int rank = running + __popc(bal & ((1u << lane) - 1u)) + 1;
+          for (int w = 0; w < warp; ++w) rank += scr.redi[w];
+          if (rank == jl) *out = start + k;
+        }
+        break;
+      }
+      running += cnt;
+    }
+  }
+  cluster.sync();  // no CTA leaves while another may still read its shared memory
+}
+
+template <int CL>
+tb_status launch_sample(const float *logits, int V, float temperature, float top_p, double u, int32_t *out,
+                        size_t smem, int n_loc, cudaStream_t s) {
+  auto kern = sample_top_p_kernel<CL>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e == cudaSuccess && CL > 8) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_sample_top_p: %s", cudaGetErrorString(e));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(CL, 1, 1);
+  cfg.blockDim = dim3(kSampThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = CL;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  e = cudaLaunchKernelEx(&cfg, kern, logits, V, n_loc, temperature, top_p, u, out);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_sample_top_p: %s", cudaGetErrorString(e));
+  return check_launch("tb_sample_top_p");
+}
+
+}  // namespace
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" {
+
+tb_status tb_sample_top_p(const float *logits, int64_t vocab, float temperature, float top_p, double u,
+                          int32_t *out, tb_stream stream) {
+  if (!logits || !out) return fail(TB_EINVAL, "tb_sample_top_p: null pointer");
+  if (vocab <= 0 || vocab > INT_MAX) return fail(TB_EINVAL, "tb_sample_top_p: vocab %lld out of range", (long long)vocab);
+  if (!(temperature > 0.f)) return fail(TB_EINVAL, "tb_sample_top_p: temperature must be positive");
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  // slices of a multiple of 4 elements, so that each starts 16-byte aligned when the row does
+  auto slice = [&](int cl) { return (int)((((vocab + cl - 1) / cl) + 3) / 4 * 4); };
+  const int n8 = slice(8), n16 = slice(16);
+  const size_t smem8 = (size_t)2 * kHistBytes + (size_t)n8 * 4, smem16 = (size_t)2 * kHistBytes + (size_t)n16 * 4;
+  const size_t room = (size_t)st->smem_optin - kStaticReserve;  // the kernel's static shared memory is below this
+  cudaStream_t s = as_stream(stream);
+  if (smem8 <= room) return launch_sample<8>(logits, (int)vocab, temperature, top_p, u, out, smem8, n8, s);
+  if (smem16 <= room)
+    return launch_sample<16>(logits, (int)vocab, temperature, top_p, u, out, smem16, n16, s);
+  return fail(TB_EINVAL, "tb_sample_top_p: vocab %lld exceeds the %lld a 16-CTA cluster holds in shared memory",
+              (long long)vocab, (long long)((room - 2 * kHistBytes) / 4 * 16));
+}
+
+}  // extern "C"

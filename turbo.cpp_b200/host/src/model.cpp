@@ -7,6 +7,7 @@
 #include <unistd.h>
 
 #include <cstring>
+#include <random>
 #include <stdexcept>
 #include <string>
 
@@ -50,8 +51,37 @@ int greedy_sample(const float *last_token_logits, size_t vocab_size) {
 int greedy_sample(const Tensor &logits) {
   const size_t V = logits.get_shape().back();
   const size_t rows = logits.numel() / V;
-  const float *last = static_cast<const float *>(logits.contiguous().device_ptr()) + (rows - 1) * V;
+  const Tensor c = logits.contiguous();  // kept alive while its memory is read
+  const float *last = static_cast<const float *>(c.device_ptr()) + (rows - 1) * V;
   return argmax_device(last, V);
+}
+
+static int sample_device(const float *x_dev, size_t n, float temperature, float top_p, double u) {
+  Tensor id = Tensor::empty({1}, DataType::INT32);
+  tb_check(tb_sample_top_p(x_dev, (int64_t)n, temperature, top_p, u,
+                           static_cast<int32_t *>(id.get_storage()->device_data_discard()), nullptr));
+  int32_t out = 0;
+  tb_check(tb_download(&out, id.get_storage()->device_data(), sizeof(out), nullptr));
+  tb_check(tb_sync(nullptr));
+  return (int)out;
+}
+
+int sample_top_p(const float *last_token_logits, size_t vocab_size, float temperature, float top_p) {
+  // The reference's generator (src/core/sampler.cpp:80-81): one random_device-seeded
+  // mt19937 for the process; the uniform number is what discrete_distribution draws.
+  static std::random_device rd;
+  static std::mt19937 gen(rd());
+  const double u = std::generate_canonical<double, 53>(gen);
+  Tensor t(std::vector<float>(last_token_logits, last_token_logits + vocab_size), {vocab_size});
+  return sample_device(static_cast<const float *>(t.device_ptr()), vocab_size, temperature, top_p, u);
+}
+
+int sample_top_p(const Tensor &logits, float temperature, float top_p, double u) {
+  const size_t V = logits.get_shape().back();
+  const size_t rows = logits.numel() / V;
+  const Tensor c = logits.contiguous();  // kept alive while its memory is read
+  const float *last = static_cast<const float *>(c.device_ptr()) + (rows - 1) * V;
+  return sample_device(last, V, temperature, top_p, u);
 }
 
 // -------------------------------------------------------------- GGUFLoader --

@@ -187,6 +187,19 @@ int main() {
     const float w[3] = {NAN, -INFINITY, NAN};
     CHECK(greedy_sample(w, 3) == 0, "greedy_sample all NaN/-inf");
   }
+  // sample_top_p: a nucleus of one is the greedy choice; equal probabilities go by id
+  {
+    const float v[6] = {0.5f, 2.0f, -1.0f, 7.0f, 1.0f, 6.5f};
+    CHECK(sample_top_p(v, 6, 0.8f, 1e-6f) == 3, "sample_top_p tiny top_p");
+    std::vector<float> flat(1000, 0.0f);
+    Tensor logits(flat, {1, 1000});
+    // 500 equal probabilities reach top_p 0.5; u = 0.25 takes the 125th of them
+    CHECK(sample_top_p(logits, 1.0f, 0.5f, 0.25) == 124, "sample_top_p ties by id");
+    CHECK(sample_top_p(logits, 1.0f, 0.5f, 0.0) == 0, "sample_top_p u = 0");
+    bool in_nucleus = true;
+    for (int i = 0; i < 20; ++i) in_nucleus = in_nucleus && sample_top_p(flat.data(), 1000, 1.0f, 0.5f) < 500;
+    CHECK(in_nucleus, "sample_top_p host draws stay in the nucleus");
+  }
   std::printf("%d passed, %d failed\n", g_pass, g_fail);
   return g_fail;
 }

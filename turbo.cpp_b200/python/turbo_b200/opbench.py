@@ -165,6 +165,20 @@ def _cases(T, torch):
     rows_case("argmax", 64, 128256, "64x128256", "sweep: argmax [64,128256]")
     rows_case("argmax", 8192, 128256, "8192x128256", "large: argmax [8192,128256] (4.2 GB)")
 
+    # ---- nucleus sampling of one row: sample_top_p(logits, 128256, 0.8, 0.9) ----------------
+    def sample_case(V, tag, cfg):
+        k = rot(V * 4)
+
+        def make():
+            X = [f32((V,), 21 + i, 2.5) for i in range(k)]
+            out = torch.empty(1, dtype=torch.int32, device=dev)
+            return (lambda i, s: T.load().tb_sample_top_p(T.ptr(X[i % k]), V, ctypes.c_float(0.8), ctypes.c_float(0.9),
+                                                          ctypes.c_double(((i * 0.6180339887) % 1.0)), T.ptr(out), s)), (X, out)
+        cases.append(Case("sample_top_p_" + tag, cfg, make, V * 4 + 4))
+
+    sample_case(128256, "128256", "decode: sample_top_p over logits[128256], T 0.8, top_p 0.9")
+    sample_case(262144, "262144", "sweep: sample_top_p over logits[262144]")
+
     # ---- A14/A17 dequant, quantize, embedding; A13 RoPE ---------------------------------
     def dequant_case(N, K):
         nb = N * K // 32

@@ -46,6 +46,8 @@ _SIGS = {
     "or_argmax": (ctypes.c_int64, [_P, _SZ]),
     "or_sample_top_p": (_I, [_P, _SZ, _F, _F, ctypes.c_double, ctypes.POINTER(_I),
                              ctypes.POINTER(_SZ), ctypes.POINTER(_SZ), ctypes.POINTER(ctypes.c_double)]),
+    "or_sample_top_p_set": (_I, [_P, _SZ, _F, _F, ctypes.c_double, ctypes.c_double, ctypes.c_double, _I, _P,
+                                 ctypes.POINTER(_I)]),
     "or_rope_tables": (None, [_SZ, _SZ, _F, _P, _P]),
     "or_rope": (_I, [_P, _VP, _SZ, _SZ, _P, _P, _SZ]),
     "or_embedding": (_I, [_P, _I, _SZ, _SZ, _P, _SZ, _P]),
@@ -209,6 +211,19 @@ def sample_top_p(logits, temperature, top_p, u):
     if st == 1:
         raise ValueError("sample_top_p: bad arguments")
     return tid.value, nuc.value, nuc32.value, (slack.value if st == 0 else 0.0)
+
+
+def sample_top_p_set(logits, temperature, top_p, u, rel_p, abs_u, accurate_sum=False):
+    """Every draw reachable when top_p moves by a factor (1 +- rel_p) and u by
+    +- abs_u; accurate_sum takes the softmax denominator as the exact sum."""
+    x = np.ascontiguousarray(logits, np.float32).ravel()
+    ids = np.zeros(x.size, np.int32)
+    n = _I()
+    st = lib().or_sample_top_p_set(ptr(x), x.size, float(temperature), float(top_p), float(u), float(rel_p),
+                                   float(abs_u), int(bool(accurate_sum)), ptr(ids), ctypes.byref(n))
+    if st == 1:
+        raise ValueError("sample_top_p: bad arguments")
+    return set(int(i) for i in ids[:n.value])
 
 
 def rope_tables(head_dim, max_seq, theta):

@@ -424,59 +424,64 @@ static uint64_t or_qmass(float p) {
   return (p > 0.f && p <= 1.f) ? (uint64_t)((double)p * 4611686018427387904.0) : 0u;
 }
 
-int or_sample_top_p(const float *logits, size_t n, float temperature, float top_p, double u,
-                    int *id, size_t *nucleus, size_t *nucleus_f32, double *slack) {
-  if (n == 0 || n > 0x7FFFFFFFu || !(temperature > 0.f)) return E_INVAL;
-  float *p = (float *)malloc(n * sizeof(float));
-  or_pb *pb = (or_pb *)malloc(n * sizeof(or_pb));
-  uint64_t *cum = (uint64_t *)malloc(n * sizeof(uint64_t));
-  if (!p || !pb || !cum) {
-    free(p), free(pb), free(cum);
-    return E_RUNTIME;
-  }
-  float mx = -INFINITY;
-  size_t mi = 0;
+/* Probabilities (the reference's bit for bit), ids ordered by descending
+ * probability then id, and the exact prefix masses in that order.  Returns
+ * the total mass (0: no positive finite probability); *mi = greedy choice. */
+typedef struct {
+  float *p;
+  or_pb *pb;
+  uint64_t *cum;
+  uint64_t tot;
+  size_t mi;
+} or_nucleus;
+
+static void or_nucleus_free(or_nucleus *t) { free(t->p), free(t->pb), free(t->cum); }
+
+static int or_nucleus_build(const float *logits, size_t n, float temperature, int accurate_sum, or_nucleus *t) {
+  t->p = (float *)malloc(n * sizeof(float));
+  t->pb = (or_pb *)malloc(n * sizeof(or_pb));
+  t->cum = (uint64_t *)malloc(n * sizeof(uint64_t));
+  t->tot = 0;
+  t->mi = 0;
+  if (!t->p || !t->pb || !t->cum) return E_RUNTIME;
+  float *p = t->p, mx = -INFINITY;
   for (size_t i = 0; i < n; ++i) {
     p[i] = logits[i] / temperature;
     if (p[i] > mx) {
       mx = p[i];
-      mi = i;
+      t->mi = i;
     }
   }
   float sum = 0.f;
+  double dsum = 0.0;
   for (size_t i = 0; i < n; ++i) {
     p[i] = expf(p[i] - mx);
     sum += p[i];
+    dsum += p[i];
   }
-  uint64_t tot = 0;
+  if (accurate_sum) sum = (float)dsum; /* the exact sum rounded once, not the reference's running sum */
   for (size_t i = 0; i < n; ++i) {
     p[i] /= sum;
     uint32_t b = 0u; /* NaN and 0 order last */
     if (p[i] > 0.f) memcpy(&b, &p[i], sizeof b);
-    pb[i].bits = b;
-    pb[i].id = (uint32_t)i;
-    tot += or_qmass(p[i]);
+    t->pb[i].bits = b;
+    t->pb[i].id = (uint32_t)i;
+    t->tot += or_qmass(p[i]);
   }
-  *id = (int)mi;
-  *nucleus = *nucleus_f32 = 1;
-  *slack = 0.0;
-  if (tot == 0) {
-    free(p), free(pb), free(cum);
-    return E_RUNTIME;
-  }
-  qsort(pb, n, sizeof(or_pb), or_pb_cmp);
+  if (t->tot == 0) return OK;
+  qsort(t->pb, n, sizeof(or_pb), or_pb_cmp);
   uint64_t acc = 0;
-  float accf = 0.f;
-  size_t nf = n;
   for (size_t i = 0; i < n; ++i) {
-    const float pi = p[pb[i].id];
-    acc += or_qmass(pi);
-    cum[i] = acc;
-    if (nf == n) {
-      accf += pi;
-      if (accf >= top_p) nf = i + 1;
-    }
+    acc += or_qmass(p[t->pb[i].id]);
+    t->cum[i] = acc;
   }
+  return OK;
+}
+
+/* The two cut points for (top_p, u); *slack as described above. */
+static void or_nucleus_pick(const or_nucleus *t, float top_p, double u, size_t *cut_out, size_t *pick_out,
+                            double *slack) {
+  const uint64_t *cum = t->cum, tot = t->tot;
   const double tq = ceil((double)top_p * 4611686018427387904.0);
   const uint64_t t1 = !(tq < (double)tot) ? tot : (tq <= 0.0 ? 0u : (uint64_t)tq);
   size_t cut = 0;
@@ -494,11 +499,64 @@ int or_sample_top_p(const float *logits, size_t n, float temperature, float top_
   if (pick > 0 && (double)(t2 - cum[pick - 1]) < s2) s2 = (double)(t2 - cum[pick - 1]);
   s1 /= (double)tot;
   s2 /= (double)C;
-  *id = (int)pb[pick].id;
+  *cut_out = cut;
+  *pick_out = pick;
+  if (slack) *slack = s1 < s2 ? s1 : s2;
+}
+
+int or_sample_top_p(const float *logits, size_t n, float temperature, float top_p, double u,
+                    int *id, size_t *nucleus, size_t *nucleus_f32, double *slack) {
+  if (n == 0 || n > 0x7FFFFFFFu || !(temperature > 0.f)) return E_INVAL;
+  or_nucleus t;
+  int st = or_nucleus_build(logits, n, temperature, 0, &t);
+  *id = (int)t.mi;
+  *nucleus = *nucleus_f32 = 1;
+  *slack = 0.0;
+  if (st != OK || t.tot == 0) {
+    or_nucleus_free(&t);
+    return E_RUNTIME;
+  }
+  size_t cut, pick, nf = n;
+  or_nucleus_pick(&t, top_p, u, &cut, &pick, slack);
+  float accf = 0.f; /* the reference's own fp32 running sum (sampler.cpp:62-70) */
+  for (size_t i = 0; i < n && nf == n; ++i) {
+    accf += t.p[t.pb[i].id];
+    if (accf >= top_p) nf = i + 1;
+  }
+  *id = (int)t.pb[pick].id;
   *nucleus = cut + 1;
   *nucleus_f32 = nf;
-  *slack = s1 < s2 ? s1 : s2;
-  free(p), free(pb), free(cum);
+  or_nucleus_free(&t);
+  return OK;
+}
+
+/* Every draw reachable when top_p moves by a factor (1 +- rel_p) and u by
+ * +- abs_u: how far rounding of the probabilities (the sum's order, exp within
+ * a few ulp) can move the two cut points.  The draw's position in the sorted
+ * order never decreases as top_p or u grows, so the reachable draws are the
+ * positions between the two corner cases.  With accurate_sum the softmax
+ * denominator is the exact sum rounded once instead of the reference's fp32
+ * running sum (whose own error reaches 5e-4 over 300k terms), for checking a
+ * device sum that is accurate to a few ulp.  ids[n] gets those draws, *n_ids
+ * their number.  Same return codes as or_sample_top_p. */
+int or_sample_top_p_set(const float *logits, size_t n, float temperature, float top_p, double u, double rel_p,
+                        double abs_u, int accurate_sum, int *ids, int *n_ids) {
+  if (n == 0 || n > 0x7FFFFFFFu || !(temperature > 0.f)) return E_INVAL;
+  or_nucleus t;
+  int st = or_nucleus_build(logits, n, temperature, accurate_sum, &t);
+  *n_ids = 1;
+  ids[0] = (int)t.mi;
+  if (st != OK || t.tot == 0) {
+    or_nucleus_free(&t);
+    return E_RUNTIME;
+  }
+  const double ulo = u - abs_u, uhi = u + abs_u;
+  size_t cut, lo, hi;
+  or_nucleus_pick(&t, (float)(top_p * (1.0 - rel_p)), ulo < 0.0 ? 0.0 : ulo, &cut, &lo, NULL);
+  or_nucleus_pick(&t, (float)(top_p * (1.0 + rel_p)), uhi >= 1.0 ? 0.9999999999 : uhi, &cut, &hi, NULL);
+  *n_ids = 0;
+  for (size_t k = lo; k <= hi; ++k) ids[(*n_ids)++] = (int)t.pb[k].id;
+  or_nucleus_free(&t);
   return OK;
 }
 

@@ -59,6 +59,8 @@ void or_softmax(const float *x, size_t rows, size_t cols, float *out);
 int64_t or_argmax(const float *x, size_t n);
 int or_sample_top_p(const float *logits, size_t n, float temperature, float top_p, double u,
                     int *id, size_t *nucleus, size_t *nucleus_f32, double *slack);
+int or_sample_top_p_set(const float *logits, size_t n, float temperature, float top_p, double u, double rel_p,
+                        double abs_u, int accurate_sum, int *ids, int *n_ids);
 
 void or_rope_tables(size_t head_dim, size_t max_seq, float theta, float *cos_t, float *sin_t);
 int or_rope(float *base, const or_view *x, size_t head_dim, size_t max_seq,

@@ -534,11 +534,17 @@ def test_argmax_ties_nan_inf():
 
 
 # -------------------------------------------------------------- sampling ----
-# Nucleus sampling with the uniform number given.  The device's exp and sum
-# order differ from the reference's within rounding, so a draw is compared
-# exactly wherever the oracle reports that top_p and u lie more than 1e-5
-# (relative) from a prefix boundary; rows whose probabilities are exact on both
-# sides (equal logits, -inf) are compared at every u.
+# Nucleus sampling with the uniform number given.  The device's exp is within
+# 2 ulp and its softmax sum is a tree, so its probabilities differ from the
+# reference's by rounding, which can move a cut point when top_p or u sits
+# close to a prefix boundary.  The oracle therefore returns the set of draws
+# reachable under a perturbation of that size:
+# - against the exact-sum oracle: top_p x (1 +- 1e-5), u +- 1e-6 -- most
+#   cases have a single answer, so this checks the selection itself;
+# - against the reference-faithful oracle (its sequential fp32 sum, whose own
+#   error reaches 5e-4 at 300k terms): top_p x (1 +- that error + 1e-5).
+# Rows whose probabilities are exact on both sides (equal logits, -inf) are
+# compared exactly.
 
 def sample_many(xd, V, temperature, top_p, us):
     out = torch.full((len(us),), -1, dtype=torch.int32, device="cuda")
@@ -550,20 +556,27 @@ def sample_many(xd, V, temperature, top_p, us):
 US = [0.0] + list((np.arange(16) + 0.37) / 16) + [0.999999]
 
 
+def reference_sum_error(x, temperature):
+    s = (np.asarray(x, np.float32) / np.float32(temperature)).astype(np.float32)
+    e = np.exp((s - s.max()).astype(np.float32))
+    return abs(float(np.cumsum(e, dtype=np.float32)[-1]) / e.astype(np.float64).sum() - 1.0)
+
+
 @pytest.mark.parametrize("V", [1, 7, 1000, 32000, 128256, 151936, 262144, 300001])
 def test_sample_top_p_matches_oracle(V):
     x = synth.normal((V,), 2.5, seed=V)
     xd = dev(x)
-    checked = total = 0
+    single = total = 0
     for temperature, top_p in [(0.8, 0.9), (1.0, 0.5), (1.3, 0.99), (0.6, 0.0), (1.0, 1.5), (0.9, 0.95)]:
         got = sample_many(xd, V, temperature, top_p, US)
+        rel_ref = 2 * reference_sum_error(x, temperature) + 1e-5
         for u, g in zip(US, got):
-            tid, nuc, _, slack = O.sample_top_p(x, temperature, top_p, u)
+            exact = O.sample_top_p_set(x, temperature, top_p, u, 1e-5, 1e-6, accurate_sum=True)
+            faithful = O.sample_top_p_set(x, temperature, top_p, u, rel_ref, 1e-6)
+            assert g in exact and g in faithful, (temperature, top_p, u, g, exact, faithful)
             total += 1
-            if slack > 1e-5:
-                assert g == tid, (temperature, top_p, u, g, tid, nuc)
-                checked += 1
-    assert checked >= 0.9 * total, (checked, total)
+            single += len(exact) == 1
+    assert single >= 0.75 * total, (single, total)
 
 
 @pytest.mark.parametrize("V,every", [(1000, 1), (128256, 1), (128256, 5), (300001, 7), (262144, 3)])
@@ -595,8 +608,7 @@ def test_sample_top_p_unaligned_row_and_errors():
     xd = dev(x)
     out = torch.full((1,), -1, dtype=torch.int32, device="cuda")
     T.call("tb_sample_top_p", T.ptr(xd[1:]), V, 0.8, 0.9, 0.4, T.ptr(out), S())  # a row 4 bytes past 16-byte alignment
-    tid, _, _, slack = O.sample_top_p(x[1:], 0.8, 0.9, 0.4)
-    assert slack > 1e-5 and host(out)[0] == tid
+    assert O.sample_top_p_set(x[1:], 0.8, 0.9, 0.4, 1e-5, 1e-6, accurate_sum=True) == {int(host(out)[0])}
     for args in [(0.0, 0.9), (-1.0, 0.9), (float("nan"), 0.9)]:
         with pytest.raises(T.TbError):
             T.call("tb_sample_top_p", T.ptr(xd), V, args[0], args[1], 0.5, T.ptr(out), S())

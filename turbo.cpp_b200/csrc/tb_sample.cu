@@ -27,7 +27,7 @@
 // the contiguous slice [r*n_loc, (r+1)*n_loc) of the row in shared memory for
 // the whole kernel (read from HBM once), turned in place into scaled logits,
 // exp values and probabilities.  Per digit level each CTA histograms its slice
-// (count and exact mass per bucket, warp-aggregated shared atomics); CTA r
+// (count and exact mass per bucket, shared atomics); CTA r
 // then owns 1/CL of the buckets, sums them over the cluster through
 // distributed shared memory, scans them, and the cluster agrees on the bucket
 // where the running mass reaches the target.  Waits are the hardware cluster
@@ -89,17 +89,12 @@ struct SampleScratch {
   int32_t qmin, qlast, owner, jl;
 };
 
-// Adds (count 1, mass q) to bucket d for every valid lane, one shared atomic
-// pair per distinct bucket of the warp.  All 32 lanes must call it.
+// Adds (count 1, mass q) to bucket d for a valid lane (shared atomics; lanes
+// of a warp that hit one bucket are serialised by the hardware).
 __device__ __forceinline__ void hist_add(uint64_t *hm, uint32_t *hc, uint32_t d, bool valid, uint64_t q) {
-  const uint32_t peers = __match_any_sync(0xffffffffu, valid ? d : 0xFFFFFFFFu);
-  if (!valid) return;
-  const uint32_t lo = (uint32_t)q & 0x1FFFFFu, mid = (uint32_t)(q >> 21) & 0x1FFFFFu, hi = (uint32_t)(q >> 42);
-  const uint64_t s = (uint64_t)__reduce_add_sync(peers, lo) + ((uint64_t)__reduce_add_sync(peers, mid) << 21) +
-                     ((uint64_t)__reduce_add_sync(peers, hi) << 42);
-  if ((int)(threadIdx.x & 31) == __ffs(peers) - 1) {
-    atomicAdd(reinterpret_cast<unsigned long long *>(&hm[d]), (unsigned long long)s);
-    atomicAdd(&hc[d], (uint32_t)__popc(peers));
+  if (valid) {
+    atomicAdd(reinterpret_cast<unsigned long long *>(&hm[d]), (unsigned long long)q);
+    atomicAdd(&hc[d], 1u);
   }
 }
 
@@ -118,7 +113,7 @@ __device__ void build_hist(const float *sl, int len, int l, const SelState &st, 
     const float p = k < len ? sl[k] : 0.f;
     const uint32_t b = pbits(p);
     const bool valid = k < len && (b & mask) == prefix;
-    if (__ballot_sync(0xffffffffu, valid)) hist_add(hm, hc, (b >> shift) & (uint32_t)(nbk - 1), valid, qmass(p));
+    hist_add(hm, hc, (b >> shift) & (uint32_t)(nbk - 1), valid, qmass(p));
   }
   __syncthreads();
 }
@@ -225,6 +220,7 @@ __device__ void select_desc(cg::cluster_group &cluster, uint64_t target, const f
   cluster_level<CL>(cluster, 0, h0m, h0c, target, st, pub, scr);
   for (int l = 1; l < 3; ++l) {
     build_hist(sl, len, l, st, h1m, h1c);
+    cluster.sync();  // every CTA's histogram of this level is complete before any is read
     cluster_level<CL>(cluster, l, h1m, h1c, target, st, pub, scr);
   }
 }

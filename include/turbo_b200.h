@@ -151,7 +151,7 @@ tb_status tb_argmax(const float *x_dev, int64_t rows, int64_t cols, int64_t *idx
  * only where top_p or u lies within fp32 rounding of a prefix boundary.  With
  * no positive finite probability (a NaN or +inf logit) *out_dev is the first
  * maximum, as greedy_sample.  temperature must be > 0; vocab at most what a
- * 16-CTA cluster holds in shared memory (about 530k).  One cluster launch, no
+ * 16-CTA cluster holds in shared memory (about 500k).  One cluster launch, no
  * allocation; *out_dev is written on the device. */
 tb_status tb_sample_top_p(const float *logits_dev, int64_t vocab, float temperature, float top_p,
                           double u, int32_t *out_dev, tb_stream stream);

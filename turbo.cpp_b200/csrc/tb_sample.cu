@@ -14,7 +14,8 @@
 // token -- are found by a radix select over the probabilities' bit patterns
 // (non-negative floats order as their bits) with each bucket's probability
 // mass summed exactly as an integer, q(p) = floor(p * 2^62), so a prefix mass
-// is exact.  Digits are bits 30..19, 18..7 and 6..0 (bit 31 is always 0);
+// is exact.  Digits are bits 29..19, 18..7 and 6..0 (bits 31 and 30 are 0
+// for 0 <= p <= 1);
 // equal probabilities are ordered by token id (std::sort leaves them in an
 // unspecified order).  The result can differ from the reference's only where
 // top_p or u lies within fp32 rounding of a prefix boundary: the device's exp
@@ -27,11 +28,10 @@
 // the contiguous slice [r*n_loc, (r+1)*n_loc) of the row in shared memory for
 // the whole kernel (read from HBM once), turned in place into scaled logits,
 // exp values and probabilities.  Per digit level each CTA histograms its slice
-// (count and exact mass per bucket, shared atomics); CTA r
-// then owns 1/CL of the buckets, sums them over the cluster through
-// distributed shared memory, scans them, and the cluster agrees on the bucket
-// where the running mass reaches the target.  Waits are the hardware cluster
-// barrier only.
+// (count and exact mass per bucket, 32-bit shared atomics); CTA r then owns
+// 1/CL of the buckets, sums them over the cluster through distributed shared
+// memory, scans them, and the cluster agrees on the bucket where the running
+// mass reaches the target.  Waits are the hardware cluster barrier only.
 #include <cooperative_groups.h>
 
 #include <climits>
@@ -44,17 +44,50 @@ namespace {
 namespace cg = cooperative_groups;
 
 constexpr int kSampThreads = 1024;
-constexpr int kSampBuckets = 4096;  // buckets of a 12-bit digit
-constexpr int kHistBytes = kSampBuckets * 12;
+constexpr int kL0Buckets = 2048;  // level 0: bits 29..19 (p <= 1 keeps bit 30 clear)
+constexpr int kL1Buckets = 4096;  // levels 1 and 2: bits 18..7, then 6..0
+constexpr int kCacheBuckets = kL0Buckets / 8;  // one CTA's level-0 bucket range (8-CTA cluster)
+// per bucket four 32-bit counters: mass bits 63..32, 31..16, 15..0 and the count
+constexpr int kFixedSmem = (kL0Buckets + kL1Buckets) * 16 + kCacheBuckets * 12;
 constexpr double kQ62 = 4611686018427387904.0;  // 2^62
 constexpr size_t kStaticReserve = 2048;  // bytes kept for the kernel's static shared memory
 
-__device__ __forceinline__ uint64_t qmass(float p) {  // floor(p * 2^62); 0 unless 0 < p <= 1
-  return (p > 0.f && p <= 1.f) ? (uint64_t)((double)p * kQ62) : 0ull;
-}
 __device__ __forceinline__ uint32_t pbits(float p) { return p > 0.f ? __float_as_uint(p) : 0u; }
+// floor(p * 2^62) from p's bits (bit 31 clear): the 24-bit significand times
+// 2^(exponent - 88), exactly; 0 for zero, subnormals (below 2^-126, whose
+// product is below 1) and anything above 1.
+__device__ __forceinline__ uint64_t qmass_bits(uint32_t b) {
+  const int e = (int)(b >> 23);
+  if (e == 0 || b > 0x3F800000u) return 0ull;
+  const uint64_t m = (uint64_t)((b & 0x7FFFFFu) | 0x800000u);
+  const int sh = e - 88;
+  return sh >= 0 ? m << sh : (sh > -64 ? m >> -sh : 0ull);
+}
+__device__ __forceinline__ uint64_t qmass(float p) { return qmass_bits(pbits(p)); }
 __device__ __forceinline__ int level_shift(int l) { return l == 0 ? 19 : (l == 1 ? 7 : 0); }
-__device__ __forceinline__ int level_width(int l) { return l == 2 ? 7 : 12; }
+__device__ __forceinline__ int level_width(int l) { return l == 0 ? 11 : (l == 1 ? 12 : 7); }
+
+// A histogram of nbk buckets in shared memory.  Each bucket's exact mass is
+// kept in three 32-bit sums (a 64-bit shared atomic costs about ten 32-bit
+// ones): bits 63..32 of the element masses, whose sum is bounded by the total
+// mass (< 2^32 * 1.1), and bits 31..16 and 15..0, whose sums are bounded by
+// 2^16 times the slice length (< 2^31).
+struct Hist {
+  uint32_t *hi, *mid, *lo, *cnt;
+};
+__device__ __forceinline__ Hist hist_at(uint32_t *base, int nbk) {
+  return Hist{base, base + nbk, base + 2 * nbk, base + 3 * nbk};
+}
+__device__ __forceinline__ void hist_clear(const Hist &h, int nbk) {
+  for (int d = threadIdx.x; d < nbk; d += blockDim.x) h.hi[d] = h.mid[d] = h.lo[d] = h.cnt[d] = 0u;
+}
+__device__ __forceinline__ void hist_add(const Hist &h, uint32_t d, uint64_t q) {
+  atomicAdd(&h.cnt[d], 1u);
+  const uint32_t hi = (uint32_t)(q >> 32), mid = (uint32_t)(q >> 16) & 0xFFFFu, lo = (uint32_t)q & 0xFFFFu;
+  if (hi) atomicAdd(&h.hi[d], hi);
+  if (mid) atomicAdd(&h.mid[d], mid);
+  if (lo) atomicAdd(&h.lo[d], lo);
+}
 
 // What each CTA publishes to the others (read through distributed shared memory).
 struct SamplePub {
@@ -89,40 +122,34 @@ struct SampleScratch {
   int32_t qmin, qlast, owner, jl;
 };
 
-// Adds (count 1, mass q) to bucket d for a valid lane (shared atomics; lanes
-// of a warp that hit one bucket are serialised by the hardware).
-__device__ __forceinline__ void hist_add(uint64_t *hm, uint32_t *hc, uint32_t d, bool valid, uint64_t q) {
-  if (valid) {
-    atomicAdd(reinterpret_cast<unsigned long long *>(&hm[d]), (unsigned long long)q);
-    atomicAdd(&hc[d], 1u);
-  }
-}
-
 // Histogram of the slice elements in the current group by the digit of level l.
-__device__ void build_hist(const float *sl, int len, int l, const SelState &st, uint64_t *hm, uint32_t *hc) {
+__device__ void build_hist(const float *sl, int len, int l, const SelState &st, const Hist &h) {
   const int shift = level_shift(l), nbk = 1 << level_width(l);
-  for (int d = threadIdx.x; d < nbk; d += blockDim.x) {
-    hm[d] = 0ull;
-    hc[d] = 0u;
-  }
+  hist_clear(h, nbk);
   __syncthreads();
   const uint32_t prefix = st.prefix, mask = st.mask;
-  const int rounds = (len + kSampThreads - 1) / kSampThreads;
-  for (int it = 0; it < rounds; ++it) {
-    const int k = it * kSampThreads + threadIdx.x;
-    const float p = k < len ? sl[k] : 0.f;
-    const uint32_t b = pbits(p);
-    const bool valid = k < len && (b & mask) == prefix;
-    hist_add(hm, hc, (b >> shift) & (uint32_t)(nbk - 1), valid, qmass(p));
+  for (int k0 = threadIdx.x; k0 < len; k0 += 4 * kSampThreads) {
+    uint32_t b[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int k = k0 + u * kSampThreads;
+      b[u] = k < len ? pbits(sl[k]) : 0u;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (k0 + u * kSampThreads < len && (b[u] & mask) == prefix)
+        hist_add(h, (b[u] >> shift) & (uint32_t)(nbk - 1), qmass_bits(b[u]));
   }
   __syncthreads();
 }
 
 // One digit level across the cluster: finds the bucket where the running mass
 // (descending order, from st.above) first reaches `target` and narrows st to it.
+// cm/cc (this CTA's range of cluster-summed buckets) are filled when `cache`
+// is 1 and read instead of the remote histograms when it is 2.
 template <int CL>
-__device__ void cluster_level(cg::cluster_group &cluster, int l, uint64_t *hm, uint32_t *hc, uint64_t target,
-                              SelState &st, SamplePub &pub, SampleScratch &scr) {
+__device__ void cluster_level(cg::cluster_group &cluster, int l, const Hist &h, uint64_t target, SelState &st,
+                              SamplePub &pub, SampleScratch &scr, uint64_t *cm, uint32_t *cc, int cache) {
   const int r = (int)cluster.block_rank(), tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nbk = 1 << level_width(l), per = nbk / CL;
   // bucket q of this CTA's range (descending digit order), summed over the cluster
@@ -131,10 +158,20 @@ __device__ void cluster_level(cg::cluster_group &cluster, int l, uint64_t *hm, u
   uint64_t gm = 0;
   uint32_t gc = 0;
   if (tid < per) {
-#pragma unroll
-    for (int rr = 0; rr < CL; ++rr) {
-      gm += *cluster.map_shared_rank(&hm[d], rr);
-      gc += *cluster.map_shared_rank(&hc[d], rr);
+    if (cache == 2) {
+      gm = cm[tid];
+      gc = cc[tid];
+    } else {
+#pragma unroll 8
+      for (int rr = 0; rr < CL; ++rr) {
+        gm += ((uint64_t)*cluster.map_shared_rank(&h.hi[d], rr) << 32) +
+              ((uint64_t)*cluster.map_shared_rank(&h.mid[d], rr) << 16) + *cluster.map_shared_rank(&h.lo[d], rr);
+        gc += *cluster.map_shared_rank(&h.cnt[d], rr);
+      }
+      if (cache == 1) {
+        cm[tid] = gm;
+        cc[tid] = gc;
+      }
     }
   }
   // inclusive scan of gm over the range (threads >= per hold 0)
@@ -210,18 +247,20 @@ __device__ __forceinline__ uint32_t tie_rank(const SelState &st, uint64_t target
   return (uint32_t)max((uint64_t)1, min(j, (uint64_t)max(st.count, 1u)));
 }
 
+// `first`: the level-0 cluster sums are read remotely and kept (cm, cc); the
+// second selection reuses them.
 template <int CL>
-__device__ void select_desc(cg::cluster_group &cluster, uint64_t target, const float *sl, int len, uint64_t *h0m,
-                            uint32_t *h0c, uint64_t *h1m, uint32_t *h1c, SelState &st, SamplePub &pub,
+__device__ void select_desc(cg::cluster_group &cluster, uint64_t target, const float *sl, int len, const Hist &h0,
+                            const Hist &h1, uint64_t *cm, uint32_t *cc, bool first, SelState &st, SamplePub &pub,
                             SampleScratch &scr) {
   __syncthreads();  // every thread is done with the previous selection's state
   if (threadIdx.x == 0) st = SelState{0u, 0u, 0ull, 0u, 1u};
   __syncthreads();
-  cluster_level<CL>(cluster, 0, h0m, h0c, target, st, pub, scr);
+  cluster_level<CL>(cluster, 0, h0, target, st, pub, scr, cm, cc, first ? 1 : 2);
   for (int l = 1; l < 3; ++l) {
-    build_hist(sl, len, l, st, h1m, h1c);
+    build_hist(sl, len, l, st, h1);
     cluster.sync();  // every CTA's histogram of this level is complete before any is read
-    cluster_level<CL>(cluster, l, h1m, h1c, target, st, pub, scr);
+    cluster_level<CL>(cluster, l, h1, target, st, pub, scr, cm, cc, 0);
   }
 }
 
@@ -231,11 +270,11 @@ __global__ void __launch_bounds__(kSampThreads, 1)
                         int32_t *__restrict__ out) {
   cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(16) uint8_t smem[];
-  uint64_t *h0m = reinterpret_cast<uint64_t *>(smem);
-  uint32_t *h0c = reinterpret_cast<uint32_t *>(h0m + kSampBuckets);
-  uint64_t *h1m = reinterpret_cast<uint64_t *>(h0c + kSampBuckets);
-  uint32_t *h1c = reinterpret_cast<uint32_t *>(h1m + kSampBuckets);
-  float *sl = reinterpret_cast<float *>(h1c + kSampBuckets);
+  uint32_t *hbase = reinterpret_cast<uint32_t *>(smem);
+  const Hist h0 = hist_at(hbase, kL0Buckets), h1 = hist_at(hbase + 4 * kL0Buckets, kL1Buckets);
+  uint64_t *cm = reinterpret_cast<uint64_t *>(hbase + 4 * (kL0Buckets + kL1Buckets));
+  uint32_t *cc = reinterpret_cast<uint32_t *>(cm + kCacheBuckets);
+  float *sl = reinterpret_cast<float *>(cc + kCacheBuckets);
   __shared__ SamplePub pub;
   __shared__ SampleScratch scr;
   __shared__ SelState st;
@@ -243,10 +282,7 @@ __global__ void __launch_bounds__(kSampThreads, 1)
   const int start = r * n_loc, len = max(0, min(n_loc, V - start));
 
   // 1. the slice, scaled by 1/temperature (a division, as the reference), and its first maximum
-  for (int d = tid; d < kSampBuckets; d += kSampThreads) {
-    h0m[d] = 0ull;
-    h0c[d] = 0u;
-  }
+  hist_clear(h0, kL0Buckets);
   float m = -INFINITY;
   int mi = INT_MAX;
   const float *src = logits + start;
@@ -336,18 +372,24 @@ __global__ void __launch_bounds__(kSampThreads, 1)
   __syncthreads();
   const float S = scr.S;
   uint64_t mass = 0;
-  {
-    const int rounds = (len + kSampThreads - 1) / kSampThreads;
-    for (int it = 0; it < rounds; ++it) {
-      const int k = it * kSampThreads + tid;
-      float p = 0.f;
+  for (int k0 = tid; k0 < len; k0 += 4 * kSampThreads) {
+    float e[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int k = k0 + u * kSampThreads;
+      e[u] = k < len ? sl[k] : 0.f;
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int k = k0 + u * kSampThreads;
       if (k < len) {
-        p = __fdiv_rn(sl[k], S);
+        const float p = __fdiv_rn(e[u], S);
         sl[k] = p;
+        const uint32_t b = pbits(p);
+        const uint64_t qm = qmass_bits(b);
+        mass += qm;
+        hist_add(h0, min(b >> 19, (uint32_t)(kL0Buckets - 1)), qm);  // p <= 1: b >> 19 <= 2032
       }
-      const uint64_t qm = qmass(p);
-      mass += qm;
-      hist_add(h0m, h0c, pbits(p) >> 19, k < len, qm);
     }
   }
 #pragma unroll
@@ -378,19 +420,19 @@ __global__ void __launch_bounds__(kSampThreads, 1)
   // 4. end of the top_p prefix: first position whose prefix mass reaches ceil(top_p * 2^62)
   const double tq = ceil((double)top_p * kQ62);
   const uint64_t t1 = !(tq < (double)tot) ? tot : (tq <= 0.0 ? 0ull : (uint64_t)tq);
-  select_desc<CL>(cluster, t1, sl, len, h0m, h0c, h1m, h1c, st, pub, scr);
+  select_desc<CL>(cluster, t1, sl, len, h0, h1, cm, cc, true, st, pub, scr);
   const uint64_t C = st.above + (uint64_t)tie_rank(st, t1) * qmass(__uint_as_float(st.prefix));
 
   // 5. the draw: first position whose prefix mass reaches ceil(u * C)
   const double uu = u > 0.0 ? u : 0.0;
   const double tu = ceil(uu * (double)C);
   const uint64_t t2 = !(tu < (double)C) ? C : (uint64_t)tu;
-  select_desc<CL>(cluster, t2, sl, len, h0m, h0c, h1m, h1c, st, pub, scr);
+  select_desc<CL>(cluster, t2, sl, len, h0, h1, cm, cc, false, st, pub, scr);
   const uint32_t j = tie_rank(st, t2);
   const uint32_t bstar = st.prefix, dlast = bstar & 0x7Fu;
   // the j-th element (by id) of the final group: find the CTA that holds it
   if (warp == 0) {
-    const uint32_t c = lane < CL ? *cluster.map_shared_rank(&h1c[dlast], lane) : 0u;
+    const uint32_t c = lane < CL ? *cluster.map_shared_rank(&h1.cnt[dlast], lane) : 0u;
     uint32_t incl = c;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -472,14 +514,15 @@ tb_status tb_sample_top_p(const float *logits, int64_t vocab, float temperature,
   // slices of a multiple of 4 elements, so that each starts 16-byte aligned when the row does
   auto slice = [&](int cl) { return (int)((((vocab + cl - 1) / cl) + 3) / 4 * 4); };
   const int n8 = slice(8), n16 = slice(16);
-  const size_t smem8 = (size_t)2 * kHistBytes + (size_t)n8 * 4, smem16 = (size_t)2 * kHistBytes + (size_t)n16 * 4;
+  const size_t fixed = kFixedSmem;
+  const size_t smem8 = fixed + (size_t)n8 * 4, smem16 = fixed + (size_t)n16 * 4;
   const size_t room = (size_t)st->smem_optin - kStaticReserve;  // the kernel's static shared memory is below this
   cudaStream_t s = as_stream(stream);
   if (smem8 <= room) return launch_sample<8>(logits, (int)vocab, temperature, top_p, u, out, smem8, n8, s);
   if (smem16 <= room)
     return launch_sample<16>(logits, (int)vocab, temperature, top_p, u, out, smem16, n16, s);
   return fail(TB_EINVAL, "tb_sample_top_p: vocab %lld exceeds the %lld a 16-CTA cluster holds in shared memory",
-              (long long)vocab, (long long)((room - 2 * kHistBytes) / 4 * 16));
+              (long long)vocab, (long long)((room - fixed) / 4 * 16));
 }
 
 }  // extern "C"

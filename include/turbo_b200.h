@@ -155,6 +155,13 @@ tb_status tb_argmax(const float *x_dev, int64_t rows, int64_t cols, int64_t *idx
  * allocation; *out_dev is written on the device. */
 tb_status tb_sample_top_p(const float *logits_dev, int64_t vocab, float temperature, float top_p,
                           double u, int32_t *out_dev, tb_stream stream);
+/* The same draw with the uniform number read on the device, u_dev[*pos_dev]
+ * (the position clamped into [0, max_seq)), and the id written as int64 to
+ * *idx_dev -- the slot tb_argmax fills -- so that a decode step recorded in a
+ * CUDA graph samples each token with the uniform number of its position. */
+tb_status tb_sample_top_p_at(const float *logits_dev, int64_t vocab, float temperature, float top_p,
+                             const double *u_dev, const int32_t *pos_dev, int64_t max_seq, int64_t *idx_dev,
+                             tb_stream stream);
 
 /* Causal mask of the prefill attention scores (src/nn/attention.cpp:120-129):
  * x[r, c] = value wherever c > r + diag_offset, for x[rows, cols] with row

@@ -50,3 +50,39 @@ def test_decode_token_ids_match_reference(model_path, golden, exact):
         first_bad[0], ref_margin[first_bad[0]], out["margins"][first_bad[0]], info)
     # the chosen logits' margins agree closely too
     assert np.max(np.abs(out["margins"] - ref_margin)) < 1e-3
+
+
+# ---- sampled decode (generate_text with temperature > 0) -----------------------
+# The graph samples each token on the device with the uniform number of its
+# position.  With u = 0 the draw is the most probable token and with a tiny
+# top_p the nucleus is that token alone, so both runs reproduce the reference's
+# greedy ids; a run with random uniform numbers is reproducible from them.
+
+STEPS_SAMPLED = 32
+
+
+@pytest.mark.parametrize("exact", [False, True])
+def test_sampled_decode_u0_is_greedy(model_path, golden, exact):
+    from turbo_b200.model import Model
+    m = Model(model_path, exact=exact)
+    n = STEPS_SAMPLED
+    out = m.generate(golden["prompt"], n, max_seq=int(golden["max_seq"]), temperature=0.8, top_p=0.9,
+                     uniforms=np.zeros(n + 1))
+    tiny = m.generate(golden["prompt"], n, max_seq=int(golden["max_seq"]), temperature=0.8, top_p=1e-6,
+                      uniforms=np.random.default_rng(1).random(n + 1))
+    m.close()
+    assert np.array_equal(out["ids"], golden["ids"][:n + 1])
+    assert np.array_equal(tiny["ids"], golden["ids"][:n + 1])
+
+
+def test_sampled_decode_reproducible(model_path, golden):
+    from turbo_b200.model import Model
+    m = Model(model_path, exact=False)
+    n = STEPS_SAMPLED
+    us = np.random.default_rng(7).random(n + 1)
+    a = m.generate(golden["prompt"], n, max_seq=int(golden["max_seq"]), temperature=0.8, top_p=0.9, uniforms=us)
+    b = m.generate(golden["prompt"], n, max_seq=int(golden["max_seq"]), temperature=0.8, top_p=0.9, uniforms=us)
+    m.close()
+    assert np.array_equal(a["ids"], b["ids"])
+    assert ((a["ids"] >= 0) & (a["ids"] < 128256)).all()
+    print("sampled ids", a["ids"][:12], "decode %.1f ms" % a["decode_ms"])

@@ -592,6 +592,23 @@ def test_sample_top_p_ties_across_slices(V, every):
             assert g == O.sample_top_p(x, 1.0, top_p, u)[0], (top_p, u)
 
 
+def test_sample_top_p_at_reads_uniform_of_position():
+    # the graph form: u = u_dev[*pos_dev] (clamped into [0, max_seq)), id as int64
+    V, max_seq = 32000, 64
+    x = synth.normal((V,), 2.5, seed=5)
+    xd = dev(x)
+    us = np.random.default_rng(3).random(max_seq)
+    ud = dev(us)
+    for pos in (0, 17, 63, 200, -5):
+        pd = dev(np.array([pos], np.int32))
+        idx = torch.full((1,), -1, dtype=torch.int64, device="cuda")
+        T.call("tb_sample_top_p_at", T.ptr(xd), V, 0.8, 0.9, T.ptr(ud), T.ptr(pd), max_seq, T.ptr(idx), S())
+        u = us[min(max(pos, 0), max_seq - 1)]
+        assert int(host(idx)[0]) == int(sample_many(xd, V, 0.8, 0.9, [u])[0]), pos
+    with pytest.raises(T.TbError):
+        T.call("tb_sample_top_p_at", T.ptr(xd), V, 0.8, 0.9, None, T.ptr(ud), max_seq, T.ptr(idx), S())
+
+
 def test_sample_top_p_degenerate_rows():
     cases = [np.array([1.0, np.nan, 3.0, 3.0], np.float32),       # NaN: greedy's first maximum
              np.full(5, -np.inf, np.float32),                     # no finite logit: 0

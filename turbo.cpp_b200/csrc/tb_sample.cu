@@ -264,10 +264,27 @@ __device__ void select_desc(cg::cluster_group &cluster, uint64_t target, const f
   }
 }
 
+// Where the uniform number comes from and where the drawn id goes: u, or
+// u_dev[*pos_dev] (position clamped into [0, max_seq)) when u_dev is set; the
+// id to out32 and/or out64.
+struct SampleIO {
+  double u;
+  const double *u_dev;
+  const int32_t *pos_dev;
+  int max_seq;
+  int32_t *out32;
+  int64_t *out64;
+};
+
+__device__ __forceinline__ void emit(const SampleIO &io, int64_t id) {
+  if (io.out32) *io.out32 = (int32_t)id;
+  if (io.out64) *io.out64 = id;
+}
+
 template <int CL>
 __global__ void __launch_bounds__(kSampThreads, 1)
-    sample_top_p_kernel(const float *__restrict__ logits, int V, int n_loc, float temperature, float top_p, double u,
-                        int32_t *__restrict__ out) {
+    sample_top_p_kernel(const float *__restrict__ logits, int V, int n_loc, float temperature, float top_p,
+                        SampleIO io) {
   cg::cluster_group cluster = cg::this_cluster();
   extern __shared__ __align__(16) uint8_t smem[];
   uint32_t *hbase = reinterpret_cast<uint32_t *>(smem);
@@ -411,7 +428,7 @@ __global__ void __launch_bounds__(kSampThreads, 1)
   }
   __syncthreads();
   tot = scr.off;
-  if (r == 0 && tid == 0) *out = scr.Mi;  // greedy choice unless a draw replaces it
+  if (r == 0 && tid == 0) emit(io, scr.Mi);  // greedy choice unless a draw replaces it
   if (tot == 0) {  // no positive finite probability (a NaN or infinite logit)
     cluster.sync();
     return;
@@ -424,6 +441,7 @@ __global__ void __launch_bounds__(kSampThreads, 1)
   const uint64_t C = st.above + (uint64_t)tie_rank(st, t1) * qmass(__uint_as_float(st.prefix));
 
   // 5. the draw: first position whose prefix mass reaches ceil(u * C)
+  const double u = io.u_dev ? io.u_dev[min(max(*io.pos_dev, 0), io.max_seq - 1)] : io.u;
   const double uu = u > 0.0 ? u : 0.0;
   const double tu = ceil(uu * (double)C);
   const uint64_t t2 = !(tu < (double)C) ? C : (uint64_t)tu;
@@ -463,7 +481,7 @@ __global__ void __launch_bounds__(kSampThreads, 1)
         if (match) {
           int rank = running + __popc(bal & ((1u << lane) - 1u)) + 1;
           for (int w = 0; w < warp; ++w) rank += scr.redi[w];
-          if (rank == jl) *out = start + k;
+          if (rank == jl) emit(io, start + k);
         }
         break;
       }
@@ -474,8 +492,8 @@ __global__ void __launch_bounds__(kSampThreads, 1)
 }
 
 template <int CL>
-tb_status launch_sample(const float *logits, int V, float temperature, float top_p, double u, int32_t *out,
-                        size_t smem, int n_loc, cudaStream_t s) {
+tb_status launch_sample(const float *logits, int V, float temperature, float top_p, const SampleIO &io, size_t smem,
+                        int n_loc, cudaStream_t s) {
   auto kern = sample_top_p_kernel<CL>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e == cudaSuccess && CL > 8) e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
@@ -492,23 +510,17 @@ tb_status launch_sample(const float *logits, int V, float temperature, float top
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  e = cudaLaunchKernelEx(&cfg, kern, logits, V, n_loc, temperature, top_p, u, out);
+  e = cudaLaunchKernelEx(&cfg, kern, logits, V, n_loc, temperature, top_p, io);
   if (e != cudaSuccess) return fail(TB_ECUDA, "tb_sample_top_p: %s", cudaGetErrorString(e));
   return check_launch("tb_sample_top_p");
 }
 
-}  // namespace
-}  // namespace tb
-
-using namespace tb;
-
-extern "C" {
-
-tb_status tb_sample_top_p(const float *logits, int64_t vocab, float temperature, float top_p, double u,
-                          int32_t *out, tb_stream stream) {
-  if (!logits || !out) return fail(TB_EINVAL, "tb_sample_top_p: null pointer");
-  if (vocab <= 0 || vocab > INT_MAX) return fail(TB_EINVAL, "tb_sample_top_p: vocab %lld out of range", (long long)vocab);
-  if (!(temperature > 0.f)) return fail(TB_EINVAL, "tb_sample_top_p: temperature must be positive");
+// Checks the arguments, picks the cluster size and launches.
+tb_status sample_launch(const char *who, const float *logits, int64_t vocab, float temperature, float top_p,
+                        const SampleIO &io, tb_stream stream) {
+  if (!logits || !(io.out32 || io.out64)) return fail(TB_EINVAL, "%s: null pointer", who);
+  if (vocab <= 0 || vocab > INT_MAX) return fail(TB_EINVAL, "%s: vocab %lld out of range", who, (long long)vocab);
+  if (!(temperature > 0.f)) return fail(TB_EINVAL, "%s: temperature must be positive", who);
   DeviceState *st;
   TB_TRY(device_state(&st));
   // slices of a multiple of 4 elements, so that each starts 16-byte aligned when the row does
@@ -518,11 +530,30 @@ tb_status tb_sample_top_p(const float *logits, int64_t vocab, float temperature,
   const size_t smem8 = fixed + (size_t)n8 * 4, smem16 = fixed + (size_t)n16 * 4;
   const size_t room = (size_t)st->smem_optin - kStaticReserve;  // the kernel's static shared memory is below this
   cudaStream_t s = as_stream(stream);
-  if (smem8 <= room) return launch_sample<8>(logits, (int)vocab, temperature, top_p, u, out, smem8, n8, s);
-  if (smem16 <= room)
-    return launch_sample<16>(logits, (int)vocab, temperature, top_p, u, out, smem16, n16, s);
-  return fail(TB_EINVAL, "tb_sample_top_p: vocab %lld exceeds the %lld a 16-CTA cluster holds in shared memory",
+  if (smem8 <= room) return launch_sample<8>(logits, (int)vocab, temperature, top_p, io, smem8, n8, s);
+  if (smem16 <= room) return launch_sample<16>(logits, (int)vocab, temperature, top_p, io, smem16, n16, s);
+  return fail(TB_EINVAL, "%s: vocab %lld exceeds the %lld a 16-CTA cluster holds in shared memory", who,
               (long long)vocab, (long long)((room - fixed) / 4 * 16));
+}
+}  // namespace
+}  // namespace tb
+
+using namespace tb;
+
+extern "C" {
+
+tb_status tb_sample_top_p(const float *logits, int64_t vocab, float temperature, float top_p, double u,
+                          int32_t *out, tb_stream stream) {
+  return sample_launch("tb_sample_top_p", logits, vocab, temperature, top_p,
+                       SampleIO{u, nullptr, nullptr, 0, out, nullptr}, stream);
+}
+
+tb_status tb_sample_top_p_at(const float *logits, int64_t vocab, float temperature, float top_p, const double *u_dev,
+                             const int32_t *pos_dev, int64_t max_seq, int64_t *idx_dev, tb_stream stream) {
+  if (!u_dev || !pos_dev || max_seq <= 0 || max_seq > INT_MAX)
+    return fail(TB_EINVAL, "tb_sample_top_p_at: uniform numbers, position or max_seq missing");
+  return sample_launch("tb_sample_top_p_at", logits, vocab, temperature, top_p,
+                       SampleIO{0.0, u_dev, pos_dev, (int)max_seq, nullptr, idx_dev}, stream);
 }
 
 }  // extern "C"

@@ -1,4 +1,5 @@
-// decode_graph.hpp -- greedy decode of MiniGPT as one CUDA graph per token.
+// decode_graph.hpp -- decode of MiniGPT as one CUDA graph per token, greedy or
+// nucleus-sampled.
 // No reference counterpart: the reference loop (src/core/generate.cpp:30-63)
 // calls MiniGPT::forward once per token.
 #pragma once
@@ -12,7 +13,7 @@ class MiniGPT;
 class KVCache;
 
 // One decode step -- embedding, the transformer blocks, final norm, LM head,
-// argmax -- recorded once as a CUDA graph.  The position, the input token and
+// argmax or nucleus sample -- recorded once as a CUDA graph.  The position, the input token and
 // the chosen tokens live in device memory, so the same graph is replayed for
 // every token with no host work in between.  The step runs the kernels
 // MiniGPT::forward runs for one token, except that each layer's attention is a
@@ -25,25 +26,31 @@ class KVCache;
 class DecodeGraph {
  public:
   // `kv` holds the prompt's keys/values (kv.get_current_seq_len() rows).
-  DecodeGraph(MiniGPT &model, KVCache &kv, bool want_margins);
+  // temperature > 0 samples each token as sample_top_p(logits, temperature,
+  // top_p) does (src/core/generate.cpp:42-47), with the uniform numbers that
+  // generate() is given; otherwise the choice is greedy.
+  DecodeGraph(MiniGPT &model, KVCache &kv, bool want_margins, float temperature = 0.f, float top_p = 0.9f);
   ~DecodeGraph();
   DecodeGraph(const DecodeGraph &) = delete;
   DecodeGraph &operator=(const DecodeGraph &) = delete;
 
   // Feeds `first` at the cache's current position and the chosen token after
   // it, `steps` times: out_ids[s] is the token chosen at step s; margins[s]
-  // (optional) its top-1 minus top-2 logit.  Advances the cache by `steps`.
-  void generate(int first, size_t steps, int *out_ids, float *margins);
+  // (optional) its logit minus the largest other logit.  When sampling,
+  // uniforms[s] in [0, 1) draws step s's token.  Advances the cache by `steps`.
+  void generate(int first, size_t steps, int *out_ids, float *margins, const double *uniforms = nullptr);
 
  private:
   void enqueue_step();
   void enqueue_step_fused();
+  void enqueue_pick(tb_stream s);  // argmax or sample, margin, advance
   void *buf(size_t bytes);
   bool fused_ = false;
 
   MiniGPT &m_;
   KVCache &kv_;
   bool margins_on_;
+  float temperature_, top_p_;
   tb_stream stream_ = nullptr;
   tb_graph graph_ = nullptr;
   size_t E_, H_, KVH_, D_, F_, V_;
@@ -54,6 +61,7 @@ class DecodeGraph {
   int n_arena_ = 0;
   int32_t *ids_, *pos_, *hist_;
   int64_t *idx_;
+  double *uniform_ = nullptr;  // [max_seq]: the uniform number of each position's draw
   float *margins_, *x_, *xn_, *h_, *q_, *k_, *v_, *ctx_, *ao_, *g_, *u_, *sw_, *fo_, *logits_;
 };
 

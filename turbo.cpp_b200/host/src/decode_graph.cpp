@@ -23,8 +23,8 @@ void *DecodeGraph::buf(size_t bytes) {
   return p;
 }
 
-DecodeGraph::DecodeGraph(MiniGPT &model, KVCache &kv, bool want_margins)
-    : m_(model), kv_(kv), margins_on_(want_margins) {
+DecodeGraph::DecodeGraph(MiniGPT &model, KVCache &kv, bool want_margins, float temperature, float top_p)
+    : m_(model), kv_(kv), margins_on_(want_margins), temperature_(temperature), top_p_(top_p) {
   if (m_.blocks.empty()) throw std::invalid_argument("DecodeGraph: the model has no blocks");
   const Tensor &emb = m_.tok_emb.get_weight();
   E_ = emb.get_shape()[0];
@@ -56,6 +56,7 @@ DecodeGraph::DecodeGraph(MiniGPT &model, KVCache &kv, bool want_margins)
   pos_ = static_cast<int32_t *>(buf(16));
   idx_ = static_cast<int64_t *>(buf(16));
   hist_ = static_cast<int32_t *>(buf(sizeof(int32_t) * (size_t)max_seq_));
+  if (temperature_ > 0.f) uniform_ = static_cast<double *>(buf(sizeof(double) * (size_t)max_seq_));
   margins_ = static_cast<float *>(buf(sizeof(float) * (size_t)max_seq_));
   const size_t f = sizeof(float);
   x_ = static_cast<float *>(buf(f * E_));
@@ -156,9 +157,7 @@ void DecodeGraph::enqueue_step_fused() {
   // the LM head (128256 rows) runs faster on the tensor-core GEMV than fused
   tb_check(tb_rmsnorm(TB_F32, x_, gptr(m_.norm), xn_, 1, E, m_.norm.epsilon, s));
   linear(m_.lm_head, xn_, logits_, s);
-  tb_check(tb_argmax(logits_, 1, V, idx_, s));
-  if (margins_on_) tb_check(tb_decode_margin(logits_, V, idx_, pos_, max_seq_, margins_, s));
-  tb_check(tb_decode_advance(idx_, ids_, pos_, hist_, max_seq_, s));
+  enqueue_pick(s);
 }
 
 void DecodeGraph::enqueue_step() {
@@ -199,13 +198,22 @@ void DecodeGraph::enqueue_step() {
   tb_check(tb_rmsnorm(TB_F32, x_, static_cast<const float *>(m_.norm.get_weight().device_ptr()), xn_, 1, E,
                       m_.norm.epsilon, s));
   linear(m_.lm_head, xn_, logits_, s);
-  tb_check(tb_argmax(logits_, 1, V, idx_, s));
+  enqueue_pick(s);
+}
+
+void DecodeGraph::enqueue_pick(tb_stream s) {
+  const int64_t V = (int64_t)V_;
+  if (uniform_)
+    tb_check(tb_sample_top_p_at(logits_, V, temperature_, top_p_, uniform_, pos_, max_seq_, idx_, s));
+  else
+    tb_check(tb_argmax(logits_, 1, V, idx_, s));
   if (margins_on_) tb_check(tb_decode_margin(logits_, V, idx_, pos_, max_seq_, margins_, s));
   tb_check(tb_decode_advance(idx_, ids_, pos_, hist_, max_seq_, s));
 }
 
-void DecodeGraph::generate(int first, size_t steps, int *out_ids, float *margins) {
+void DecodeGraph::generate(int first, size_t steps, int *out_ids, float *margins, const double *uniforms) {
   if (steps == 0) return;
+  if (uniform_ && !uniforms) throw std::invalid_argument("DecodeGraph: sampling needs a uniform number per step");
   const int pos0 = kv_.get_current_seq_len();
   if (first < 0 || (size_t)first >= V_)
     throw std::out_of_range("Token ID " + std::to_string(first) + " exceeds vocabulary size " + std::to_string(V_));
@@ -215,6 +223,7 @@ void DecodeGraph::generate(int first, size_t steps, int *out_ids, float *margins
   const int32_t init[2] = {first, pos0};
   tb_check(tb_upload(ids_, &init[0], sizeof(int32_t), stream_));
   tb_check(tb_upload(pos_, &init[1], sizeof(int32_t), stream_));
+  if (uniform_) tb_check(tb_upload(uniform_ + pos0, uniforms, sizeof(double) * steps, stream_));
   // the first step runs eagerly: it sets every kernel's attributes before capture
   enqueue_step();
   if (steps > 1) {

@@ -6,6 +6,7 @@
 #include <cmath>
 #include <cstring>
 #include <memory>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -67,20 +68,23 @@ TBM_API void *tbm_model_load(const char *path, int exact) {
 
 TBM_API void tbm_model_free(void *h) { delete static_cast<Model *>(h); }
 
-// Prefill `prompt`, then `steps` greedy steps.  out_ids[steps + 1] receives the
-// token chosen after the prefill and after each step.  margins (optional)
-// receives top-1 minus top-2 logit of each choice, last_logits (optional) the
-// final step's logits -- both diagnostics read back from the device.
-TBM_API int tbm_model_generate(void *h, const int *prompt, size_t n_prompt, size_t steps, size_t max_seq,
-                               int *out_ids, float *margins, float *last_logits, double *prefill_ms,
-                               double *decode_ms) {
-  auto *m = static_cast<Model *>(h);
+// Prefill `prompt`, then `steps` decode steps.  out_ids[steps + 1] receives
+// the token chosen after the prefill and after each step: greedy, or with
+// temperature > 0 sample_top_p(logits, temperature, top_p) drawn with
+// uniforms[steps + 1] (src/core/generate.cpp:42-47).  margins (optional)
+// receives each choice's logit minus the largest other logit, last_logits
+// (optional) the final step's logits -- diagnostics read back from the device.
+static int generate_impl(Model *m, const int *prompt, size_t n_prompt, size_t steps, size_t max_seq, float temperature,
+                         float top_p, const double *uniforms, int *out_ids, float *margins, float *last_logits,
+                         double *prefill_ms, double *decode_ms) {
   return guarded([&] {
+    if (temperature > 0.f && !uniforms) throw std::invalid_argument("sampling needs a uniform number per token");
     turbo::MiniGPT &model = *m->model;
     turbo::KVCache kv((int)max_seq, (int)model.get_num_layers(), (int)model.get_num_kv_heads(),
                       (int)model.get_head_dim());
     auto pick = [&](const Tensor &logits, size_t slot) {
-      const int id = turbo::greedy_sample(logits);
+      const int id = temperature > 0.f ? turbo::sample_top_p(logits, temperature, top_p, uniforms[slot])
+                                       : turbo::greedy_sample(logits);
       out_ids[slot] = id;
       if (margins || last_logits) {
         const size_t V = logits.get_shape().back();
@@ -104,8 +108,9 @@ TBM_API int tbm_model_generate(void *h, const int *prompt, size_t n_prompt, size
     auto t1 = std::chrono::steady_clock::now();
     if (!m->exact && steps > 0 && !last_logits) {
       turbo::device_synchronize();  // the prefill's cache writes, before the decode stream starts
-      turbo::DecodeGraph dg(model, kv, margins != nullptr);
-      dg.generate(next, steps, out_ids + 1, margins ? margins + 1 : nullptr);
+      turbo::DecodeGraph dg(model, kv, margins != nullptr, temperature, top_p);
+      dg.generate(next, steps, out_ids + 1, margins ? margins + 1 : nullptr,
+                  temperature > 0.f ? uniforms + 1 : nullptr);
     } else {
       for (size_t s = 0; s < steps; ++s) {
         logits = model.forward(std::vector<int>{next}, &kv);
@@ -118,4 +123,20 @@ TBM_API int tbm_model_generate(void *h, const int *prompt, size_t n_prompt, size
     if (prefill_ms) *prefill_ms = std::chrono::duration<double, std::milli>(t1 - t0).count();
     if (decode_ms) *decode_ms = std::chrono::duration<double, std::milli>(t2 - t1).count();
   });
+}
+
+TBM_API int tbm_model_generate(void *h, const int *prompt, size_t n_prompt, size_t steps, size_t max_seq,
+                               int *out_ids, float *margins, float *last_logits, double *prefill_ms,
+                               double *decode_ms) {
+  return generate_impl(static_cast<Model *>(h), prompt, n_prompt, steps, max_seq, 0.f, 0.f, nullptr, out_ids,
+                       margins, last_logits, prefill_ms, decode_ms);
+}
+
+// generate_text with temperature > 0 (src/core/generate.cpp:42-47; top_p is
+// 0.9 there): uniforms[steps + 1] are the uniform numbers of the draws.
+TBM_API int tbm_model_generate_sampled(void *h, const int *prompt, size_t n_prompt, size_t steps, size_t max_seq,
+                                       float temperature, float top_p, const double *uniforms, int *out_ids,
+                                       float *margins, double *prefill_ms, double *decode_ms) {
+  return generate_impl(static_cast<Model *>(h), prompt, n_prompt, steps, max_seq, temperature, top_p, uniforms,
+                       out_ids, margins, nullptr, prefill_ms, decode_ms);
 }

@@ -63,6 +63,7 @@ SIGNATURES = {
     "tb_softmax": [_P, _P, _I64, _I64, _P],
     "tb_argmax": [_P, _I64, _I64, _P, _P],
     "tb_sample_top_p": [_P, _I64, _F, _F, ctypes.c_double, _P, _P],
+    "tb_sample_top_p_at": [_P, _I64, _F, _F, _P, _P, _I64, _P, _P],
     "tb_rope": [_VP, _P, _P, _I64, _I64, _I64, _P],
     "tb_fill_upper": [_P, _I64, _I64, _I64, _I64, _F, _P],
     "tb_dequant": [_I, _P, _I64, _P, _P],

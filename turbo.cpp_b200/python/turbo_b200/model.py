@@ -25,6 +25,11 @@ def lib():
         L.tbm_model_generate.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t,
                                          ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                          ctypes.POINTER(ctypes.c_double), ctypes.POINTER(ctypes.c_double)]
+        L.tbm_model_generate_sampled.restype = ctypes.c_int
+        L.tbm_model_generate_sampled.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t,
+                                                 ctypes.c_size_t, ctypes.c_float, ctypes.c_float, ctypes.c_void_p,
+                                                 ctypes.c_void_p, ctypes.c_void_p, ctypes.POINTER(ctypes.c_double),
+                                                 ctypes.POINTER(ctypes.c_double)]
         _lib = L
     return _lib
 
@@ -35,16 +40,33 @@ class Model:
         if not self.h:
             raise RuntimeError("tbm_model_load: " + lib().tbm_last_error().decode())
 
-    def generate(self, prompt, steps, max_seq=1024, want_margins=True, want_logits=False, vocab=128256):
+    def generate(self, prompt, steps, max_seq=1024, want_margins=True, want_logits=False, vocab=128256,
+                 temperature=0.0, top_p=0.9, uniforms=None):
+        """Prefill, then `steps` tokens: greedy, or with temperature > 0 nucleus
+        sampled (the reference's generate loop), token s drawn with
+        uniforms[s] in [0, 1) (steps + 1 numbers; drawn here when not given)."""
         prompt = np.ascontiguousarray(prompt, np.int32)
         ids = np.zeros(steps + 1, np.int32)
         margins = np.zeros(steps + 1, np.float32) if want_margins else None
         logits = np.zeros(vocab, np.float32) if want_logits else None
         pre, dec = ctypes.c_double(), ctypes.c_double()
-        st = lib().tbm_model_generate(self.h, prompt.ctypes.data, prompt.size, steps, max_seq, ids.ctypes.data,
-                                      margins.ctypes.data if margins is not None else None,
-                                      logits.ctypes.data if logits is not None else None,
-                                      ctypes.byref(pre), ctypes.byref(dec))
+        if temperature > 0:
+            if want_logits:
+                raise ValueError("want_logits is for greedy runs")
+            if uniforms is None:
+                uniforms = np.random.default_rng().random(steps + 1)
+            uniforms = np.ascontiguousarray(uniforms, np.float64)
+            if uniforms.size != steps + 1:
+                raise ValueError("need steps + 1 uniform numbers")
+            st = lib().tbm_model_generate_sampled(self.h, prompt.ctypes.data, prompt.size, steps, max_seq,
+                                                  float(temperature), float(top_p), uniforms.ctypes.data,
+                                                  ids.ctypes.data, margins.ctypes.data if margins is not None else None,
+                                                  ctypes.byref(pre), ctypes.byref(dec))
+        else:
+            st = lib().tbm_model_generate(self.h, prompt.ctypes.data, prompt.size, steps, max_seq, ids.ctypes.data,
+                                          margins.ctypes.data if margins is not None else None,
+                                          logits.ctypes.data if logits is not None else None,
+                                          ctypes.byref(pre), ctypes.byref(dec))
         if st:
             raise RuntimeError("tbm_model_generate: " + lib().tbm_last_error().decode())
         return dict(ids=ids, margins=margins, logits=logits, prefill_ms=pre.value, decode_ms=dec.value)

@@ -15,9 +15,8 @@
 // (non-negative floats order as their bits) with each bucket's probability
 // mass summed exactly as an integer, q(p) = floor(p * 2^62), so a prefix mass
 // is exact.  Digits are bits 29..19, 18..7 and 6..0 (bits 31 and 30 are 0
-// for 0 <= p <= 1);
-// equal probabilities are ordered by token id (std::sort leaves them in an
-// unspecified order).  The result can differ from the reference's only where
+// for 0 <= p <= 1); equal probabilities are ordered by token id (std::sort
+// leaves them in an unspecified order).  The result can differ from the reference's only where
 // top_p or u lies within fp32 rounding of a prefix boundary: the device's exp
 // is CUDA's expf (within 2 ulp), its sum is taken in another order, and the
 // reference's prefix sums are fp32 running sums.  A NaN logit makes the sum

@@ -69,7 +69,7 @@ def _cases(T, torch):
             return (lambda i, s: T.load().tb_binary(0, T.byref(va[i % k]), T.byref(vb[i % k]), T.byref(vo[i % k]), s)), keep
         cases.append(Case("add_" + tag, cfg, make, 3 * n * es))
 
-    add_case(128, 2048, torch.float32, "f32_1x128x2048", "configs[0]: x+a fp32 [1,128,2048]")
+    add_case(128, 2048, torch.float32, "f32_1x128x2048", "small shapes: x+a fp32 [1,128,2048]")
     add_case(1 << 20, 4096, torch.float32, "f32_16GiB", "sweep: [1048576,4096] fp32 (16 GiB per tensor)")
     add_case(1 << 18, 4096, torch.bfloat16, "bf16_2GiB", "sweep: [262144,4096] bf16")
 
@@ -127,7 +127,7 @@ def _cases(T, torch):
                                                       1e-5, s)), (X, g, Y)
         cases.append(Case("rmsnorm_" + tag, cfg, make, 2 * n * 4 + cols * 4))
 
-    rms_case(128, 2048, "128x2048", "configs[0]: RMSNorm [128,2048] eps 1e-5")
+    rms_case(128, 2048, "128x2048", "small shapes: RMSNorm [128,2048] eps 1e-5")
     rms_case(1 << 18, 4096, "4GiB", "sweep: [262144,4096] fp32")
 
     def swiglu_case(n, tag, cfg):
@@ -140,7 +140,7 @@ def _cases(T, torch):
             return (lambda i, s: T.load().tb_swiglu(T.F32, T.ptr(G[i % k]), T.ptr(U[i % k]), T.ptr(Y[i % k]), n, s)), (G, U, Y)
         cases.append(Case("swiglu_" + tag, cfg, make, 3 * n * 4))
 
-    swiglu_case(128 * 8192, "1x128x8192", "configs[0]: SwiGLU [1,128,8192]")
+    swiglu_case(128 * 8192, "1x128x8192", "small shapes: SwiGLU [1,128,8192]")
     swiglu_case((1 << 18) * 4096, "4GiB", "sweep: [262144,4096] fp32")
 
     # ---- A9 softmax, A15 argmax -----------------------------------------------------------
@@ -157,11 +157,11 @@ def _cases(T, torch):
             return (lambda i, s: T.load().tb_argmax(T.ptr(X[i % k]), rows, cols, T.ptr(idx), s)), (X, idx)
         cases.append(Case(kind + "_" + tag, cfg, make, (2 if kind == "softmax" else 1) * n * 4 + (0 if kind == "softmax" else 8 * rows)))
 
-    rows_case("softmax", 1, 128256, "1x128256", "configs[0]: softmax logits[1,128256]")
+    rows_case("softmax", 1, 128256, "1x128256", "small shapes: softmax logits[1,128256]")
     rows_case("softmax", 64, 128256, "64x128256", "sweep: softmax [64,128256]")
     rows_case("softmax", 1024, 128256, "1024x128256", "sweep: softmax [1024,128256] (525 MB)")
     rows_case("softmax", 8192, 128256, "8192x128256", "large: softmax [8192,128256] (4.2 GB)")
-    rows_case("argmax", 1, 128256, "1x128256", "configs[0]: argmax [1,128256]")
+    rows_case("argmax", 1, 128256, "1x128256", "small shapes: argmax [1,128256]")
     rows_case("argmax", 64, 128256, "64x128256", "sweep: argmax [64,128256]")
     rows_case("argmax", 8192, 128256, "8192x128256", "large: argmax [8192,128256] (4.2 GB)")
 
@@ -189,7 +189,7 @@ def _cases(T, torch):
             W = [qblocks(nb, 34, 11 + i) for i in range(kk)]
             Y = [torch.empty(N * K, device=dev) for _ in range(kk)]
             return (lambda i, s: T.load().tb_dequant(T.Q8_0, T.ptr(W[i % kk]), nb, T.ptr(Y[i % kk]), s)), (W, Y)
-        cases.append(Case("dequant_q8_0_8192x2048", "configs[1]: exact block dequant of W[8192,2048]", make, nb * 34 + N * K * 4))
+        cases.append(Case("dequant_q8_0_8192x2048", "decode: exact block dequant of W[8192,2048]", make, nb * 34 + N * K * 4))
 
     dequant_case(8192, 2048)
 
@@ -203,7 +203,7 @@ def _cases(T, torch):
             return (lambda i, s: T.load().tb_quantize_q8_0(T.ptr(X[i % k]), M, K, T.ptr(Q[i % k]), s)), (X, Q)
         cases.append(Case("quantize_q8_0_%dx%d" % (M, K), cfg, make, nbytes))
 
-    quantize_case(512, 8192, "configs[2]: X[512,8192] -> Q8_0")
+    quantize_case(512, 8192, "prefill: X[512,8192] -> Q8_0")
     quantize_case(65536, 8192, "sweep: X[65536,8192] -> Q8_0 (2.1 GB in)")
 
     def embed_case(n, dim, vocab):
@@ -212,7 +212,7 @@ def _cases(T, torch):
             ids = torch.from_numpy(np.random.default_rng(0).integers(0, vocab, n).astype(np.int32)).to(dev)
             Y = torch.empty((n, dim), device=dev)
             return (lambda i, s: T.load().tb_embedding(T.Q8_0, T.ptr(W), dim, vocab, T.ptr(ids), n, T.ptr(Y), s)), (W, ids, Y)
-        cases.append(Case("embedding_q8_0_512ids", "configs[3]: token_embd gather of 512 ids, dim 2048", make,
+        cases.append(Case("embedding_q8_0_512ids", "1B model: token_embd gather of 512 ids, dim 2048", make,
                           n * (dim // 32 * 34 + dim * 4)))
 
     embed_case(512, 2048, 128256)
@@ -224,7 +224,7 @@ def _cases(T, torch):
             s_ = torch.rand(1024 * D // 2, device=dev)
             v = T.view(X, 0, (1, H, S, D), (S * H * D, D, H * D, 1))
             return (lambda i, s: T.load().tb_rope(T.byref(v), T.ptr(c), T.ptr(s_), D, 1024, 0, s)), (X, c, s_, v)
-        cases.append(Case("rope_q_1x32x512x64", "configs[3]: RoPE on Q [1,32,512,64] view", make, 2 * H * S * D * 4 + S * D * 4))
+        cases.append(Case("rope_q_1x32x512x64", "1B model: RoPE on Q [1,32,512,64] view", make, 2 * H * S * D * 4 + S * D * 4))
 
     rope_case(32, 512, 64)
 
@@ -241,10 +241,10 @@ def _cases(T, torch):
             return (lambda i, s: fn(T.Q8_0, T.ptr(x), 1, K, T.ptr(W[i % k]), N, T.ptr(y), s)), (W, x, y)
         cases.append(Case(tag, cfg, make, wb + K * 4 + N * 4))
 
-    gemv_case(8192, 2048, "tb_matmul_quant", "gemv_q8_0_8192x2048", "configs[1]: decode GEMV (default, 1e-5)")
-    gemv_case(8192, 2048, "tb_matmul_quant_exact", "gemv_q8_0_8192x2048_exact", "configs[1]: decode GEMV, bit-exact")
-    gemv_case(2048, 8192, "tb_matmul_quant", "gemv_q8_0_2048x8192", "configs[3]: ffn_down GEMV")
-    gemv_case(128256, 2048, "tb_matmul_quant", "gemv_q8_0_128256x2048", "configs[3]: tied lm_head GEMV")
+    gemv_case(8192, 2048, "tb_matmul_quant", "gemv_q8_0_8192x2048", "decode: decode GEMV (default, 1e-5)")
+    gemv_case(8192, 2048, "tb_matmul_quant_exact", "gemv_q8_0_8192x2048_exact", "decode: decode GEMV, bit-exact")
+    gemv_case(2048, 8192, "tb_matmul_quant", "gemv_q8_0_2048x8192", "1B model: ffn_down GEMV")
+    gemv_case(128256, 2048, "tb_matmul_quant", "gemv_q8_0_128256x2048", "1B model: tied lm_head GEMV")
 
     def gemm_case(dt, M, K, N, tag, cfg):
         def make():
@@ -255,8 +255,8 @@ def _cases(T, torch):
         wb = N * K // 32 * (34 if dt == T.Q8_0 else 18)
         cases.append(Case(tag, cfg, make, wb + M * K * 4 + M * N * 4, flops=2 * M * N * K))
 
-    gemm_case(T.Q4_0, 512, 8192, 2048, "gemm_q4_0_512x8192x2048", "configs[2]: Q4_0 down GEMM")
-    gemm_case(T.Q8_0, 512, 2048, 8192, "gemm_q8_0_512x2048x8192", "configs[2]: Q8_0 gate/up GEMM")
+    gemm_case(T.Q4_0, 512, 8192, 2048, "gemm_q4_0_512x8192x2048", "prefill: Q4_0 down GEMM")
+    gemm_case(T.Q8_0, 512, 2048, 8192, "gemm_q8_0_512x2048x8192", "prefill: Q8_0 gate/up GEMM")
     return cases
 
 

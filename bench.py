@@ -39,6 +39,11 @@ ROW_BYTES = K_COLS // 32 * 34
 W_BYTES = N_ROWS * ROW_BYTES                      # 17,825,792
 ALGO_BYTES = W_BYTES + K_COLS * 4 + N_ROWS * 4    # 17,866,752 per GEMV
 N_COPIES = 32
+REF_SAMPLE_S = 10.0             # seconds of reference CPU GEMVs per measurement
+GRAPH_MAX = 256                 # GEMV launches per captured graph
+L2_FLUSH_BYTES = 256 << 20      # written before the timed region: twice the 126 MB L2
+SLEEP_CYCLES_BASE = 200000      # ~0.1 ms of device sleep ahead of the start event
+SLEEP_CYCLES_PER_REPLAY = 40000  # + ~20 us per graph replay the host must enqueue
 METRIC = "Q8_0 decode GEMV HBM GB/s (W[8192,2048] Q8_0, x fp32[1,2048])"
 WORKLOAD = "q8_0_gemv_8192x2048"
 
@@ -150,6 +155,13 @@ def cpu_reference_rate(seconds=10.0, max_steps=None):
     return ALGO_BYTES * steps / dt / 1e9, steps, cores, dt
 
 
+def bench_config(n_gpus):
+    """The workload both arms run (the same dict in both JSON lines)."""
+    return {"workload": WORKLOAD, "N": N_ROWS, "K": K_COLS, "M": 1, "parallelism": "row-shard x%d" % n_gpus,
+            "l2": "inputs larger than L2 (%d rotating weight copies, %.0f MB) and L2 flushed before the "
+                  "timed region" % (N_COPIES, N_COPIES * W_BYTES / 1e6)}
+
+
 def run_reference(args):
     ws, rank, _ = dist_env()
     if rank != 0:
@@ -158,17 +170,19 @@ def run_reference(args):
     if not R.available():
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libturbo_ref.so was not built"}))
         return 0
-    # warmup steps, then a bounded sample of the K requested steps (<= ~60 s)
-    gbs, steps, cores, dt = cpu_reference_rate(seconds=60.0, max_steps=args.steps)
+    # a bounded sample of about REF_SAMPLE_S seconds of full GEMVs, the same
+    # sample the cpu_baseline leg of our own arm takes (a step of K = 20 GEMVs
+    # is ~25 ms of CPU work: too short to time the reference's OpenMP loop)
+    gbs, steps, cores, dt = cpu_reference_rate(seconds=REF_SAMPLE_S)
     ms = dt / steps * 1e3
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s",
         "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
-        "data": "synthetic", "config": {"workload": WORKLOAD, "N": N_ROWS, "K": K_COLS, "M": 1,
-                                        "requested_steps": args.steps},
+        "data": "synthetic", "config": bench_config(args.gpus),
         "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "reference",
-                         "sample": "%d full GEMVs (Tensor::matmul Q8_0, OpenMP over %d threads)" % (steps, cores)},
+                         "sample": "%d full GEMVs in %.1f s (Tensor::matmul Q8_0, OpenMP over %d threads)" % (
+                             steps, dt, cores)},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line))
@@ -230,7 +244,13 @@ def run_ours(args):
     stream.synchronize()
 
     # --- value: K steps replayed from CUDA graphs --------------------------------
-    G = N_COPIES
+    # One graph of G = min(K, GRAPH_MAX) GEMVs (weight copy i % 32 at step i),
+    # replayed K // G times, plus a graph of the K % G remaining ones.  Every
+    # graph is replayed once before the timed region (upload and first-launch
+    # costs stay outside it).  Then L2 is flushed, and a device-side sleep is
+    # queued ahead of the start event, so that the host has enqueued every
+    # replay before the first timed GEMV starts: the region measures the GPU.
+    G = min(args.steps, GRAPH_MAX)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
         for i in range(G):
@@ -241,19 +261,27 @@ def run_ours(args):
         graph_tail = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph_tail, stream=stream):
             for i in range(tail):
-                gemv(i, s=T.stream_handle(torch.cuda.current_stream()))
+                gemv(G + i, s=T.stream_handle(torch.cuda.current_stream()))
+    warm_replays = 0
     with torch.cuda.stream(stream):
-        graph.replay()
+        for g in (graph, graph_tail):
+            if g is not None:
+                g.replay()
+                warm_replays += 1
     stream.synchronize()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
 
     if ws > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_replays = args.steps // G
     with ClockSampler(local) as clocks:
         with torch.cuda.stream(stream):
+            flush.fill_(1)
+            torch.cuda._sleep(SLEEP_CYCLES_BASE + SLEEP_CYCLES_PER_REPLAY * (n_replays + 1))
             start.record(stream)
-            for _ in range(args.steps // G):
+            for _ in range(n_replays):
                 graph.replay()
             if graph_tail is not None:
                 graph_tail.replay()
@@ -261,6 +289,7 @@ def run_ours(args):
         stream.synchronize()
     torch.cuda.synchronize()
     total_ms = start.elapsed_time(end)
+    del flush
     if ws > 1:
         t = torch.tensor([total_ms], device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -313,7 +342,7 @@ def run_ours(args):
     if not args.no_cpu_baseline and ws == 1:
         from oracle import refbind as R
         if R.available():
-            gbs, steps, cores, dt = cpu_reference_rate(seconds=10.0)
+            gbs, steps, cores, dt = cpu_reference_rate(seconds=REF_SAMPLE_S)
             cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": cores, "kind": "reference",
                    "sample": "%d full GEMVs on the reference library (%.1f s, OpenMP %d threads)" % (steps, dt, cores)}
     line = {
@@ -321,10 +350,12 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": round(total_ms / args.steps, 6), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
         "data": "synthetic (N(0,0.02) weights quantized Q8_0, x N(0,1), seeded)",
-        "config": {"workload": WORKLOAD, "N": N_ROWS, "K": K_COLS, "M": 1, "parallelism": "row-shard x%d" % ws,
-                   "entry": entry, "tolerance": "bit-exact" if args.exact else "1e-5 * sum|w x| per output",
-                   "l2": "inputs larger than L2: %d rotating weight copies (%.0f MB)" % (N_COPIES, N_COPIES * W_BYTES / 1e6),
-                   "launch": "CUDA graph of %d GEMVs" % G},
+        "config": bench_config(ws),
+        "method": {"entry": entry, "tolerance": "bit-exact" if args.exact else "1e-5 * sum|w x| per output",
+                   "launch": "CUDA graph of %d GEMVs replayed %d times%s; every graph replayed once before "
+                             "timing (%d warm replays); L2 flushed and replays queued behind a device sleep "
+                             "before the start event" % (G, n_replays, " + a %d-GEMV tail graph" % tail if tail else "",
+                                                          warm_replays)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": load_traffic(),
                      "peak_source": peak_kind, "kernel_us": round(kernel_ms * 1e3, 3),
@@ -336,8 +367,82 @@ def run_ours(args):
         "clocks": clocks.summary(),
         "cpu_baseline": cpu,
     }
+    if ws == 1 and not args.no_decode:
+        line["decode_1b"] = decode_1b_leg(args)
     print(json.dumps(line))
     return 0
+
+
+DECODE_WEIGHT_BYTES = 1312980992  # Q8_0 layer blocks + the tied 128256 x 2048 LM head, per token
+REF_DECODE_PROMPT, REF_DECODE_STEPS = 16, 8
+
+
+def decode_1b_leg(args):
+    """The second half of the headline metric: the Llama-3.2-1B-shaped Q8_0
+    greedy decode (prompt of 512 seeded ids, then 128 steps) through the C++
+    host layer's public model API (libturbo_b200_host.so: one CUDA graph per
+    token), its token ids against the reference's run of the same model
+    (tests/golden/decode_1b.npz), and the reference's own CPU decode timed on
+    this host in the same run on a bounded sample."""
+    import ctypes as C
+    import numpy as np
+    from turbo_b200 import gguf_synth
+    from turbo_b200.model import Model
+    golden = np.load(os.path.join(ROOT, "tests", "golden", "decode_1b.npz"))
+    t0 = time.perf_counter()
+    path = gguf_synth.ensure_model()
+    synth_s = time.perf_counter() - t0
+    steps, max_seq = int(golden["steps"]), int(golden["max_seq"])
+    prompt = golden["prompt"]
+    t0 = time.perf_counter()
+    m = Model(path, exact=False)
+    load_s = time.perf_counter() - t0
+    m.generate(prompt, 4, max_seq=max_seq, want_margins=False)  # warm-up (graph capture, first launches)
+    runs = [m.generate(prompt, steps, max_seq=max_seq, want_margins=False) for _ in range(2)]
+    best = min(runs, key=lambda r: r["decode_ms"])
+    same = all(bool(np.array_equal(r["ids"], golden["ids"])) for r in runs)
+    short = m.generate(prompt[:REF_DECODE_PROMPT], REF_DECODE_STEPS, max_seq=max_seq, want_margins=False)
+    m.close()
+    tok_s = steps / (best["decode_ms"] / 1e3)
+    kv_bytes = 16 * 2 * 512 * 4 * (prompt.size + steps / 2)  # K and V rows read per token, mean context
+    per_tok = DECODE_WEIGHT_BYTES + kv_bytes
+    peak, peak_kind = load_peaks()
+    out = {"metric": "Q8_0 1B-shape greedy decode tokens/sec", "value": round(tok_s, 1), "unit": "tok/s",
+           "steps": steps, "prompt": int(prompt.size), "runs": len(runs),
+           "decode_ms": round(best["decode_ms"], 2), "prefill_ms": round(best["prefill_ms"], 1),
+           "ids_identical_to_reference": same,
+           "path": "tbm_model_generate: one CUDA graph per token, fused layer kernels",
+           "roofline": {"bound": "hbm", "bytes_per_token": int(per_tok), "achieved": round(per_tok * tok_s / 1e9, 1),
+                        "peak": peak, "unit": "GB/s", "frac": round(per_tok * tok_s / 1e9 / peak, 4),
+                        "peak_source": peak_kind},
+           "model": {"path_kind": "synthetic GGUF, seed 0 (turbo_b200.gguf_synth)", "write_s": round(synth_s, 1),
+                     "load_upload_s": round(load_s, 2)}}
+    from oracle import refbind as R
+    if args.no_cpu_baseline or not R.available():
+        out["reference_cpu"] = None
+        return out
+    cores = os.cpu_count() or 1
+    os.environ["OMP_NUM_THREADS"] = str(cores)
+    L = R.lib()
+    h = L.ref_model_load(path.encode())
+    if not h:
+        out["reference_cpu"] = {"unavailable": "the reference failed to load the model"}
+        return out
+    sp = np.ascontiguousarray(prompt[:REF_DECODE_PROMPT], np.int32)
+    ids = np.zeros(REF_DECODE_STEPS + 1, np.int32)
+    pre, dec = C.c_double(), C.c_double()
+    R.check(L.ref_model_generate(h, R.ptr(sp), sp.size, REF_DECODE_STEPS, max_seq, R.ptr(ids), None, None,
+                                 C.byref(pre), C.byref(dec)), "ref_model_generate")
+    L.ref_model_free(h)
+    ref_tok_s = REF_DECODE_STEPS / (dec.value / 1e3)
+    out["reference_cpu"] = {
+        "value": round(ref_tok_s, 3), "unit": "tok/s", "cores": cores, "kind": "reference",
+        "sample": "reference MiniGPT (its sources compiled under oracle/_ref), prompt of %d ids then %d greedy "
+                  "steps (context %d-%d), OpenMP %d threads; prefill %.1f s" % (
+                      REF_DECODE_PROMPT, REF_DECODE_STEPS, REF_DECODE_PROMPT, REF_DECODE_PROMPT + REF_DECODE_STEPS,
+                      cores, pre.value / 1e3),
+        "ids_identical_on_sample": bool(np.array_equal(ids, short["ids"]))}
+    return out
 
 
 def ops_cpu_reference():
@@ -393,9 +498,6 @@ def run_ops_suite(args):
     return 0
 
 
-DECODE_MODEL = "/tmp/turbo_b200_llama1b_q8_0_seed0.gguf"
-
-
 def run_decode_suite(args):
     """The 1B-shaped Q8_0 greedy decode (prefill 512 ids, then 128 steps) through
     the C++ host layer, both paths; token ids checked against the reference's
@@ -408,12 +510,10 @@ def run_decode_suite(args):
     from turbo_b200 import gguf_synth
     from turbo_b200.model import Model
     golden = np.load(os.path.join(ROOT, "tests", "golden", "decode_1b.npz"))
-    if not os.path.exists(DECODE_MODEL):
-        gguf_synth.write_model(DECODE_MODEL + ".part")
-        os.replace(DECODE_MODEL + ".part", DECODE_MODEL)
+    model_path = gguf_synth.ensure_model()
     steps = int(golden["steps"])
     for exact in ([False] if args.only != "both" else [False, True]):
-        m = Model(DECODE_MODEL, exact=exact)
+        m = Model(model_path, exact=exact)
         m.generate(golden["prompt"], 4, max_seq=int(golden["max_seq"]), want_margins=False)  # warm-up
         runs = [m.generate(golden["prompt"], steps, max_seq=int(golden["max_seq"]), want_margins=False)
                 for _ in range(max(1, args.reps))]
@@ -463,6 +563,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true",
+                    help="skip the 1B-shaped decode leg of the N=1 line (it writes a 1.3 GB synthetic model once)")
     ap.add_argument("--exact", action="store_true",
                     help="time tb_matmul_quant_exact (bit-identical to the reference) instead")
     ap.add_argument("--suite", default="headline", choices=["headline", "ops", "decode", "sharded"],

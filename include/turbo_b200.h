@@ -97,6 +97,14 @@ tb_status tb_sync(tb_stream stream);
 /* Reads and clears the device error word set by bounded waits and by
  * device-side index checks (bit 0: timeout, bit 1: index out of range). */
 tb_status tb_take_device_errors(uint32_t *flags_out);
+/* Limit, in nanoseconds, of the bounded waits of the Q4_0 matmul kernels
+ * (tb_matmul_quant / tb_matmul_quant_exact with TB_Q4_0 on the CUDA cores, and
+ * tb_matmul_q4_0_static_scratch); default 2e9.  A wait that gives up sets bit 0
+ * of the device error word and the kernel leaves its rows unwritten, after
+ * waiting for its own copies in flight.  0 lets no wait wait at all, a
+ * host-side way to exercise that path.  Read at launch (a captured graph keeps
+ * the value it was captured with).  No reference counterpart. */
+tb_status tb_set_wait_limit_ns(uint64_t ns);
 
 /* ------------------------------------------------------ elementwise (A3-A8) -- */
 
@@ -239,7 +247,10 @@ tb_status tb_matmul_quant_exact(int dtype, const float *x_dev, int64_t M, int64_
  * Calls no cudaMalloc/cudaFree.  The first call on a device looks up the
  * buffer's address (cudaGetSymbolAddress); make it before any stream capture.
  * All calls share the one buffer: calls that may overlap on the GPU (other
- * streams, other host threads) race and must be serialized by the caller. */
+ * streams, other host threads) race and must be serialized by the caller.
+ * A bounded wait that gives up inside the kernel sets bit 0 of this entry
+ * point's own device error word (also a file-scope device variable), which
+ * tb_take_device_errors reads and clears with the regular one. */
 tb_status tb_matmul_q4_0_static_scratch(const float *x_dev, int64_t M, int64_t K,
                                         const void *w_dev, int64_t N, float *y_dev,
                                         tb_stream stream);

@@ -127,11 +127,26 @@ def matmul_q8_0(x, w_bytes, N):
     return y
 
 
-def matmul_q4_0(x, w_bytes, N):
+def matmul_q4_0(x, w_bytes, N, threads=1):
+    """or_matmul_q4_0; with threads > 1 the rows of x are split over host
+    threads (ctypes releases the GIL during each call; rows are independent)."""
     x = np.ascontiguousarray(x, np.float32)
     M, K = x.shape
     y = np.zeros((M, N), np.float32)
-    lib().or_matmul_q4_0(ptr(x), M, K, ptr(w_bytes), N, ptr(y))
+    L = lib()
+    if threads <= 1 or M < 2:
+        L.or_matmul_q4_0(ptr(x), M, K, ptr(w_bytes), N, ptr(y))
+        return y
+    from concurrent.futures import ThreadPoolExecutor
+    cuts = np.linspace(0, M, min(threads, M) + 1).astype(int)
+
+    def part(i):
+        a, b = int(cuts[i]), int(cuts[i + 1])
+        if b > a:
+            L.or_matmul_q4_0(ptr(x[a:b]), b - a, K, ptr(w_bytes), N, ptr(y[a:b]))
+
+    with ThreadPoolExecutor(len(cuts) - 1) as ex:
+        list(ex.map(part, range(len(cuts) - 1)))
     return y
 
 

@@ -28,7 +28,7 @@ MAX_SEQ = 1024
 
 
 def main():
-    path = sys.argv[1] if len(sys.argv) > 1 else "/tmp/llama1b_q8_0_seed0.gguf"
+    path = sys.argv[1] if len(sys.argv) > 1 else gguf_synth.default_model_path()
     if not os.path.exists(path):
         t0 = time.time()
         gguf_synth.write_model(path)

@@ -15,15 +15,11 @@ from turbo_b200 import gguf_synth
 pytestmark = pytest.mark.gpu
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "decode_1b.npz")
-MODEL = "/tmp/turbo_b200_llama1b_q8_0_seed0.gguf"
 
 
 @pytest.fixture(scope="module")
 def model_path():
-    if not os.path.exists(MODEL):
-        gguf_synth.write_model(MODEL + ".part")
-        os.replace(MODEL + ".part", MODEL)
-    return MODEL
+    return gguf_synth.ensure_model()
 
 
 @pytest.fixture(scope="module")
@@ -86,3 +82,27 @@ def test_sampled_decode_reproducible(model_path, golden):
     assert np.array_equal(a["ids"], b["ids"])
     assert ((a["ids"] >= 0) & (a["ids"] < 128256)).all()
     print("sampled ids", a["ids"][:12], "decode %.1f ms" % a["decode_ms"])
+
+
+@pytest.mark.parametrize("exact", [False, True])
+def test_sampled_decode_reads_each_positions_uniform(model_path, golden, exact):
+    # u = 0 draws the greedy id at every step but one, s_star, whose u just
+    # below 1 draws the last id of the 0.9 nucleus (never the top id: the
+    # nucleus of this model's flat logits holds many ids).  The first step that
+    # differs from the greedy ids must be s_star itself: a step that read its
+    # neighbour's uniform number would move the deviation or miss it.
+    from turbo_b200.model import Model
+    m = Model(model_path, exact=exact)
+    n = 10
+    ref = golden["ids"]
+    try:
+        for s_star in ((0, 1, 2, 7, 10) if not exact else (1, 6)):
+            us = np.zeros(n + 1)
+            us[s_star] = 1.0 - 1e-9
+            out = m.generate(golden["prompt"], n, max_seq=int(golden["max_seq"]), temperature=0.8, top_p=0.9,
+                             uniforms=us, want_margins=False)
+            ids = out["ids"]
+            assert np.array_equal(ids[:s_star], ref[:s_star]), (s_star, ids[:s_star + 1], ref[:s_star + 1])
+            assert ids[s_star] != ref[s_star], (s_star, ids[s_star])
+    finally:
+        m.close()

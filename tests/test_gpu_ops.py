@@ -7,6 +7,7 @@ RMSNorm and softmax at 1e-5 relative (fp32), 1e-2 for bf16.  SwiGLU uses a
 correctly rounded exp; it differs from glibc's expf only where glibc misrounds.
 """
 import ctypes
+import os
 
 import numpy as np
 import pytest
@@ -172,11 +173,35 @@ def test_matmul_q8_0_unaligned_weight_base():
     assert_bits(host(y), O.matmul_q8_0(x, wq, N))
 
 
-@pytest.mark.parametrize("M,K,N", [(1, 8192, 2048), (3, 8192, 130), (5, 64, 7)])
+# (512, 8192, 2048): the prefill down projection X[512, 8192] . W_down
+@pytest.mark.parametrize("M,K,N", [(1, 8192, 2048), (3, 8192, 130), (5, 64, 7), (512, 8192, 2048)])
 def test_matmul_q4_0_bit_exact(M, K, N):
     wq = synth.quantize_q4_0(synth.normal((N, K), 0.02, seed=K + N))
     x = synth.normal((M, K), 1.0, seed=M + 1)
-    assert_bits(run_matmul(T.Q4_0, x, wq, N), O.matmul_q4_0(x, wq, N))
+    assert_bits(run_matmul(T.Q4_0, x, wq, N), O.matmul_q4_0(x, wq, N, threads=os.cpu_count() or 1))
+
+
+def test_matmul_q4_0_wait_timeout_is_reported():
+    # A bounded wait that gives up (wait limit 0: no waiting allowed) leaves the
+    # rows unwritten and sets bit 0 of the device error word; the context stays
+    # usable and the next call, with the default limit, is exact again.
+    M, K, N = 4, 2048, 300
+    wq = synth.quantize_q4_0(synth.normal((N, K), 0.02, seed=3))
+    x = synth.normal((M, K), 1.0, seed=4)
+    dx, dw = dev(x), dev(wq)
+    assert T.take_device_errors() == 0
+    y = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+    T.call("tb_set_wait_limit_ns", 0)
+    try:
+        T.call("tb_matmul_quant_exact", T.Q4_0, T.ptr(dx), M, K, T.ptr(dw), N, T.ptr(y), S())
+        torch.cuda.synchronize()
+    finally:
+        T.call("tb_set_wait_limit_ns", 2000000000)
+    assert T.take_device_errors() & 1
+    assert np.isnan(host(y)).all()
+    T.call("tb_matmul_quant_exact", T.Q4_0, T.ptr(dx), M, K, T.ptr(dw), N, T.ptr(y), S())
+    assert_bits(host(y), O.matmul_q4_0(x, wq, N))
+    assert T.take_device_errors() == 0
 
 
 def assert_gemm_tol(got, xd, wd, tol=F32_REL):

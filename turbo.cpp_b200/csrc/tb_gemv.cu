@@ -434,7 +434,7 @@ tb_status launch_span(const float *x, int64_t K, const void *w, int64_t N, float
 template <int NW>
 __global__ void __launch_bounds__(NW * 32) matmul_q4_0_kernel(
     const uint8_t *__restrict__ W, const uint8_t *__restrict__ XQ, float *__restrict__ Y, int N,
-    int K, int M, int rows_per_cta, int use_tma, uint32_t *__restrict__ err) {
+    int K, int M, int rows_per_cta, int use_tma, uint32_t *__restrict__ err, uint64_t wait_ns) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int nb = K / 32;
   const int rb = nb * 18;
@@ -460,8 +460,14 @@ __global__ void __launch_bounds__(NW * 32) matmul_q4_0_kernel(
       reinterpret_cast<uint16_t *>(xsm)[i] = reinterpret_cast<const uint16_t *>(xq)[i];
     __syncthreads();
     if (!ready) {
-      const bool ok = mbar_wait_bounded(bar, 0, err);
-      if (__syncthreads_or(!ok)) return;
+      const bool ok = mbar_wait_limit(bar, 0, err, wait_ns);
+      if (__syncthreads_or(!ok)) {
+        // ERR_TIMEOUT is set; the weight copy may still be in flight into this
+        // CTA's shared memory, so one thread waits for it (bounded) before the
+        // CTA leaves.
+        if (threadIdx.x == 0) mbar_wait_bounded(bar, 0, err);
+        return;
+      }
       ready = true;
     }
     for (int r0 = warp * 4; r0 < n1 - n0; r0 += NW * 4) {
@@ -566,7 +572,7 @@ tb_status launch_q4_0_exact(const uint8_t *xq, int64_t M, int64_t K, const void 
   TB_TRY(ensure_smem_for(matmul_q4_0_kernel<NW>, smem));
   unsigned grid = (unsigned)((N + rows - 1) / rows);
   matmul_q4_0_kernel<NW><<<grid, NW * 32, smem, s>>>((const uint8_t *)w, xq, y, (int)N, (int)K, (int)M,
-                                                     rows, use_tma, st->err_word);
+                                                     rows, use_tma, st->err_word, wait_limit_ns());
   return check_launch("tb_matmul_quant(Q4_0)");
 }
 

@@ -28,6 +28,14 @@ tb_status device_state(DeviceState **out);
 // Records `msg` as the calling thread's last error and returns `s`.
 tb_status fail(tb_status s, const char *fmt, ...);
 
+// Limit of the bounded waits that take it from the host (tb_set_wait_limit_ns;
+// default 2 s).
+uint64_t wait_limit_ns();
+
+// Reads and clears the error word of tb_matmul_q4_0_static_scratch on the
+// current device (0 when that entry point was never called there).
+tb_status static_scratch_take_errors(uint32_t *flags);
+
 // Maps a pending launch error to TB_ECUDA.
 tb_status check_launch(const char *what);
 
@@ -165,6 +173,18 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t phase,
       return false;
     }
   }
+}
+
+// A bounded wait with a caller-given limit (tb_set_wait_limit_ns).  Limit 0
+// allows no waiting at all: the wait gives up before testing the barrier, so a
+// caller can exercise a kernel's timeout path without any stalled copy.
+__device__ __forceinline__ bool mbar_wait_limit(uint64_t *bar, uint32_t phase, uint32_t *err,
+                                                uint64_t limit_ns) {
+  if (limit_ns == 0) {
+    if (err) atomicOr(err, ERR_TIMEOUT);
+    return false;
+  }
+  return mbar_wait_bounded(bar, phase, err, limit_ns);
 }
 
 // Bulk global->shared copy completing on `bar` (16-byte aligned addresses,

@@ -11,7 +11,10 @@
 // The array (kScratchBytes, 8 MiB) lives in every GPU that loads the library,
 // for as long as the process runs.  Its host-side name is only a stand-in for
 // the symbol, never a device address; the device address is looked up once
-// per device with cudaGetSymbolAddress and cached.
+// per device with cudaGetSymbolAddress and cached.  A second file-scope word
+// is this entry point's device error word (a bounded wait that gave up sets
+// bit 0), found the same way; tb_take_device_errors reads and clears it
+// together with the library's regular error word.
 #include <atomic>
 #include <mutex>
 
@@ -30,9 +33,12 @@ constexpr size_t kScratchBytes = size_t(8) << 20;  // 8 MiB: X[512, 8192] as Q8_
 
 // Holds the Q8_0 copy of X between the two kernels of a call.
 static __device__ __align__(256) uint8_t g_q4_scratch[kScratchBytes];
+// The kernels' error word for calls through this entry point.
+static __device__ uint32_t g_q4_scratch_err;
 
 struct ScratchSlot {
   std::atomic<void *> addr{nullptr};
+  uint32_t *err = nullptr;  // device address of g_q4_scratch_err
   int sm_count = 0;
   int smem_optin = 0;
 };
@@ -55,10 +61,14 @@ tb_status scratch_for_device(ScratchSlot **out) {
       if (e == cudaSuccess) e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
       if (e != cudaSuccess) return tb::fail(TB_ECUDA, "device attributes: %s", cudaGetErrorString(e));
       if (major != 10) return tb::fail(TB_ECUDA, "device %d is not an sm_100 part", dev);
-      void *p = nullptr;
+      void *p = nullptr, *pe = nullptr;
       e = cudaGetSymbolAddress(&p, g_q4_scratch);
       if (e != cudaSuccess || p == nullptr)
         return tb::fail(TB_ECUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(e));
+      e = cudaGetSymbolAddress(&pe, g_q4_scratch_err);
+      if (e != cudaSuccess || pe == nullptr)
+        return tb::fail(TB_ECUDA, "cudaGetSymbolAddress(error word): %s", cudaGetErrorString(e));
+      slot.err = static_cast<uint32_t *>(pe);
       slot.sm_count = sms;
       slot.smem_optin = optin;
       slot.addr.store(p, std::memory_order_release);
@@ -69,6 +79,25 @@ tb_status scratch_for_device(ScratchSlot **out) {
 }
 
 }  // namespace
+
+namespace tb {
+// Reads and clears this entry point's error word on the current device; a
+// device where the entry point never ran has none and reports 0.
+tb_status static_scratch_take_errors(uint32_t *flags) {
+  *flags = 0;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64 || g_slots[dev].addr.load(std::memory_order_acquire) == nullptr) return TB_OK;
+  uint32_t *w = g_slots[dev].err;
+  uint32_t v = 0;
+  e = cudaMemcpy(&v, w, sizeof(v), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && v) e = cudaMemset(w, 0, sizeof(uint32_t));
+  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_take_device_errors(static scratch): %s", cudaGetErrorString(e));
+  *flags = v;
+  return TB_OK;
+}
+}  // namespace tb
 
 using namespace tb;
 
@@ -100,10 +129,10 @@ extern "C" tb_status tb_matmul_q4_0_static_scratch(const float *x, int64_t M, in
   // Every byte of the scratch that the matmul reads is written by the
   // quantisation first, so nothing needs clearing between calls.
   TB_TRY(launch_quantize_q8_0(x, M, K, scratch, s, slot->sm_count));
-  DeviceState st;  // launch parameters only: no error word, nothing allocated
+  DeviceState st;  // launch parameters only; nothing allocated
   st.device = -1;
   st.sm_count = slot->sm_count;
   st.smem_optin = slot->smem_optin;
-  st.err_word = nullptr;
+  st.err_word = slot->err;
   return launch_q4_0_exact(static_cast<const uint8_t *>(scratch), M, K, w, N, y, s, &st);
 }

@@ -1,5 +1,6 @@
 // tb_runtime.cu -- per-device state, error reporting, the HBM arena and the
 // host<->device copies of the C ABI.
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -33,6 +34,12 @@ constexpr size_t kMinSegment = size_t(256) << 20;
 
 size_t round_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 }  // namespace
+
+namespace {
+std::atomic<uint64_t> g_wait_limit{2000000000ull};
+}
+
+uint64_t wait_limit_ns() { return g_wait_limit.load(std::memory_order_relaxed); }
 
 tb_status fail(tb_status s, const char *fmt, ...) {
   va_list ap;
@@ -253,7 +260,14 @@ tb_status tb_take_device_errors(uint32_t *flags) {
     e = cudaMemset(st->err_word, 0, sizeof(uint32_t));
     if (e != cudaSuccess) return fail(TB_ECUDA, "tb_take_device_errors: %s", cudaGetErrorString(e));
   }
-  *flags = v;
+  uint32_t vs = 0;
+  TB_TRY(static_scratch_take_errors(&vs));
+  *flags = v | vs;
+  return TB_OK;
+}
+
+tb_status tb_set_wait_limit_ns(uint64_t ns) {
+  g_wait_limit.store(ns, std::memory_order_relaxed);
   return TB_OK;
 }
 

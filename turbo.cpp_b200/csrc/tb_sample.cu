@@ -509,6 +509,17 @@ tb_status launch_sample(const float *logits, int V, float temperature, float top
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  // The mid-bit mass sums of a bucket (16-bit parts of up to n_loc elements)
+  // stay below 2^32 only while n_loc < 2^16.
+  if (n_loc >= 65536) return fail(TB_EINVAL, "tb_sample_top_p: slice of %d elements per CTA", n_loc);
+  if (CL > 8) {
+    // A 16-CTA cluster of 1024-thread CTAs with nearly all of each SM's shared
+    // memory is a non-portable size: check that the GPU can place one.
+    int clusters = 0;
+    e = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+    if (e != cudaSuccess) return fail(TB_ECUDA, "tb_sample_top_p: %s", cudaGetErrorString(e));
+    if (clusters < 1) return fail(TB_EINVAL, "tb_sample_top_p: a %d-CTA cluster does not fit this GPU", CL);
+  }
   e = cudaLaunchKernelEx(&cfg, kern, logits, V, n_loc, temperature, top_p, io);
   if (e != cudaSuccess) return fail(TB_ECUDA, "tb_sample_top_p: %s", cudaGetErrorString(e));
   return check_launch("tb_sample_top_p");

@@ -55,6 +55,7 @@ SIGNATURES = {
     "tb_memset": [_P, _I, _SZ, _P],
     "tb_sync": [_P],
     "tb_take_device_errors": [ctypes.POINTER(ctypes.c_uint32)],
+    "tb_set_wait_limit_ns": [ctypes.c_uint64],
     "tb_binary": [_I, _VP, _VP, _VP, _P],
     "tb_scale": [_VP, _F, _VP, _P],
     "tb_copy": [_VP, _VP, _P],

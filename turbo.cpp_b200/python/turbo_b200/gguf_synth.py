@@ -50,14 +50,40 @@ def tensor_specs(cfg):
     return specs
 
 
-def tensor_bytes(dims, kind, qtype, rng, std):
+def tensor_chunks(dims, kind, qtype, rng, std, chunk_values=1 << 22):
+    """The tensor's bytes in row chunks of about `chunk_values` weights (the
+    generator's stream is the same however the rows are split, so the bytes
+    equal one draw of the whole [N, K] matrix)."""
     if kind == "norm":
-        return np.ones(dims[0], np.float32).tobytes(), GGML_F32
+        yield np.ones(dims[0], np.float32).tobytes()
+        return
     K, N = dims
-    w = (rng.standard_normal((N, K), dtype=np.float32) * np.float32(std)).astype(np.float32)
-    if qtype == GGML_Q8_0:
-        return synth.quantize_q8_0(w).tobytes(), GGML_Q8_0
-    return synth.quantize_q4_0(w).tobytes(), GGML_Q4_0
+    rows = max(1, chunk_values // K)
+    quant = synth.quantize_q8_0 if qtype == GGML_Q8_0 else synth.quantize_q4_0
+    for r0 in range(0, N, rows):
+        n = min(rows, N - r0)
+        w = (rng.standard_normal((n, K), dtype=np.float32) * np.float32(std)).astype(np.float32)
+        yield quant(w).tobytes()
+
+
+def default_model_path():
+    """Where the tests and the bench keep the synthetic 1B-shaped model: the
+    TURBO_B200_MODEL environment variable, else a file in the system's
+    temporary directory."""
+    import os
+    import tempfile
+    return os.environ.get("TURBO_B200_MODEL") or os.path.join(tempfile.gettempdir(),
+                                                              "turbo_b200_llama1b_q8_0_seed0.gguf")
+
+
+def ensure_model(path=None):
+    """Writes the seed-0 1B-shaped Q8_0 model at `path` unless it is there."""
+    import os
+    path = path or default_model_path()
+    if not os.path.exists(path):
+        write_model(path + ".part")
+        os.replace(path + ".part", path)
+    return path
 
 
 def write_model(path, cfg=LLAMA_1B, seed=0, std=0.02, qtype=GGML_Q8_0, alignment=32):
@@ -90,9 +116,11 @@ def write_model(path, cfg=LLAMA_1B, seed=0, std=0.02, qtype=GGML_Q8_0, alignment
     with open(path, "wb") as f:
         f.write(head + b"\0" * pad)
         for (name, dims, kind), sz in zip(specs, sizes):
-            data, _ = tensor_bytes(dims, kind, qtype, rng, std)
-            assert len(data) == sz
-            f.write(data)
+            n = 0
+            for data in tensor_chunks(dims, kind, qtype, rng, std):
+                f.write(data)
+                n += len(data)
+            assert n == sz
             f.write(b"\0" * ((alignment - sz % alignment) % alignment))
     return path
 

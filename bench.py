@@ -411,7 +411,8 @@ def decode_1b_leg(args):
            "steps": steps, "prompt": int(prompt.size), "runs": len(runs),
            "decode_ms": round(best["decode_ms"], 2), "prefill_ms": round(best["prefill_ms"], 1),
            "ids_identical_to_reference": same,
-           "path": "tbm_model_generate: one CUDA graph per token, fused layer kernels",
+           "path": "tbm_model_generate: one CUDA graph per token holding the persistent decode kernel "
+                   "(tb_decode_step_persistent) and the argmax/advance kernels",
            "roofline": {"bound": "hbm", "bytes_per_token": int(per_tok), "achieved": round(per_tok * tok_s / 1e9, 1),
                         "peak": peak, "unit": "GB/s", "frac": round(per_tok * tok_s / 1e9 / peak, 4),
                         "peak_source": peak_kind},
@@ -512,8 +513,9 @@ def run_decode_suite(args):
     golden = np.load(os.path.join(ROOT, "tests", "golden", "decode_1b.npz"))
     model_path = gguf_synth.ensure_model()
     steps = int(golden["steps"])
-    for exact in ([False] if args.only != "both" else [False, True]):
-        m = Model(model_path, exact=exact)
+    paths = [("persistent", False, True), ("fused", False, False)] + ([("exact", True, False)] if args.only == "both" else [])
+    for name, exact, persistent in paths:
+        m = Model(model_path, exact=exact, persistent=persistent)
         m.generate(golden["prompt"], 4, max_seq=int(golden["max_seq"]), want_margins=False)  # warm-up
         runs = [m.generate(golden["prompt"], steps, max_seq=int(golden["max_seq"]), want_margins=False)
                 for _ in range(max(1, args.reps))]
@@ -522,7 +524,8 @@ def run_decode_suite(args):
         same = all(bool(np.array_equal(r["ids"], golden["ids"])) for r in runs)
         line = {"suite": "decode", "metric": "Q8_0 1B-shape greedy decode tokens/sec",
                 "value": round(steps / (best["decode_ms"] / 1e3), 1), "unit": "tok/s",
-                "path": "exact op-by-op" if exact else "CUDA graph per token, fused layer",
+                "path": {"exact": "exact op-by-op", "fused": "CUDA graph per token, fused layer kernels",
+                         "persistent": "CUDA graph per token: one persistent kernel for the step + pick"}[name],
                 "prefill_ms": round(best["prefill_ms"], 1), "decode_ms": round(best["decode_ms"], 1),
                 "steps": steps, "prompt": int(golden["prompt"].size), "runs": len(runs),
                 "ids_identical_to_reference": same,

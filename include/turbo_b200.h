@@ -289,6 +289,43 @@ tb_status tb_argmax_shard_keys(const float *x_dev, int64_t rows, int64_t cols, i
 tb_status tb_argmax_key_index(const int64_t *keys_dev, int64_t rows, int64_t *idx_dev,
                               tb_stream stream);
 
+/* A group of n_ranks GPUs, one per process or thread, for the shard-level ops
+ * below (the reference runs them whole on one CPU: src/nn/softmax.cpp:13-54,
+ * src/core/sampler.cpp:13-26, src/tensor/tensor.cpp:328-382).  Rank 0 makes
+ * an id (tb_shard_group_unique_id), the caller passes it to every rank, and
+ * each rank calls tb_shard_group_create with its device current.  The
+ * exchange is NCCL over NVLink, loaded at run time (libnccl.so.2).  Creation
+ * is bounded by timeout_s (TB_ETIMEOUT, communicator aborted);  max_rows
+ * bounds the rows of later calls.  Every rank issues the same calls in the
+ * same order; they are asynchronous on `stream`.  tb_shard_group_wait waits
+ * at most timeout_s for a stream's work and aborts the group otherwise (a
+ * rank that never joins a collective cannot hang the others past it). */
+#define TB_SHARD_ID_BYTES 128
+typedef struct tb_shard_group_s *tb_shard_group;
+tb_status tb_shard_group_unique_id(void *id_out);
+tb_status tb_shard_group_create(int n_ranks, int rank, const void *id, int64_t max_rows, double timeout_s,
+                                tb_shard_group *out);
+tb_status tb_shard_group_wait(tb_shard_group group, tb_stream stream, double timeout_s);
+tb_status tb_shard_group_abort(tb_shard_group group);
+tb_status tb_shard_group_destroy(tb_shard_group group);
+/* Softmax over rows split by columns: this rank holds x[rows, cols] (row
+ * stride ld), its slice of the full rows; y (row stride ld_y) gets the same
+ * slice of the full rows' softmax.  One all-gather of each rank's per-row
+ * (max, sum of exp) and a combine in rank order; then exp(x - M) / S. */
+tb_status tb_softmax_vocab_sharded(tb_shard_group group, const float *x_dev, int64_t rows, int64_t cols,
+                                   int64_t ld, float *y_dev, int64_t ld_y, tb_stream stream);
+/* greedy_sample over rows split by columns: this rank's columns start at
+ * global column col_base; idx_dev[rows] gets the global first-maximum column
+ * on every rank (one int64 MAX all-reduce of tb_argmax_shard_keys). */
+tb_status tb_argmax_vocab_sharded(tb_shard_group group, const float *x_dev, int64_t rows, int64_t cols,
+                                  int64_t ld, int64_t col_base, int64_t *idx_dev, tb_stream stream);
+/* Tensor-parallel Q8_0 GEMV (Tensor::matmul, src/tensor/tensor.cpp:328-382,
+ * rows split): this rank holds rows [rank n_local, (rank + 1) n_local) of W
+ * (their Q8_0 blocks) and the full x[K]; y_dev[n_ranks * n_local] gets the
+ * full product on every rank (the rank's rows, then one in-place all-gather). */
+tb_status tb_gemv_q8_0_row_sharded(tb_shard_group group, const float *x_dev, int64_t K, const void *w_local_dev,
+                                   int64_t n_local, float *y_dev, tb_stream stream);
+
 /* ------------------------------------------- decode step with a device position -- */
 
 /* tb_rope with the position offset read from device memory (*pos_dev) when
@@ -325,6 +362,43 @@ tb_status tb_decode_margin(const float *logits_dev, int64_t vocab, const int64_t
  * history[*pos] = *idx, *pos += 1. */
 tb_status tb_decode_advance(const int64_t *idx_dev, int32_t *ids_dev, int32_t *pos_dev, int32_t *history_dev,
                             int64_t max_seq, tb_stream stream);
+
+/* One whole decode step of a Llama-shaped MiniGPT in a single persistent
+ * kernel: MiniGPT::forward({token}, &kv) at S = 1 (src/model/minigpt.cpp:55-74,
+ * the per-layer sequence of src/nn/transformer_block.cpp, attention.cpp:41-148,
+ * ffn.cpp:17-27), from the token's embedding to the logits, with RoPE and the
+ * KV-cache append of the new key/value at *pos_dev.  The choice of the next
+ * token (tb_argmax / tb_sample_top_p_at, tb_decode_advance) follows it.
+ * Layout and arithmetic are those of the fused decode kernels above (Q8_0
+ * projections, fp32 activations, caches [max_seq, kv_heads * head_dim]); only
+ * summation orders differ, within the GEMV and softmax tolerances.
+ * Shapes: hidden 2048, head_dim 64, heads * head_dim = hidden, at most 4 query
+ * heads per key/value head, ffn 2048, 4096 or 8192, max_seq <= 2048; every
+ * weight Q8_0 and 16-byte aligned.  Runs one cooperative CTA per SM; a grid
+ * barrier that waits 2 s without progress gives up, sets bit 0 of the device
+ * error word and ends the kernel (the workspace must then be zeroed again).
+ * The workspace (tb_decode_workspace_bytes, 256-byte aligned) holds the
+ * step's activations and its barrier counter: zero it once before the first
+ * step and keep it for the following steps. */
+typedef struct tb_decode_layer {
+  const void *wq, *wk, *wv, *wo, *w_gate, *w_up, *w_down; /* Q8_0, GGUF rows */
+  const float *attn_norm, *ffn_norm;                      /* RMSNorm weights */
+  float *k_cache, *v_cache;                               /* [max_seq, kv_heads * head_dim] */
+} tb_decode_layer;
+typedef struct tb_decode_model {
+  int32_t n_layers;
+  int64_t hidden, ffn, heads, kv_heads, head_dim, vocab, max_seq, rope_max_seq;
+  float eps_attn, eps_ffn, eps_final, attn_scale;
+  const tb_decode_layer *layers_dev;        /* device array of n_layers entries */
+  const void *tok_emb, *lm_head;            /* Q8_0 [vocab rows of hidden] */
+  const float *final_norm, *rope_cos, *rope_sin; /* RoPE tables [rope_max_seq, head_dim / 2] */
+  const int32_t *token_dev, *pos_dev;       /* the step's input token and position */
+  float *logits;                            /* out: [vocab] */
+  void *workspace;
+  size_t workspace_bytes;
+} tb_decode_model;
+tb_status tb_decode_workspace_bytes(const tb_decode_model *model, size_t *bytes_out);
+tb_status tb_decode_step_persistent(const tb_decode_model *model, tb_stream stream);
 
 /* Fused decode-step GEMVs (Q8_0 weights, one input row x[K], K a multiple of
  * 256; x, gamma and weights 16-byte aligned).  When gamma is non-NULL the input

@@ -29,10 +29,12 @@ def golden():
     return np.load(GOLDEN)
 
 
-@pytest.mark.parametrize("exact", [True, False])
-def test_decode_token_ids_match_reference(model_path, golden, exact):
+# exact: the bit-identical kernels, one per reference op; fused: one CUDA graph
+# per token of fused per-op kernels; persistent: one kernel per token
+@pytest.mark.parametrize("path", ["exact", "fused", "persistent"])
+def test_decode_token_ids_match_reference(model_path, golden, path):
     from turbo_b200.model import Model
-    m = Model(model_path, exact=exact)
+    m = Model(model_path, exact=path == "exact", persistent=path == "persistent")
     steps = int(golden["steps"])
     out = m.generate(golden["prompt"], steps, max_seq=int(golden["max_seq"]))
     m.close()

@@ -110,3 +110,104 @@ def _tp_rank(rank, world, port):
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_tensor_parallel_gemv_nccl_two_gpus():
     mp.start_processes(_tp_rank, args=(2, _free_port()), nprocs=2, join=True, start_method="spawn")
+
+
+# ---- the same protocol through the C ABI (tb_shard_group_*), as a C++ host
+# would call it: no torch.distributed on the path
+
+def _abi_case(T, O, synth, group, rank, world, stream, rows=64, vocab=128256):
+    """softmax and argmax of [rows, vocab] logits split by columns, and the
+    row-split GEMV, on this rank's shard, against the oracle."""
+    x = synth.normal((rows, vocab), 2.0, seed=7)
+    x[5, 17] = 40.0
+    x[5, vocab - 2] = 40.0  # a tie across the shards
+    x[9, :] = -np.inf       # no candidate: index 0
+    base, cols = rank * vocab // world, (rank + 1) * vocab // world - rank * vocab // world
+    local = torch.from_numpy(np.ascontiguousarray(x[:, base:base + cols])).cuda()
+    y = torch.empty_like(local)
+    idx = torch.empty(rows, dtype=torch.int64, device="cuda")
+    T.call("tb_argmax_vocab_sharded", group, T.ptr(local), rows, cols, cols, base, T.ptr(idx), stream)
+    x[9, :] = 0.0  # the softmax check uses a row with finite values
+    local[9].zero_()
+    T.call("tb_softmax_vocab_sharded", group, T.ptr(local), rows, cols, cols, T.ptr(y), cols, stream)
+    T.call("tb_shard_group_wait", group, stream, 30.0)
+    idx = idx.cpu().numpy()
+    x9 = x.copy()
+    x9[9, :] = -np.inf
+    for r in range(rows):
+        assert idx[r] == O.argmax(x9[r]), (rank, r, idx[r])
+    a = x.astype(np.float64)
+    e = np.exp(a - a.max(axis=1, keepdims=True))
+    want = (e / e.sum(axis=1, keepdims=True))[:, base:base + cols]
+    got = y.cpu().numpy()
+    assert np.max(np.abs(got - want) / np.maximum(want, want.max() * 1e-3)) <= 1e-5
+    # row-split Q8_0 GEMV, 8192 x 2048
+    N, K = 8192, 2048
+    wq = synth.quantize_q8_0(synth.normal((N, K), 0.02, seed=31))
+    xh = synth.normal((K,), 1.0, seed=32)
+    n_local = N // world
+    rb = K // 32 * 34
+    w_local = torch.from_numpy(wq.ravel()[rank * n_local * rb:(rank + 1) * n_local * rb].copy()).cuda()
+    xd = torch.from_numpy(xh).cuda()
+    yv = torch.empty(N, dtype=torch.float32, device="cuda")
+    T.call("tb_gemv_q8_0_row_sharded", group, T.ptr(xd), K, T.ptr(w_local), n_local, T.ptr(yv), stream)
+    T.call("tb_shard_group_wait", group, stream, 30.0)
+    ref = O.matmul_q8_0(xh.reshape(1, K), wq, N)[0].astype(np.float64)
+    scale = np.abs(synth.dequantize_q8_0(wq, K)).astype(np.float64) @ np.abs(xh).astype(np.float64)
+    assert np.max(np.abs(yv.cpu().numpy() - ref) / scale) <= 1e-5
+    assert T.take_device_errors() == 0
+
+
+def test_shard_group_abi_one_rank():
+    import turbo_b200 as T
+    from oracle import orbind as O
+    from turbo_b200 import synth
+    T.call("tb_init", 0)
+    uid = ctypes.create_string_buffer(128)
+    T.call("tb_shard_group_unique_id", uid)
+    g = ctypes.c_void_p()
+    T.call("tb_shard_group_create", 1, 0, uid, 64, 30.0, ctypes.byref(g))
+    try:
+        _abi_case(T, O, synth, g, 0, 1, T.stream_handle())
+        with pytest.raises(T.TbError):  # rows above the group's bound
+            T.call("tb_argmax_vocab_sharded", g, None, 65, 8, 8, 0, None, T.stream_handle())
+    finally:
+        T.call("tb_shard_group_destroy", g)
+
+
+def _abi_rank(rank, world, q_id, q_done):
+    sys.path.insert(0, ROOT)
+    sys.path.insert(0, os.path.join(ROOT, "turbo.cpp_b200", "python"))
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    import turbo_b200 as T
+    from oracle import orbind as O
+    from turbo_b200 import synth
+    T.call("tb_init", rank)
+    if rank == 0:
+        uid = ctypes.create_string_buffer(128)
+        T.call("tb_shard_group_unique_id", uid)
+        for _ in range(world - 1):
+            q_id.put(uid.raw)
+    else:
+        uid = ctypes.create_string_buffer(q_id.get(timeout=60), 128)
+    g = ctypes.c_void_p()
+    T.call("tb_shard_group_create", world, rank, uid, 64, 60.0, ctypes.byref(g))
+    try:
+        _abi_case(T, O, synth, g, rank, world, T.stream_handle())
+    finally:
+        T.call("tb_shard_group_destroy", g)
+    q_done.put(rank)
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_shard_group_abi_two_gpus():
+    ctx = mp.get_context("spawn")
+    q_id, q_done = ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_abi_rank, args=(r, 2, q_id, q_done)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert sorted(q_done.get(timeout=5) for _ in range(2)) == [0, 1]

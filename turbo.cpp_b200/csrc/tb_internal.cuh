@@ -198,6 +198,12 @@ __device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src_gmem, u
       : "memory");
 }
 
+// L2 prefetch of [src, src + bytes) (16-byte aligned address, size a multiple
+// of 16); nothing is returned to the SM.
+__device__ __forceinline__ void prefetch_l2(const void *src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+
 // ---- packed fp32 pairs (sm_100a f32x2 arithmetic; each lane op is IEEE rn) ---
 
 __device__ __forceinline__ uint64_t pack2(float lo, float hi) {

@@ -1,0 +1,302 @@
+// tb_shard.cu -- vocab-sharded softmax and argmax, and the row-sharded Q8_0
+// GEMV, for a group of GPUs, each held by one process (or thread) that owns
+// one shard, exchanging over NCCL.
+//
+// The reference runs these ops whole on one CPU (src/nn/softmax.cpp:13-54,
+// src/core/sampler.cpp:13-26, src/tensor/tensor.cpp:328-382); here each rank
+// holds a contiguous slice of the columns (logits) or rows (weights):
+//   softmax  per-shard row statistics (max m, sum of exp(x - m)) from
+//            tb_softmax_shard_stats, ONE all-gather of the (m, s) pairs, a
+//            combine in rank order (M = max m_r, S = sum_r s_r exp(m_r - M)),
+//            then tb_softmax_shard_finish writes exp(x - M) / S;
+//   argmax   per-shard 64-bit keys (tb_argmax_shard_keys), one int64 MAX
+//            all-reduce, then tb_argmax_key_index;
+//   GEMV     the rank's rows into its slot of y, one in-place all-gather.
+// NCCL is loaded at run time (dlopen of libnccl.so.2, preferring a copy the
+// process already has loaded), so the library has no link-time dependency on
+// it.  The communicator is created non-blocking with a host-side time limit,
+// and aborted when the limit passes; tb_shard_group_wait bounds the wait for
+// a stream's collectives the same way.
+#include <dlfcn.h>
+#include <nccl.h>
+
+#include <chrono>
+#include <cstring>
+#include <mutex>
+#include <thread>
+
+#include "tb_internal.cuh"
+
+namespace tb {
+namespace {
+
+struct NcclApi {
+  ncclResult_t (*GetUniqueId)(ncclUniqueId *);
+  ncclResult_t (*CommInitRankConfig)(ncclComm_t *, int, ncclUniqueId, int, ncclConfig_t *);
+  ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *);
+  ncclResult_t (*CommAbort)(ncclComm_t);
+  ncclResult_t (*CommDestroy)(ncclComm_t);
+  ncclResult_t (*AllGather)(const void *, void *, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+  ncclResult_t (*AllReduce)(const void *, void *, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t, cudaStream_t);
+  const char *(*GetErrorString)(ncclResult_t);
+  bool ok = false;
+};
+
+NcclApi g_nccl;
+std::mutex g_nccl_mu;
+
+tb_status nccl_api(NcclApi **out) {
+  std::lock_guard<std::mutex> lk(g_nccl_mu);
+  if (!g_nccl.ok) {
+    void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_NOLOAD);
+    if (!h) h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) h = dlopen("libnccl.so", RTLD_NOW | RTLD_GLOBAL);
+    if (!h) return fail(TB_ERUNTIME, "tb_shard_group: cannot load libnccl.so.2: %s", dlerror());
+#define TB_NCCL_SYM(field, name)                                                                        \
+  *reinterpret_cast<void **>(&g_nccl.field) = dlsym(h, name);                                           \
+  if (!g_nccl.field) return fail(TB_ERUNTIME, "tb_shard_group: libnccl.so.2 lacks %s", name);
+    TB_NCCL_SYM(GetUniqueId, "ncclGetUniqueId")
+    TB_NCCL_SYM(CommInitRankConfig, "ncclCommInitRankConfig")
+    TB_NCCL_SYM(CommGetAsyncError, "ncclCommGetAsyncError")
+    TB_NCCL_SYM(CommAbort, "ncclCommAbort")
+    TB_NCCL_SYM(CommDestroy, "ncclCommDestroy")
+    TB_NCCL_SYM(AllGather, "ncclAllGather")
+    TB_NCCL_SYM(AllReduce, "ncclAllReduce")
+    TB_NCCL_SYM(GetErrorString, "ncclGetErrorString")
+#undef TB_NCCL_SYM
+    g_nccl.ok = true;
+  }
+  *out = &g_nccl;
+  return TB_OK;
+}
+
+// M[r] = max_k m_k[r], S[r] = sum over k in rank order of s_k[r] exp(m_k[r] - M[r]),
+// from the gathered stats [n_ranks][2][rows] (m then s per rank).  The rescale
+// is tb_softmax_shard_rescale's (__expf of the difference).
+__global__ void combine_stats_kernel(const float *__restrict__ g, int n, int rows, float *__restrict__ M,
+                                     float *__restrict__ S) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  float m = -INFINITY;
+  for (int k = 0; k < n; ++k) m = fmaxf(m, g[(size_t)k * 2 * rows + r]);
+  float s = 0.f;
+  for (int k = 0; k < n; ++k) {
+    const float mk = g[(size_t)k * 2 * rows + r], sk = g[(size_t)k * 2 * rows + rows + r];
+    const float w = mk == -INFINITY ? 0.f : __expf(__fsub_rn(mk, m));
+    s = __fadd_rn(s, __fmul_rn(sk, w));
+  }
+  M[r] = m;
+  S[r] = s;
+}
+
+}  // namespace
+}  // namespace tb
+
+struct tb_shard_group_s {
+  ncclComm_t comm = nullptr;
+  int rank = 0, n = 1, device = 0;
+  int64_t max_rows = 0;
+  float *stats = nullptr;   // [2][max_rows]: this rank's m then s
+  float *gathered = nullptr;  // [n][2][max_rows]
+  float *gm = nullptr, *gs = nullptr;  // [max_rows] combined
+  int64_t *keys = nullptr;  // [max_rows]
+  double timeout_s = 30.0;
+};
+
+using namespace tb;
+
+namespace {
+
+// Waits (bounded) until a non-blocking communicator's last call has finished.
+tb_status nccl_settle(NcclApi *api, ncclComm_t comm, ncclResult_t r, double timeout_s, const char *what) {
+  const auto t0 = std::chrono::steady_clock::now();
+  while (r == ncclInProgress) {
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > timeout_s) {
+      api->CommAbort(comm);
+      return fail(TB_ETIMEOUT, "%s: no progress within %.1f s; communicator aborted", what, timeout_s);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(100));
+    if (api->CommGetAsyncError(comm, &r) != ncclSuccess) break;
+  }
+  if (r != ncclSuccess) return fail(TB_ERUNTIME, "%s: %s", what, api->GetErrorString(r));
+  return TB_OK;
+}
+
+tb_status check_group(tb_shard_group g, const char *who) {
+  if (!g || !g->comm) return fail(TB_EINVAL, "%s: no shard group", who);
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev != g->device)
+    return fail(TB_EINVAL, "%s: the group's device %d is not the current device %d", who, g->device, dev);
+  return TB_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+tb_status tb_shard_group_unique_id(void *id_out) {
+  if (!id_out) return fail(TB_EINVAL, "tb_shard_group_unique_id: null pointer");
+  NcclApi *api;
+  TB_TRY(nccl_api(&api));
+  ncclUniqueId id;
+  ncclResult_t r = api->GetUniqueId(&id);
+  if (r != ncclSuccess) return fail(TB_ERUNTIME, "ncclGetUniqueId: %s", api->GetErrorString(r));
+  static_assert(sizeof(ncclUniqueId) == TB_SHARD_ID_BYTES, "NCCL unique id size");
+  std::memcpy(id_out, &id, sizeof(id));
+  return TB_OK;
+}
+
+tb_status tb_shard_group_create(int n_ranks, int rank, const void *id, int64_t max_rows, double timeout_s,
+                                tb_shard_group *out) {
+  if (!out || !id) return fail(TB_EINVAL, "tb_shard_group_create: null pointer");
+  *out = nullptr;
+  if (n_ranks < 1 || rank < 0 || rank >= n_ranks || max_rows < 1 || max_rows > (1 << 24) || !(timeout_s > 0))
+    return fail(TB_EINVAL, "tb_shard_group_create: bad rank %d of %d, max_rows %lld or timeout", rank, n_ranks,
+                (long long)max_rows);
+  NcclApi *api;
+  TB_TRY(nccl_api(&api));
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  tb_shard_group g = new tb_shard_group_s();
+  g->rank = rank;
+  g->n = n_ranks;
+  g->device = st->device;
+  g->max_rows = max_rows;
+  g->timeout_s = timeout_s;
+  const size_t R = (size_t)max_rows;
+  void *p = nullptr;
+  tb_status s = tb_alloc(&p, sizeof(float) * R * (2 + 2 * (size_t)n_ranks + 2) + sizeof(int64_t) * R + 256);
+  if (s != TB_OK) {
+    delete g;
+    return s;
+  }
+  g->stats = static_cast<float *>(p);
+  g->gathered = g->stats + 2 * R;
+  g->gm = g->gathered + 2 * R * (size_t)n_ranks;
+  g->gs = g->gm + R;
+  g->keys = reinterpret_cast<int64_t *>((reinterpret_cast<uintptr_t>(g->gs + R) + 255) & ~uintptr_t(255));
+  ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+  cfg.blocking = 0;
+  ncclUniqueId uid;
+  std::memcpy(&uid, id, sizeof(uid));
+  ncclResult_t r = api->CommInitRankConfig(&g->comm, n_ranks, uid, rank, &cfg);
+  if (r != ncclSuccess && r != ncclInProgress) {
+    tb_free(p);
+    delete g;
+    return fail(TB_ERUNTIME, "ncclCommInitRankConfig: %s", api->GetErrorString(r));
+  }
+  s = nccl_settle(api, g->comm, r, timeout_s, "tb_shard_group_create");
+  if (s != TB_OK) {
+    tb_free(p);
+    delete g;
+    return s;
+  }
+  *out = g;
+  return TB_OK;
+}
+
+tb_status tb_shard_group_destroy(tb_shard_group g) {
+  if (!g) return TB_OK;
+  NcclApi *api;
+  TB_TRY(nccl_api(&api));
+  if (g->comm) {
+    int dev = -1;
+    cudaGetDevice(&dev);
+    cudaSetDevice(g->device);
+    api->CommDestroy(g->comm);
+    cudaSetDevice(dev);
+  }
+  if (g->stats) tb_free(g->stats);
+  delete g;
+  return TB_OK;
+}
+
+tb_status tb_shard_group_abort(tb_shard_group g) {
+  if (!g || !g->comm) return fail(TB_EINVAL, "tb_shard_group_abort: no shard group");
+  NcclApi *api;
+  TB_TRY(nccl_api(&api));
+  api->CommAbort(g->comm);
+  g->comm = nullptr;
+  return TB_OK;
+}
+
+tb_status tb_shard_group_wait(tb_shard_group g, tb_stream stream, double timeout_s) {
+  TB_TRY(check_group(g, "tb_shard_group_wait"));
+  NcclApi *api;
+  TB_TRY(nccl_api(&api));
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t e = cudaStreamQuery(as_stream(stream));
+    if (e == cudaSuccess) return TB_OK;
+    if (e != cudaErrorNotReady) return fail(TB_ECUDA, "tb_shard_group_wait: %s", cudaGetErrorString(e));
+    ncclResult_t ar = ncclSuccess;
+    api->CommGetAsyncError(g->comm, &ar);
+    if (ar != ncclSuccess && ar != ncclInProgress) {
+      api->CommAbort(g->comm);
+      g->comm = nullptr;
+      return fail(TB_ERUNTIME, "tb_shard_group_wait: %s; communicator aborted", api->GetErrorString(ar));
+    }
+    if (std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count() > timeout_s) {
+      api->CommAbort(g->comm);
+      g->comm = nullptr;
+      return fail(TB_ETIMEOUT, "tb_shard_group_wait: the stream did not finish within %.1f s; communicator aborted",
+                  timeout_s);
+    }
+    std::this_thread::sleep_for(std::chrono::microseconds(50));
+  }
+}
+
+tb_status tb_softmax_vocab_sharded(tb_shard_group g, const float *x_dev, int64_t rows, int64_t cols, int64_t ld,
+                                   float *y_dev, int64_t ld_y, tb_stream stream) {
+  TB_TRY(check_group(g, "tb_softmax_vocab_sharded"));
+  if (rows < 0 || rows > g->max_rows) return fail(TB_EINVAL, "tb_softmax_vocab_sharded: rows %lld above the group's %lld",
+                                                  (long long)rows, (long long)g->max_rows);
+  if (rows == 0) return TB_OK;
+  NcclApi *api;
+  TB_TRY(nccl_api(&api));
+  cudaStream_t s = as_stream(stream);
+  TB_TRY(tb_softmax_shard_stats(x_dev, rows, cols, ld, g->stats, g->stats + rows, stream));
+  const float *gm = g->stats, *gs = g->stats + rows;
+  if (g->n > 1) {
+    ncclResult_t r = api->AllGather(g->stats, g->gathered, (size_t)(2 * rows), ncclFloat32, g->comm, s);
+    TB_TRY(nccl_settle(api, g->comm, r, g->timeout_s, "tb_softmax_vocab_sharded(all-gather)"));
+    combine_stats_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(g->gathered, g->n, (int)rows, g->gm, g->gs);
+    TB_TRY(check_launch("tb_softmax_vocab_sharded"));
+    gm = g->gm;
+    gs = g->gs;
+  }
+  return tb_softmax_shard_finish(x_dev, rows, cols, ld, gm, gs, y_dev, ld_y, stream);
+}
+
+tb_status tb_argmax_vocab_sharded(tb_shard_group g, const float *x_dev, int64_t rows, int64_t cols, int64_t ld,
+                                  int64_t col_base, int64_t *idx_dev, tb_stream stream) {
+  TB_TRY(check_group(g, "tb_argmax_vocab_sharded"));
+  if (rows < 0 || rows > g->max_rows) return fail(TB_EINVAL, "tb_argmax_vocab_sharded: rows %lld above the group's %lld",
+                                                  (long long)rows, (long long)g->max_rows);
+  if (rows == 0) return TB_OK;
+  NcclApi *api;
+  TB_TRY(nccl_api(&api));
+  TB_TRY(tb_argmax_shard_keys(x_dev, rows, cols, ld, col_base, g->keys, stream));
+  if (g->n > 1) {
+    ncclResult_t r = api->AllReduce(g->keys, g->keys, (size_t)rows, ncclInt64, ncclMax, g->comm, as_stream(stream));
+    TB_TRY(nccl_settle(api, g->comm, r, g->timeout_s, "tb_argmax_vocab_sharded(all-reduce)"));
+  }
+  return tb_argmax_key_index(g->keys, rows, idx_dev, stream);
+}
+
+tb_status tb_gemv_q8_0_row_sharded(tb_shard_group g, const float *x_dev, int64_t K, const void *w_local_dev,
+                                   int64_t n_local, float *y_dev, tb_stream stream) {
+  TB_TRY(check_group(g, "tb_gemv_q8_0_row_sharded"));
+  if (n_local <= 0 || K <= 0) return fail(TB_EINVAL, "tb_gemv_q8_0_row_sharded: bad extents");
+  NcclApi *api;
+  TB_TRY(nccl_api(&api));
+  float *slot = y_dev + (int64_t)g->rank * n_local;
+  TB_TRY(tb_matmul_quant(TB_Q8_0, x_dev, 1, K, w_local_dev, n_local, slot, stream));
+  if (g->n > 1) {
+    ncclResult_t r = api->AllGather(slot, y_dev, (size_t)n_local, ncclFloat32, g->comm, as_stream(stream));
+    TB_TRY(nccl_settle(api, g->comm, r, g->timeout_s, "tb_gemv_q8_0_row_sharded(all-gather)"));
+  }
+  return TB_OK;
+}
+
+}  // extern "C"

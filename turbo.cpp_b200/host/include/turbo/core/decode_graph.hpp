@@ -12,6 +12,12 @@ namespace turbo {
 class MiniGPT;
 class KVCache;
 
+// Selects the single-kernel decode step where the model's shapes allow it
+// (default on); off keeps the fused per-op graph.  Read when a DecodeGraph is
+// created.
+void set_persistent_decode(bool on);
+bool persistent_decode();
+
 // One decode step -- embedding, the transformer blocks, final norm, LM head,
 // argmax or nucleus sample -- recorded once as a CUDA graph.  The position, the input token and
 // the chosen tokens live in device memory, so the same graph is replayed for
@@ -23,6 +29,10 @@ class KVCache;
 // selected (set_exact_matmul), a layer with Q8_0 projections runs as five
 // launches: RMSNorm + Q/K/V GEMVs, RoPE + cache append + attention, O GEMV +
 // residual, RMSNorm + gate/up GEMVs + SwiGLU, down GEMV + residual.
+// When the shapes allow it (hidden 2048, head_dim 64, Q8_0 weights; see
+// tb_decode_step_persistent) and persistent decode is on (the default,
+// set_persistent_decode), the whole step up to the logits is instead ONE
+// persistent kernel, followed by the argmax or sample and the advance.
 class DecodeGraph {
  public:
   // `kv` holds the prompt's keys/values (kv.get_current_seq_len() rows).
@@ -43,6 +53,10 @@ class DecodeGraph {
  private:
   void enqueue_step();
   void enqueue_step_fused();
+  void setup_persistent();  // tables and workspace of the single-kernel step
+  void enqueue_step_persistent();
+  bool persistent_ = false;
+  tb_decode_model pm_{};
   void enqueue_pick(tb_stream s);  // argmax or sample, margin, advance
   void *buf(size_t bytes);
   bool fused_ = false;
@@ -57,7 +71,7 @@ class DecodeGraph {
   int max_seq_;
   float scale_;
   // device buffers
-  void *arena_[32] = {};
+  void *arena_[40] = {};
   int n_arena_ = 0;
   int32_t *ids_, *pos_, *hist_;
   int64_t *idx_;

@@ -16,7 +16,15 @@ using turbo::detail::tb_dtype_of;
 
 namespace turbo {
 
+namespace {
+bool g_persistent = true;
+}
+void set_persistent_decode(bool on) { g_persistent = on; }
+bool persistent_decode() { return g_persistent; }
+
 void *DecodeGraph::buf(size_t bytes) {
+  if (n_arena_ >= (int)(sizeof(arena_) / sizeof(arena_[0])))
+    throw std::runtime_error("DecodeGraph: too many device buffers");
   void *p = nullptr;
   tb_check(tb_alloc(&p, bytes));
   arena_[n_arena_++] = p;
@@ -72,6 +80,78 @@ DecodeGraph::DecodeGraph(MiniGPT &model, KVCache &kv, bool want_margins, float t
   sw_ = static_cast<float *>(buf(f * F_));
   fo_ = static_cast<float *>(buf(f * E_));
   logits_ = static_cast<float *>(buf(f * V_));
+  if (fused_ && persistent_decode()) setup_persistent();
+}
+
+// The single-kernel step needs hidden 2048, head_dim 64, ffn 2048/4096/8192,
+// <= 4 query heads per key/value head, max_seq <= 2048, Q8_0 embedding and LM
+// head, one epsilon per norm kind; otherwise the fused graph stays in use.
+void DecodeGraph::setup_persistent() {
+  const Tensor &emb = m_.tok_emb.get_weight();
+  const Tensor &lm = m_.lm_head.get_weight();
+  const nn::TransformerBlock &b0 = m_.blocks[0];
+  bool ok = E_ == 2048 && D_ == 64 && (F_ == 2048 || F_ == 4096 || F_ == 8192) && H_ / KVH_ <= 4 && KVH_ <= 56 &&
+            max_seq_ <= 2048 && emb.dtype() == DataType::Q8_0 && lm.dtype() == DataType::Q8_0 &&
+            (reinterpret_cast<uintptr_t>(lm.get_storage()->device_data()) & 15) == 0 &&
+            (reinterpret_cast<uintptr_t>(emb.get_storage()->device_data()) & 15) == 0;
+  for (const auto &b : m_.blocks)
+    ok = ok && b.attention_norm.epsilon == b0.attention_norm.epsilon && b.ffn_norm.epsilon == b0.ffn_norm.epsilon;
+  if (!ok) return;
+  std::vector<tb_decode_layer> layers(m_.blocks.size());
+  auto wptr = [](nn::Linear &l) { return (const void *)l.get_weight().get_storage()->device_data(); };
+  for (size_t l = 0; l < m_.blocks.size(); ++l) {
+    nn::TransformerBlock &b = m_.blocks[l];
+    tb_decode_layer &d = layers[l];
+    d.wq = wptr(b.attention.q_proj);
+    d.wk = wptr(b.attention.k_proj);
+    d.wv = wptr(b.attention.v_proj);
+    d.wo = wptr(b.attention.o_proj);
+    d.w_gate = wptr(b.ffn.gate_proj);
+    d.w_up = wptr(b.ffn.up_proj);
+    d.w_down = wptr(b.ffn.down_proj);
+    d.attn_norm = static_cast<const float *>(b.attention_norm.get_weight().device_ptr());
+    d.ffn_norm = static_cast<const float *>(b.ffn_norm.get_weight().device_ptr());
+    d.k_cache = static_cast<float *>(kv_.get_k_cache((int)l).device_ptr());
+    d.v_cache = static_cast<float *>(kv_.get_v_cache((int)l).device_ptr());
+  }
+  tb_decode_layer *ldev = static_cast<tb_decode_layer *>(buf(sizeof(tb_decode_layer) * layers.size()));
+  tb_check(tb_upload(ldev, layers.data(), sizeof(tb_decode_layer) * layers.size(), stream_));
+  nn::MultiHeadAttention &a0 = m_.blocks[0].attention;
+  tb_decode_model &pm = pm_;
+  pm.n_layers = (int32_t)m_.blocks.size();
+  pm.hidden = (int64_t)E_;
+  pm.ffn = (int64_t)F_;
+  pm.heads = (int64_t)H_;
+  pm.kv_heads = (int64_t)KVH_;
+  pm.head_dim = (int64_t)D_;
+  pm.vocab = (int64_t)V_;
+  pm.max_seq = max_seq_;
+  pm.rope_max_seq = (int64_t)a0.rope.max_seq_len;
+  pm.eps_attn = b0.attention_norm.epsilon;
+  pm.eps_ffn = b0.ffn_norm.epsilon;
+  pm.eps_final = m_.norm.epsilon;
+  pm.attn_scale = scale_;
+  pm.layers_dev = ldev;
+  pm.tok_emb = emb.get_storage()->device_data();
+  pm.lm_head = lm.get_storage()->device_data();
+  pm.final_norm = static_cast<const float *>(m_.norm.get_weight().device_ptr());
+  pm.rope_cos = static_cast<const float *>(a0.rope.dev_cos->device_ptr());
+  pm.rope_sin = static_cast<const float *>(a0.rope.dev_sin->device_ptr());
+  pm.token_dev = ids_;
+  pm.pos_dev = pos_;
+  pm.logits = logits_;
+  size_t ws = 0;
+  tb_check(tb_decode_workspace_bytes(&pm, &ws));
+  pm.workspace = buf(ws);
+  pm.workspace_bytes = ws;
+  tb_check(tb_memset(pm.workspace, 0, ws, stream_));
+  tb_check(tb_sync(stream_));
+  persistent_ = true;
+}
+
+void DecodeGraph::enqueue_step_persistent() {
+  tb_check(tb_decode_step_persistent(&pm_, stream_));
+  enqueue_pick(stream_);
 }
 
 DecodeGraph::~DecodeGraph() {
@@ -161,6 +241,7 @@ void DecodeGraph::enqueue_step_fused() {
 }
 
 void DecodeGraph::enqueue_step() {
+  if (persistent_) return enqueue_step_persistent();
   if (fused_) return enqueue_step_fused();
   tb_stream s = stream_;
   const int64_t E = (int64_t)E_, F = (int64_t)F_, V = (int64_t)V_;

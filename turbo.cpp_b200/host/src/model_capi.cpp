@@ -68,6 +68,11 @@ TBM_API void *tbm_model_load(const char *path, int exact) {
 
 TBM_API void tbm_model_free(void *h) { delete static_cast<Model *>(h); }
 
+// persistent != 0 (the default): decode steps run as one persistent kernel per
+// token where the model's shapes allow it (turbo::set_persistent_decode);
+// 0 keeps the fused per-op CUDA graph.  Applies to later generate calls.
+TBM_API void tbm_set_persistent_decode(int persistent) { turbo::set_persistent_decode(persistent != 0); }
+
 // Prefill `prompt`, then `steps` decode steps.  out_ids[steps + 1] receives
 // the token chosen after the prefill and after each step: greedy, or with
 // temperature > 0 sample_top_p(logits, temperature, top_p) drawn with

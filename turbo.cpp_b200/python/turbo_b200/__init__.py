@@ -79,6 +79,16 @@ SIGNATURES = {
     "tb_softmax_shard_finish": [_P, _I64, _I64, _I64, _P, _P, _P, _I64, _P],
     "tb_argmax_shard_keys": [_P, _I64, _I64, _I64, _I64, _P, _P],
     "tb_argmax_key_index": [_P, _I64, _P, _P],
+    "tb_shard_group_unique_id": [_P],
+    "tb_shard_group_create": [_I, _I, _P, _I64, ctypes.c_double, ctypes.POINTER(_P)],
+    "tb_shard_group_wait": [_P, _P, ctypes.c_double],
+    "tb_shard_group_abort": [_P],
+    "tb_shard_group_destroy": [_P],
+    "tb_softmax_vocab_sharded": [_P, _P, _I64, _I64, _I64, _P, _I64, _P],
+    "tb_argmax_vocab_sharded": [_P, _P, _I64, _I64, _I64, _I64, _P, _P],
+    "tb_gemv_q8_0_row_sharded": [_P, _P, _I64, _P, _I64, _P, _P],
+    "tb_decode_workspace_bytes": [_P, ctypes.POINTER(_SZ)],
+    "tb_decode_step_persistent": [_P, _P],
     "tb_selfcheck_exp": [_P],
     "tb_rope_at": [_VP, _P, _P, _I64, _I64, _P, _P],
     "tb_kv_append": [_P, _P, _P, _P, _I64, _I64, _P, _P],

@@ -21,6 +21,8 @@ def lib():
         L.tbm_model_load.restype = ctypes.c_void_p
         L.tbm_model_load.argtypes = [ctypes.c_char_p, ctypes.c_int]
         L.tbm_model_free.argtypes = [ctypes.c_void_p]
+        L.tbm_set_persistent_decode.argtypes = [ctypes.c_int]
+        L.tbm_set_persistent_decode.restype = None
         L.tbm_model_generate.restype = ctypes.c_int
         L.tbm_model_generate.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t,
                                          ctypes.c_size_t, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
@@ -35,10 +37,15 @@ def lib():
 
 
 class Model:
-    def __init__(self, path, exact=True):
+    def __init__(self, path, exact=True, persistent=True):
+        """exact: the bit-identical matmul kernels and the op-by-op step;
+        otherwise one CUDA graph per token, whose step is a single persistent
+        kernel when `persistent` and the model's shapes allow it, else the
+        fused per-op kernels."""
         self.h = lib().tbm_model_load(path.encode(), 1 if exact else 0)
         if not self.h:
             raise RuntimeError("tbm_model_load: " + lib().tbm_last_error().decode())
+        self.persistent = persistent
 
     def generate(self, prompt, steps, max_seq=1024, want_margins=True, want_logits=False, vocab=128256,
                  temperature=0.0, top_p=0.9, uniforms=None):
@@ -50,6 +57,7 @@ class Model:
         margins = np.zeros(steps + 1, np.float32) if want_margins else None
         logits = np.zeros(vocab, np.float32) if want_logits else None
         pre, dec = ctypes.c_double(), ctypes.c_double()
+        lib().tbm_set_persistent_decode(1 if self.persistent else 0)
         if temperature > 0:
             if want_logits:
                 raise ValueError("want_logits is for greedy runs")

@@ -411,8 +411,7 @@ def decode_1b_leg(args):
            "steps": steps, "prompt": int(prompt.size), "runs": len(runs),
            "decode_ms": round(best["decode_ms"], 2), "prefill_ms": round(best["prefill_ms"], 1),
            "ids_identical_to_reference": same,
-           "path": "tbm_model_generate: one CUDA graph per token holding the persistent decode kernel "
-                   "(tb_decode_step_persistent) and the argmax/advance kernels",
+           "path": "tbm_model_generate: one CUDA graph per token of the fused layer kernels (5 per layer)",
            "roofline": {"bound": "hbm", "bytes_per_token": int(per_tok), "achieved": round(per_tok * tok_s / 1e9, 1),
                         "peak": peak, "unit": "GB/s", "frac": round(per_tok * tok_s / 1e9 / peak, 4),
                         "peak_source": peak_kind},
@@ -513,7 +512,7 @@ def run_decode_suite(args):
     golden = np.load(os.path.join(ROOT, "tests", "golden", "decode_1b.npz"))
     model_path = gguf_synth.ensure_model()
     steps = int(golden["steps"])
-    paths = [("persistent", False, True), ("fused", False, False)] + ([("exact", True, False)] if args.only == "both" else [])
+    paths = [("fused", False, False), ("persistent", False, True)] + ([("exact", True, False)] if args.only == "both" else [])
     for name, exact, persistent in paths:
         m = Model(model_path, exact=exact, persistent=persistent)
         m.generate(golden["prompt"], 4, max_seq=int(golden["max_seq"]), want_margins=False)  # warm-up

@@ -17,7 +17,7 @@ using turbo::detail::tb_dtype_of;
 namespace turbo {
 
 namespace {
-bool g_persistent = true;
+bool g_persistent = false;
 }
 void set_persistent_decode(bool on) { g_persistent = on; }
 bool persistent_decode() { return g_persistent; }

@@ -68,9 +68,9 @@ TBM_API void *tbm_model_load(const char *path, int exact) {
 
 TBM_API void tbm_model_free(void *h) { delete static_cast<Model *>(h); }
 
-// persistent != 0 (the default): decode steps run as one persistent kernel per
-// token where the model's shapes allow it (turbo::set_persistent_decode);
-// 0 keeps the fused per-op CUDA graph.  Applies to later generate calls.
+// persistent != 0: decode steps run as one persistent kernel per token where
+// the model's shapes allow it (turbo::set_persistent_decode); 0 (the default)
+// keeps the fused per-op CUDA graph.  Applies to later generate calls.
 TBM_API void tbm_set_persistent_decode(int persistent) { turbo::set_persistent_decode(persistent != 0); }
 
 // Prefill `prompt`, then `steps` decode steps.  out_ids[steps + 1] receives

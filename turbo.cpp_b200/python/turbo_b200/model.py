@@ -37,7 +37,7 @@ def lib():
 
 
 class Model:
-    def __init__(self, path, exact=True, persistent=True):
+    def __init__(self, path, exact=True, persistent=False):
         """exact: the bit-identical matmul kernels and the op-by-op step;
         otherwise one CUDA graph per token, whose step is a single persistent
         kernel when `persistent` and the model's shapes allow it, else the

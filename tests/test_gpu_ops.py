@@ -162,6 +162,33 @@ def test_matmul_q8_0_default_within_tolerance(M, K, N):
     assert_dot_tol(run_matmul(T.Q8_0, x, wq, N, "tb_matmul_quant"), x, wq, K)
 
 
+def test_matmul_q8_0_digit_path_and_its_fallbacks():
+    # 8192 x 2048 at M = 1 takes x as int8 digits per block (dp4a); a block that
+    # digits cannot hold (NaN, infinity, a tiny nonzero maximum) sends the
+    # whole product to the fp32 dot; a block of wide range stays on digits.
+    N, K = 8192, 2048
+    wq = synth.quantize_q8_0(synth.normal((N, K), 0.02, seed=41))
+    base = synth.normal((1, K), 1.0, seed=42)
+    cases = {"plain": base.copy(), "zeros": np.zeros((1, K), np.float32), "wide": base.copy(),
+             "tiny": base.copy(), "nan": base.copy(), "inf": base.copy()}
+    cases["wide"][0, 64:96] *= 1e-4
+    cases["wide"][0, 70] = 1e3
+    cases["tiny"][0, 128:160] *= 1e-33
+    cases["nan"][0, 300] = np.nan
+    cases["inf"][0, 5] = np.inf
+    for name, x in cases.items():
+        got = run_matmul(T.Q8_0, x, wq, N, "tb_matmul_quant")
+        ref = O.matmul_q8_0(x, wq, N)
+        if name in ("nan", "inf"):
+            assert np.array_equal(np.isnan(got), np.isnan(ref)), name
+            assert np.array_equal(got[~np.isnan(got)], ref[~np.isnan(ref)]), name
+            continue
+        if name == "zeros":
+            assert np.array_equal(got, ref), name
+            continue
+        assert_dot_tol(got, x, wq, K)
+
+
 def test_matmul_q8_0_unaligned_weight_base():
     N, K = 33, 2048
     wq = synth.quantize_q8_0(synth.normal((N, K), 0.02, seed=1)).ravel()

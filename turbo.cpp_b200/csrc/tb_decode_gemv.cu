@@ -48,13 +48,14 @@ struct FusedArgs {
 // Programmatic dependent launch: the first span's copy is issued before
 // griddepcontrol.wait (weights never depend on the previous kernel).
 // SWIGLU: segment 0 = gate, segment 1 = up (same rows), y[0] = silu(g) * u.
-template <bool NORM, bool SWIGLU>
+template <bool NORM, bool SWIGLU, bool DIG>
 __global__ void __launch_bounds__(kStreamWarps * 32, 4) gemv_stream_kernel(const FusedArgs a,
                                                                            uint32_t *__restrict__ err) {
   constexpr int NW = kStreamWarps;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ int done[kStreamMaxSlots];
   __shared__ int abort_flag;
+  __shared__ int dig_special;  // DIG: a block of x needs the fp32 dot
   __shared__ float red[NW];
   __shared__ double tab[SWIGLU ? 64 : 1];  // exp_cr table (SWIGLU epilogue)
   const int K = a.K, nb = K / 32, rb = nb * 34;
@@ -62,7 +63,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 4) gemv_stream_kernel(const
   const int slots = a.slots;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem);  // [kStreamMaxSlots]
   float *xs = reinterpret_cast<float *>(smem + 8 * kStreamMaxSlots);
-  uint8_t *ring = reinterpret_cast<uint8_t *>(xs + 32 * XS);
+  uint8_t *ring = reinterpret_cast<uint8_t *>(xs + 32 * XS + (DIG ? 3 * 16 * 32 + 64 : 0));
   ring = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(ring) + 127) & ~uintptr_t(127));
   constexpr int kRowsPerSlot = SWIGLU ? 2 * NW : NW;
   const size_t slot_bytes = (size_t)kRowsPerSlot * rb;
@@ -122,6 +123,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 4) gemv_stream_kernel(const
       done[i] = 0;
     }
     abort_flag = 0;
+    dig_special = 0;
     fence_mbar_init();
     if (nspans > 0) issue(0);  // the rest after x is staged (below)
   }
@@ -171,9 +173,21 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 4) gemv_stream_kernel(const
   // weight range (measured: 6.4 us against 6.8-7.1 us per 8192 x 2048 GEMV).
   if (threadIdx.x == 0)
     for (int k = 1; k < slots && k < nspans; ++k) issue(k);
-  float2 xp[32];
-  if (nb <= 64) q8_pair_x(xp, xs, XS, 2 * lane, 2 * lane < nb);
+  // DIG (K = 2048, one block pair per lane): x as int8 digits and dp4a row
+  // dots, unless a block of x cannot be written so (then the whole CTA takes
+  // the fp32 dot)
+  bool use_dig = false;
+  uint32_t *dgs = reinterpret_cast<uint32_t *>(xs + 32 * XS);  // DIG: [3][16][32] digits, then sx[64]
+  float *sxs = reinterpret_cast<float *>(dgs + 3 * 16 * 32);
+  if (DIG) {
+    const int t = threadIdx.x;  // NW * 32 = 2 * 64 threads: half a block each
+    if (q8_make_digits(xs, XS, t >> 1, t & 1, dgs, sxs)) atomicOr(&dig_special, 1);
+    __syncthreads();
+    use_dig = *(volatile int *)&dig_special == 0;
+  }
 
+  // Runs the CTA's spans with row dot `dot(wrow)` (every lane returns it).
+  auto spans = [&](auto &&dot) {
   for (int k = 0; k < nspans; ++k) {
     const int slot = k % slots;
     const int nr = min(NW, cnt - k * NW);
@@ -187,11 +201,11 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 4) gemv_stream_kernel(const
       const uint8_t *wrow = ring + slot * slot_bytes + (size_t)warp * rb;
       const int r = n0 + k * NW + warp;
       if (SWIGLU) {
-        const float g = q8_row_dot_pairs(wrow, nb, xp, xs, XS, lane);
-        const float u = q8_row_dot_pairs(wrow + (size_t)NW * rb, nb, xp, xs, XS, lane);
+        const float g = dot(wrow);
+        const float u = dot(wrow + (size_t)NW * rb);
         if (lane == 0) a.y[0][r] = swiglu_f32(g, u, tab);
       } else {
-        const float v = q8_row_dot_pairs(wrow, nb, xp, xs, XS, lane);
+        const float v = dot(wrow);
         if (lane == 0) store(r, v);
       }
       // With a ring (nspans > slots), the last of the span's nr warps refills
@@ -212,37 +226,33 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 4) gemv_stream_kernel(const
       __syncwarp();
     }
   }
+  };
+  if (use_dig) {
+    uint32_t dgr[3][16];
+    float sxr[2];
+#pragma unroll
+    for (int j = 0; j < 3; ++j)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) dgr[j][i] = dgs[(j * 16 + i) * 32 + lane];
+    sxr[0] = sxs[2 * lane];
+    sxr[1] = sxs[2 * lane + 1];
+    spans([&](const uint8_t *wrow) { return q8_row_dot_digits(wrow, dgr, sxr, lane); });
+  } else {
+    float2 xp[32];
+    if (nb <= 64) q8_pair_x(xp, xs, XS, 2 * lane, 2 * lane < nb);
+    spans([&](const uint8_t *wrow) { return q8_row_dot_pairs(wrow, nb, xp, xs, XS, lane); });
+  }
 }
 
-size_t stream_fixed_smem(int K) {
+size_t stream_fixed_smem(int K, bool dig = false) {
   const int nb = K / 32;
-  const size_t s = 8 * kStreamMaxSlots + (size_t)32 * (nb + 2) * 4;
+  const size_t s = 8 * kStreamMaxSlots + (size_t)32 * (nb + 2) * 4 + (dig ? (3 * 16 * 32 + 64) * 4 : 0);
   return (s + 127) & ~size_t(127);
 }
 
-// Grid and span buffers: four CTAs per SM when at least two buffers (or all
-// the CTA's spans) fit in a quarter of the SM's shared memory, else fewer CTAs
-// per SM; then as many buffers as the CTA has spans, up to what fits.
-template <bool NORM, bool SWIGLU>
-tb_status launch_stream(FusedArgs a, int total_rows, cudaStream_t s, const DeviceState *st) {
-  const int nb = a.K / 32;
-  const size_t slot_bytes = (size_t)(SWIGLU ? 2 : 1) * kStreamWarps * nb * 34;
-  const size_t fixed = stream_fixed_smem(a.K);
-  auto kern = gemv_stream_kernel<NORM, SWIGLU>;
-  int cps = 4, slots = 0, grid = 1;
-  for (; cps >= 1; --cps) {
-    grid = std::max(1, std::min(total_rows, st->sm_count * cps));
-    const int maxcnt = (total_rows + grid - 1) / grid;
-    const int nspans = (maxcnt + kStreamWarps - 1) / kStreamWarps;
-    const int64_t budget = std::min<int64_t>((int64_t)st->smem_per_sm / cps - st->smem_reserved - 2048,
-                                             (int64_t)st->smem_optin) - (int64_t)fixed;
-    const int fit = budget > 0 ? (int)std::min<int64_t>(budget / (int64_t)slot_bytes, kStreamMaxSlots) : 0;
-    slots = std::min(nspans, fit);
-    if (slots >= std::min(nspans, 2)) break;
-  }
-  if (cps < 1 || slots < 1) return fail(TB_EINVAL, "streaming GEMV: K=%d too large", a.K);
-  a.slots = slots;
-  const size_t smem = fixed + (size_t)slots * slot_bytes;
+template <bool NORM, bool SWIGLU, bool DIG>
+tb_status launch_stream_as(FusedArgs a, int grid, size_t smem, cudaStream_t s, const DeviceState *st) {
+  auto kern = gemv_stream_kernel<NORM, SWIGLU, DIG>;
   TB_TRY(ensure_smem_for(kern, smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid, 1, 1);
@@ -257,6 +267,45 @@ tb_status launch_stream(FusedArgs a, int total_rows, cudaStream_t s, const Devic
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a, st->err_word);
   if (e != cudaSuccess) return fail(TB_ECUDA, "streaming GEMV launch: %s", cudaGetErrorString(e));
   return TB_OK;
+}
+
+// Grid and span buffers: four CTAs per SM when at least two buffers (or all
+// the CTA's spans) fit in a quarter of the SM's shared memory, else fewer CTAs
+// per SM; then as many buffers as the CTA has spans, up to what fits.  At
+// K = 2048 with at least kDigitRows rows per CTA the row dots take x as int8
+// digits (dp4a); below that the per-CTA digit preparation costs more than it
+// saves (2048 x 2048: 3.6 against 3.1 us; 8192 x 2048: 5.1 against 6.2 us,
+// lab copies timed back to back).
+constexpr int kDigitRows = 8;
+
+template <bool NORM, bool SWIGLU>
+tb_status launch_stream(FusedArgs a, int total_rows, cudaStream_t s, const DeviceState *st) {
+  const int nb = a.K / 32;
+  const size_t slot_bytes = (size_t)(SWIGLU ? 2 : 1) * kStreamWarps * nb * 34;
+  for (int dig = nb == 64 ? 1 : 0; dig >= 0; --dig) {
+    const size_t fixed = stream_fixed_smem(a.K, dig != 0);
+    int cps = 4, slots = 0, grid = 1, maxcnt = 0;
+    for (; cps >= 1; --cps) {
+      grid = std::max(1, std::min(total_rows, st->sm_count * cps));
+      maxcnt = (total_rows + grid - 1) / grid;
+      const int nspans = (maxcnt + kStreamWarps - 1) / kStreamWarps;
+      const int64_t budget = std::min<int64_t>((int64_t)st->smem_per_sm / cps - st->smem_reserved - 2048,
+                                               (int64_t)st->smem_optin) - (int64_t)fixed;
+      const int fit = budget > 0 ? (int)std::min<int64_t>(budget / (int64_t)slot_bytes, kStreamMaxSlots) : 0;
+      slots = std::min(nspans, fit);
+      if (slots >= std::min(nspans, 2)) break;
+    }
+    if (cps < 1 || slots < 1) {
+      if (dig) continue;
+      return fail(TB_EINVAL, "streaming GEMV: K=%d too large", a.K);
+    }
+    if (dig && maxcnt < kDigitRows) continue;
+    a.slots = slots;
+    const size_t smem = fixed + (size_t)slots * slot_bytes;
+    return dig ? launch_stream_as<NORM, SWIGLU, true>(a, grid, smem, s, st)
+               : launch_stream_as<NORM, SWIGLU, false>(a, grid, smem, s, st);
+  }
+  return fail(TB_EINVAL, "streaming GEMV: K=%d too large", a.K);
 }
 
 }  // namespace

@@ -289,6 +289,171 @@ __global__ void __launch_bounds__(NT) softmax_cluster_kernel(
   cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
 }
 
+// One or a few rows of whole float4s (the 128256-wide logits of a decode
+// step): a cluster of up to 16 CTAs per row, each thread holding up to VPT
+// float4s of its CTA's slice in registers, all loaded at once -- no
+// shared-memory staging.  Same arithmetic as softmax_cluster_kernel: max under
+// '>' (NaN never wins), e = exp(x - M), S = block sums added in cluster-rank
+// order, y = e * (1/S).  Slices are multiples of 4 columns and row strides
+// multiples of 4, so every load and store is a float4.
+template <int MODE, int NT, int VPT>
+__global__ void __launch_bounds__(NT) softmax_cluster_reg_kernel(
+    const float *__restrict__ x, float *__restrict__ y, int64_t rows, int64_t cols, int64_t ldx, int64_t ldy,
+    int span, float *__restrict__ out_max, float *__restrict__ out_sum) {
+  __shared__ float scratch[32];
+  __shared__ float part[2];
+  cg::cluster_group cluster = cg::this_cluster();
+  const int crank = (int)cluster.block_rank();
+  const int csize = (int)cluster.num_blocks();
+  const int64_t row = blockIdx.x / csize;
+  if (row >= rows) return;  // whole clusters share a row
+  const int64_t c0 = (int64_t)crank * span;
+  const int64_t c1 = (c0 + span < cols) ? c0 + span : cols;
+  const int n4 = c1 > c0 ? (int)((c1 - c0) >> 2) : 0;
+  const float4 *xr = reinterpret_cast<const float4 *>(x + row * ldx + c0);
+  float4 v[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = threadIdx.x + j * NT;
+    if (i < n4) v[j] = MODE == 0 ? __ldcs(xr + i) : __ldg(xr + i);
+  }
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    if (threadIdx.x + j * NT < n4) {
+      m = v[j].x > m ? v[j].x : m;
+      m = v[j].y > m ? v[j].y : m;
+      m = v[j].z > m ? v[j].z : m;
+      m = v[j].w > m ? v[j].w : m;
+    }
+  }
+  m = block_max(m, scratch);
+  if (threadIdx.x == 0) part[0] = m;
+  cluster.sync();
+  float M = -INFINITY;
+  for (int c = 0; c < csize; ++c) {
+    const float pm = *cluster.map_shared_rank(&part[0], c);
+    M = pm > M ? pm : M;
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    if (threadIdx.x + j * NT < n4) {
+      v[j].x = __expf(__fsub_rn(v[j].x, M));
+      v[j].y = __expf(__fsub_rn(v[j].y, M));
+      v[j].z = __expf(__fsub_rn(v[j].z, M));
+      v[j].w = __expf(__fsub_rn(v[j].w, M));
+      s = __fadd_rn(s, __fadd_rn(__fadd_rn(v[j].x, v[j].y), __fadd_rn(v[j].z, v[j].w)));
+    }
+  }
+  s = block_sum(s, scratch);
+  if (threadIdx.x == 0) part[1] = s;
+  cluster.sync();
+  float S = 0.f;
+  for (int c = 0; c < csize; ++c) S = __fadd_rn(S, *cluster.map_shared_rank(&part[1], c));
+  if (MODE == 1) {
+    if (crank == 0 && threadIdx.x == 0) {
+      out_max[row] = M;
+      out_sum[row] = S;
+    }
+  } else {
+    const float inv = __frcp_rn(S);
+    float4 *yr = reinterpret_cast<float4 *>(y + row * ldy + c0);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int i = threadIdx.x + j * NT;
+      if (i < n4)
+        __stcs(yr + i, make_float4(__fmul_rn(v[j].x, inv), __fmul_rn(v[j].y, inv), __fmul_rn(v[j].z, inv),
+                                   __fmul_rn(v[j].w, inv)));
+    }
+  }
+  cluster.sync();  // keep this CTA's shared memory alive until every peer has read it
+}
+
+// Tens of rows of whole float4s (a batch of logits): two launches with no
+// cluster barriers.  Chunk stats: CTA (row, chunk) writes its chunk's max m_c
+// and sum of exp(x - m_c) (x read once from HBM, kept in registers).  Finish
+// (programmatic dependent launch): M = max_c m_c, S = sum over chunks in order
+// of s_c exp(m_c - M), then y = exp(x - M) * (1/S) for the chunk, x read again
+// (from L2 when the batch fits there).
+template <int NT, int VPT>
+__global__ void __launch_bounds__(NT) softmax_chunk_stats_kernel(const float *__restrict__ x, int64_t cols,
+                                                                  int64_t ldx, int span, int chunks,
+                                                                  float2 *__restrict__ part) {
+  __shared__ float scratch[32];
+  pdl_launch_dependents();
+  const int64_t row = blockIdx.x / chunks;
+  const int c = blockIdx.x % chunks;
+  const int64_t c0 = (int64_t)c * span, c1 = (c0 + span < cols) ? c0 + span : cols;
+  const int n4 = c1 > c0 ? (int)((c1 - c0) >> 2) : 0;
+  const float4 *xr = reinterpret_cast<const float4 *>(x + row * ldx + c0);
+  float4 v[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = threadIdx.x + j * NT;
+    if (i < n4) v[j] = __ldg(xr + i);
+  }
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    if (threadIdx.x + j * NT < n4) {
+      m = v[j].x > m ? v[j].x : m;
+      m = v[j].y > m ? v[j].y : m;
+      m = v[j].z > m ? v[j].z : m;
+      m = v[j].w > m ? v[j].w : m;
+    }
+  }
+  m = block_max(m, scratch);
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    if (threadIdx.x + j * NT < n4) {
+      s = __fadd_rn(s, __fadd_rn(__fadd_rn(__expf(__fsub_rn(v[j].x, m)), __expf(__fsub_rn(v[j].y, m))),
+                                 __fadd_rn(__expf(__fsub_rn(v[j].z, m)), __expf(__fsub_rn(v[j].w, m)))));
+    }
+  }
+  s = block_sum(s, scratch);
+  if (threadIdx.x == 0) part[blockIdx.x] = make_float2(m, s);
+}
+
+template <int NT, int VPT>
+__global__ void __launch_bounds__(NT) softmax_chunk_finish_kernel(const float *__restrict__ x, float *__restrict__ y,
+                                                                   int64_t cols, int64_t ldx, int64_t ldy, int span,
+                                                                   int chunks, const float2 *__restrict__ part) {
+  const int64_t row = blockIdx.x / chunks;
+  const int c = blockIdx.x % chunks;
+  const int64_t c0 = (int64_t)c * span, c1 = (c0 + span < cols) ? c0 + span : cols;
+  const int n4 = c1 > c0 ? (int)((c1 - c0) >> 2) : 0;
+  const float4 *xr = reinterpret_cast<const float4 *>(x + row * ldx + c0);
+  float4 v[VPT];
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {  // x does not depend on the stats kernel: load before the wait
+    const int i = threadIdx.x + j * NT;
+    if (i < n4) v[j] = __ldcs(xr + i);
+  }
+  pdl_wait();
+  const float2 *pr = part + row * chunks;
+  float M = -INFINITY;
+  for (int k = 0; k < chunks; ++k) {
+    const float pm = pr[k].x;
+    M = pm > M ? pm : M;
+  }
+  float S = 0.f;
+  for (int k = 0; k < chunks; ++k) {
+    const float2 p = pr[k];
+    S = __fadd_rn(S, p.x == -INFINITY ? 0.f : __fmul_rn(p.y, __expf(__fsub_rn(p.x, M))));
+  }
+  const float inv = __frcp_rn(S);
+  float4 *yr = reinterpret_cast<float4 *>(y + row * ldy + c0);
+#pragma unroll
+  for (int j = 0; j < VPT; ++j) {
+    const int i = threadIdx.x + j * NT;
+    if (i < n4)
+      __stcs(yr + i, make_float4(__fmul_rn(__expf(__fsub_rn(v[j].x, M)), inv), __fmul_rn(__expf(__fsub_rn(v[j].y, M)), inv),
+                                 __fmul_rn(__expf(__fsub_rn(v[j].z, M)), inv), __fmul_rn(__expf(__fsub_rn(v[j].w, M)), inv)));
+  }
+}
+
 // Many rows: one CTA per row, persistent over rows (grid = one CTA per SM).
 // Pass 1 reads the row once from HBM keeping a running (max, sum of exp) per
 // thread (the sum rescaled whenever the max grows), combined over the block;
@@ -609,6 +774,87 @@ int softmax_span(int64_t cols, int cs) {
   return (int)((span + 3) / 4 * 4);
 }
 
+constexpr int kRegNT = 256, kRegVPT = 8;  // softmax_cluster_reg_kernel: 8192 floats per CTA
+
+// Launches softmax_cluster_reg_kernel when the rows are few, whole float4s
+// and at most 16 x 8192 wide; returns false (nothing launched) otherwise.
+template <int MODE>
+bool softmax_reg_launch(const float *x, float *y, int64_t rows, int64_t cols, int64_t ldx, int64_t ldy, float *mx,
+                        float *sm, cudaStream_t s, const DeviceState *st, tb_status *status) {
+  if (rows >= st->sm_count || cols % 4 != 0 || ldx % 4 != 0 || (MODE == 0 && ldy % 4 != 0) ||
+      (reinterpret_cast<uintptr_t>(x) & 15) || (MODE == 0 && (reinterpret_cast<uintptr_t>(y) & 15)))
+    return false;
+  constexpr int64_t per_cta = (int64_t)kRegNT * kRegVPT * 4;
+  int cl = 1;
+  while (cl < 16 && (cols + cl - 1) / cl > per_cta) cl *= 2;
+  if ((cols + cl - 1) / cl > per_cta) return false;
+  auto kern = softmax_cluster_reg_kernel<MODE, kRegNT, kRegVPT>;
+  if (cl > 8) {
+    // a 16-CTA cluster is a non-portable size: check once that one fits
+    static int fits[64] = {0};
+    if (fits[st->device] == 0) {
+      int n = 0;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(16, 1, 1);
+      cfg.blockDim = dim3(kRegNT, 1, 1);
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 16;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e == cudaSuccess) e = cudaOccupancyMaxActiveClusters(&n, kern, &cfg);
+      fits[st->device] = (e == cudaSuccess && n > 0) ? 1 : -1;
+    }
+    if (fits[st->device] < 0) return false;
+  }
+  *status = launch_cluster_nt<kRegNT>(kern, rows, cl, 0, s, x, y, rows, cols, ldx, ldy, softmax_span(cols, cl), mx, sm);
+  return true;
+}
+
+// Launches the two-kernel chunked softmax (8 to sm_count rows of whole
+// float4s, at most 16 x 8192 wide); false (nothing launched) otherwise.  The
+// chunk statistics live in stream-ordered scratch.
+bool softmax_chunks_launch(const float *x, float *y, int64_t rows, int64_t cols, cudaStream_t s, const DeviceState *st,
+                           tb_status *status) {
+  if (rows < 8 || rows >= st->sm_count || cols % 4 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) ||
+      (reinterpret_cast<uintptr_t>(y) & 15))
+    return false;
+  constexpr int64_t per_cta = (int64_t)kRegNT * kRegVPT * 4;
+  int chunks = 1;
+  while (chunks < 16 && (cols + chunks - 1) / chunks > per_cta) chunks *= 2;
+  if ((cols + chunks - 1) / chunks > per_cta) return false;
+  const int span = softmax_span(cols, chunks);
+  const int64_t grid = rows * chunks;
+  float2 *part = nullptr;
+  cudaError_t e = cudaMallocAsync(reinterpret_cast<void **>(&part), (size_t)grid * sizeof(float2), s);
+  if (e != cudaSuccess) {
+    *status = fail(TB_ENOMEM, "tb_softmax: scratch: %s", cudaGetErrorString(e));
+    return true;
+  }
+  softmax_chunk_stats_kernel<kRegNT, kRegVPT><<<(unsigned)grid, kRegNT, 0, s>>>(x, cols, cols, span, chunks, part);
+  *status = check_launch("tb_softmax (chunk stats)");
+  if (*status == TB_OK) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)grid, 1, 1);
+    cfg.blockDim = dim3(kRegNT, 1, 1);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, softmax_chunk_finish_kernel<kRegNT, kRegVPT>, x, y, cols, cols, cols, span, chunks,
+                           (const float2 *)part);
+    if (e != cudaSuccess) *status = fail(TB_ECUDA, "tb_softmax (chunk finish): %s", cudaGetErrorString(e));
+  }
+  e = cudaFreeAsync(part, s);
+  if (*status == TB_OK && e != cudaSuccess) *status = fail(TB_ECUDA, "tb_softmax: scratch: %s", cudaGetErrorString(e));
+  return true;
+}
+
 }  // namespace
 }  // namespace tb
 
@@ -681,6 +927,9 @@ tb_status tb_softmax(const float *x, float *y, int64_t rows, int64_t cols, tb_st
     softmax_rows_kernel<<<st->sm_count, 1024, smem, s>>>(x, y, rows, cols, stash_f4);
     return check_launch("tb_softmax");
   }
+  tb_status rs = TB_OK;
+  if (softmax_chunks_launch(x, y, rows, cols, s, st, &rs)) return rs;
+  if (rows < 8 && softmax_reg_launch<0>(x, y, rows, cols, cols, cols, nullptr, nullptr, s, st, &rs)) return rs;
   if (rows * cs <= st->sm_count)  // few rows: wide CTAs shorten each row's critical path
     return launch_cluster_nt<1024>(softmax_cluster_kernel<0, 1024>, rows, cs, (size_t)span * 4, s, x, y,
                                    rows, cols, cols, cols, span, (float *)nullptr, (float *)nullptr,
@@ -715,6 +964,9 @@ tb_status tb_softmax_shard_stats(const float *x, int64_t rows, int64_t cols, int
   int cs = cluster_for(cols, kSliceFloats);
   if (cs == 0) return fail(TB_EINVAL, "tb_softmax_shard_stats: shard too wide (%lld columns)", (long long)cols);
   const int span = softmax_span(cols, cs);
+  tb_status rs = TB_OK;
+  if (rows < 8 && softmax_reg_launch<1>(x, nullptr, rows, cols, ld, 0, row_max, row_sum, as_stream(stream), st, &rs))
+    return rs;
   if (rows * cs <= st->sm_count)
     return launch_cluster_nt<1024>(softmax_cluster_kernel<1, 1024>, rows, cs, (size_t)span * 4, as_stream(stream),
                                    x, (float *)nullptr, rows, cols, ld, (int64_t)0, span, row_max, row_sum,

@@ -363,6 +363,21 @@ tb_status tb_decode_margin(const float *logits_dev, int64_t vocab, const int64_t
 tb_status tb_decode_advance(const int64_t *idx_dev, int32_t *ids_dev, int32_t *pos_dev, int32_t *history_dev,
                             int64_t max_seq, tb_stream stream);
 
+/* Causal grouped-query attention of a prompt in one launch: the 32-head loop
+ * of MultiHeadAttention::forward (src/nn/attention.cpp:104-141) for S query
+ * tokens at positions pos0 .. pos0 + S - 1 whose keys and values are already
+ * in the caches (rows 0 .. pos0 + S - 1, [max_seq, kv_heads * head_dim]).
+ * q: [S, heads * head_dim] rows (row stride ldq, RoPE applied); out: the
+ * context [S, heads * head_dim] (row stride ldo).  Scores are the fp32
+ * matmul's fma chain over d times `scale`; a query's later keys are masked;
+ * softmax divides by the sum; p . V is the fma chain over keys in increasing
+ * order.  Only exp and the order of the softmax sum differ from the reference
+ * (the softmax tolerance).  head_dim 64, at most 4 query heads per key/value
+ * head. */
+tb_status tb_attention_prefill(const float *q_dev, int64_t ldq, const float *k_cache_dev, const float *v_cache_dev,
+                               int64_t S, int64_t pos0, int64_t heads, int64_t kv_heads, int64_t head_dim,
+                               float scale, float *out_dev, int64_t ldo, tb_stream stream);
+
 /* One whole decode step of a Llama-shaped MiniGPT in a single persistent
  * kernel: MiniGPT::forward({token}, &kv) at S = 1 (src/model/minigpt.cpp:55-74,
  * the per-layer sequence of src/nn/transformer_block.cpp, attention.cpp:41-148,

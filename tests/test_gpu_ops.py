@@ -1077,3 +1077,42 @@ def test_rope_attention_decode_equals_separate_ops(p):
            T.ptr(kc2), T.ptr(vc2), max_seq, scale, T.ptr(bad), T.ptr(out2), S())
     assert T.take_device_errors() & 2
     assert_bits(host(kc2), host(kc1))
+
+
+# ---- causal GQA prefill attention (attention.cpp:104-141, all heads at once) ------
+def attention_ref(q, kc, vc, S, pos0, H, KVH, D, scale):
+    """float64 causal attention and, per output, sum_t p_t |v_t| (the scale of
+    its rounding error)."""
+    G = H // KVH
+    out = np.zeros((S, H * D))
+    mag = np.zeros((S, H * D))
+    for h in range(H):
+        kvh = h // G
+        qh = q[:, h * D:(h + 1) * D].astype(np.float64)
+        K = kc[:pos0 + S, kvh * D:(kvh + 1) * D].astype(np.float64)
+        V = vc[:pos0 + S, kvh * D:(kvh + 1) * D].astype(np.float64)
+        sc = (qh @ K.T) * scale
+        mask = np.arange(pos0 + S)[None, :] > (pos0 + np.arange(S))[:, None]
+        sc[mask] = -np.inf
+        p = np.exp(sc - sc.max(axis=1, keepdims=True))
+        p /= p.sum(axis=1, keepdims=True)
+        out[:, h * D:(h + 1) * D] = p @ V
+        mag[:, h * D:(h + 1) * D] = p @ np.abs(V)
+    return out, mag
+
+
+@pytest.mark.parametrize("n,pos0,H,KVH", [(512, 0, 32, 8), (37, 100, 32, 8), (1, 600, 32, 8), (200, 0, 8, 8),
+                                          (64, 1200, 32, 8), (100, 1900, 32, 8)])
+def test_attention_prefill(n, pos0, H, KVH):
+    D, max_seq = 64, 2048
+    q = synth.normal((n, H * D), 1.0, seed=n + pos0)
+    kc = synth.normal((max_seq, KVH * D), 1.0, seed=7)
+    vc = synth.normal((max_seq, KVH * D), 1.0, seed=8)
+    scale = np.float32(1.0 / np.sqrt(D))
+    out = torch.full((n, H * D), float("nan"), dtype=torch.float32, device="cuda")
+    T.call("tb_attention_prefill", T.ptr(dev(q)), H * D, T.ptr(dev(kc)), T.ptr(dev(vc)), n, pos0, H, KVH, D,
+           float(scale), T.ptr(out), H * D, S())
+    ref, mag = attention_ref(q, kc, vc, n, pos0, H, KVH, D, float(scale))
+    got = host(out).astype(np.float64)
+    err = np.abs(got - ref) / np.maximum(mag, 1e-30)
+    assert err.max() <= 1e-5, err.max()

@@ -204,19 +204,33 @@ Tensor MultiHeadAttention::forward(const Tensor &input, size_t position_offset, 
   rope.apply_in_place(Q, position_offset);
   rope.apply_in_place(K, position_offset);
 
+  const size_t n_rep = num_heads / num_kv_heads;
+  const float scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
   if (kv_cache != nullptr && layer_idx >= 0) {
     const size_t start = (size_t)kv_cache->get_current_seq_len();
     Tensor &Kc = kv_cache->get_k_cache(layer_idx);
     Tensor &Vc = kv_cache->get_v_cache(layer_idx);
     Kc.slice(0, start, start + S).copy_(K.squeeze(0).transpose(0, 1));
     Vc.slice(0, start, start + S).copy_(V.squeeze(0).transpose(0, 1));
+    if (B == 1 && head_dim == 64 && n_rep <= 4 && !exact_matmul()) {
+      // every head of the prompt in one launch: Q rows [S, H * D] as the
+      // projection wrote them (RoPE applied in place), keys/values from the
+      // cache rows 0 .. start + S; the context comes out as [S, H * D], the
+      // layout the per-head loop's transpose + contiguous would give
+      Tensor context = Tensor::empty({B, S, embed_dim});
+      tb_check(tb_attention_prefill(static_cast<const float *>(Q.device_ptr()), (int64_t)(num_heads * head_dim),
+                                    static_cast<const float *>(Kc.device_ptr()),
+                                    static_cast<const float *>(Vc.device_ptr()), (int64_t)S, (int64_t)start,
+                                    (int64_t)num_heads, (int64_t)num_kv_heads, (int64_t)head_dim, scale,
+                                    static_cast<float *>(context.get_storage()->device_data_discard()),
+                                    (int64_t)embed_dim, nullptr));
+      return o_proj.forward(context);
+    }
     K = Kc.slice(0, 0, start + S).transpose(0, 1).unsqueeze(0);
     V = Vc.slice(0, 0, start + S).transpose(0, 1).unsqueeze(0);
   }
 
   Tensor context = Tensor::zeros({B, num_heads, S, head_dim});
-  const size_t n_rep = num_heads / num_kv_heads;
-  const float scale = 1.0f / std::sqrt(static_cast<float>(head_dim));
   for (size_t b = 0; b < B; ++b) {
     for (size_t h = 0; h < num_heads; ++h) {
       const size_t kvh = h / n_rep;

@@ -88,6 +88,7 @@ SIGNATURES = {
     "tb_argmax_vocab_sharded": [_P, _P, _I64, _I64, _I64, _I64, _P, _P],
     "tb_gemv_q8_0_row_sharded": [_P, _P, _I64, _P, _I64, _P, _P],
     "tb_decode_workspace_bytes": [_P, ctypes.POINTER(_SZ)],
+    "tb_attention_prefill": [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _I64, _P],
     "tb_decode_step_persistent": [_P, _P],
     "tb_selfcheck_exp": [_P],
     "tb_rope_at": [_VP, _P, _P, _I64, _I64, _P, _P],

@@ -220,10 +220,11 @@ tb_status tb_embedding(int dtype, const void *w_dev, int64_t dim, int64_t vocab,
  *    bit for bit, then multiplied with the Q4_0 rows in the order of
  *    vec_dot_q4_0_q8_0_avx2 (quant_math.hpp:184-248).
  *  - M >= 32 with K a multiple of 256 and 16-byte aligned X and W runs on the
- *    tensor cores (both dtypes): exact per-block integer (Q4_0) or 22-bit
- *    (Q8_0) products accumulated in fp32 tensor memory, block scales applied
- *    in fp32 -- within 1e-5 of sum |w x| per output, typically ~1e-7; it
- *    allocates stream-ordered scratch for the packed operands.
+ *    tensor cores (both dtypes): per 256-wide K chunk, w = q d (with X as
+ *    Q8_0, q_x d_x, for TB_Q4_0) held exactly as two fp16 values, three fp16
+ *    products per pair accumulated in fp32 tensor memory, chunk sums added
+ *    in fp32 -- within 1e-5 of sum |w x| per output, typically 1e-7 to 6e-7;
+ *    it allocates stream-ordered scratch for the packed operands.
  * K must be a multiple of 32. */
 tb_status tb_matmul_quant(int dtype, const float *x_dev, int64_t M, int64_t K,
                           const void *w_dev, int64_t N, float *y_dev, tb_stream stream);
@@ -254,6 +255,30 @@ tb_status tb_matmul_quant_exact(int dtype, const float *x_dev, int64_t M, int64_
 tb_status tb_matmul_q4_0_static_scratch(const float *x_dev, int64_t M, int64_t K,
                                         const void *w_dev, int64_t N, float *y_dev,
                                         tb_stream stream);
+
+/* Weights packed once for the tensor-core matmul (M >= 32), so a prefill
+ * that multiplies by the same W many times does not convert it on every
+ * call.  No counterpart in the reference (its matmul reads the GGUF blocks
+ * directly, src/tensor/tensor.cpp:328-432); tb_matmul_quant packs W into
+ * scratch on every call and is otherwise the same computation.
+ * The packed form holds, per 128 rows x 256 K, the products q * d as two
+ * fp16 planes scaled by a power of two (4 bytes per weight), plus the scales:
+ * about 7x the Q4_0 bytes, 3.8x the Q8_0 bytes.
+ *  - tb_packed_quant_weights_bytes: the size for N rows of K (K a positive
+ *    multiple of 256, at most 2^20; dtype TB_Q8_0 or TB_Q4_0), else TB_EINVAL.
+ *  - tb_pack_quant_weights: W (N rows of K/32 blocks, 16-byte aligned) into
+ *    `packed_dev` (16-byte aligned, at least that many bytes), on `stream`.
+ *    The packed copy does not follow later changes of W.
+ *  - tb_matmul_quant_packed: Y[M, N] = X[M, K] . W from the packed copy, M >=
+ *    32 (TB_EINVAL below: those shapes belong to tb_matmul_quant), the same
+ *    dtype as packed (it decides how X is treated: TB_Q4_0 quantizes X rows
+ *    to Q8_0 first).  Results are identical to tb_matmul_quant on the same
+ *    arguments. */
+tb_status tb_packed_quant_weights_bytes(int dtype, int64_t N, int64_t K, size_t *bytes);
+tb_status tb_pack_quant_weights(int dtype, const void *w_dev, int64_t N, int64_t K, void *packed_dev,
+                                size_t packed_bytes, tb_stream stream);
+tb_status tb_matmul_quant_packed(int dtype, const float *x_dev, int64_t M, int64_t K,
+                                 const void *packed_dev, int64_t N, float *y_dev, tb_stream stream);
 
 /* Batched strided fp32 matmul, out = a @ b over matching leading (batch) dims,
  * `out` contiguous [batch..., M, N]: Tensor::matmul fp32 branch

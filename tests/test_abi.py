@@ -3,6 +3,7 @@ include/*.h declares (no compute calls: this suite runs on CPU)."""
 import glob
 import os
 import re
+import ctypes
 import subprocess
 
 import pytest
@@ -67,3 +68,18 @@ def test_host_library_exports_model_interface():
     out = subprocess.run(["nm", "-D", "--defined-only", host], capture_output=True, text=True).stdout
     for sym in ("tbm_model_load", "tbm_model_generate", "tbm_model_free", "tbm_last_error"):
         assert sym in out
+
+
+def test_packed_weight_size_needs_no_device():
+    """The packed-weight size is host arithmetic: both fp16 planes of every
+    128-row tile (4 bytes per weight), then one scale per row and 256 K, each
+    part rounded up to 1 KiB."""
+    n = ctypes.c_size_t(0)
+    T.call("tb_packed_quant_weights_bytes", T.Q4_0, 300, 512, ctypes.byref(n))
+    assert n.value == 384 * 512 * 4 + 3072
+    T.call("tb_packed_quant_weights_bytes", T.Q8_0, 128, 256, ctypes.byref(n))
+    assert n.value == 128 * 256 * 4 + 1024
+    for dt, N, K in [(T.Q4_0, 300, 480), (T.Q4_0, 0, 512), (T.F32, 128, 256), (T.Q8_0, 128, 0)]:
+        with pytest.raises(T.TbError) as e:
+            T.call("tb_packed_quant_weights_bytes", dt, N, K, ctypes.byref(n))
+        assert e.value.status == T.EINVAL

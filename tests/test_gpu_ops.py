@@ -276,6 +276,47 @@ def test_matmul_q4_0_tensor_cores_within_tolerance(M, K, N):
         assert (np.abs(got - ref) / scale).max() <= F32_REL
 
 
+# packed weights: the same kernel as tb_matmul_quant, W converted once.  The
+# shapes reach both token tiles (128, 256) and K split over clusters of 2-8.
+@pytest.mark.parametrize("dtype,M,K,N", [("q8", 512, 2048, 1000), ("q4", 300, 8192, 640), ("q4", 33, 4096, 2049),
+                                         ("q8", 64, 2048, 1000), ("q4", 200, 8192, 256)])
+def test_matmul_quant_packed_matches_unpacked(dtype, M, K, N):
+    dt = T.Q8_0 if dtype == "q8" else T.Q4_0
+    w = synth.normal((N, K), 0.02, seed=K + 3 * N)
+    wq = synth.quantize_q8_0(w) if dtype == "q8" else synth.quantize_q4_0(w)
+    x = synth.normal((M, K), 1.0, seed=M + 7)
+    want = run_matmul(dt, x, wq, N, "tb_matmul_quant")
+    nbytes = ctypes.c_size_t(0)
+    T.call("tb_packed_quant_weights_bytes", dt, N, K, ctypes.byref(nbytes))
+    packed = torch.empty(nbytes.value, dtype=torch.uint8, device="cuda")
+    T.call("tb_pack_quant_weights", dt, T.ptr(dev(wq)), N, K, T.ptr(packed), nbytes.value, S())
+    xd = dev(x)
+    for _ in range(2):  # the packed copy is reusable
+        y = torch.full((M, N), float("nan"), dtype=torch.float32, device="cuda")
+        T.call("tb_matmul_quant_packed", dt, T.ptr(xd), M, K, T.ptr(packed), N, T.ptr(y), S())
+        assert_bits(host(y), want)
+
+
+def test_matmul_quant_packed_rejects_bad_arguments():
+    K, N = 512, 130
+    wq = synth.quantize_q8_0(synth.normal((N, K), 0.02, seed=5))
+    nbytes = ctypes.c_size_t(0)
+    T.call("tb_packed_quant_weights_bytes", T.Q8_0, N, K, ctypes.byref(nbytes))
+    packed = torch.empty(nbytes.value, dtype=torch.uint8, device="cuda")
+    with pytest.raises(T.TbError) as e:  # too small a buffer
+        T.call("tb_pack_quant_weights", T.Q8_0, T.ptr(dev(wq)), N, K, T.ptr(packed), nbytes.value - 16, S())
+    assert e.value.status == T.EINVAL
+    T.call("tb_pack_quant_weights", T.Q8_0, T.ptr(dev(wq)), N, K, T.ptr(packed), nbytes.value, S())
+    x = dev(synth.normal((31, K), 1.0, seed=1))
+    y = torch.empty((31, N), dtype=torch.float32, device="cuda")
+    with pytest.raises(T.TbError) as e:  # M < 32 belongs to tb_matmul_quant
+        T.call("tb_matmul_quant_packed", T.Q8_0, T.ptr(x), 31, K, T.ptr(packed), N, T.ptr(y), S())
+    assert e.value.status == T.EINVAL
+    with pytest.raises(T.TbError) as e:  # K not a multiple of 256
+        T.call("tb_matmul_quant_packed", T.Q8_0, T.ptr(x), 32, 480, T.ptr(packed), N, T.ptr(y), S())
+    assert e.value.status == T.EINVAL
+
+
 def test_matmul_quant_rejects_bad_k():
     x = torch.zeros((1, 40), device="cuda")
     with pytest.raises(T.TbError) as e:

@@ -11,6 +11,9 @@
 //    GPU.
 //  - Quantized matmuls use the library's default GEMV/GEMM (within 1e-5 of the
 //    reference); set_exact_matmul(true) selects the bit-identical kernels.
+//  - A quantized weight multiplied by 32 or more rows keeps a packed copy for
+//    the tensor cores (tb_pack_quant_weights, 4 bytes per weight) beside its
+//    blocks, made on first use; set_weight_packing(false) turns this off.
 #pragma once
 #include <cstddef>
 #include <cstdint>
@@ -43,6 +46,10 @@ namespace turbo {
 // Selects the bit-identical quantized matmul kernels for every Tensor::matmul.
 void set_exact_matmul(bool exact);
 bool exact_matmul();
+// Lets quantized weights keep a packed copy for prefill-sized matmuls
+// (default on).  Turning it off frees nothing already packed.
+void set_weight_packing(bool on);
+bool weight_packing();
 // Blocks until every queued device op has finished.
 void device_synchronize();
 }  // namespace turbo
@@ -70,12 +77,23 @@ class Storage {
   // Device address for an op that overwrites the bytes (no write-back).
   void *device_data_discard() const;
 
+  // The bytes, as N rows of K quantized values of `dtype` (TB_Q8_0 or
+  // TB_Q4_0), packed for the tensor-core matmul: made on first use and kept
+  // until data() or device_data_discard() hands out the bytes for writing.
+  // A caller that writes the bytes through device_data() must call
+  // drop_packed() itself.
+  const void *packed_quant(int dtype, int64_t N, int64_t K) const;
+  void drop_packed() const;
+
  private:
   void *dev_ = nullptr;
   size_t size_bytes_ = 0;
   bool owns_memory_ = true;
   mutable std::vector<uint8_t> host_;
   mutable int state_ = 0;  // 0: device newer, 1: host newer, 2: both equal
+  mutable void *packed_ = nullptr;
+  mutable int packed_dtype_ = 0;
+  mutable int64_t packed_N_ = 0, packed_K_ = 0;
 };
 
 class Tensor {

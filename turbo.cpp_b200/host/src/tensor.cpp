@@ -13,9 +13,12 @@
 namespace turbo {
 namespace {
 bool g_exact = false;
+bool g_packing = true;
 }
 void set_exact_matmul(bool exact) { g_exact = exact; }
 bool exact_matmul() { return g_exact; }
+void set_weight_packing(bool on) { g_packing = on; }
+bool weight_packing() { return g_packing; }
 void device_synchronize() { detail::tb_check(tb_sync(nullptr)); }
 }  // namespace turbo
 
@@ -52,10 +55,36 @@ Storage::Storage(void *external_ptr, size_t size_bytes) : size_bytes_(size_bytes
 Storage::~Storage() {
   // All host-layer ops run on the default stream, so a later kernel that gets
   // this block from the arena is ordered after every kernel that used it.
+  drop_packed();
   if (dev_) tb_free(dev_);
 }
 
+void Storage::drop_packed() const {
+  if (packed_) tb_free(packed_);
+  packed_ = nullptr;
+}
+
+const void *Storage::packed_quant(int dtype, int64_t N, int64_t K) const {
+  if (packed_ && packed_dtype_ == dtype && packed_N_ == N && packed_K_ == K) return packed_;
+  drop_packed();
+  size_t bytes = 0;
+  tb_check(tb_packed_quant_weights_bytes(dtype, N, K, &bytes));
+  void *p = nullptr;
+  tb_check(tb_alloc(&p, bytes));
+  const tb_status rs = tb_pack_quant_weights(dtype, device_data(), N, K, p, bytes, nullptr);
+  if (rs != TB_OK) {
+    tb_free(p);
+    tb_check(rs);
+  }
+  packed_ = p;
+  packed_dtype_ = dtype;
+  packed_N_ = N;
+  packed_K_ = K;
+  return packed_;
+}
+
 uint8_t *Storage::data() const {
+  drop_packed();  // the caller may write through the pointer
   if (size_bytes_ == 0) return nullptr;
   if (state_ == 0) {
     host_.resize(size_bytes_);
@@ -77,6 +106,7 @@ void *Storage::device_data() const {
 }
 
 void *Storage::device_data_discard() const {
+  drop_packed();
   state_ = 0;
   return dev_;
 }
@@ -314,10 +344,16 @@ Tensor Tensor::matmul(const Tensor &other) const {
     const float *x = static_cast<const float *>(device_ptr());
     const void *w = other.storage->device_data();
     float *y = static_cast<float *>(out.storage->device_data_discard());
-    if (turbo::exact_matmul())
+    if (turbo::exact_matmul()) {
       tb_check(tb_matmul_quant_exact(dt, x, (int64_t)M, (int64_t)K, w, (int64_t)N, y, nullptr));
-    else
+    } else if (turbo::weight_packing() && M >= 32 && K >= 256 && K % 256 == 0 && K <= (1u << 20) &&
+               (reinterpret_cast<uintptr_t>(x) & 15) == 0 && (reinterpret_cast<uintptr_t>(w) & 15) == 0) {
+      // prefill: the tensor cores with W packed once (identical results)
+      const void *pk = other.storage->packed_quant(dt, (int64_t)N, (int64_t)K);
+      tb_check(tb_matmul_quant_packed(dt, x, (int64_t)M, (int64_t)K, pk, (int64_t)N, y, nullptr));
+    } else {
       tb_check(tb_matmul_quant(dt, x, (int64_t)M, (int64_t)K, w, (int64_t)N, y, nullptr));
+    }
     return out;
   }
   if (rank() != other.rank()) throw std::invalid_argument("matmul requires both tensors to have the same rank");

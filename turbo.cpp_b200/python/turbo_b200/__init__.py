@@ -73,6 +73,9 @@ SIGNATURES = {
     "tb_matmul_quant": [_I, _P, _I64, _I64, _P, _I64, _P, _P],
     "tb_matmul_quant_exact": [_I, _P, _I64, _I64, _P, _I64, _P, _P],
     "tb_matmul_q4_0_static_scratch": [_P, _I64, _I64, _P, _I64, _P, _P],
+    "tb_packed_quant_weights_bytes": [_I, _I64, _I64, _P],
+    "tb_pack_quant_weights": [_I, _P, _I64, _I64, _P, _SZ, _P],
+    "tb_matmul_quant_packed": [_I, _P, _I64, _I64, _P, _I64, _P, _P],
     "tb_matmul_f32": [_VP, _VP, _VP, _P],
     "tb_softmax_shard_stats": [_P, _I64, _I64, _I64, _P, _P, _P],
     "tb_softmax_shard_rescale": [_P, _P, _P, _I64, _P],

@@ -52,6 +52,7 @@ constexpr int kCB = 8;                      // blocks per chunk (one accumulator
 constexpr int kEpiWarps = 8;
 constexpr int kF16Threads = (2 + kEpiWarps) * 32;
 constexpr int kStageRoom = 192 * 1024;      // shared memory of the operand ring
+constexpr int kPF = 12;                     // L2 prefetch distance, blocks
 
 __host__ __device__ constexpr int op_off(int r, int c) { return (r >> 3) * 512 + c * 128 + (r & 7) * 16; }
 
@@ -223,6 +224,7 @@ __global__ void __launch_bounds__(256) pack_w_kernel(const uint8_t *__restrict__
 template <bool Q4, int TN>
 __global__ void __launch_bounds__(256) pack_x_kernel(const float *__restrict__ x, int M, int M_pad, int K,
                                                      uint8_t *__restrict__ Bp, float *__restrict__ sX) {
+  pdl_launch_dependents();  // the tensor-core kernel may set up meanwhile
   const int nb = K / 32, nc = nb / kCB, lane = threadIdx.x & 31;
   const int t = lane >> 2, g = lane & 3;
   const int64_t total = (int64_t)(M_pad / 8) * nc;
@@ -304,6 +306,53 @@ struct F16Args {
   int cl;                // 1: the splits of a tile are one cluster and sum there into out = Y
 };
 
+// Y rows [z * 128 / NZ, (z + 1) * 128 / NZ) of the tile = the sum over the
+// cluster's NZ partial tiles ([128][TN + 4] in each CTA's shared memory), in
+// split order.  Items are (row, four tokens), consecutive threads on
+// consecutive rows; each thread loads 16 / NZ items from every CTA before it
+// adds, so the remote loads overlap.
+template <int NZ, int TN>
+__device__ __forceinline__ void cluster_sum(const cg::cluster_group &cluster, const float *pt, int z, const F16Args &a,
+                                            int rt, int tt) {
+  constexpr int ROWS = kRowsT / NZ, ITEMS = ROWS * (TN / 4), B = 16 / NZ;
+  for (int it0 = threadIdx.x; it0 < ITEMS; it0 += B * kF16Threads) {
+    float4 v[B][NZ];
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const int it = it0 + b * kF16Threads;
+      if (it < ITEMS) {
+        const int r = z * ROWS + it % ROWS, k = 4 * (it / ROWS);
+        const float *src = pt + r * (TN + 4) + k;
+#pragma unroll
+        for (int zz = 0; zz < NZ; ++zz) v[b][zz] = *reinterpret_cast<const float4 *>(cluster.map_shared_rank(src, zz));
+      }
+    }
+#pragma unroll
+    for (int b = 0; b < B; ++b) {
+      const int it = it0 + b * kF16Threads;
+      if (it < ITEMS) {
+        const int r = z * ROWS + it % ROWS, k = 4 * (it / ROWS);
+        const int n = rt * kRowsT + r, tok = tt * TN + k;
+        float4 acc = v[b][0];
+#pragma unroll
+        for (int zz = 1; zz < NZ; ++zz) {
+          acc.x = __fadd_rn(acc.x, v[b][zz].x);
+          acc.y = __fadd_rn(acc.y, v[b][zz].y);
+          acc.z = __fadd_rn(acc.z, v[b][zz].z);
+          acc.w = __fadd_rn(acc.w, v[b][zz].w);
+        }
+        if (n < a.N) {
+          float *o = a.out + (int64_t)tok * a.N + n;
+          if (tok < a.M) o[0] = acc.x;
+          if (tok + 1 < a.M) o[a.N] = acc.y;
+          if (tok + 2 < a.M) o[2 * (int64_t)a.N] = acc.z;
+          if (tok + 3 < a.M) o[3 * (int64_t)a.N] = acc.w;
+        }
+      }
+    }
+  }
+}
+
 template <int TN>
 __global__ void __launch_bounds__(kF16Threads, 1) gemm_f16_kernel(const F16Args a, uint32_t *__restrict__ err) {
   constexpr int NS = num_stages<TN>();
@@ -346,12 +395,21 @@ __global__ void __launch_bounds__(kF16Threads, 1) gemm_f16_kernel(const F16Args 
   __syncthreads();
   fence_after();
   const uint32_t tmem = tmem_base;
+  pdl_wait();  // the packed operands are written by the kernels before this one
 
   if (warp == 0) {
     // ---- producer: one block (both planes of weights and x) per stage ---------------
     if (lane == 0) {
+      // blocks kPF ahead of the ring go to L2 early, so the ring's copies find
+      // them there instead of waiting on HBM
+      auto prefetch = [&](int i) {
+        prefetch_l2(a.Ap + ((int64_t)rt * a.nb + b0 + i) * 2 * kOpTile, 2 * kOpTile);
+        prefetch_l2(a.Bp + ((int64_t)tt * a.nb + b0 + i) * 2 * x_tile<TN>(), 2 * x_tile<TN>());
+      };
+      for (int i = NS; i < kPF && i < nblk; ++i) prefetch(i);
       for (int i = 0; i < nblk; ++i) {
         const int s = i % NS, b = b0 + i;
+        if (i + kPF < nblk) prefetch(i + kPF);
         if (i >= NS && !mbar_wait_bounded(&empty[s], (uint32_t)(((i / NS) + 1) & 1), err)) {
           abort_flag = 1;
           break;
@@ -462,36 +520,11 @@ __global__ void __launch_bounds__(kF16Threads, 1) gemm_f16_kernel(const F16Args 
     // bounded), so the cluster barriers complete
     cg::cluster_group cluster = cg::this_cluster();
     const int nz = (int)cluster.num_blocks(), z = (int)cluster.block_rank();
-    const int rows = kRowsT / nz;  // this CTA's share of the tile's rows
     cluster.sync();
     const float *pt = reinterpret_cast<const float *>(base);
-    // items: (row, four tokens); consecutive threads take consecutive rows, so
-    // each store instruction writes consecutive elements of a Y row
-    for (int it = threadIdx.x; it < rows * (TN / 4); it += kF16Threads) {
-      const int r = z * rows + it % rows, k = 4 * (it / rows);
-      const int n = rt * kRowsT + r, tok = tt * TN + k;
-      const float *src = pt + r * (TN + 4) + k;
-      float4 v[8];
-#pragma unroll
-      for (int zz = 0; zz < 8; ++zz)  // all loads first, then the sum in split order
-        if (zz < nz) v[zz] = *reinterpret_cast<const float4 *>(cluster.map_shared_rank(src, zz));
-      float4 acc = v[0];
-#pragma unroll
-      for (int zz = 1; zz < 8; ++zz)
-        if (zz < nz) {
-          acc.x = __fadd_rn(acc.x, v[zz].x);
-          acc.y = __fadd_rn(acc.y, v[zz].y);
-          acc.z = __fadd_rn(acc.z, v[zz].z);
-          acc.w = __fadd_rn(acc.w, v[zz].w);
-        }
-      if (n < a.N) {
-        float *o = a.out + (int64_t)tok * a.N + n;
-        if (tok < a.M) o[0] = acc.x;
-        if (tok + 1 < a.M) o[a.N] = acc.y;
-        if (tok + 2 < a.M) o[2 * (int64_t)a.N] = acc.z;
-        if (tok + 3 < a.M) o[3 * (int64_t)a.N] = acc.w;
-      }
-    }
+    if (nz == 2) cluster_sum<2, TN>(cluster, pt, z, a, rt, tt);
+    else if (nz == 4) cluster_sum<4, TN>(cluster, pt, z, a, rt, tt);
+    else if (nz == 8) cluster_sum<8, TN>(cluster, pt, z, a, rt, tt);
     cluster.sync();  // the peers' shared memory stays alive until every CTA has read it
   }
 }
@@ -624,13 +657,15 @@ tb_status run_gemm_f16(bool q4, const float *x, int64_t M, int64_t K, const uint
       cfg.blockDim = dim3(kF16Threads, 1, 1);
       cfg.dynamicSmemBytes = f16_smem<TN>();
       cfg.stream = s;
-      cudaLaunchAttribute attr[1];
+      cudaLaunchAttribute attr[2];
       attr[0].id = cudaLaunchAttributeClusterDimension;
       attr[0].val.clusterDim.x = 1;
       attr[0].val.clusterDim.y = 1;
       attr[0].val.clusterDim.z = cl ? (unsigned)splits : 1u;
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[1].val.programmaticStreamSerializationAllowed = 1;
       cfg.attrs = attr;
-      cfg.numAttrs = 1;
+      cfg.numAttrs = 2;
       e = cudaLaunchKernelEx(&cfg, gemm_f16_kernel<TN>, a, st->err_word);
       if (e != cudaSuccess) rs = fail(TB_ECUDA, "tb_matmul_quant (tensor cores): %s", cudaGetErrorString(e));
     }

@@ -255,8 +255,27 @@ def _cases(T, torch):
         wb = N * K // 32 * (34 if dt == T.Q8_0 else 18)
         cases.append(Case(tag, cfg, make, wb + M * K * 4 + M * N * 4, flops=2 * M * N * K))
 
+    def packed_case(dt, M, K, N, tag, cfg):
+        # W packed once outside the timed region (tb_pack_quant_weights), as
+        # the host layer keeps it for a model's prefill
+        def make():
+            W = qblocks(N * K // 32, 34 if dt == T.Q8_0 else 18, 17)
+            X = f32((M, K), 18)
+            Y = torch.empty((M, N), device=dev)
+            nbytes = ctypes.c_size_t(0)
+            T.call("tb_packed_quant_weights_bytes", dt, N, K, ctypes.byref(nbytes))
+            P = torch.empty(nbytes.value, dtype=torch.uint8, device=dev)
+            T.call("tb_pack_quant_weights", dt, T.ptr(W), N, K, T.ptr(P), nbytes.value, None)
+            torch.cuda.synchronize()
+            return (lambda i, s: T.load().tb_matmul_quant_packed(dt, T.ptr(X), M, K, T.ptr(P), N, T.ptr(Y), s)), (
+                W, X, Y, P)
+        wb = N * K // 32 * (34 if dt == T.Q8_0 else 18)
+        cases.append(Case(tag, cfg, make, wb + M * K * 4 + M * N * 4, flops=2 * M * N * K))
+
     gemm_case(T.Q4_0, 512, 8192, 2048, "gemm_q4_0_512x8192x2048", "prefill: Q4_0 down GEMM")
     gemm_case(T.Q8_0, 512, 2048, 8192, "gemm_q8_0_512x2048x8192", "prefill: Q8_0 gate/up GEMM")
+    packed_case(T.Q4_0, 512, 8192, 2048, "gemm_packed_q4_0_512x8192x2048", "prefill: Q4_0 down GEMM, W packed once")
+    packed_case(T.Q8_0, 512, 2048, 8192, "gemm_packed_q8_0_512x2048x8192", "prefill: Q8_0 gate/up GEMM, W packed once")
     return cases
 
 

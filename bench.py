@@ -551,7 +551,7 @@ def run_sharded_suite(args):
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", local))
     try:
         from turbo_b200 import opbench
-        opbench.run_sharded()
+        opbench.run_sharded(only=args.only.split(",") if args.only else None)
     finally:
         dist.barrier()
         dist.destroy_process_group()
@@ -573,7 +573,8 @@ def main():
                     help="ops: per-op throughput of every hot-path kernel (one JSON line per op); "
                          "decode: the 1B-shaped greedy decode in tokens/sec")
     ap.add_argument("--reps", type=int, default=3, help="with --suite decode: timed generate calls")
-    ap.add_argument("--only", default="", help="with --suite ops: comma-separated op name filters")
+    ap.add_argument("--only", default="", help="with --suite ops: comma-separated op name filters; with --suite "
+                    "sharded: sections (sweep, tp, peer, lm_head, vocab)")
     args = ap.parse_args()
     if args.suite == "ops":
         return run_ops_suite(args)

@@ -333,6 +333,15 @@ tb_status tb_shard_group_create(int n_ranks, int rank, const void *id, int64_t m
 tb_status tb_shard_group_wait(tb_shard_group group, tb_stream stream, double timeout_s);
 tb_status tb_shard_group_abort(tb_shard_group group);
 tb_status tb_shard_group_destroy(tb_shard_group group);
+/* Lets the group's ranks store into one another's memory over NVLink (no
+ * counterpart in the reference): every rank allocates an exchange buffer for
+ * up to max_elems floats (twice, plus 256 bytes of flags) and maps the other
+ * ranks' buffers through CUDA IPC handles, exchanged with one all-gather.
+ * Collective (every rank calls it); needs one process per GPU and peer access
+ * between the GPUs, else an error and the group keeps using NCCL.  A group of
+ * one rank needs nothing (TB_OK).  Afterwards tb_gemv_q8_0_row_sharded with
+ * n_ranks * n_local <= max_elems exchanges through these buffers. */
+tb_status tb_shard_group_enable_peer(tb_shard_group group, int64_t max_elems);
 /* Softmax over rows split by columns: this rank holds x[rows, cols] (row
  * stride ld), its slice of the full rows; y (row stride ld_y) gets the same
  * slice of the full rows' softmax.  One all-gather of each rank's per-row
@@ -347,7 +356,17 @@ tb_status tb_argmax_vocab_sharded(tb_shard_group group, const float *x_dev, int6
 /* Tensor-parallel Q8_0 GEMV (Tensor::matmul, src/tensor/tensor.cpp:328-382,
  * rows split): this rank holds rows [rank n_local, (rank + 1) n_local) of W
  * (their Q8_0 blocks) and the full x[K]; y_dev[n_ranks * n_local] gets the
- * full product on every rank (the rank's rows, then one in-place all-gather). */
+ * full product on every rank.  Every rank passes the same n_local.  With NCCL:
+ * the rank's rows, then one in-place all-gather.  After
+ * tb_shard_group_enable_peer (and n_ranks * n_local within its max_elems):
+ * the GEMV kernel also writes its rows into this GPU's exchange buffer; then a
+ * kernel on each rank publishes the call's number to the other ranks, waits
+ * for theirs (bounded by tb_set_wait_limit_ns: on expiry bit 0 of the device
+ * error word is set and y keeps the old values of those rows) and reads their
+ * rows from their exchange buffers over NVLink into y.  No host work per call,
+ * so the calls can be captured in a CUDA graph.  Calls of one group go in
+ * order on one stream per rank.  W and x 16-byte aligned, K a multiple of 256
+ * on that path. */
 tb_status tb_gemv_q8_0_row_sharded(tb_shard_group group, const float *x_dev, int64_t K, const void *w_local_dev,
                                    int64_t n_local, float *y_dev, tb_stream stream);
 

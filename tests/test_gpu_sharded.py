@@ -158,6 +158,42 @@ def _abi_case(T, O, synth, group, rank, world, stream, rows=64, vocab=128256):
     assert T.take_device_errors() == 0
 
 
+def _q8_scale(wq, xh, N, K):
+    """sum_k |w_nk x_k| per row, in chunks of rows (the tolerance's scale)."""
+    from turbo_b200 import synth
+    out = np.empty(N)
+    rb = K // 32 * 34
+    flat = wq.reshape(-1)
+    for r0 in range(0, N, 8192):
+        r1 = min(N, r0 + 8192)
+        wd = synth.dequantize_q8_0(flat[r0 * rb:r1 * rb].reshape(r1 - r0, rb), K).astype(np.float64)
+        out[r0:r1] = np.abs(wd) @ np.abs(xh).astype(np.float64)
+    return out
+
+
+def _peer_case(T, O, synth, group, rank, world, stream):
+    """The row-split GEMV with the rows exchanged by NVLink peer stores
+    (tb_shard_group_enable_peer): the decode projections' shapes and the
+    vocabulary-sized LM head (tensor-core GEMV per shard), several calls so
+    that both exchange buffers are used, each against the oracle."""
+    T.call("tb_shard_group_enable_peer", group, 128256)
+    for i, (N, K) in enumerate([(8192, 2048), (2048, 8192), (8192, 2048), (128256, 2048), (2048, 8192)]):
+        wq = synth.quantize_q8_0(synth.normal((N, K), 0.02, seed=40 + i))
+        xh = synth.normal((K,), 1.0, seed=50 + i)
+        n_local = N // world
+        rb = K // 32 * 34
+        w_local = torch.from_numpy(wq.ravel()[rank * n_local * rb:(rank + 1) * n_local * rb].copy()).cuda()
+        xd = torch.from_numpy(xh).cuda()
+        yv = torch.full((N,), float("nan"), dtype=torch.float32, device="cuda")
+        T.call("tb_gemv_q8_0_row_sharded", group, T.ptr(xd), K, T.ptr(w_local), n_local, T.ptr(yv), stream)
+        T.call("tb_shard_group_wait", group, stream, 30.0)
+        assert T.take_device_errors() == 0, (rank, N, K)
+        ref = O.matmul_q8_0(xh.reshape(1, K), wq, N)[0].astype(np.float64)
+        got = yv.cpu().numpy()
+        assert not np.isnan(got).any(), (rank, N, K)
+        assert np.max(np.abs(got - ref) / _q8_scale(wq, xh, N, K)) <= 1e-5, (rank, N, K)
+
+
 def test_shard_group_abi_one_rank():
     import turbo_b200 as T
     from oracle import orbind as O
@@ -169,13 +205,14 @@ def test_shard_group_abi_one_rank():
     T.call("tb_shard_group_create", 1, 0, uid, 64, 30.0, ctypes.byref(g))
     try:
         _abi_case(T, O, synth, g, 0, 1, T.stream_handle())
+        T.call("tb_shard_group_enable_peer", g, 8192)  # a group of one: nothing to map
         with pytest.raises(T.TbError):  # rows above the group's bound
             T.call("tb_argmax_vocab_sharded", g, None, 65, 8, 8, 0, None, T.stream_handle())
     finally:
         T.call("tb_shard_group_destroy", g)
 
 
-def _abi_rank(rank, world, q_id, q_done):
+def _abi_rank(rank, world, q_id, q_done, q_sync):
     sys.path.insert(0, ROOT)
     sys.path.insert(0, os.path.join(ROOT, "turbo.cpp_b200", "python"))
     os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
@@ -195,6 +232,26 @@ def _abi_rank(rank, world, q_id, q_done):
     T.call("tb_shard_group_create", world, rank, uid, 64, 60.0, ctypes.byref(g))
     try:
         _abi_case(T, O, synth, g, rank, world, T.stream_handle())
+        _peer_case(T, O, synth, g, rank, world, T.stream_handle())
+        # a rank that skips a call: the others' waits give up (bounded) and
+        # report it in the device error word; nothing faults or hangs
+        if rank == 0:
+            K, n_local = 2048, 4096
+            w_local = torch.zeros(n_local * (K // 32) * 34, dtype=torch.uint8, device="cuda")
+            xd = torch.zeros(K, dtype=torch.float32, device="cuda")
+            yv = torch.zeros(world * n_local, dtype=torch.float32, device="cuda")
+            T.call("tb_set_wait_limit_ns", 50_000_000)
+            try:
+                T.call("tb_gemv_q8_0_row_sharded", g, T.ptr(xd), K, T.ptr(w_local), n_local, T.ptr(yv),
+                       T.stream_handle())
+                T.call("tb_shard_group_wait", g, T.stream_handle(), 30.0)
+            finally:
+                T.call("tb_set_wait_limit_ns", 2_000_000_000)
+            assert T.take_device_errors() & 1
+            for _ in range(world - 1):
+                q_sync.put("done")
+        else:
+            q_sync.get(timeout=120)  # rank 0's stores into this rank's buffer have landed
     finally:
         T.call("tb_shard_group_destroy", g)
     q_done.put(rank)
@@ -203,8 +260,8 @@ def _abi_rank(rank, world, q_id, q_done):
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2, reason="needs two GPUs")
 def test_shard_group_abi_two_gpus():
     ctx = mp.get_context("spawn")
-    q_id, q_done = ctx.Queue(), ctx.Queue()
-    procs = [ctx.Process(target=_abi_rank, args=(r, 2, q_id, q_done)) for r in range(2)]
+    q_id, q_done, q_sync = ctx.Queue(), ctx.Queue(), ctx.Queue()
+    procs = [ctx.Process(target=_abi_rank, args=(r, 2, q_id, q_done, q_sync)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

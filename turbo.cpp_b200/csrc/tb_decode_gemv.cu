@@ -34,6 +34,7 @@ struct FusedArgs {
   float eps;
   int K;
   int slots;  // span buffers per CTA (kStreamMaxSlots at most)
+  PeerOut peer;  // single segment, no residual: a second copy of the outputs (peer.dst)
 };
 
 // Streaming Q8_0 GEMV (M = 1), default tolerance.  Each CTA owns a contiguous
@@ -100,6 +101,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 4) gemv_stream_kernel(const
       }
     }
   };
+  int64_t pbuf = 0;  // the exchange buffer of this call (set after griddepcontrol.wait)
   // logical row r's output: y[r] of its segment, plus the segment's residual
   auto store = [&](int r, float v) {
     int i = r;
@@ -115,7 +117,9 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 4) gemv_stream_kernel(const
         res = a.res[2];
       }
     }
-    y[i] = res ? __fadd_rn(res[i], v) : v;
+    const float o = res ? __fadd_rn(res[i], v) : v;
+    y[i] = o;
+    peer_store(a.peer, pbuf, i, o);
   };
   if (threadIdx.x == 0) {
     for (int i = 0; i < slots; ++i) {
@@ -130,6 +134,7 @@ __global__ void __launch_bounds__(kStreamWarps * 32, 4) gemv_stream_kernel(const
   pdl_launch_dependents();
   if (SWIGLU) exp_cr_table_init(tab);  // visible after the barrier below
   pdl_wait();  // x and the residuals come from the previous kernel
+  pbuf = peer_buffer(a.peer);
 
   // x (RMS-normalised as tb_rmsnorm does when gamma is given) -> smem, transposed
   const float4 *x4 = reinterpret_cast<const float4 *>(a.x);
@@ -319,9 +324,10 @@ bool stream_gemv_fits(int64_t K, const DeviceState *st) {
 // tb_matmul_quant(Q8_0), M = 1, default tolerance: one weight matrix, no norm,
 // no residual.  Operands as check_gemv_input requires (the caller checks).
 tb_status launch_stream_gemv(const float *x, int64_t K, const void *w, int64_t N, float *y, cudaStream_t s,
-                             const DeviceState *st) {
+                             const DeviceState *st, const PeerOut *peer) {
   if (N <= 0 || N > 0x7FFFFFFF) return fail(TB_EINVAL, "tb_matmul_quant: N=%lld out of range", (long long)N);
   FusedArgs a = {};
+  if (peer) a.peer = *peer;
   a.w[0] = static_cast<const uint8_t *>(w);
   a.y[0] = y;
   a.n[0] = (int)N;

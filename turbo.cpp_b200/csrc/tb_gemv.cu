@@ -523,11 +523,20 @@ size_t q4_smem_bytes(int K, int rows) {
 // pipelined GEMV (exact or fast arithmetic); everything else the one-shot
 // kernel, which always follows the reference's order.
 bool gemv_tc_eligible(int64_t K, int64_t N, const void *w, const float *x);
-tb_status launch_stream_gemv(const float *x, int64_t K, const void *w, int64_t N, float *y, cudaStream_t s,
-                             const DeviceState *st);
 bool stream_gemv_fits(int64_t K, const DeviceState *st);
-tb_status launch_gemv_tc(const float *x, int64_t K, const void *w, int64_t N, float *y, cudaStream_t s,
-                         const DeviceState *st);
+
+// The default M = 1 GEMV with a second copy of its outputs (PeerOut): the
+// tensor-core GEMV for vocabulary-sized N, else the streaming GEMV.  TB_EINVAL
+// when neither takes the operands.
+tb_status launch_q8_0_gemv_peer(const float *x, int64_t K, const void *w, int64_t N, float *y, const PeerOut &peer,
+                                cudaStream_t s, const DeviceState *st) {
+  const int64_t rbytes = K / 32 * 34;
+  if ((reinterpret_cast<uintptr_t>(w) & 15) != 0 || rbytes % 16 != 0 || (reinterpret_cast<uintptr_t>(x) & 15) != 0)
+    return fail(TB_EINVAL, "row-sharded GEMV: W and x must be 16-byte aligned and K a multiple of 256");
+  if (gemv_tc_eligible(K, N, w, x)) return launch_gemv_tc(x, K, w, N, y, s, st, &peer);
+  if (stream_gemv_fits(K, st)) return launch_stream_gemv(x, K, w, N, y, s, st, &peer);
+  return fail(TB_EINVAL, "row-sharded GEMV: K=%lld too large", (long long)K);
+}
 
 tb_status launch_q8_0(const float *x, int64_t M, int64_t K, const void *w, int64_t N, float *y,
                       bool exact, cudaStream_t s, const DeviceState *st) {

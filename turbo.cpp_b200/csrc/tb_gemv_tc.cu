@@ -105,6 +105,7 @@ struct GemvTcArgs {
   int tile_rows;     // TMA box rows (<= 128)
   int raw_stages;
   int raw_stride;    // bytes per raw stage: tile_rows * 272 rounded up to 128
+  PeerOut peer;      // a second copy of the outputs (peer.dst)
 };
 
 // Shared memory (dynamic, from a 1 KiB-aligned base):
@@ -175,6 +176,7 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tc_kernel(const __grid_const
     for (int i = 0; i < RS && i < total; ++i) produce(i);
   pdl_launch_dependents();
   pdl_wait();  // x comes from the previous kernel
+  const int64_t pbuf = peer_buffer(a.peer);
 
   // ---- x -> three int8 digits per element in the B tiles (warps 0-7) ----------
   if (warp < 8) {
@@ -327,7 +329,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_tc_kernel(const __grid_const
       if (lane == 0) mbar_arrive(&stage_free[as]);
       if (kc == nchunks - 1) {
         const int row = t * TR + j;
-        if (j < TR && row < cnt) a.y[n0 + row] = acc;
+        if (j < TR && row < cnt) {
+          a.y[n0 + row] = acc;
+          peer_store(a.peer, pbuf, n0 + row, acc);
+        }
         acc = 0.f;
       }
     }
@@ -369,7 +374,7 @@ bool gemv_tc_eligible(int64_t K, int64_t N, const void *w, const float *x) {
 }
 
 tb_status launch_gemv_tc(const float *x, int64_t K, const void *w, int64_t N, float *y, cudaStream_t s,
-                         const DeviceState *st) {
+                         const DeviceState *st, const PeerOut *peer) {
   const int nb = (int)(K / 32);
   const int rb = nb * 34;
   const int G0 = st->sm_count;
@@ -402,6 +407,7 @@ tb_status launch_gemv_tc(const float *x, int64_t K, const void *w, int64_t N, fl
   a.tile_rows = TR;
   a.raw_stages = RS;
   a.raw_stride = (int)per_raw;
+  a.peer = peer ? *peer : PeerOut{};
   TB_TRY(ensure_smem_for(gemv_tc_kernel, smem));
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)grid, 1, 1);

@@ -283,4 +283,43 @@ __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
 
+// ---- a second copy of a GEMV's outputs, for other GPUs to read (NVLink) ---------
+
+// The GEMV also stores y[i] at dst[(e & 1) * par_stride + i], where the call
+// number e = *ctr + 1 (ctr: this rank's count of finished exchanges, advanced
+// by the kernel that follows; read after griddepcontrol.wait).  dst is this
+// GPU's exchange buffer 0 at this rank's rows; other GPUs read it once that
+// kernel has published e.  Plain local stores: the launch boundary makes them
+// visible.
+struct PeerOut {
+  float *dst;  // null: no second copy
+  const unsigned long long *ctr;
+  int64_t par_stride;  // floats between the two buffers
+};
+
+// The offset of this call's buffer: read once per thread, after
+// griddepcontrol.wait, and passed to peer_store.
+__device__ __forceinline__ int64_t peer_buffer(const PeerOut &p) {
+  return p.dst ? (int64_t)((*reinterpret_cast<const volatile unsigned long long *>(p.ctr) + 1) & 1) * p.par_stride
+               : 0;
+}
+
+__device__ __forceinline__ void peer_store(const PeerOut &p, int64_t buf, int64_t i, float v) {
+  if (p.dst) p.dst[buf + i] = v;
+}
+
+// Q8_0 GEMV launchers (M = 1); `peer` adds the peer stores.
+tb_status launch_stream_gemv(const float *x, int64_t K, const void *w, int64_t N, float *y, cudaStream_t s,
+                             const DeviceState *st, const PeerOut *peer = nullptr);
+tb_status launch_gemv_tc(const float *x, int64_t K, const void *w, int64_t N, float *y, cudaStream_t s,
+                         const DeviceState *st, const PeerOut *peer = nullptr);
+tb_status launch_q8_0_gemv_peer(const float *x, int64_t K, const void *w, int64_t N, float *y, const PeerOut &peer,
+                                cudaStream_t s, const DeviceState *st);
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+
 }  // namespace tb

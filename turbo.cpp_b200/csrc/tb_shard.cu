@@ -11,7 +11,11 @@
 //            then tb_softmax_shard_finish writes exp(x - M) / S;
 //   argmax   per-shard 64-bit keys (tb_argmax_shard_keys), one int64 MAX
 //            all-reduce, then tb_argmax_key_index;
-//   GEMV     the rank's rows into its slot of y, one in-place all-gather.
+//   GEMV     the rank's rows into its slot of y, one in-place all-gather; or,
+//            after tb_shard_group_enable_peer, the GEMV also writes its rows
+//            into this GPU's exchange buffer, and a small kernel on each rank
+//            publishes the call's number in the other ranks' flags, waits for
+//            theirs and reads their rows from their buffers over NVLink.
 // NCCL is loaded at run time (dlopen of libnccl.so.2, preferring a copy the
 // process already has loaded), so the library has no link-time dependency on
 // it.  The communicator is created non-blocking with a host-side time limit,
@@ -20,10 +24,12 @@
 #include <dlfcn.h>
 #include <nccl.h>
 
+#include <algorithm>
 #include <chrono>
 #include <cstring>
 #include <mutex>
 #include <thread>
+#include <vector>
 
 #include "tb_internal.cuh"
 
@@ -89,6 +95,104 @@ __global__ void combine_stats_kernel(const float *__restrict__ g, int n, int row
   S[r] = s;
 }
 
+struct PeerRegions {
+  const uint8_t *r[8];  // rank j's exchange region (this rank's own at [rank])
+};
+
+// The row-sharded GEMV's exchange, launched right after the GEMV.
+// griddepcontrol.wait: the local GEMV has finished, so this rank's rows are in
+// its slot of y and of its exchange buffer e & 1 (e = *ctr + 1, the call
+// number).  Thread 0 of CTA 0 publishes e in every other rank's flag for this
+// rank (release, system scope: the rows are in this GPU's memory, where the
+// other GPUs read them); thread 0 of each CTA waits (bounded) until every
+// other rank has published e here, then the CTA reads those ranks' slots of
+// their buffer e & 1 over NVLink into y.  A rank does not start call e + 2's
+// GEMV (which rewrites buffer e & 1) before its exchange of call e + 1, which
+// waits for this rank's flag of e + 1, published only after this kernel has
+// finished.  The last CTA to finish (a ticket counter in this GPU's memory)
+// sets *ctr = e.
+__global__ void peer_gather_kernel(PeerRegions pr, int n, int rank, int64_t cap, int64_t n_local, float *y,
+                                   uint64_t wait_ns, uint32_t *err) {
+  pdl_launch_dependents();  // the next kernel may set up meanwhile; it waits for this one's end
+  pdl_wait();
+  unsigned long long *region = reinterpret_cast<unsigned long long *>(const_cast<uint8_t *>(pr.r[rank]));
+  const unsigned long long *flags = region;
+  unsigned long long *ctr = region + 9, *ticket = region + 10;
+  const unsigned long long e = *reinterpret_cast<volatile unsigned long long *>(ctr) + 1;
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    for (int j = 0; j < n; ++j)  // st.release orders the rows (visible here since griddepcontrol.wait) first
+      if (j != rank) {
+        unsigned long long *f = reinterpret_cast<unsigned long long *>(const_cast<uint8_t *>(pr.r[j])) + rank;
+        asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(f), "l"(e) : "memory");
+      }
+  }
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    const uint64_t t0 = globaltimer_ns();
+    for (int j = 0; j < n && ok; ++j) {
+      if (j == rank) continue;
+      for (uint32_t it = 1; ld_acquire_sys(flags + j) < e; ++it)
+        if ((it & 63u) == 0 && globaltimer_ns() - t0 > wait_ns) {
+          atomicOr(err, ERR_TIMEOUT);
+          ok = 0;
+          break;
+        }
+    }
+  }
+  __syncthreads();
+  if (ok) {
+    // remote reads cost a round trip over NVLink each: every thread issues
+    // four 16-byte loads before it stores any (n_local % 4 == 0, y 16-byte
+    // aligned and cap % 4 == 0; else one float at a time)
+    const int64_t buf = (int64_t)(e & 1) * cap;
+    const int64_t total = (int64_t)n * n_local, nth = (int64_t)gridDim.x * blockDim.x;
+    const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (n_local % 4 == 0 && (reinterpret_cast<uintptr_t>(y) & 15) == 0) {
+      const int64_t nv = total / 4;
+      for (int64_t v0 = tid; v0 < nv; v0 += 4 * nth) {
+        float4 r[4];
+        bool use[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int64_t v = v0 + u * nth;
+          const int j = v < nv ? (int)(4 * v / n_local) : rank;
+          use[u] = j != rank;
+          if (use[u]) {
+            const float *src = reinterpret_cast<const float *>(pr.r[j] + 256) + buf + 4 * v;
+            asm volatile("ld.relaxed.sys.global.v4.f32 {%0, %1, %2, %3}, [%4];"
+                         : "=f"(r[u].x), "=f"(r[u].y), "=f"(r[u].z), "=f"(r[u].w)
+                         : "l"(src)
+                         : "memory");
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (use[u]) reinterpret_cast<float4 *>(y)[v0 + u * nth] = r[u];
+      }
+    } else {
+      for (int64_t i = tid; i < total; i += nth) {
+        const int j = (int)(i / n_local);
+        if (j != rank) {
+          const float *src = reinterpret_cast<const float *>(pr.r[j] + 256) + buf + i;
+          float v;
+          asm volatile("ld.relaxed.sys.global.f32 %0, [%1];" : "=f"(v) : "l"(src) : "memory");
+          y[i] = v;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    if (atomicAdd(ticket, 1ull) + 1 == gridDim.x) {  // every CTA has read ctr
+      *ticket = 0;
+      __threadfence();
+      *ctr = e;
+    }
+  }
+}
+
 }  // namespace
 }  // namespace tb
 
@@ -101,6 +205,14 @@ struct tb_shard_group_s {
   float *gm = nullptr, *gs = nullptr;  // [max_rows] combined
   int64_t *keys = nullptr;  // [max_rows]
   double timeout_s = 30.0;
+  // peer exchange (tb_shard_group_enable_peer): this rank's region holds, as
+  // 64-bit words, the flags [0, 8) (per rank, the last call number it
+  // published), this rank's count of finished calls [9] and the exchange
+  // kernel's ticket counter [10]; from byte 256 two buffers of xcap floats
+  // (calls alternate between them).  peer[j] maps rank j's region.
+  uint8_t *xbase = nullptr;
+  uint8_t *peer[8] = {};
+  int64_t xcap = 0;
 };
 
 using namespace tb;
@@ -207,7 +319,69 @@ tb_status tb_shard_group_destroy(tb_shard_group g) {
     cudaSetDevice(dev);
   }
   if (g->stats) tb_free(g->stats);
+  if (g->xbase) {
+    int dev = -1;
+    cudaGetDevice(&dev);
+    cudaSetDevice(g->device);
+    cudaDeviceSynchronize();  // this rank's stores into the peers have landed
+    for (int j = 0; j < g->n; ++j)
+      if (g->peer[j]) cudaIpcCloseMemHandle(g->peer[j]);
+    cudaFree(g->xbase);
+    cudaSetDevice(dev);
+  }
   delete g;
+  return TB_OK;
+}
+
+tb_status tb_shard_group_enable_peer(tb_shard_group g, int64_t max_elems) {
+  TB_TRY(check_group(g, "tb_shard_group_enable_peer"));
+  if (max_elems < 1 || max_elems > (int64_t(1) << 28))
+    return fail(TB_EINVAL, "tb_shard_group_enable_peer: max_elems %lld out of range", (long long)max_elems);
+  if (g->n > 8) return fail(TB_EINVAL, "tb_shard_group_enable_peer: %d ranks (at most 8)", g->n);
+  if (g->xbase) return fail(TB_EINVAL, "tb_shard_group_enable_peer: already enabled");
+  if (g->n == 1) return TB_OK;  // nothing to exchange
+  NcclApi *api;
+  TB_TRY(nccl_api(&api));
+  const int64_t cap = (max_elems + 3) / 4 * 4;  // 16-byte aligned buffers
+  const size_t bytes = 256 + 2 * (size_t)cap * sizeof(float);
+  uint8_t *base = nullptr;
+  cudaError_t e = cudaMalloc(reinterpret_cast<void **>(&base), bytes);
+  if (e != cudaSuccess) return fail(TB_ENOMEM, "tb_shard_group_enable_peer: %s", cudaGetErrorString(e));
+  uint8_t *hb = nullptr;  // the ranks' IPC handles, gathered
+  tb_status rs = TB_OK;
+  uint8_t *opened[8] = {};
+  cudaIpcMemHandle_t h;
+  std::vector<uint8_t> all((size_t)g->n * sizeof(h));
+  e = cudaMemset(base, 0, bytes);
+  if (e == cudaSuccess) e = cudaIpcGetMemHandle(&h, base);
+  if (e != cudaSuccess) rs = fail(TB_ECUDA, "tb_shard_group_enable_peer: %s", cudaGetErrorString(e));
+  if (rs == TB_OK) rs = tb_alloc(reinterpret_cast<void **>(&hb), all.size());
+  if (rs == TB_OK) rs = tb_upload(hb + (size_t)g->rank * sizeof(h), &h, sizeof(h), nullptr);
+  if (rs == TB_OK) {
+    ncclResult_t r = api->AllGather(hb + (size_t)g->rank * sizeof(h), hb, sizeof(h), ncclUint8, g->comm, nullptr);
+    rs = nccl_settle(api, g->comm, r, g->timeout_s, "tb_shard_group_enable_peer(all-gather)");
+  }
+  if (rs == TB_OK) rs = tb_download(all.data(), hb, all.size(), nullptr);
+  if (rs == TB_OK) rs = tb_sync(nullptr);
+  for (int j = 0; j < g->n && rs == TB_OK; ++j) {
+    if (j == g->rank) continue;
+    cudaIpcMemHandle_t hj;
+    std::memcpy(&hj, all.data() + (size_t)j * sizeof(h), sizeof(h));
+    e = cudaIpcOpenMemHandle(reinterpret_cast<void **>(&opened[j]), hj, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess)
+      rs = fail(TB_ECUDA, "tb_shard_group_enable_peer: mapping rank %d's buffer: %s (one process per GPU, peer "
+                "access between the GPUs)", j, cudaGetErrorString(e));
+  }
+  if (hb) tb_free(hb);
+  if (rs != TB_OK) {
+    for (int j = 0; j < g->n; ++j)
+      if (opened[j]) cudaIpcCloseMemHandle(opened[j]);
+    cudaFree(base);
+    return rs;
+  }
+  g->xbase = base;
+  for (int j = 0; j < g->n; ++j) g->peer[j] = opened[j];
+  g->xcap = cap;
   return TB_OK;
 }
 
@@ -288,9 +462,35 @@ tb_status tb_gemv_q8_0_row_sharded(tb_shard_group g, const float *x_dev, int64_t
                                    int64_t n_local, float *y_dev, tb_stream stream) {
   TB_TRY(check_group(g, "tb_gemv_q8_0_row_sharded"));
   if (n_local <= 0 || K <= 0) return fail(TB_EINVAL, "tb_gemv_q8_0_row_sharded: bad extents");
+  float *slot = y_dev + (int64_t)g->rank * n_local;
+  if (g->n > 1 && g->xbase && (int64_t)g->n * n_local <= g->xcap) {
+    DeviceState *st;
+    TB_TRY(device_state(&st));
+    cudaStream_t s = as_stream(stream);
+    PeerOut po = {};
+    po.dst = reinterpret_cast<float *>(g->xbase + 256) + (int64_t)g->rank * n_local;
+    po.ctr = reinterpret_cast<const unsigned long long *>(g->xbase) + 9;
+    po.par_stride = g->xcap;
+    TB_TRY(launch_q8_0_gemv_peer(x_dev, K, w_local_dev, n_local, slot, po, s, st));
+    PeerRegions pr = {};
+    for (int j = 0; j < g->n; ++j) pr.r[j] = j == g->rank ? g->xbase : g->peer[j];
+    const int64_t total = (int64_t)g->n * n_local;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)std::min<int64_t>(64, std::max<int64_t>(1, total / 4096)), 1, 1);
+    cfg.blockDim = dim3(256, 1, 1);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cudaError_t e = cudaLaunchKernelEx(&cfg, peer_gather_kernel, pr, g->n, g->rank, (int64_t)g->xcap,
+                                       (int64_t)n_local, y_dev, (uint64_t)wait_limit_ns(), st->err_word);
+    if (e != cudaSuccess) return fail(TB_ECUDA, "tb_gemv_q8_0_row_sharded (exchange): %s", cudaGetErrorString(e));
+    return check_launch("tb_gemv_q8_0_row_sharded (exchange)");
+  }
   NcclApi *api;
   TB_TRY(nccl_api(&api));
-  float *slot = y_dev + (int64_t)g->rank * n_local;
   TB_TRY(tb_matmul_quant(TB_Q8_0, x_dev, 1, K, w_local_dev, n_local, slot, stream));
   if (g->n > 1) {
     ncclResult_t r = api->AllGather(slot, y_dev, (size_t)n_local, ncclFloat32, g->comm, as_stream(stream));

@@ -89,6 +89,7 @@ SIGNATURES = {
     "tb_shard_group_destroy": [_P],
     "tb_softmax_vocab_sharded": [_P, _P, _I64, _I64, _I64, _P, _I64, _P],
     "tb_argmax_vocab_sharded": [_P, _P, _I64, _I64, _I64, _I64, _P, _P],
+    "tb_shard_group_enable_peer": [_P, _I64],
     "tb_gemv_q8_0_row_sharded": [_P, _P, _I64, _P, _I64, _P, _P],
     "tb_decode_workspace_bytes": [_P, ctypes.POINTER(_SZ)],
     "tb_attention_prefill": [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _I64, _P],

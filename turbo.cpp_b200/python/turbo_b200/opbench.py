@@ -348,7 +348,7 @@ def _rand_q8(torch, rows, K, seed):
     return w.reshape(-1)
 
 
-def run_sharded(reps=20, sizes=None):
+def run_sharded(reps=20, sizes=None, only=None):
     """The sharded sweep on every rank of a torch.distributed job (one GPU per
     rank, NCCL).  Row-sharded ops (add, row-vector mul, RMSNorm, SwiGLU,
     contiguous() of a transposed slab) on [R, 4096] tensors of 1 MiB, 64 MiB,
@@ -357,12 +357,16 @@ def run_sharded(reps=20, sizes=None):
     [64, 128256] split over the ranks (two float all-reduces / one int64
     all-reduce per call).  Time per call = max over ranks of the CUDA-event
     time; GB/s = bytes moved by all ranks / that time.  Rank 0 prints one JSON
-    line per op and size."""
+    line per op and size.  `only`: section names to run (sweep, tp, peer,
+    lm_head, vocab)."""
     import torch
     import torch.distributed as dist
 
     import turbo_b200 as T
     from .sharded import VocabShardGroup, shard_range
+
+    def want(section):
+        return not only or section in only
 
     ws, rank = dist.get_world_size(), dist.get_rank()
     peak, kind = _peak()
@@ -395,7 +399,8 @@ def run_sharded(reps=20, sizes=None):
 
     C = 4096
     sizes = sizes or [1 << 20, 1 << 26, 1 << 30, 1 << 34]  # bytes per tensor, whole job
-    for tdt, code, es, tag in ((torch.float32, T.F32, 4, "f32"), (torch.bfloat16, T.BF16, 2, "bf16")):
+    for tdt, code, es, tag in (() if not want("sweep") else
+                               ((torch.float32, T.F32, 4, "f32"), (torch.bfloat16, T.BF16, 2, "bf16"))):
         for total in sizes:
             R_total = total // (C * es)
             _, R = shard_range(R_total, ws, rank)
@@ -430,7 +435,7 @@ def run_sharded(reps=20, sizes=None):
     # tensor-parallel Q8_0 GEMV (row split + all-gather of y) and the
     # vocab-split LM head feeding the sharded argmax (no gather)
     from .sharded import RowShardedGemv
-    for N, K in ((8192, 2048), (2048, 8192)):
+    for N, K in (((8192, 2048), (2048, 8192)) if want("tp") else ()):
         tp = RowShardedGemv(N, K)
         rb = K // 32 * 34
         w_local = _rand_q8(torch, tp.rows, K, seed=40 + rank)
@@ -440,28 +445,90 @@ def run_sharded(reps=20, sizes=None):
         report("tp_gemv_q8_0_%dx%d" % (N, K), ms, N * rb + K * 4 * ws + N * 4,
                "W[%d,%d] Q8_0 rows split over %d ranks, NCCL all-gather of y" % (N, K, ws))
         del w_local
-    V, K = 128256, 2048
-    grp = VocabShardGroup(V)
-    w_local = _rand_q8(torch, grp.cols, K, seed=50 + rank)
-    x = torch.randn(K, device=dev, generator=torch.Generator(dev).manual_seed(51))
-    logits = torch.empty((1, grp.cols), dtype=torch.float32, device=dev)
+    # the same GEMVs (and the LM head) through the C entry with the rows
+    # exchanged by NVLink peer stores (tb_shard_group_enable_peer), timed as
+    # replays of a CUDA graph of `n` calls: at one GPU the group of one is a
+    # plain tb_matmul_quant, so the two counts compare like for like
+    def timed_graph(fn_s, n):
+        s2 = torch.cuda.Stream()
+        s2.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s2):
+            fn_s(ctypes.c_void_p(s2.cuda_stream))
+        s2.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s2):
+            cs = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+            for _ in range(n):
+                fn_s(cs)
+        with torch.cuda.stream(s2):
+            g.replay()
+        s2.synchronize()
+        dist.barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s2):
+            a.record()
+            g.replay()
+            b.record()
+        s2.synchronize()
+        t = torch.tensor([a.elapsed_time(b) / n], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        del g
+        return float(t.item())
 
-    def lm_head_argmax():
-        T.check(L.tb_matmul_quant(T.Q8_0, T.ptr(x), 1, K, T.ptr(w_local), grp.cols, T.ptr(logits), sh),
-                "tb_matmul_quant")
-        return grp.argmax(logits)
-    ms = timed(lm_head_argmax, 100)
-    report("tp_lm_head_argmax_%dx%d" % (V, K), ms, V * (K // 32 * 34) + K * 4 * ws + V * 4,
-           "LM head W[%d,%d] Q8_0 vocab rows split over %d ranks -> sharded argmax" % (V, K, ws))
-    del w_local
-    torch.cuda.empty_cache()
+    uid = ctypes.create_string_buffer(128)
+    if rank == 0:
+        T.call("tb_shard_group_unique_id", uid)
+    obj = [uid.raw if want("peer") else None]
+    dist.broadcast_object_list(obj, src=0)
+    cgrp = ctypes.c_void_p()
+    if want("peer"):
+        uid = ctypes.create_string_buffer(obj[0], 128)
+        T.call("tb_shard_group_create", ws, rank, uid, 64, 60.0, ctypes.byref(cgrp))
+        T.call("tb_shard_group_enable_peer", cgrp, 128256)
+    for N, K in (((8192, 2048), (2048, 8192), (128256, 2048)) if want("peer") else ()):
+        n_local = N // ws
+        rb = K // 32 * 34
+        w_local = _rand_q8(torch, n_local, K, seed=60 + rank)
+        x = torch.randn(K, device=dev, generator=torch.Generator(dev).manual_seed(61))
+        y = torch.empty(N, dtype=torch.float32, device=dev)
 
-    V, rows = 128256, 64
-    grp = VocabShardGroup(V)
-    full = torch.randn((rows, V), device=dev, generator=torch.Generator(dev).manual_seed(7)) * 2.0
-    local = full[:, grp.col_base:grp.col_base + grp.cols].contiguous()
-    out = torch.empty_like(local)
-    ms = timed(lambda: grp.softmax(local, out), reps)
-    report("vocab_sharded_softmax", ms, 2 * 4 * rows * V, "logits [%d,%d] split over %d ranks, NCCL" % (rows, V, ws))
-    ms = timed(lambda: grp.argmax(local), reps)
-    report("vocab_sharded_argmax", ms, 4 * rows * V, "logits [%d,%d] split over %d ranks, NCCL" % (rows, V, ws))
+        def call(sh_):
+            T.check(L.tb_gemv_q8_0_row_sharded(cgrp, T.ptr(x), K, T.ptr(w_local), n_local, T.ptr(y), sh_),
+                    "tb_gemv_q8_0_row_sharded")
+        ms = timed_graph(call, 100)
+        report("tp_gemv_peer_q8_0_%dx%d" % (N, K), ms, N * rb + K * 4 * ws + N * 4,
+               "W[%d,%d] Q8_0 rows split over %d ranks, rows exchanged by NVLink peer stores, CUDA graph of "
+               "100 calls" % (N, K, ws))
+        del w_local
+    torch.cuda.synchronize()
+    dist.barrier()
+    if cgrp:
+        T.call("tb_shard_group_destroy", cgrp)
+
+    if want("lm_head"):
+        V, K = 128256, 2048
+        grp = VocabShardGroup(V)
+        w_local = _rand_q8(torch, grp.cols, K, seed=50 + rank)
+        x = torch.randn(K, device=dev, generator=torch.Generator(dev).manual_seed(51))
+        logits = torch.empty((1, grp.cols), dtype=torch.float32, device=dev)
+
+        def lm_head_argmax():
+            T.check(L.tb_matmul_quant(T.Q8_0, T.ptr(x), 1, K, T.ptr(w_local), grp.cols, T.ptr(logits), sh),
+                    "tb_matmul_quant")
+            return grp.argmax(logits)
+        ms = timed(lm_head_argmax, 100)
+        report("tp_lm_head_argmax_%dx%d" % (V, K), ms, V * (K // 32 * 34) + K * 4 * ws + V * 4,
+               "LM head W[%d,%d] Q8_0 vocab rows split over %d ranks -> sharded argmax" % (V, K, ws))
+        del w_local
+        torch.cuda.empty_cache()
+
+    if want("vocab"):
+        V, rows = 128256, 64
+        grp = VocabShardGroup(V)
+        full = torch.randn((rows, V), device=dev, generator=torch.Generator(dev).manual_seed(7)) * 2.0
+        local = full[:, grp.col_base:grp.col_base + grp.cols].contiguous()
+        out = torch.empty_like(local)
+        ms = timed(lambda: grp.softmax(local, out), reps)
+        report("vocab_sharded_softmax", ms, 2 * 4 * rows * V, "logits [%d,%d] split over %d ranks, NCCL" % (rows, V, ws))
+        ms = timed(lambda: grp.argmax(local), reps)
+        report("vocab_sharded_argmax", ms, 4 * rows * V, "logits [%d,%d] split over %d ranks, NCCL" % (rows, V, ws))

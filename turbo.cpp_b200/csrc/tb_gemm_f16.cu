@@ -52,7 +52,6 @@ constexpr int kCB = 8;                      // blocks per chunk (one accumulator
 constexpr int kEpiWarps = 8;
 constexpr int kF16Threads = (2 + kEpiWarps) * 32;
 constexpr int kStageRoom = 192 * 1024;      // shared memory of the operand ring
-constexpr int kPF = 12;                     // L2 prefetch distance, blocks
 
 __host__ __device__ constexpr int op_off(int r, int c) { return (r >> 3) * 512 + c * 128 + (r & 7) * 16; }
 
@@ -400,16 +399,8 @@ __global__ void __launch_bounds__(kF16Threads, 1) gemm_f16_kernel(const F16Args 
   if (warp == 0) {
     // ---- producer: one block (both planes of weights and x) per stage ---------------
     if (lane == 0) {
-      // blocks kPF ahead of the ring go to L2 early, so the ring's copies find
-      // them there instead of waiting on HBM
-      auto prefetch = [&](int i) {
-        prefetch_l2(a.Ap + ((int64_t)rt * a.nb + b0 + i) * 2 * kOpTile, 2 * kOpTile);
-        prefetch_l2(a.Bp + ((int64_t)tt * a.nb + b0 + i) * 2 * x_tile<TN>(), 2 * x_tile<TN>());
-      };
-      for (int i = NS; i < kPF && i < nblk; ++i) prefetch(i);
       for (int i = 0; i < nblk; ++i) {
         const int s = i % NS, b = b0 + i;
-        if (i + kPF < nblk) prefetch(i + kPF);
         if (i >= NS && !mbar_wait_bounded(&empty[s], (uint32_t)(((i / NS) + 1) & 1), err)) {
           abort_flag = 1;
           break;

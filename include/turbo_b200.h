@@ -493,11 +493,15 @@ tb_status tb_rope_kv_append(float *q_dev, float *k_dev, const float *v_dev, int6
 
 /* Asks L2 to fetch up to 8 device byte ranges (each trimmed inward to 16-byte
  * boundaries) in the background, for weights that a later kernel of the same
- * step will read: the copies overlap the kernels in between, which leave HBM
- * idle.  A hint: results never depend on it.  The launch completes only after
- * the preceding kernel of the stream has (programmatic dependent launch), so
- * it may sit anywhere in a dependent chain.  No reference counterpart (the
- * reference's weights are host memory). */
+ * step will read: the copies overlap the kernels in between.  A hint: results
+ * never depend on it.  The launch completes only after the preceding kernel of
+ * the stream has (programmatic dependent launch), so it may sit anywhere in a
+ * dependent chain.  Measured NEGATIVE where this library could use it: in the
+ * 1B-shaped decode step (each layer's O/gate/up/down and the next layer's
+ * Q/K/V prefetched at the layer's start) 1359 against 1396 tokens/s, since
+ * those GEMVs are latency-bound, not HBM-bound; the decode does not call it.
+ * Kept for callers whose kernels between two weight reads leave HBM idle.  No
+ * reference counterpart (the reference's weights are host memory). */
 tb_status tb_prefetch_l2(const void *const *ptrs_dev, const int64_t *bytes, int n, tb_stream stream);
 
 /* Streams and CUDA graphs for callers without the CUDA runtime: capture a
@@ -512,15 +516,6 @@ tb_status tb_graph_destroy(tb_graph graph);
 
 /* ---------------------------------------------------------------- diagnostics -- */
 
-/* Evaluates the fp32 exp functions of the SwiGLU and softmax kernels on every
- * fp32 bit pattern against exp in double precision rounded to float, on the
- * current device, synchronously.  counts[0]: inputs where the correctly-
- * rounding version (SwiGLU) differs; counts[1]: its largest distance in ulp;
- * counts[2]: inputs in [-87, 0] where the softmax kernels' exp (the __expf
- * intrinsic) exceeds its documented 2 + 1.173|x| ulp; counts[3]: its largest
- * distance over [-20, 0].  No reference counterpart: the reference calls glibc
- * expf. */
-tb_status tb_selfcheck_exp(uint64_t counts[4]);
 
 #if defined(__GNUC__)
 #pragma GCC visibility pop

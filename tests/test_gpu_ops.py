@@ -573,8 +573,13 @@ def test_softmax_special_values_match_reference(cols):
 
 
 def test_exp_selfcheck_every_float():
+    # a test-only library (turbo.cpp_b200/csrc/test), built beside the product one
+    lib = ctypes.CDLL(os.path.join(os.path.dirname(T.LIB_PATH), "libturbo_b200_selfcheck.so"))
+    lib.tb_selfcheck_exp.argtypes = [ctypes.c_void_p]
+    lib.tb_selfcheck_exp.restype = ctypes.c_int
+    torch.cuda.init()
     counts = (ctypes.c_uint64 * 4)()
-    T.call("tb_selfcheck_exp", ctypes.cast(counts, ctypes.c_void_p))
+    assert lib.tb_selfcheck_exp(ctypes.cast(counts, ctypes.c_void_p)) == 0
     n_cr, max_cr, n_fast, max_fast = list(counts)
     print("exp_cr: %d of 2^32 inputs differ from the double-precision exp (max %d ulp); "
           "__expf: %d beyond its documented bound on [-87, 0] (max %d ulp on [-20, 0])"

@@ -55,7 +55,24 @@ def build(force=False, verbose=False):
         cmd = [NVCC, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", OUT] + objs
         subprocess.check_call(cmd)
     build_host(force)
+    build_selfcheck(force)
     return OUT
+
+
+SELFCHECK_SRCS = os.path.join(CSRC, "test")
+SELFCHECK_OUT = os.path.join(HERE, "libturbo_b200_selfcheck.so")
+
+
+def build_selfcheck(force=False):
+    """Test-only device checks (csrc/test/*.cu) in a library of their own, so
+    that nothing the product library exports exists only for the tests."""
+    srcs = sorted(glob.glob(os.path.join(SELFCHECK_SRCS, "*.cu")))
+    newest = max(os.path.getmtime(f) for f in srcs + headers())
+    if not force and os.path.exists(SELFCHECK_OUT) and os.path.getmtime(SELFCHECK_OUT) >= newest:
+        return SELFCHECK_OUT
+    cmd = [NVCC] + FLAGS + ["-shared", "-o", SELFCHECK_OUT] + srcs
+    subprocess.check_call(cmd)
+    return SELFCHECK_OUT
 
 
 HOST = os.path.join(HERE, "host")

@@ -1,5 +1,7 @@
 // tb_selfcheck.cu -- device self-check of the exp implementations used by the
-// softmax and SwiGLU kernels, over every fp32 bit pattern.
+// softmax and SwiGLU kernels, over every fp32 bit pattern.  Test code: built
+// into its own library (libturbo_b200_selfcheck.so), not the product one; it
+// shares only the device functions of tb_internal.cuh.
 #include "tb_internal.cuh"
 
 namespace tb {
@@ -62,20 +64,24 @@ __global__ void exp_check_kernel(unsigned long long *out) {
 
 using namespace tb;
 
-extern "C" tb_status tb_selfcheck_exp(uint64_t *counts) {
-  if (!counts) return fail(TB_EINVAL, "tb_selfcheck_exp: null pointer");
-  DeviceState *st;
-  TB_TRY(device_state(&st));
+// counts[0]: inputs where exp_cr differs from the double-precision exp rounded
+// to float; counts[1]: its largest distance in ulp; counts[2]: inputs in
+// [-87, 0] where __expf exceeds its documented 2 + 1.173|x| ulp; counts[3]:
+// its largest distance over [-20, 0].  Synchronous, on the current device.
+// Returns TB_EINVAL for a null pointer, TB_ECUDA for a CUDA failure.
+extern "C" __attribute__((visibility("default"))) int tb_selfcheck_exp(uint64_t *counts) {
+  if (!counts) return TB_EINVAL;
+  int dev = 0, sms = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e == cudaSuccess) e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   unsigned long long *d = nullptr;
-  cudaError_t e = cudaMalloc(&d, 4 * sizeof(unsigned long long));
-  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_selfcheck_exp: %s", cudaGetErrorString(e));
-  e = cudaMemset(d, 0, 4 * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMalloc(&d, 4 * sizeof(unsigned long long));
+  if (e == cudaSuccess) e = cudaMemset(d, 0, 4 * sizeof(unsigned long long));
   if (e == cudaSuccess) {
-    exp_check_kernel<<<st->sm_count * 8, 256>>>(d);
+    exp_check_kernel<<<sms * 8, 256>>>(d);
     e = cudaGetLastError();
   }
   if (e == cudaSuccess) e = cudaMemcpy(counts, d, 4 * sizeof(unsigned long long), cudaMemcpyDeviceToHost);
-  cudaFree(d);
-  if (e != cudaSuccess) return fail(TB_ECUDA, "tb_selfcheck_exp: %s", cudaGetErrorString(e));
-  return TB_OK;
+  if (d) cudaFree(d);
+  return e == cudaSuccess ? TB_OK : TB_ECUDA;
 }

@@ -94,7 +94,6 @@ SIGNATURES = {
     "tb_decode_workspace_bytes": [_P, ctypes.POINTER(_SZ)],
     "tb_attention_prefill": [_P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _P, _I64, _P],
     "tb_decode_step_persistent": [_P, _P],
-    "tb_selfcheck_exp": [_P],
     "tb_rope_at": [_VP, _P, _P, _I64, _I64, _P, _P],
     "tb_kv_append": [_P, _P, _P, _P, _I64, _I64, _P, _P],
     "tb_attention_decode": [_P, _P, _P, _I64, _I64, _I64, _I64, _F, _P, _P, _P],

@@ -322,7 +322,7 @@ tb_status launch_stream_auto(const FusedArgs &a, int total_rows, cudaStream_t s,
   const int64_t per = (total_rows + grid - 1) / grid, nspans = (per + kWideWarps - 1) / kWideWarps;
   const size_t need = stream_fixed_smem(a.K, a.K == 2048) +
                       (size_t)std::min<int64_t>(nspans, 2) * (SWIGLU ? 2 : 1) * kWideWarps * (a.K / 32) * 34;
-  if (per >= kWideWarps && need <= (size_t)st->smem_optin)
+  if (2 * per >= kWideWarps && need <= (size_t)st->smem_optin)
     return launch_stream<kWideWarps, NORM, SWIGLU>(a, total_rows, s, st);
   return launch_stream<kStreamWarps, NORM, SWIGLU>(a, total_rows, s, st);
 }

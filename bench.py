@@ -41,8 +41,8 @@ ALGO_BYTES = W_BYTES + K_COLS * 4 + N_ROWS * 4    # 17,866,752 per GEMV
 N_COPIES = 32
 REF_SAMPLE_S = 10.0             # seconds of reference CPU GEMVs per measurement
 GRAPH_MAX = 256                 # GEMV launches per captured graph
-L2_FLUSH_BYTES = 256 << 20      # written before the timed region: twice the 126 MB L2
-SLEEP_CYCLES_BASE = 200000      # ~0.1 ms of device sleep ahead of the start event
+L2_FLUSH_BYTES = 256 << 20      # read before the timed region: twice the 126 MB L2
+SLEEP_CYCLES_BASE = 2000000     # ~1 ms of device sleep ahead of the start event
 SLEEP_CYCLES_PER_REPLAY = 40000  # + ~20 us per graph replay the host must enqueue
 METRIC = "Q8_0 decode GEMV HBM GB/s (W[8192,2048] Q8_0, x fp32[1,2048])"
 WORKLOAD = "q8_0_gemv_8192x2048"
@@ -247,7 +247,8 @@ def run_ours(args):
     # One graph of G = min(K, GRAPH_MAX) GEMVs (weight copy i % 32 at step i),
     # replayed K // G times, plus a graph of the K % G remaining ones.  Every
     # graph is replayed once before the timed region (upload and first-launch
-    # costs stay outside it).  Then L2 is flushed, and a device-side sleep is
+    # costs stay outside it).  Then L2 is flushed (by reading a 256 MB buffer,
+    # so that it holds only clean lines), and a device-side sleep is
     # queued ahead of the start event, so that the host has enqueued every
     # replay before the first timed GEMV starts: the region measures the GPU.
     G = min(args.steps, GRAPH_MAX)
@@ -262,6 +263,13 @@ def run_ours(args):
         with torch.cuda.graph(graph_tail, stream=stream):
             for i in range(tail):
                 gemv(G + i, s=T.stream_handle(torch.cuda.current_stream()))
+    # The flush buffer is written here, before the warm replays evict (and write
+    # back) its lines; the timed region is preceded by a READ of it, which
+    # leaves L2 holding clean flush lines and none of the weights.  A write
+    # right before the region would leave 126 MB of dirty lines for the first
+    # timed GEMVs to write back (~20 us, measured as a fixed 1 us per step at
+    # 20 steps).
+    flush = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.int32, device="cuda")
     warm_replays = 0
     with torch.cuda.stream(stream):
         for g in (graph, graph_tail):
@@ -269,7 +277,6 @@ def run_ours(args):
                 g.replay()
                 warm_replays += 1
     stream.synchronize()
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
 
     if ws > 1:
         torch.distributed.barrier()
@@ -278,7 +285,7 @@ def run_ours(args):
     n_replays = args.steps // G
     with ClockSampler(local) as clocks:
         with torch.cuda.stream(stream):
-            flush.fill_(1)
+            flush_sum = flush.sum()
             torch.cuda._sleep(SLEEP_CYCLES_BASE + SLEEP_CYCLES_PER_REPLAY * (n_replays + 1))
             start.record(stream)
             for _ in range(n_replays):
@@ -289,6 +296,7 @@ def run_ours(args):
         stream.synchronize()
     torch.cuda.synchronize()
     total_ms = start.elapsed_time(end)
+    assert int(flush_sum.item()) == L2_FLUSH_BYTES // 4
     del flush
     if ws > 1:
         t = torch.tensor([total_ms], device="cuda")
@@ -353,7 +361,7 @@ def run_ours(args):
         "config": bench_config(ws),
         "method": {"entry": entry, "tolerance": "bit-exact" if args.exact else "1e-5 * sum|w x| per output",
                    "launch": "CUDA graph of %d GEMVs replayed %d times%s; every graph replayed once before "
-                             "timing (%d warm replays); L2 flushed and replays queued behind a device sleep "
+                             "timing (%d warm replays); L2 flushed by reading a 256 MB buffer and replays queued behind a device sleep "
                              "before the start event" % (G, n_replays, " + a %d-GEMV tail graph" % tail if tail else "",
                                                           warm_replays)},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

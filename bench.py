@@ -41,7 +41,8 @@ ALGO_BYTES = W_BYTES + K_COLS * 4 + N_ROWS * 4    # 17,866,752 per GEMV
 N_COPIES = 32
 REF_SAMPLE_S = 10.0             # seconds of reference CPU GEMVs per measurement
 GRAPH_MAX = 256                 # GEMV launches per captured graph
-L2_FLUSH_BYTES = 256 << 20      # read before the timed region: twice the 126 MB L2
+L2_FLUSH_BYTES = 256 << 20      # read before a short timed region: twice the 126 MB L2
+L2_ROTATION_MIN = 15            # steps whose distinct weight copies (267 MB) exceed twice the L2
 SLEEP_CYCLES_BASE = 2000000     # ~1 ms of device sleep ahead of the start event
 SLEEP_CYCLES_PER_REPLAY = 40000  # + ~20 us per graph replay the host must enqueue
 METRIC = "Q8_0 decode GEMV HBM GB/s (W[8192,2048] Q8_0, x fp32[1,2048])"
@@ -158,8 +159,9 @@ def cpu_reference_rate(seconds=10.0, max_steps=None):
 def bench_config(n_gpus):
     """The workload both arms run (the same dict in both JSON lines)."""
     return {"workload": WORKLOAD, "N": N_ROWS, "K": K_COLS, "M": 1, "parallelism": "row-shard x%d" % n_gpus,
-            "l2": "inputs larger than L2 (%d rotating weight copies, %.0f MB) and L2 flushed before the "
-                  "timed region" % (N_COPIES, N_COPIES * W_BYTES / 1e6)}
+            "l2": "inputs larger than L2: %d rotating weight copies (%.0f MB), a step's copy was last read "
+                  ">= 14 copies (250 MB) earlier; a 256 MB read flushes L2 before regions under %d steps"
+                  % (N_COPIES, N_COPIES * W_BYTES / 1e6, L2_ROTATION_MIN)}
 
 
 def run_reference(args):
@@ -247,15 +249,31 @@ def run_ours(args):
     # One graph of G = min(K, GRAPH_MAX) GEMVs (weight copy i % 32 at step i),
     # replayed K // G times, plus a graph of the K % G remaining ones.  Every
     # graph is replayed once before the timed region (upload and first-launch
-    # costs stay outside it).  Then L2 is flushed (by reading a 256 MB buffer,
-    # so that it holds only clean lines), and a device-side sleep is
-    # queued ahead of the start event, so that the host has enqueued every
-    # replay before the first timed GEMV starts: the region measures the GPU.
+    # costs stay outside it).  A device-side sleep is queued ahead of the timed
+    # replays, so that the host has enqueued every replay before the first
+    # timed GEMV starts: the region measures the GPU.  With K <= GRAPH_MAX the
+    # start and end events are recorded inside the graph, around its K GEMVs
+    # (the graph's own launch stays outside the region); longer runs put them
+    # around the replays.
+    # L2: the K GEMVs of the region read K distinct weight copies, so from
+    # K >= L2_ROTATION_MIN on every copy's lines have been evicted by the other
+    # copies' reads before the region reaches it again (inputs larger than L2,
+    # no flush).  Shorter runs read a 256 MB buffer before the region (a read:
+    # it leaves clean lines, so the region does not write back a previous
+    # write's dirty lines).
     G = min(args.steps, GRAPH_MAX)
+    in_graph = args.steps <= GRAPH_MAX
+    start = torch.cuda.Event(enable_timing=True, external=in_graph)
+    end = torch.cuda.Event(enable_timing=True, external=in_graph)
     graph = torch.cuda.CUDAGraph()
     with torch.cuda.graph(graph, stream=stream):
+        cur = torch.cuda.current_stream()
+        if in_graph:
+            start.record(cur)
         for i in range(G):
-            gemv(i, s=T.stream_handle(torch.cuda.current_stream()))
+            gemv(i, s=T.stream_handle(cur))
+        if in_graph:
+            end.record(cur)
     tail = args.steps % G
     graph_tail = None
     if tail:
@@ -263,13 +281,10 @@ def run_ours(args):
         with torch.cuda.graph(graph_tail, stream=stream):
             for i in range(tail):
                 gemv(G + i, s=T.stream_handle(torch.cuda.current_stream()))
-    # The flush buffer is written here, before the warm replays evict (and write
-    # back) its lines; the timed region is preceded by a READ of it, which
-    # leaves L2 holding clean flush lines and none of the weights.  A write
-    # right before the region would leave 126 MB of dirty lines for the first
-    # timed GEMVs to write back (~20 us, measured as a fixed 1 us per step at
-    # 20 steps).
-    flush = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.int32, device="cuda")
+    flush = None
+    if args.steps < L2_ROTATION_MIN:
+        # written before the warm replays, which evict (and write back) its lines
+        flush = torch.ones(L2_FLUSH_BYTES // 4, dtype=torch.int32, device="cuda")
     warm_replays = 0
     with torch.cuda.stream(stream):
         for g in (graph, graph_tail):
@@ -281,23 +296,25 @@ def run_ours(args):
     if ws > 1:
         torch.distributed.barrier()
     torch.cuda.synchronize()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n_replays = args.steps // G
     with ClockSampler(local) as clocks:
         with torch.cuda.stream(stream):
-            flush_sum = flush.sum()
+            flush_sum = flush.sum() if flush is not None else None
             torch.cuda._sleep(SLEEP_CYCLES_BASE + SLEEP_CYCLES_PER_REPLAY * (n_replays + 1))
-            start.record(stream)
+            if not in_graph:
+                start.record(stream)
             for _ in range(n_replays):
                 graph.replay()
             if graph_tail is not None:
                 graph_tail.replay()
-            end.record(stream)
+            if not in_graph:
+                end.record(stream)
         stream.synchronize()
     torch.cuda.synchronize()
     total_ms = start.elapsed_time(end)
-    assert int(flush_sum.item()) == L2_FLUSH_BYTES // 4
-    del flush
+    if flush is not None:
+        assert int(flush_sum.item()) == L2_FLUSH_BYTES // 4
+        del flush
     if ws > 1:
         t = torch.tensor([total_ms], device="cuda")
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
@@ -361,9 +378,11 @@ def run_ours(args):
         "config": bench_config(ws),
         "method": {"entry": entry, "tolerance": "bit-exact" if args.exact else "1e-5 * sum|w x| per output",
                    "launch": "CUDA graph of %d GEMVs replayed %d times%s; every graph replayed once before "
-                             "timing (%d warm replays); L2 flushed by reading a 256 MB buffer and replays queued behind a device sleep "
-                             "before the start event" % (G, n_replays, " + a %d-GEMV tail graph" % tail if tail else "",
-                                                          warm_replays)},
+                             "timing (%d warm replays); replays queued behind a device sleep; %s%s"
+                             % (G, n_replays, " + a %d-GEMV tail graph" % tail if tail else "", warm_replays,
+                                "start/end events recorded inside the graph around its GEMVs" if in_graph
+                                else "start/end events around the replays",
+                                "; L2 flushed by a 256 MB read" if args.steps < L2_ROTATION_MIN else "")},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": load_traffic(),
                      "peak_source": peak_kind, "kernel_us": round(kernel_ms * 1e3, 3),

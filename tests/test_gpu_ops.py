@@ -515,7 +515,7 @@ def test_rmsnorm_kat_and_bf16():
     assert_rel(yb.float().cpu().numpy(), O.rmsnorm(xb.float().cpu().numpy(), g), BF16_REL)
 
 
-@pytest.mark.parametrize("rows,cols", [(1, 128256), (3, 37), (64, 128256), (16, 640), (2, 300000)])
+@pytest.mark.parametrize("rows,cols", [(1, 128256), (3, 37), (64, 128256), (16, 640), (2, 300000), (8, 65536)])
 def test_softmax(rows, cols):
     x = synth.normal((rows, cols), 2.0, seed=cols)
     y = torch.empty((rows, cols), dtype=torch.float32, device="cuda")
@@ -528,6 +528,18 @@ def test_softmax_many_rows_two_pass(rows, cols):
     # at least one row per SM: the persistent CTA-per-row kernel; 8000 columns
     # stay in registers between the passes, 60000 in registers and shared
     # memory, the longer rows also re-read part of the row from L2
+    check_softmax_special_rows(rows, cols)
+
+
+@pytest.mark.parametrize("rows,cols", [(40, 128256), (64, 128256), (15, 300000), (100, 4004), (100, 128256)])
+def test_softmax_few_rows_special_values(rows, cols):
+    # 8 rows to one per SM: the two-launch chunked kernels (rows split into
+    # chunks of at most 8192 columns, statistics combined in the second
+    # launch), or clusters for rows wider than 16 chunks
+    check_softmax_special_rows(rows, cols)
+
+
+def check_softmax_special_rows(rows, cols):
     from oracle import refbind as R
     x = synth.normal((rows, cols), 2.0, seed=rows)
     x[7, min(12345, cols - 1)] = 30.0

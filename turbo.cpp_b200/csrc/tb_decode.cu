@@ -55,23 +55,28 @@ __global__ void kv_append_kernel(float *__restrict__ kc, float *__restrict__ vc,
 // [r * chunk, (r + 1) * chunk):
 //   score[c] = (fma chain over d of q[d] * K[c][d]) * scale   -- the fp32
 //              matmul's order (tb_matmul_f32), then Tensor::operator*(float)
-//   p[c]     = exp(score[c] - max) * (1 / sum)                 -- tb_softmax;
-//              max and sum exchanged through distributed shared memory
-//   out[d]   = sum over c of p[c] * V[c][d]: per CTA four consecutive ranges
-//              of its keys, each an fma chain, then the CTAs' partials added
-//              in cluster-rank order by rank 0
-// fma chain over d of q[d] * k[d] (the fp32 matmul's order); k from global
-// memory through the read-only path, or from shared memory
-template <int D, bool GLOBAL>
-__device__ __forceinline__ float qk_dot(const float *qs, const float4 *kr) {
+//   per CTA: m_r = max of its scores, e[c] = exp(score[c] - m_r),
+//              s_r = sum of e, o_r[d] = sum over its keys of e[c] * V[c][d]
+//              (four consecutive key ranges, each an fma chain, added in order)
+//   out[d]   = (sum over r of o_r[d] exp(m_r - M)) * (1 / S), with M = max m_r
+//              and S = sum over r of s_r exp(m_r - M), both in rank order,
+//              combined by rank 0 from the cluster's distributed shared memory
+// That is softmax(score) . V with the normalisation applied once per output
+// instead of once per key (within 1e-5 of sum p |v| of the exact result).
+// Latency is what bounds one token's attention, so the kernel makes one pass:
+// as soon as the position is known every thread loads the key row it scores
+// (16 float4s) and the first kVPre values it multiplies, before q is staged,
+// and the cluster meets once to combine.
+// fma chain over d of q[d] * k[d], k held in registers
+template <int D>
+__device__ __forceinline__ float qk_dot_reg(const float *qs, const float4 (&kv)[D / 4]) {
   float acc = 0.f;
 #pragma unroll
   for (int d4 = 0; d4 < D / 4; ++d4) {
-    const float4 kv = GLOBAL ? __ldg(kr + d4) : kr[d4];
-    acc = __fmaf_rn(qs[4 * d4 + 0], kv.x, acc);
-    acc = __fmaf_rn(qs[4 * d4 + 1], kv.y, acc);
-    acc = __fmaf_rn(qs[4 * d4 + 2], kv.z, acc);
-    acc = __fmaf_rn(qs[4 * d4 + 3], kv.w, acc);
+    acc = __fmaf_rn(qs[4 * d4 + 0], kv[d4].x, acc);
+    acc = __fmaf_rn(qs[4 * d4 + 1], kv[d4].y, acc);
+    acc = __fmaf_rn(qs[4 * d4 + 2], kv[d4].z, acc);
+    acc = __fmaf_rn(qs[4 * d4 + 3], kv[d4].w, acc);
   }
   return acc;
 }
@@ -91,6 +96,8 @@ struct AttnArgs {
   float *out;  // [H, D]
 };
 
+constexpr int kVPre = 8;  // values per thread loaded ahead of the scores
+
 // ROPE: RoPE of q and of the new key at pos (tb_rope_at's arithmetic) and the
 // cache append of this token's key and value, fused in: each cluster rotates
 // its query head and its key/value head's new key itself, uses the new key and
@@ -99,13 +106,14 @@ struct AttnArgs {
 // cache row pos, so the writes race with nothing.
 template <int D, int NC, bool ROPE>
 __global__ void __launch_bounds__(256) attention_decode_kernel(const AttnArgs a, uint32_t *__restrict__ err) {
-  extern __shared__ float sc[];  // this CTA's scores, ceil(max_seq / NC) floats
+  extern __shared__ float sc[];  // this CTA's scores, then exp(score - m_r); ceil(max_seq / NC) floats
   __shared__ float qs[D];
-  __shared__ float kn[ROPE ? D : 1], vn[ROPE ? D : 1];  // the new key (rotated) and value
+  __shared__ __align__(16) float kn[ROPE ? D : 4];
+  __shared__ float vn[ROPE ? D : 1];  // the new key (rotated) and value
   __shared__ float red[8];
-  __shared__ float part[2];           // this CTA's [max, sum]
+  __shared__ float part[2];           // this CTA's [m_r, s_r]
   __shared__ float pv[256 / D][D];    // partial outputs of the four key ranges
-  __shared__ float octa[D];           // this CTA's partial output
+  __shared__ float octa[D];           // this CTA's o_r
   cg::cluster_group cluster = cg::this_cluster();
   const int cr = (int)cluster.block_rank();
   const int H = a.H, KVH = a.KVH;
@@ -121,9 +129,30 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(const AttnArgs a,
   const int chunk = (ctx + NC - 1) / NC;
   const int c0 = min(ctx, cr * chunk), c1 = min(ctx, c0 + chunk);
   const int rs = KVH * D;  // cache row stride (floats)
+  const int t = threadIdx.x;
+  // loads that depend only on pos: this thread's first key row and its first
+  // kVPre values (the key and value of row pos come from shared memory with ROPE)
+  const int ck = c0 + t;
+  const bool own_k = ck < c1 && !(ROPE && ck == pos);
+  float4 kreg[D / 4];
+  if (own_k) {
+    const float4 *kr = reinterpret_cast<const float4 *>(a.kc + (int64_t)ck * rs + kvh * D);
+#pragma unroll
+    for (int d4 = 0; d4 < D / 4; ++d4) kreg[d4] = __ldg(kr + d4);
+  }
+  constexpr int NCH = 256 / D;
+  const int d = t % D, ch = t / D;
+  const int n = c1 - c0, len = (n + NCH - 1) / NCH;
+  const int a0 = c0 + ch * len, a1 = min(c1, a0 + len);
+  const float *vcol = a.vc + kvh * D + d;
+  float vreg[kVPre];
+#pragma unroll
+  for (int j = 0; j < kVPre; ++j) {
+    const int c = a0 + j;
+    vreg[j] = (c < a1 && !(ROPE && c == pos)) ? __ldg(vcol + (int64_t)c * rs) : 0.f;
+  }
   if (ROPE) {
     constexpr int half = D / 2;
-    const int t = threadIdx.x;
     if (t < 2 * half) {
       const bool isq = t < half;
       const int i = isq ? t : t - half;
@@ -137,78 +166,81 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(const AttnArgs a,
       vn[t - 2 * half] = a.v_new[kvh * D + t - 2 * half];
     }
     __syncthreads();
-    if (h % (H / KVH) == 0 && cr == 0 && threadIdx.x < D) {
-      a.kc_w[(int64_t)pos * rs + kvh * D + threadIdx.x] = kn[threadIdx.x];
-      a.vc_w[(int64_t)pos * rs + kvh * D + threadIdx.x] = vn[threadIdx.x];
+    if (h % (H / KVH) == 0 && cr == 0 && t < D) {
+      a.kc_w[(int64_t)pos * rs + kvh * D + t] = kn[t];
+      a.vc_w[(int64_t)pos * rs + kvh * D + t] = vn[t];
     }
   } else {
-    if (threadIdx.x < D) qs[threadIdx.x] = a.q[h * D + threadIdx.x];
+    if (t < D) qs[t] = a.q[h * D + t];
     __syncthreads();
   }
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = t >> 5, lane = t & 31;
 
+  // scores and this CTA's maximum
   float m = -INFINITY;
-  for (int c = c0 + threadIdx.x; c < c1; c += 256) {
-    const float acc = (ROPE && c == pos)
-                          ? qk_dot<D, false>(qs, reinterpret_cast<const float4 *>(kn))
-                          : qk_dot<D, true>(qs, reinterpret_cast<const float4 *>(a.kc + (int64_t)c * rs + kvh * D));
-    const float s = __fmul_rn(acc, a.scale);
-    sc[c - c0] = s;
-    m = s > m ? s : m;
+  for (int c = ck; c < c1; c += 256) {
+    if (c != ck || !own_k) {  // a later key row (more than 256 keys per CTA), or the new key
+      const float4 *kr = (ROPE && c == pos) ? reinterpret_cast<const float4 *>(kn)
+                                            : reinterpret_cast<const float4 *>(a.kc + (int64_t)c * rs + kvh * D);
+#pragma unroll
+      for (int d4 = 0; d4 < D / 4; ++d4) kreg[d4] = (ROPE && c == pos) ? kr[d4] : __ldg(kr + d4);
+    }
+    const float sv = __fmul_rn(qk_dot_reg<D>(qs, kreg), a.scale);
+    sc[c - c0] = sv;
+    m = sv > m ? sv : m;
   }
   m = warp_max_f(m);
   if (lane == 0) red[warp] = m;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = red[0];
-    for (int w = 1; w < 8; ++w) t = fmaxf(t, red[w]);
-    part[0] = t;
-  }
-  cluster.sync();
-  float M = -INFINITY;
-  for (int r = 0; r < NC; ++r) M = fmaxf(M, *cluster.map_shared_rank(&part[0], r));
+  m = red[0];
+  for (int w = 1; w < 8; ++w) m = fmaxf(m, red[w]);
+  // exp(score - m_r) and their sum
   float s = 0.f;
-  for (int c = c0 + threadIdx.x; c < c1; c += 256) {
-    const float e = __expf(__fsub_rn(sc[c - c0], M));
+  for (int c = ck; c < c1; c += 256) {
+    const float e = __expf(__fsub_rn(sc[c - c0], m));
     sc[c - c0] = e;
     s = __fadd_rn(s, e);
   }
   s = warp_sum_f(s);
-  __syncthreads();  // the max's red[] reads are done
+  __syncthreads();  // red[] reads above are done; sc[] is complete
   if (lane == 0) red[warp] = s;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    float t = 0.f;
-    for (int w = 0; w < 8; ++w) t = __fadd_rn(t, red[w]);
-    part[1] = t;
-  }
-  cluster.sync();
-  float S = 0.f;
-  for (int r = 0; r < NC; ++r) S = __fadd_rn(S, *cluster.map_shared_rank(&part[1], r));
-  const float inv = __frcp_rn(S);
-
-  constexpr int NCH = 256 / D;
-  const int d = threadIdx.x % D, ch = threadIdx.x / D;
-  const int n = c1 - c0, len = (n + NCH - 1) / NCH;
-  const int a0 = c0 + ch * len, a1 = min(c1, a0 + len);
-  const float *vcol = a.vc + kvh * D + d;
+  // o_r: four consecutive key ranges, each an fma chain over its keys
   float acc = 0.f;
-  for (int c = a0; c < a1; ++c) {
+#pragma unroll
+  for (int j = 0; j < kVPre; ++j) {
+    const int c = a0 + j;
+    if (c < a1) acc = __fmaf_rn(sc[c - c0], (ROPE && c == pos) ? vn[d] : vreg[j], acc);
+  }
+  for (int c = a0 + kVPre; c < a1; ++c) {
     const float v = (ROPE && c == pos) ? vn[d] : __ldg(vcol + (int64_t)c * rs);
-    acc = __fmaf_rn(__fmul_rn(sc[c - c0], inv), v, acc);
+    acc = __fmaf_rn(sc[c - c0], v, acc);
   }
   pv[ch][d] = acc;
   __syncthreads();
-  if (threadIdx.x < D) {
-    float o = pv[0][threadIdx.x];
-    for (int k = 1; k < NCH; ++k) o = __fadd_rn(o, pv[k][threadIdx.x]);
-    octa[threadIdx.x] = o;
+  if (t < D) {
+    float o = pv[0][t];
+    for (int k = 1; k < NCH; ++k) o = __fadd_rn(o, pv[k][t]);
+    octa[t] = o;
+  }
+  if (t == 0) {
+    float tot = 0.f;
+    for (int w = 0; w < 8; ++w) tot = __fadd_rn(tot, red[w]);
+    part[0] = m;
+    part[1] = tot;
   }
   cluster.sync();
-  if (cr == 0 && threadIdx.x < D) {
-    float o = octa[threadIdx.x];
-    for (int r = 1; r < NC; ++r) o = __fadd_rn(o, *cluster.map_shared_rank(&octa[threadIdx.x], r));
-    a.out[h * D + threadIdx.x] = o;
+  if (cr == 0 && t < D) {
+    float M = -INFINITY;
+    for (int r = 0; r < NC; ++r) M = fmaxf(M, *cluster.map_shared_rank(&part[0], r));
+    float S = 0.f, o = 0.f;
+    for (int r = 0; r < NC; ++r) {
+      const float mr = *cluster.map_shared_rank(&part[0], r);
+      if (mr == -INFINITY) continue;  // a CTA without keys
+      const float w = __expf(__fsub_rn(mr, M));
+      S = __fadd_rn(S, __fmul_rn(*cluster.map_shared_rank(&part[1], r), w));
+      o = __fmaf_rn(*cluster.map_shared_rank(&octa[t], r), w, o);
+    }
+    a.out[h * D + t] = __fmul_rn(o, __frcp_rn(S));
   }
   cluster.sync();  // peers' shared memory stays alive until rank 0 has read it
 }

@@ -204,11 +204,14 @@ __global__ void __launch_bounds__(NW * 32) gemv_q8_0_kernel(
 // Few large copies per SM stream at the same rate as plain 16-byte loads from
 // every thread; many small copies do not.
 //
-// Programmatic dependent launch: the weight copies are issued before
+// Programmatic dependent launch: the first span's copies are issued before
 // griddepcontrol.wait (weights never depend on the previous kernel), x is
 // read and y written only after it, and the kernel lets its dependents launch
 // at once.  A GEMV that follows another kernel in the stream therefore starts
-// streaming its weights while the predecessor drains.
+// streaming its weights while the predecessor drains.  The second span's
+// copies go out right after the first loads of x, so that x does not queue
+// behind them (8192 x 2048: 8.77 against 9.46 us with both spans issued before
+// the wait).
 
 struct SpanCfg {
   int span_rows;  // rows per span buffer
@@ -258,10 +261,7 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gemv_q8_0_span_kernel(
       bulk_g2s(buf0 + (size_t)(k & 1) * span_rows * rb + (size_t)a * rb,
                W + ((int64_t)n0 + r0 + a) * rb, bytes, bq);
   };
-  if (threadIdx.x < 4) {
-    if (nspans > 0) issue(0);
-    if (nspans > 1) issue(1);
-  }
+  if (threadIdx.x < 4 && nspans > 0) issue(0);  // span 1 once x's first loads are out (below)
   pdl_launch_dependents();
   pdl_wait();  // x (and the order of our y writes) depend on the previous kernel
 
@@ -276,6 +276,7 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gemv_q8_0_span_kernel(
         const int iv = base4 + u * NWARP * 32 + threadIdx.x;
         v[u] = iv < nv ? __ldg(x4 + iv) : make_float4(0.f, 0.f, 0.f, 0.f);
       }
+      if (base4 == 0 && threadIdx.x < 4 && nspans > 1) issue(1);
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int iv = base4 + u * NWARP * 32 + threadIdx.x;

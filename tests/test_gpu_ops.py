@@ -346,6 +346,34 @@ def test_matmul_f32_batched_bit_exact():
     assert_bits(host(out), ref)
 
 
+@pytest.mark.parametrize("case", ["scores", "context", "odd", "a_transposed", "batched"])
+def test_matmul_f32_tiled_bit_exact(case):
+    # from 32 rows and 32 columns on: 64x64 output tiles staged through shared
+    # memory, each output still the k-ordered fma chain (attention.cpp:115-132
+    # at prefill shapes: Q_h K_h^T, then P V_h)
+    if case == "batched":
+        a = synth.normal((2 * 3 * 70 * 33,), 1.0, seed=40)
+        b = synth.normal((2 * 3 * 33 * 45,), 1.0, seed=41)
+        sa, sta = (2, 3, 70, 33), (6930, 2310, 33, 1)
+        sb, stb = (2, 3, 33, 45), (4455, 1485, 45, 1)
+        oa = ob = 0
+    else:
+        M, K, N, sta, stb, oa, ob = {
+            "scores": (512, 64, 512, (2048, 1), (1, 512), 3, 5),    # Q_h [S,64] x K_h^T (cache rows of 512)
+            "context": (512, 512, 64, (512, 1), (512, 1), 0, 7),    # P [S,ctx] x V_h [ctx,64]
+            "odd": (96, 130, 77, (2048, 1), (1, 512), 3, 5),
+            "a_transposed": (64, 40, 70, (1, 64), (70, 1), 0, 0),
+        }[case]
+        sa, sb = (M, K), (K, N)
+        a = synth.normal((oa + (sa[0] - 1) * sta[0] + (sa[1] - 1) * sta[1] + 1,), 1.0, seed=42)
+        b = synth.normal((ob + (sb[0] - 1) * stb[0] + (sb[1] - 1) * stb[1] + 1,), 1.0, seed=43)
+    ref = O.matmul_f32(a, oa, sa, sta, b, ob, sb, stb)
+    out = torch.empty(tuple(sa[:-1]) + (sb[-1],), dtype=torch.float32, device="cuda")
+    T.call("tb_matmul_f32", T.byref(T.view(dev(a), oa, sa, sta)), T.byref(T.view(dev(b), ob, sb, stb)),
+           T.byref(T.view(out)), S())
+    assert_bits(host(out), ref)
+
+
 # ------------------------------------------------------------ elementwise ----
 
 @pytest.mark.parametrize("sa,sb", [((1, 128, 2048), (1, 128, 2048)), ((4, 1, 8), (3, 1)),

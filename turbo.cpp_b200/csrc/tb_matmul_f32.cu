@@ -4,8 +4,13 @@
 // Each output is the FMA chain over k = 0..K-1 in increasing order starting
 // from 0, which is what the reference's packed AVX2 kernel computes per output
 // element (src/tensor/tensor.cpp:503-538), so results are bit-identical.  The
-// products are small in the decode path (K = head_dim = 64); a CTA computes a
-// 32x8 tile of outputs, one per thread, walking k in order.
+// products are small in the decode path (K = head_dim = 64): there a CTA
+// computes a 32x8 tile of outputs, one per thread, walking k in order.  From
+// 32 rows and 32 columns on (prefill attention, fp32 Linear layers) a CTA
+// computes a 64x64 tile with 4x4 outputs per thread: k-tiles of 16 of A and B
+// are staged in shared memory (loaded along whichever of the view's strides is
+// 1), the next k-tile is fetched into registers while the current one is
+// used, and every output is still one fma chain over k in increasing order.
 #include <algorithm>
 
 #include "tb_internal.cuh"
@@ -62,6 +67,95 @@ __global__ void __launch_bounds__(TN * TM) matmul_f32_kernel(const float *__rest
   }
 }
 
+// 64x64 output tile per CTA, 256 threads, thread (ty, tx) owns rows
+// 4 ty .. 4 ty + 3 and columns 4 tx .. 4 tx + 3.  A k-tile of A (64 x 16) and
+// of B (16 x 64) is staged per step: thread i loads elements i + 256 j,
+// mapped so that consecutive threads walk the view's unit-stride dimension
+// (a_kfast: A's k stride is 1, else its m stride; b_nfast likewise).
+constexpr int BT = 64, BK = 16;
+
+__global__ void __launch_bounds__(256) matmul_f32_tiled_kernel(const float *__restrict__ a,
+                                                               const float *__restrict__ b,
+                                                               float *__restrict__ out, MMView v, bool a_kfast,
+                                                               bool b_nfast) {
+  __shared__ float As[BK][BT + 4];  // [k][m]
+  __shared__ float Bs[BK][BT + 4];  // [k][n]
+  const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
+  const int64_t tiles_n = (v.N + BT - 1) / BT, tiles_m = (v.M + BT - 1) / BT;
+  const int64_t tiles = v.batch * tiles_m * tiles_n;
+  for (int64_t t = blockIdx.x; t < tiles; t += gridDim.x) {
+    const int64_t bi = t / (tiles_m * tiles_n), rem = t % (tiles_m * tiles_n);
+    const int64_t m0 = (rem / tiles_n) * BT, n0 = (rem % tiles_n) * BT;
+    int64_t ao = v.oa, bo = v.ob, tb_ = bi;
+    for (int d = v.rank - 3; d >= 0; --d) {
+      const int64_t idx = tb_ % v.bshape[d];
+      tb_ /= v.bshape[d];
+      ao += idx * v.sa_b[d];
+      bo += idx * v.sb_b[d];
+    }
+    // this thread's four A and four B elements of a k-tile: (m, k) and (k, n)
+    // offsets inside the tile
+    int am[4], ak[4], bk[4], bn[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int i = tid + 256 * j;
+      am[j] = a_kfast ? i / BK : i % BT;
+      ak[j] = a_kfast ? i % BK : i / BT;
+      bn[j] = b_nfast ? i % BT : i / BK;
+      bk[j] = b_nfast ? i / BT : i % BK;
+    }
+    float ra[4], rb[4];
+    auto fetch = [&](int64_t k0) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t m = m0 + am[j], k = k0 + ak[j];
+        ra[j] = (m < v.M && k < v.K) ? __ldg(a + ao + m * v.sam + k * v.sak) : 0.f;
+        const int64_t kk = k0 + bk[j], n = n0 + bn[j];
+        rb[j] = (kk < v.K && n < v.N) ? __ldg(b + bo + kk * v.sbk + n * v.sbn) : 0.f;
+      }
+    };
+    float c[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) c[i][j] = 0.f;
+    fetch(0);
+    for (int64_t k0 = 0; k0 < v.K; k0 += BK) {
+      __syncthreads();  // the previous k-tile's reads are done
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        As[ak[j]][am[j]] = ra[j];
+        Bs[bk[j]][bn[j]] = rb[j];
+      }
+      __syncthreads();
+      if (k0 + BK < v.K) fetch(k0 + BK);  // in flight while this k-tile is used
+      const int kmax = (int)min((int64_t)BK, v.K - k0);
+#pragma unroll 4
+      for (int kk = 0; kk < kmax; ++kk) {
+        const float4 av = *reinterpret_cast<const float4 *>(&As[kk][4 * ty]);
+        const float4 bv = *reinterpret_cast<const float4 *>(&Bs[kk][4 * tx]);
+        const float ar[4] = {av.x, av.y, av.z, av.w}, br[4] = {bv.x, bv.y, bv.z, bv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+#pragma unroll
+          for (int j = 0; j < 4; ++j) c[i][j] = __fmaf_rn(ar[i], br[j], c[i][j]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int64_t m = m0 + 4 * ty + i;
+      if (m >= v.M) continue;
+      float *orow = out + (bi * v.M + m) * v.N;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int64_t n = n0 + 4 * tx + j;
+        if (n < v.N) orow[n] = c[i][j];
+      }
+    }
+    __syncthreads();  // shared tiles are reused by the CTA's next output tile
+  }
+}
+
 }  // namespace
 }  // namespace tb
 
@@ -102,10 +196,18 @@ extern "C" tb_status tb_matmul_f32(const tb_view *a, const tb_view *b, const tb_
   v.sbn = b->strides[r - 1];
   v.oa = a->offset;
   v.ob = b->offset;
-  int64_t tiles = v.batch * ((v.M + TM - 1) / TM) * ((v.N + TN - 1) / TN);
-  if (tiles == 0) return TB_OK;
+  if (v.batch * v.M * v.N == 0) return TB_OK;
   DeviceState *st;
   TB_TRY(device_state(&st));
+  if (v.M >= 32 && v.N >= 32) {
+    const int64_t t64 = v.batch * ((v.M + BT - 1) / BT) * ((v.N + BT - 1) / BT);
+    const int g = (int)std::min<int64_t>(t64, (int64_t)st->sm_count * 8);
+    matmul_f32_tiled_kernel<<<g, 256, 0, as_stream(stream)>>>(
+        static_cast<const float *>(a->data), static_cast<const float *>(b->data),
+        static_cast<float *>(out->data) + out->offset, v, v.sak == 1, v.sbn == 1);
+    return check_launch("tb_matmul_f32");
+  }
+  int64_t tiles = v.batch * ((v.M + TM - 1) / TM) * ((v.N + TN - 1) / TN);
   int grid = (int)std::min<int64_t>(tiles, (int64_t)st->sm_count * 16);
   matmul_f32_kernel<<<grid, dim3(TN, TM), 0, as_stream(stream)>>>(
       static_cast<const float *>(a->data), static_cast<const float *>(b->data),

@@ -86,6 +86,19 @@ def _cases(T, torch):
 
     mul_case(1 << 18, 4096)
 
+    # ---- A12: fp32 matmul (the reference's benchmark_gemm shape, and the prefill
+    # attention's per-head products) ---------------------------------------------
+    def mm_case(M, K, N, tag, cfg):
+        def make():
+            A, B = f32((M, K), 6), f32((K, N), 7)
+            Y = torch.empty((M, N), device=dev)
+            va, vb, vy = T.view(A), T.view(B), T.view(Y)
+            return (lambda i, s: T.load().tb_matmul_f32(T.byref(va), T.byref(vb), T.byref(vy), s)), (A, B, Y, va, vb, vy)
+        cases.append(Case("matmul_f32_" + tag, cfg, make, 4 * (M * K + K * N + M * N), flops=2 * M * K * N))
+
+    mm_case(2048, 2048, 2048, "2048x2048x2048", "reference benchmark_gemm: fp32 2048^3")
+    mm_case(512, 64, 512, "512x64x512", "prefill attention scores of one head (S = 512, head_dim 64)")
+
     # ---- A5/A6: copies ----------------------------------------------------------------
     def transpose_copy(rows, cols):
         n = rows * cols

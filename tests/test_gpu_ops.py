@@ -346,11 +346,12 @@ def test_matmul_f32_batched_bit_exact():
     assert_bits(host(out), ref)
 
 
-@pytest.mark.parametrize("case", ["scores", "context", "odd", "a_transposed", "batched"])
+@pytest.mark.parametrize("case", ["scores", "context", "odd", "a_transposed", "batched", "wide"])
 def test_matmul_f32_tiled_bit_exact(case):
-    # from 32 rows and 32 columns on: 64x64 output tiles staged through shared
-    # memory, each output still the k-ordered fma chain (attention.cpp:115-132
-    # at prefill shapes: Q_h K_h^T, then P V_h)
+    # from 32 rows and 32 columns on: 64x64 (or, with at least one per SM,
+    # 128x128) output tiles staged through shared memory, each output still the
+    # k-ordered fma chain (attention.cpp:115-132 at prefill shapes: Q_h K_h^T,
+    # then P V_h)
     if case == "batched":
         a = synth.normal((2 * 3 * 70 * 33,), 1.0, seed=40)
         b = synth.normal((2 * 3 * 33 * 45,), 1.0, seed=41)
@@ -363,6 +364,7 @@ def test_matmul_f32_tiled_bit_exact(case):
             "context": (512, 512, 64, (512, 1), (512, 1), 0, 7),    # P [S,ctx] x V_h [ctx,64]
             "odd": (96, 130, 77, (2048, 1), (1, 512), 3, 5),
             "a_transposed": (64, 40, 70, (1, 64), (70, 1), 0, 0),
+            "wide": (1600, 37, 1700, (37, 1), (1, 37), 0, 0),       # 128x128 tiles, B read along k
         }[case]
         sa, sb = (M, K), (K, N)
         a = synth.normal((oa + (sa[0] - 1) * sta[0] + (sa[1] - 1) * sta[1] + 1,), 1.0, seed=42)

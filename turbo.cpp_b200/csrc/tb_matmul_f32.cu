@@ -7,7 +7,8 @@
 // products are small in the decode path (K = head_dim = 64): there a CTA
 // computes a 32x8 tile of outputs, one per thread, walking k in order.  From
 // 32 rows and 32 columns on (prefill attention, fp32 Linear layers) a CTA
-// computes a 64x64 tile with 4x4 outputs per thread: k-tiles of 16 of A and B
+// computes a 64x64 tile with 4x4 outputs per thread (128x128 with 8x8 when
+// there are at least as many such tiles as SMs): k-tiles of A and B
 // are staged in shared memory (loaded along whichever of the view's strides is
 // 1), the next k-tile is fetched into registers while the current one is
 // used, and every output is still one fma chain over k in increasing order.
@@ -67,19 +68,24 @@ __global__ void __launch_bounds__(TN * TM) matmul_f32_kernel(const float *__rest
   }
 }
 
-// 64x64 output tile per CTA, 256 threads, thread (ty, tx) owns rows
-// 4 ty .. 4 ty + 3 and columns 4 tx .. 4 tx + 3.  A k-tile of A (64 x 16) and
-// of B (16 x 64) is staged per step: thread i loads elements i + 256 j,
-// mapped so that consecutive threads walk the view's unit-stride dimension
-// (a_kfast: A's k stride is 1, else its m stride; b_nfast likewise).
-constexpr int BT = 64, BK = 16;
-
-__global__ void __launch_bounds__(256) matmul_f32_tiled_kernel(const float *__restrict__ a,
+// BT x BT output tile per CTA (BT = 64 or 128), 256 threads as 16 x 16:
+// thread (ty, tx) owns R = BT / 16 rows and R columns, taken as R / 4 groups
+// of four, BT / 2 apart (rows h BT/2 + 4 ty + 0..3, likewise columns), so that
+// its shared-memory reads are float4s that a warp serves without bank
+// conflicts.  A k-tile of A (BT x BK) and of B (BK x BT) is staged per step
+// (BK = 16 for 64-wide tiles, 8 for 128-wide ones, to stay within 128 registers):
+// thread i loads elements i + 256 j, mapped so that consecutive threads walk
+// the view's unit-stride dimension (a_kfast: A's k stride is 1, else its m
+// stride; b_nfast likewise), and the next k-tile is fetched into registers
+// while the current one is used.
+template <int BT, int BK>
+__global__ void __launch_bounds__(256, BT == 128 ? 2 : 1) matmul_f32_tiled_kernel(const float *__restrict__ a,
                                                                const float *__restrict__ b,
                                                                float *__restrict__ out, MMView v, bool a_kfast,
                                                                bool b_nfast) {
-  __shared__ float As[BK][BT + 4];  // [k][m]
-  __shared__ float Bs[BK][BT + 4];  // [k][n]
+  constexpr int R = BT / 16, H = R / 4, L = BT * BK / 256;  // outputs per side, groups, loads per operand
+  __shared__ __align__(16) float As[BK][BT + 4];  // [k][m]
+  __shared__ __align__(16) float Bs[BK][BT + 4];  // [k][n]
   const int tid = threadIdx.x, tx = tid & 15, ty = tid >> 4;
   const int64_t tiles_n = (v.N + BT - 1) / BT, tiles_m = (v.M + BT - 1) / BT;
   const int64_t tiles = v.batch * tiles_m * tiles_n;
@@ -93,62 +99,62 @@ __global__ void __launch_bounds__(256) matmul_f32_tiled_kernel(const float *__re
       ao += idx * v.sa_b[d];
       bo += idx * v.sb_b[d];
     }
-    // this thread's four A and four B elements of a k-tile: (m, k) and (k, n)
-    // offsets inside the tile
-    int am[4], ak[4], bk[4], bn[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int i = tid + 256 * j;
-      am[j] = a_kfast ? i / BK : i % BT;
-      ak[j] = a_kfast ? i % BK : i / BT;
-      bn[j] = b_nfast ? i % BT : i / BK;
-      bk[j] = b_nfast ? i / BT : i % BK;
-    }
-    float ra[4], rb[4];
+    // this thread's L elements of A and of B in a k-tile: (m, k) and (k, n),
+    // element i = tid + 256 j (recomputed where used, to save registers)
+    auto am = [&](int j) { const int i = tid + 256 * j; return a_kfast ? i / BK : i % BT; };
+    auto ak = [&](int j) { const int i = tid + 256 * j; return a_kfast ? i % BK : i / BT; };
+    auto bn = [&](int j) { const int i = tid + 256 * j; return b_nfast ? i % BT : i / BK; };
+    auto bk = [&](int j) { const int i = tid + 256 * j; return b_nfast ? i / BT : i % BK; };
+    float ra[L], rb[L];
     auto fetch = [&](int64_t k0) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int64_t m = m0 + am[j], k = k0 + ak[j];
+      for (int j = 0; j < L; ++j) {
+        const int64_t m = m0 + am(j), k = k0 + ak(j);
         ra[j] = (m < v.M && k < v.K) ? __ldg(a + ao + m * v.sam + k * v.sak) : 0.f;
-        const int64_t kk = k0 + bk[j], n = n0 + bn[j];
+        const int64_t kk = k0 + bk(j), n = n0 + bn(j);
         rb[j] = (kk < v.K && n < v.N) ? __ldg(b + bo + kk * v.sbk + n * v.sbn) : 0.f;
       }
     };
-    float c[4][4];
+    float c[R][R];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < R; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) c[i][j] = 0.f;
+      for (int j = 0; j < R; ++j) c[i][j] = 0.f;
     fetch(0);
     for (int64_t k0 = 0; k0 < v.K; k0 += BK) {
       __syncthreads();  // the previous k-tile's reads are done
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        As[ak[j]][am[j]] = ra[j];
-        Bs[bk[j]][bn[j]] = rb[j];
+      for (int j = 0; j < L; ++j) {
+        As[ak(j)][am(j)] = ra[j];
+        Bs[bk(j)][bn(j)] = rb[j];
       }
       __syncthreads();
       if (k0 + BK < v.K) fetch(k0 + BK);  // in flight while this k-tile is used
       const int kmax = (int)min((int64_t)BK, v.K - k0);
 #pragma unroll 4
       for (int kk = 0; kk < kmax; ++kk) {
-        const float4 av = *reinterpret_cast<const float4 *>(&As[kk][4 * ty]);
-        const float4 bv = *reinterpret_cast<const float4 *>(&Bs[kk][4 * tx]);
-        const float ar[4] = {av.x, av.y, av.z, av.w}, br[4] = {bv.x, bv.y, bv.z, bv.w};
+        float ar[R], br[R];
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
+        for (int h = 0; h < H; ++h) {
+          const float4 av = *reinterpret_cast<const float4 *>(&As[kk][h * (BT / 2) + 4 * ty]);
+          const float4 bv = *reinterpret_cast<const float4 *>(&Bs[kk][h * (BT / 2) + 4 * tx]);
+          ar[4 * h + 0] = av.x; ar[4 * h + 1] = av.y; ar[4 * h + 2] = av.z; ar[4 * h + 3] = av.w;
+          br[4 * h + 0] = bv.x; br[4 * h + 1] = bv.y; br[4 * h + 2] = bv.z; br[4 * h + 3] = bv.w;
+        }
 #pragma unroll
-          for (int j = 0; j < 4; ++j) c[i][j] = __fmaf_rn(ar[i], br[j], c[i][j]);
+        for (int i = 0; i < R; ++i)
+#pragma unroll
+          for (int j = 0; j < R; ++j) c[i][j] = __fmaf_rn(ar[i], br[j], c[i][j]);
       }
     }
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int64_t m = m0 + 4 * ty + i;
+    for (int i = 0; i < R; ++i) {
+      const int64_t m = m0 + (i / 4) * (BT / 2) + 4 * ty + (i % 4);
       if (m >= v.M) continue;
       float *orow = out + (bi * v.M + m) * v.N;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int64_t n = n0 + 4 * tx + j;
+      for (int j = 0; j < R; ++j) {
+        const int64_t n = n0 + (j / 4) * (BT / 2) + 4 * tx + (j % 4);
         if (n < v.N) orow[n] = c[i][j];
       }
     }
@@ -200,11 +206,18 @@ extern "C" tb_status tb_matmul_f32(const tb_view *a, const tb_view *b, const tb_
   DeviceState *st;
   TB_TRY(device_state(&st));
   if (v.M >= 32 && v.N >= 32) {
-    const int64_t t64 = v.batch * ((v.M + BT - 1) / BT) * ((v.N + BT - 1) / BT);
-    const int g = (int)std::min<int64_t>(t64, (int64_t)st->sm_count * 8);
-    matmul_f32_tiled_kernel<<<g, 256, 0, as_stream(stream)>>>(
-        static_cast<const float *>(a->data), static_cast<const float *>(b->data),
-        static_cast<float *>(out->data) + out->offset, v, v.sak == 1, v.sbn == 1);
+    // 128x128 tiles where there is at least one per SM, else 64x64 ones
+    const int64_t t128 = v.batch * ((v.M + 127) / 128) * ((v.N + 127) / 128);
+    const float *pa = static_cast<const float *>(a->data), *pb = static_cast<const float *>(b->data);
+    float *po = static_cast<float *>(out->data) + out->offset;
+    if (t128 >= (int64_t)st->sm_count) {
+      const int g = (int)std::min<int64_t>(t128, (int64_t)st->sm_count * 2);
+      matmul_f32_tiled_kernel<128, 8><<<g, 256, 0, as_stream(stream)>>>(pa, pb, po, v, v.sak == 1, v.sbn == 1);
+    } else {
+      const int64_t t64 = v.batch * ((v.M + 63) / 64) * ((v.N + 63) / 64);
+      const int g = (int)std::min<int64_t>(t64, (int64_t)st->sm_count * 8);
+      matmul_f32_tiled_kernel<64, 16><<<g, 256, 0, as_stream(stream)>>>(pa, pb, po, v, v.sak == 1, v.sbn == 1);
+    }
     return check_launch("tb_matmul_f32");
   }
   int64_t tiles = v.batch * ((v.M + TM - 1) / TM) * ((v.N + TN - 1) / TN);

@@ -89,7 +89,12 @@ const char *tb_version(void);
 tb_status tb_alloc(void **ptr_dev, size_t bytes);
 tb_status tb_free(void *ptr_dev);
 /* Host <-> device copies: the mmap constructor Storage(void*, size_t)
- * (tensor.hpp:76-77) uploads weights once; data_ptr() reads back. */
+ * (tensor.hpp:76-77) uploads weights once; data_ptr() reads back.
+ * Asynchronous on `stream`.  Page-locked host buffers of up to 256 KB whose
+ * address and size are multiples of 16 bytes are copied by a kernel through
+ * the buffer's device mapping (a few microseconds less per call than a DMA
+ * copy, and the next kernel may start behind it); the host buffer must stay
+ * valid until the stream reaches the copy.  Other buffers use DMA. */
 tb_status tb_upload(void *dst_dev, const void *src_host, size_t bytes, tb_stream stream);
 tb_status tb_download(void *dst_host, const void *src_dev, size_t bytes, tb_stream stream);
 tb_status tb_memset(void *dst_dev, int value, size_t bytes, tb_stream stream);

@@ -376,6 +376,49 @@ def test_matmul_f32_tiled_bit_exact(case):
     assert_bits(host(out), ref)
 
 
+@pytest.mark.parametrize("nbytes", [16, 8192, 32768, 262144, 262160, 100])
+def test_upload_download_pinned_and_pageable(nbytes):
+    # page-locked buffers of up to 256 KB in 16-byte units move by a copy kernel
+    # through the host mapping; pageable, larger or unaligned ones by DMA: the
+    # bytes arrive unchanged either way
+    src = np.random.default_rng(nbytes).integers(0, 256, nbytes + 4, dtype=np.uint8)
+    d = torch.empty(nbytes + 64, dtype=torch.uint8, device="cuda")
+    pin = torch.from_numpy(src.copy()).pin_memory()
+    back = torch.zeros(nbytes + 4, dtype=torch.uint8).pin_memory()
+    for off in (0, 4):  # 4: a host address not on a 16-byte boundary (DMA)
+        L = T.load()
+        T.check(L.tb_upload(T.ptr(d), ctypes.c_void_p(pin.data_ptr() + off), nbytes, S()))
+        T.check(L.tb_download(ctypes.c_void_p(back.data_ptr() + off), T.ptr(d), nbytes, S()))
+        torch.cuda.synchronize()
+        assert np.array_equal(back.numpy()[off:off + nbytes], src[off:off + nbytes])
+        page = np.zeros(nbytes, np.uint8)
+        T.check(L.tb_download(ctypes.c_void_p(page.ctypes.data), T.ptr(d), nbytes, S()))
+        torch.cuda.synchronize()
+        assert np.array_equal(page, src[off:off + nbytes])
+
+
+def test_small_upload_waits_for_the_previous_reader():
+    # x is read by a GEMV and then overwritten by a small upload from pinned
+    # memory, then read again, all on one stream: each GEMV sees its own x
+    N, K = 4096, 2048
+    wq = synth.quantize_q8_0(synth.normal((N, K), 0.02, seed=70))
+    xa, xb = synth.normal((1, K), 1.0, seed=71), synth.normal((1, K), 1.0, seed=72)
+    dw = dev(wq)
+    x = dev(xa)
+    pa, pb = torch.from_numpy(xa).pin_memory(), torch.from_numpy(xb).pin_memory()
+    y1 = torch.empty((1, N), device="cuda")
+    y2 = torch.empty((1, N), device="cuda")
+    L = T.load()
+    for _ in range(3):
+        T.call("tb_matmul_quant_exact", T.Q8_0, T.ptr(x), 1, K, T.ptr(dw), N, T.ptr(y1), S())
+        T.check(L.tb_upload(T.ptr(x), ctypes.c_void_p(pb.data_ptr()), K * 4, S()))
+        T.call("tb_matmul_quant_exact", T.Q8_0, T.ptr(x), 1, K, T.ptr(dw), N, T.ptr(y2), S())
+        T.check(L.tb_upload(T.ptr(x), ctypes.c_void_p(pa.data_ptr()), K * 4, S()))
+        torch.cuda.synchronize()
+        assert_bits(host(y1), O.matmul_q8_0(xa, wq, N))
+        assert_bits(host(y2), O.matmul_q8_0(xb, wq, N))
+
+
 # ------------------------------------------------------------ elementwise ----
 
 @pytest.mark.parametrize("sa,sb", [((1, 128, 2048), (1, 128, 2048)), ((4, 1, 8), (3, 1)),

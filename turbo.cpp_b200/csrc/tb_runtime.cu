@@ -1,5 +1,6 @@
 // tb_runtime.cu -- per-device state, error reporting, the HBM arena and the
 // host<->device copies of the C ABI.
+#include <algorithm>
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
@@ -133,6 +134,80 @@ tb_status validate_view(const tb_view *v, const char *name) {
 
 }  // namespace tb
 
+namespace tb {
+namespace {
+// Small copies between page-locked host memory and the device run as a kernel
+// that reads or writes the host buffer through its device mapping instead of
+// on a copy engine: a transfer of a few KB (a decode step's token, one row of
+// activations) then costs one kernel's latency instead of a DMA round trip
+// and its hand-offs with the compute engine, and, being a kernel launched with
+// programmatic dependent launch, the next kernel's weight prefetch overlaps it.
+// Uploads read the host buffer before griddepcontrol.wait (the host data does
+// not depend on the previous kernel; the device buffer may still be read by
+// it), downloads read the device buffer after it.  Pageable host memory, sizes
+// above kSmallCopyMax and addresses or sizes not in 16-byte units keep the
+// DMA copy.
+constexpr size_t kSmallCopyMax = size_t(256) << 10;
+
+template <bool UP>
+__global__ void __launch_bounds__(256) small_copy_kernel(uint4 *__restrict__ dst, const uint4 *__restrict__ src,
+                                                         int64_t n16) {
+  pdl_launch_dependents();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (UP) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (i + u * stride < n16) v[u] = src[i + u * stride];
+    pdl_wait();
+#pragma unroll
+    for (int u = 0; u < 4; ++u)
+      if (i + u * stride < n16) dst[i + u * stride] = v[u];
+  } else {
+    pdl_wait();
+    for (; i < n16; i += stride) dst[i] = src[i];
+  }
+}
+
+// The device address of `host` when it is page-locked memory mapped into the
+// device's address space and the copy qualifies for small_copy_kernel; else null.
+const void *small_pinned_alias(const void *host, const void *dev, size_t bytes) {
+  if (bytes > kSmallCopyMax || bytes % 16 != 0 || ((reinterpret_cast<uintptr_t>(host) |
+                                                     reinterpret_cast<uintptr_t>(dev)) & 15) != 0)
+    return nullptr;
+  cudaPointerAttributes at;
+  if (cudaPointerGetAttributes(&at, host) != cudaSuccess) {
+    cudaGetLastError();  // not a pointer the runtime knows: pageable memory
+    return nullptr;
+  }
+  if (at.type != cudaMemoryTypeHost || !at.devicePointer) return nullptr;
+  return at.devicePointer;
+}
+
+tb_status launch_small_copy(void *dst, const void *src, size_t bytes, bool up, cudaStream_t s, const char *who) {
+  const int64_t n16 = (int64_t)(bytes / 16);
+  // four 16-byte elements per thread (kSmallCopyMax / 16 / 4 / 256 = 16 CTAs at most)
+  const int grid = (int)std::max<int64_t>(1, (n16 + 4 * 256 - 1) / (4 * 256));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = up ? cudaLaunchKernelEx(&cfg, small_copy_kernel<true>, static_cast<uint4 *>(dst),
+                                          static_cast<const uint4 *>(src), n16)
+                     : cudaLaunchKernelEx(&cfg, small_copy_kernel<false>, static_cast<uint4 *>(dst),
+                                          static_cast<const uint4 *>(src), n16);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "%s: %s", who, cudaGetErrorString(e));
+  return TB_OK;
+}
+}  // namespace
+}  // namespace tb
+
 using namespace tb;
 
 extern "C" {
@@ -222,6 +297,8 @@ tb_status tb_free(void *p) {
 tb_status tb_upload(void *dst, const void *src, size_t bytes, tb_stream s) {
   if (bytes == 0) return TB_OK;
   if (!dst || !src) return fail(TB_EINVAL, "tb_upload: null pointer");
+  const void *src_dev = small_pinned_alias(src, dst, bytes);
+  if (src_dev) return launch_small_copy(dst, src_dev, bytes, true, as_stream(s), "tb_upload");
   cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, as_stream(s));
   if (e != cudaSuccess) return fail(TB_ECUDA, "tb_upload: %s", cudaGetErrorString(e));
   return TB_OK;
@@ -230,6 +307,8 @@ tb_status tb_upload(void *dst, const void *src, size_t bytes, tb_stream s) {
 tb_status tb_download(void *dst, const void *src, size_t bytes, tb_stream s) {
   if (bytes == 0) return TB_OK;
   if (!dst || !src) return fail(TB_EINVAL, "tb_download: null pointer");
+  const void *dst_dev = small_pinned_alias(dst, src, bytes);
+  if (dst_dev) return launch_small_copy(const_cast<void *>(dst_dev), src, bytes, false, as_stream(s), "tb_download");
   cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, as_stream(s));
   if (e != cudaSuccess) return fail(TB_ECUDA, "tb_download: %s", cudaGetErrorString(e));
   return TB_OK;

@@ -162,11 +162,13 @@ def test_matmul_q8_0_default_within_tolerance(M, K, N):
     assert_dot_tol(run_matmul(T.Q8_0, x, wq, N, "tb_matmul_quant"), x, wq, K)
 
 
-def test_matmul_q8_0_digit_path_and_its_fallbacks():
-    # 8192 x 2048 at M = 1 takes x as int8 digits per block (dp4a); a block that
+@pytest.mark.parametrize("N,K", [(8192, 2048), (2048, 8192), (3000, 4096)])
+def test_matmul_q8_0_digit_path_and_its_fallbacks(N, K):
+    # M = 1 at K = 2048 takes x as int8 digits per block (dp4a); a block that
     # digits cannot hold (NaN, infinity, a tiny nonzero maximum) sends the
     # whole product to the fp32 dot; a block of wide range stays on digits.
-    N, K = 8192, 2048
+    # K = 4096 and 8192 (the decode's down projection) take the fp32 dot with
+    # the same special values.
     wq = synth.quantize_q8_0(synth.normal((N, K), 0.02, seed=41))
     base = synth.normal((1, K), 1.0, seed=42)
     cases = {"plain": base.copy(), "zeros": np.zeros((1, K), np.float32), "wide": base.copy(),
@@ -1032,7 +1034,7 @@ def _q8_dev(N, K, seed):
     return wq, dev(wq)
 
 
-@pytest.mark.parametrize("sizes,K", [((2048, 512, 512), 2048), ((37, 100, 5), 256), ((300,), 8192)])
+@pytest.mark.parametrize("sizes,K", [((2048, 512, 512), 2048), ((37, 100, 5), 256), ((300,), 8192), ((2048,), 8192)])
 def test_gemv_multi_segments_and_residual(sizes, K):
     # each segment within tolerance of the oracle; the residual epilogue is
     # exactly tb_binary(add) of the residual and the plain product

@@ -118,7 +118,14 @@ def test_tensor_parallel_gemv_nccl_two_gpus():
 def _abi_case(T, O, synth, group, rank, world, stream, rows=64, vocab=128256):
     """softmax and argmax of [rows, vocab] logits split by columns, and the
     row-split GEMV, on this rank's shard, against the oracle."""
-    x = synth.normal((rows, vocab), 2.0, seed=7)
+    _vocab_case(T, O, synth, group, rank, world, stream, rows, vocab)
+    _gemv_case(T, O, synth, group, rank, world, stream)
+
+
+def _vocab_case(T, O, synth, group, rank, world, stream, rows=64, vocab=128256, seed=7):
+    """softmax and argmax of [rows, vocab] logits split by columns against the
+    oracle: a tie across the shards, a row without candidates."""
+    x = synth.normal((rows, vocab), 2.0, seed=seed)
     x[5, 17] = 40.0
     x[5, vocab - 2] = 40.0  # a tie across the shards
     x[9, :] = -np.inf       # no candidate: index 0
@@ -141,7 +148,11 @@ def _abi_case(T, O, synth, group, rank, world, stream, rows=64, vocab=128256):
     want = (e / e.sum(axis=1, keepdims=True))[:, base:base + cols]
     got = y.cpu().numpy()
     assert np.max(np.abs(got - want) / np.maximum(want, want.max() * 1e-3)) <= 1e-5
-    # row-split Q8_0 GEMV, 8192 x 2048
+    assert T.take_device_errors() == 0
+
+
+def _gemv_case(T, O, synth, group, rank, world, stream):
+    """the row-split Q8_0 GEMV, 8192 x 2048, against the oracle"""
     N, K = 8192, 2048
     wq = synth.quantize_q8_0(synth.normal((N, K), 0.02, seed=31))
     xh = synth.normal((K,), 1.0, seed=32)
@@ -175,8 +186,11 @@ def _peer_case(T, O, synth, group, rank, world, stream):
     """The row-split GEMV with the rows exchanged by NVLink peer stores
     (tb_shard_group_enable_peer): the decode projections' shapes and the
     vocabulary-sized LM head (tensor-core GEMV per shard), several calls so
-    that both exchange buffers are used, each against the oracle."""
+    that both exchange buffers are used, each against the oracle; between
+    them the vocab-sharded softmax and argmax, whose (m, s) pairs and keys
+    take the same exchange (and its call numbers)."""
     T.call("tb_shard_group_enable_peer", group, 128256)
+    _vocab_case(T, O, synth, group, rank, world, stream, seed=8)
     for i, (N, K) in enumerate([(8192, 2048), (2048, 8192), (8192, 2048), (128256, 2048), (2048, 8192)]):
         wq = synth.quantize_q8_0(synth.normal((N, K), 0.02, seed=40 + i))
         xh = synth.normal((K,), 1.0, seed=50 + i)
@@ -192,6 +206,8 @@ def _peer_case(T, O, synth, group, rank, world, stream):
         got = yv.cpu().numpy()
         assert not np.isnan(got).any(), (rank, N, K)
         assert np.max(np.abs(got - ref) / _q8_scale(wq, xh, N, K)) <= 1e-5, (rank, N, K)
+        if i == 1:
+            _vocab_case(T, O, synth, group, rank, world, stream, rows=13, seed=9)
 
 
 def test_shard_group_abi_one_rank():

@@ -6,11 +6,13 @@
 // src/core/sampler.cpp:13-26, src/tensor/tensor.cpp:328-382); here each rank
 // holds a contiguous slice of the columns (logits) or rows (weights):
 //   softmax  per-shard row statistics (max m, sum of exp(x - m)) from
-//            tb_softmax_shard_stats, ONE all-gather of the (m, s) pairs, a
+//            tb_softmax_shard_stats, ONE all-gather of the (m, s) pairs (over
+//            NVLink peer memory after tb_shard_group_enable_peer), a
 //            combine in rank order (M = max m_r, S = sum_r s_r exp(m_r - M)),
 //            then tb_softmax_shard_finish writes exp(x - M) / S;
 //   argmax   per-shard 64-bit keys (tb_argmax_shard_keys), one int64 MAX
-//            all-reduce, then tb_argmax_key_index;
+//            all-reduce (or, with peer memory, a gather of the keys and a
+//            max over the ranks), then tb_argmax_key_index;
 //   GEMV     the rank's rows into its slot of y, one in-place all-gather; or,
 //            after tb_shard_group_enable_peer, the GEMV also writes its rows
 //            into this GPU's exchange buffer, and a small kernel on each rank
@@ -193,6 +195,34 @@ __global__ void peer_gather_kernel(PeerRegions pr, int n, int rank, int64_t cap,
   }
 }
 
+// This rank's n_local floats (the previous kernel's output) into its slot of
+// y and of its exchange buffer for the coming exchange call (e = count of
+// finished calls + 1, read after griddepcontrol.wait: the previous exchange
+// kernel set it), ahead of peer_gather_kernel.  The vocab-sharded softmax and
+// argmax send their per-row statistics and keys this way.
+__global__ void peer_stage_kernel(const float *__restrict__ src, int64_t n_local, uint8_t *xbase, int64_t cap,
+                                  int rank, float *__restrict__ y) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const unsigned long long e = *reinterpret_cast<volatile unsigned long long *>(xbase + 9 * 8) + 1;
+  float *dst = reinterpret_cast<float *>(xbase + 256) + (int64_t)(e & 1) * cap + (int64_t)rank * n_local;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n_local; i += (int64_t)gridDim.x * blockDim.x) {
+    const float v = src[i];
+    dst[i] = v;
+    y[(int64_t)rank * n_local + i] = v;
+  }
+}
+
+// out[r] = the largest of the ranks' keys for row r (signed 64-bit order,
+// as the all-reduce's ncclMax over ncclInt64)
+__global__ void combine_keys_kernel(const int64_t *__restrict__ g, int n, int rows, int64_t *__restrict__ out) {
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  int64_t k = g[r];
+  for (int j = 1; j < n; ++j) k = max(k, g[(int64_t)j * rows + r]);
+  out[r] = k;
+}
+
 }  // namespace
 }  // namespace tb
 
@@ -232,6 +262,31 @@ tb_status nccl_settle(NcclApi *api, ncclComm_t comm, ncclResult_t r, double time
   }
   if (r != ncclSuccess) return fail(TB_ERUNTIME, "%s: %s", what, api->GetErrorString(r));
   return TB_OK;
+}
+
+// Stages n_local floats of this rank (src) and gathers every rank's into
+// y[n][n_local] over NVLink peer memory (tb_shard_group_enable_peer).
+tb_status peer_exchange(tb_shard_group g, const float *src, int64_t n_local, float *y, cudaStream_t s,
+                        const char *who) {
+  DeviceState *st;
+  TB_TRY(device_state(&st));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, 1, 1);
+  cfg.blockDim = dim3(256, 1, 1);
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, peer_stage_kernel, src, n_local, g->xbase, (int64_t)g->xcap, g->rank, y);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "%s (stage): %s", who, cudaGetErrorString(e));
+  PeerRegions pr = {};
+  for (int j = 0; j < g->n; ++j) pr.r[j] = j == g->rank ? g->xbase : g->peer[j];
+  e = cudaLaunchKernelEx(&cfg, peer_gather_kernel, pr, g->n, g->rank, (int64_t)g->xcap, n_local, y,
+                         (uint64_t)wait_limit_ns(), st->err_word);
+  if (e != cudaSuccess) return fail(TB_ECUDA, "%s (exchange): %s", who, cudaGetErrorString(e));
+  return check_launch(who);
 }
 
 tb_status check_group(tb_shard_group g, const char *who) {
@@ -432,8 +487,12 @@ tb_status tb_softmax_vocab_sharded(tb_shard_group g, const float *x_dev, int64_t
   TB_TRY(tb_softmax_shard_stats(x_dev, rows, cols, ld, g->stats, g->stats + rows, stream));
   const float *gm = g->stats, *gs = g->stats + rows;
   if (g->n > 1) {
-    ncclResult_t r = api->AllGather(g->stats, g->gathered, (size_t)(2 * rows), ncclFloat32, g->comm, s);
-    TB_TRY(nccl_settle(api, g->comm, r, g->timeout_s, "tb_softmax_vocab_sharded(all-gather)"));
+    if (g->xbase && (int64_t)g->n * 2 * rows <= g->xcap) {  // the (m, s) pairs over NVLink peer memory
+      TB_TRY(peer_exchange(g, g->stats, 2 * rows, g->gathered, s, "tb_softmax_vocab_sharded"));
+    } else {
+      ncclResult_t r = api->AllGather(g->stats, g->gathered, (size_t)(2 * rows), ncclFloat32, g->comm, s);
+      TB_TRY(nccl_settle(api, g->comm, r, g->timeout_s, "tb_softmax_vocab_sharded(all-gather)"));
+    }
     combine_stats_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(g->gathered, g->n, (int)rows, g->gm, g->gs);
     TB_TRY(check_launch("tb_softmax_vocab_sharded"));
     gm = g->gm;
@@ -452,8 +511,17 @@ tb_status tb_argmax_vocab_sharded(tb_shard_group g, const float *x_dev, int64_t 
   TB_TRY(nccl_api(&api));
   TB_TRY(tb_argmax_shard_keys(x_dev, rows, cols, ld, col_base, g->keys, stream));
   if (g->n > 1) {
-    ncclResult_t r = api->AllReduce(g->keys, g->keys, (size_t)rows, ncclInt64, ncclMax, g->comm, as_stream(stream));
-    TB_TRY(nccl_settle(api, g->comm, r, g->timeout_s, "tb_argmax_vocab_sharded(all-reduce)"));
+    if (g->xbase && (int64_t)g->n * 2 * rows <= g->xcap) {  // the keys over NVLink peer memory
+      int64_t *all = reinterpret_cast<int64_t *>(g->gathered);  // [n][rows] keys
+      TB_TRY(peer_exchange(g, reinterpret_cast<const float *>(g->keys), 2 * rows, g->gathered, as_stream(stream),
+                           "tb_argmax_vocab_sharded"));
+      combine_keys_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, as_stream(stream)>>>(all, g->n, (int)rows,
+                                                                                          g->keys);
+      TB_TRY(check_launch("tb_argmax_vocab_sharded"));
+    } else {
+      ncclResult_t r = api->AllReduce(g->keys, g->keys, (size_t)rows, ncclInt64, ncclMax, g->comm, as_stream(stream));
+      TB_TRY(nccl_settle(api, g->comm, r, g->timeout_s, "tb_argmax_vocab_sharded(all-reduce)"));
+    }
   }
   return tb_argmax_key_index(g->keys, rows, idx_dev, stream);
 }

@@ -513,6 +513,26 @@ def run_sharded(reps=20, sizes=None, only=None):
                "W[%d,%d] Q8_0 rows split over %d ranks, rows exchanged by NVLink peer stores, CUDA graph of "
                "100 calls" % (N, K, ws))
         del w_local
+    if want("peer"):
+        # the vocab-sharded softmax and argmax through the C entries, (m, s)
+        # pairs and argmax keys exchanged over NVLink peer memory
+        V, rows = 128256, 64
+        base, cols = rank * V // ws, (rank + 1) * V // ws - rank * V // ws
+        full = torch.randn((rows, V), device=dev, generator=torch.Generator(dev).manual_seed(7)) * 2.0
+        local = full[:, base:base + cols].contiguous()
+        out = torch.empty_like(local)
+        idx = torch.empty(rows, dtype=torch.int64, device=dev)
+        ms = timed_graph(lambda sh_: T.check(L.tb_softmax_vocab_sharded(cgrp, T.ptr(local), rows, cols, cols,
+                                                                        T.ptr(out), cols, sh_)), 50)
+        report("vocab_sharded_softmax_peer", ms, 2 * 4 * rows * V,
+               "logits [%d,%d] split over %d ranks, (m, s) pairs over NVLink peer memory, CUDA graph of 50 calls"
+               % (rows, V, ws))
+        ms = timed_graph(lambda sh_: T.check(L.tb_argmax_vocab_sharded(cgrp, T.ptr(local), rows, cols, cols, base,
+                                                                       T.ptr(idx), sh_)), 50)
+        report("vocab_sharded_argmax_peer", ms, 4 * rows * V,
+               "logits [%d,%d] split over %d ranks, keys over NVLink peer memory, CUDA graph of 50 calls"
+               % (rows, V, ws))
+        del full, local, out
     torch.cuda.synchronize()
     dist.barrier()
     if cgrp:

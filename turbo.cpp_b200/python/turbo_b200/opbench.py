@@ -533,6 +533,24 @@ def run_sharded(reps=20, sizes=None, only=None):
                "logits [%d,%d] split over %d ranks, keys over NVLink peer memory, CUDA graph of 50 calls"
                % (rows, V, ws))
         del full, local, out
+        # a decode step's pick at the tied LM head: each rank's vocabulary
+        # rows (tensor-core GEMV), then the argmax over the ranks' logits
+        K = 2048
+        w_local = _rand_q8(torch, cols, K, seed=70 + rank)
+        x = torch.randn(K, device=dev, generator=torch.Generator(dev).manual_seed(71))
+        logits = torch.empty((1, cols), dtype=torch.float32, device=dev)
+        idx1 = torch.empty(1, dtype=torch.int64, device=dev)
+
+        def pick(sh_):
+            T.check(L.tb_matmul_quant(T.Q8_0, T.ptr(x), 1, K, T.ptr(w_local), cols, T.ptr(logits), sh_),
+                    "tb_matmul_quant")
+            T.check(L.tb_argmax_vocab_sharded(cgrp, T.ptr(logits), 1, cols, cols, base, T.ptr(idx1), sh_),
+                    "tb_argmax_vocab_sharded")
+        ms = timed_graph(pick, 50)
+        report("tp_lm_head_argmax_peer_%dx%d" % (V, K), ms, V * (K // 32 * 34) + K * 4 * ws + V * 4,
+               "LM head W[%d,%d] Q8_0 vocab rows split over %d ranks -> argmax keys over NVLink peer memory, "
+               "CUDA graph of 50 calls" % (V, K, ws))
+        del w_local
     torch.cuda.synchronize()
     dist.barrier()
     if cgrp:

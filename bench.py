@@ -407,7 +407,8 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": load_traffic(),
                      "peak_source": peak_kind, "kernel_us": round(kernel_ms * 1e3, 3),
-                     "timing": "CUDA events around the timed graph replays / launches"},
+                     "timing": "CUDA events on the launching stream, recorded inside the graph around its GEMVs"
+                               if in_graph else "CUDA events on the launching stream around the graph replays"},
         "e2e": {"value": round(e2e_gbs, 2), "unit": "GB/s", "h2d_bytes_per_step": K_COLS * 4,
                 "d2h_bytes_per_step": N_ROWS * 4, "steps": e2e_steps,
                 "note": "tb_upload(x) + tb_matmul_quant + tb_download(y) per step from pinned host buffers, "

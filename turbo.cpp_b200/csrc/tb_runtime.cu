@@ -171,17 +171,22 @@ __global__ void __launch_bounds__(256) small_copy_kernel(uint4 *__restrict__ dst
 }
 
 // The device address of `host` when it is page-locked memory mapped into the
-// device's address space and the copy qualifies for small_copy_kernel; else null.
+// device's address space, `dev` is device memory and the copy qualifies for
+// small_copy_kernel; else null (the DMA copy then runs, and reports a pointer
+// of the wrong kind as an error instead of a kernel touching it).
 const void *small_pinned_alias(const void *host, const void *dev, size_t bytes) {
   if (bytes > kSmallCopyMax || bytes % 16 != 0 || ((reinterpret_cast<uintptr_t>(host) |
                                                      reinterpret_cast<uintptr_t>(dev)) & 15) != 0)
     return nullptr;
-  cudaPointerAttributes at;
-  if (cudaPointerGetAttributes(&at, host) != cudaSuccess) {
+  cudaPointerAttributes at, ad;
+  if (cudaPointerGetAttributes(&at, host) != cudaSuccess || cudaPointerGetAttributes(&ad, dev) != cudaSuccess) {
     cudaGetLastError();  // not a pointer the runtime knows: pageable memory
     return nullptr;
   }
   if (at.type != cudaMemoryTypeHost || !at.devicePointer) return nullptr;
+  if (ad.type != cudaMemoryTypeDevice && ad.type != cudaMemoryTypeManaged) return nullptr;
+  int cur = -1;
+  if (cudaGetDevice(&cur) != cudaSuccess || ad.device != cur) return nullptr;  // another GPU's memory: DMA
   return at.devicePointer;
 }
 

@@ -60,7 +60,8 @@ __global__ void kv_append_kernel(float *__restrict__ kc, float *__restrict__ vc,
 //              (four consecutive key ranges, each an fma chain, added in order)
 //   out[d]   = (sum over r of o_r[d] exp(m_r - M)) * (1 / S), with M = max m_r
 //              and S = sum over r of s_r exp(m_r - M), both in rank order,
-//              combined by rank 0 from the cluster's distributed shared memory
+//              combined by rank 0 after every CTA has stored its (m_r, s_r, o_r)
+//              into rank 0's shared memory (distributed shared memory)
 // That is softmax(score) . V with the normalisation applied once per output
 // instead of once per key (within 1e-5 of sum p |v| of the exact result).
 // Latency is what bounds one token's attention, so the kernel makes one pass:
@@ -111,9 +112,9 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(const AttnArgs a,
   __shared__ __align__(16) float kn[ROPE ? D : 4];
   __shared__ float vn[ROPE ? D : 1];  // the new key (rotated) and value
   __shared__ float red[8];
-  __shared__ float part[2];           // this CTA's [m_r, s_r]
   __shared__ float pv[256 / D][D];    // partial outputs of the four key ranges
-  __shared__ float octa[D];           // this CTA's o_r
+  __shared__ float gpart[NC][2];      // rank 0: every CTA's [m_r, s_r], written by that CTA
+  __shared__ float gocta[NC][D];      // rank 0: every CTA's o_r, written by that CTA
   cg::cluster_group cluster = cg::this_cluster();
   const int cr = (int)cluster.block_rank();
   const int H = a.H, KVH = a.KVH;
@@ -217,32 +218,34 @@ __global__ void __launch_bounds__(256) attention_decode_kernel(const AttnArgs a,
   }
   pv[ch][d] = acc;
   __syncthreads();
+  // Every CTA stores its (m_r, s_r) and o_r into rank 0's shared memory; after
+  // the cluster barrier rank 0 combines them from its own memory, and no CTA
+  // reads another's, so the others may exit at once (one cluster barrier).
   if (t < D) {
     float o = pv[0][t];
     for (int k = 1; k < NCH; ++k) o = __fadd_rn(o, pv[k][t]);
-    octa[t] = o;
+    *cluster.map_shared_rank(&gocta[cr][t], 0) = o;
   }
   if (t == 0) {
     float tot = 0.f;
     for (int w = 0; w < 8; ++w) tot = __fadd_rn(tot, red[w]);
-    part[0] = m;
-    part[1] = tot;
+    *cluster.map_shared_rank(&gpart[cr][0], 0) = m;
+    *cluster.map_shared_rank(&gpart[cr][1], 0) = tot;
   }
   cluster.sync();
   if (cr == 0 && t < D) {
     float M = -INFINITY;
-    for (int r = 0; r < NC; ++r) M = fmaxf(M, *cluster.map_shared_rank(&part[0], r));
+    for (int r = 0; r < NC; ++r) M = fmaxf(M, gpart[r][0]);
     float S = 0.f, o = 0.f;
     for (int r = 0; r < NC; ++r) {
-      const float mr = *cluster.map_shared_rank(&part[0], r);
+      const float mr = gpart[r][0];
       if (mr == -INFINITY) continue;  // a CTA without keys
       const float w = __expf(__fsub_rn(mr, M));
-      S = __fadd_rn(S, __fmul_rn(*cluster.map_shared_rank(&part[1], r), w));
-      o = __fmaf_rn(*cluster.map_shared_rank(&octa[t], r), w, o);
+      S = __fadd_rn(S, __fmul_rn(gpart[r][1], w));
+      o = __fmaf_rn(gocta[r][t], w, o);
     }
     a.out[h * D + t] = __fmul_rn(o, __frcp_rn(S));
   }
-  cluster.sync();  // peers' shared memory stays alive until rank 0 has read it
 }
 
 template <bool ROPE>
